@@ -1,0 +1,204 @@
+/*
+ * egnn_b200.h — C ABI of libegnn_b200.so, the B200 (sm_100a) EGNN layer.
+ *
+ * The library replaces the E(n)-equivariant graph convolution of
+ * SatxaFortuny/PyMolecular, models/EGNN/egnn_clean.py:
+ *   E_GCL.forward            egnn_clean.py:95-103   -> egnn_layer_fwd
+ *   autograd of E_GCL         (implied by :49-103)   -> egnn_layer_bwd
+ *   unsorted_segment_sum/mean egnn_clean.py:149-164  -> fused into both
+ *   edge list -> dst CSR      egnn_clean.py:167-191, forward_kernel.py:19-21
+ *                                                    -> egnn_csr_build
+ * and the reference's fused-kernel entry points, which take the same CSR
+ * triple (row_ptr, col_indices, edge_id):
+ *   egnn_forward_kernel_node_parallel   forward_kernel.py:13-43
+ *   egnn_backward_kernel_node_parallel  backward_kernel.py:13-50
+ *
+ * Conventions
+ *  - Every pointer except descriptors is a DEVICE pointer of the current
+ *    device.  `stream` is a cudaStream_t passed as void* (NULL = legacy
+ *    default stream).  All calls are asynchronous on `stream` unless noted.
+ *  - The library allocates no device memory: callers pass `workspace` of at
+ *    least the size the matching *_workspace_size function returns.
+ *  - Edges are (row, col) = (destination i, source j), as in egnn_clean.py:85-86.
+ *    Aggregation runs over rows.  CSR order = stable sort of the edges by row.
+ *  - Tensors are dense row-major float32: h (N,H), x (N,3), edge_attr (E_in,d)
+ *    indexed by the ORIGINAL edge id.  Parameters use nn.Linear layout
+ *    W (out,in) row-major, b (out).
+ *  - Return value: EGNN_OK or an egnn_status code; egnn_last_error() gives a
+ *    message for the calling thread.
+ */
+#ifndef EGNN_B200_H
+#define EGNN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EGNN_API __attribute__((visibility("default")))
+#else
+#define EGNN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  EGNN_OK = 0,
+  EGNN_ERR_INVALID_ARG = 1,   /* null pointer, bad size, unsupported shape */
+  EGNN_ERR_INDEX = 2,         /* CSR / edge index out of range, row_ptr not monotone */
+  EGNN_ERR_CUDA = 3,          /* a CUDA runtime call failed */
+  EGNN_ERR_UNSUPPORTED = 4,   /* flag / size combination not built */
+  EGNN_ERR_WORKSPACE = 5      /* workspace too small */
+} egnn_status;
+
+/* Layer flags: the E_GCL constructor switches (egnn_clean.py:11). */
+enum {
+  EGNN_FLAG_RESIDUAL = 1,     /* residual=True   (egnn_clean.py:68-69) */
+  EGNN_FLAG_ATTENTION = 2,    /* attention=True  (egnn_clean.py:44-47, 55-57) */
+  EGNN_FLAG_NORMALIZE = 4,    /* normalize=True  (egnn_clean.py:89-91) */
+  EGNN_FLAG_TANH = 8,         /* tanh=True       (egnn_clean.py:40-41) */
+  EGNN_FLAG_COORDS_SUM = 16   /* coords_agg='sum' instead of 'mean' (egnn_clean.py:75-78) */
+};
+
+/* GEMM input precision. Accumulation and coordinates are always float32. */
+enum { EGNN_PREC_FP32 = 0, EGNN_PREC_BF16 = 1 };
+
+typedef struct {
+  int64_t n_nodes;        /* N */
+  int64_t n_edges;        /* E (< 2^31) */
+  int32_t hidden;         /* H = input_nf = output_nf = hidden_nf; multiple of 32, <= 256 */
+  int32_t edge_attr_dim;  /* edges_in_d (0..16) */
+  int32_t flags;          /* EGNN_FLAG_* */
+  int32_t precision;      /* EGNN_PREC_* */
+} egnn_layer_desc;
+
+/* A destination-sorted CSR and its transpose (built by egnn_csr_build /
+ * egnn_csr_transpose).  Positions k in [0,E) are CSR positions. */
+typedef struct {
+  const int32_t* row_ptr;   /* (N+1) edge offsets of each destination row */
+  const int32_t* col_idx;   /* (E) source node of CSR edge k */
+  const int32_t* row_idx;   /* (E) destination node of CSR edge k */
+  const int32_t* edge_id;   /* (E) original edge index of CSR edge k (edge_attr row) */
+  const int32_t* src_ptr;   /* (N+1) offsets of each source node in src order */
+  const int32_t* src_edge;  /* (E) CSR position of the k-th edge in src order */
+} egnn_graph;
+
+/* Parameters of one E_GCL (nn.Linear layout, float32). */
+typedef struct {
+  const float* edge_w1;  const float* edge_b1;   /* edge_mlp.0: (H, 2H+1+d), (H) */
+  const float* edge_w2;  const float* edge_b2;   /* edge_mlp.2: (H, H), (H)      */
+  const float* node_w1;  const float* node_b1;   /* node_mlp.0: (H, 2H), (H)     */
+  const float* node_w2;  const float* node_b2;   /* node_mlp.2: (H, H), (H)      */
+  const float* coord_w1; const float* coord_b1;  /* coord_mlp.0: (H, H), (H)     */
+  const float* coord_w2;                         /* coord_mlp.2: (1, H), no bias */
+  const float* att_w;    const float* att_b;     /* att_mlp.0: (1, H), (1); attention only */
+} egnn_layer_params;
+
+/* Gradient outputs, same shapes as egnn_layer_params; overwritten (not
+ * accumulated).  att_* may be NULL when attention is off. */
+typedef struct {
+  float* edge_w1;  float* edge_b1;
+  float* edge_w2;  float* edge_b2;
+  float* node_w1;  float* node_b1;
+  float* node_w2;  float* node_b2;
+  float* coord_w1; float* coord_b1;
+  float* coord_w2;
+  float* att_w;    float* att_b;
+} egnn_layer_grads;
+
+enum { EGNN_WS_FWD = 0, EGNN_WS_BWD = 1 };
+
+/* ---- graph construction ------------------------------------------------ */
+
+/* Scratch bytes egnn_csr_build / egnn_csr_transpose need. */
+EGNN_API size_t egnn_csr_workspace_size(int64_t n_nodes, int64_t n_edges);
+
+/* Stable sort of the edge list (row, col) (int64, length E) by row into a
+ * dst CSR: row_ptr (N+1), col_idx, row_idx, edge_id (E).  Validates every
+ * index; returns EGNN_ERR_INDEX on a row/col outside [0,N).  Synchronises
+ * `stream` (reads back the validation flag).  Replaces the host-side CSR of
+ * test_mem.py:62-65 / datasets_loaders.py:7-11. */
+EGNN_API int egnn_csr_build(int64_t n_nodes, int64_t n_edges, const int64_t* row, const int64_t* col,
+                   int32_t* row_ptr, int32_t* col_idx, int32_t* row_idx, int32_t* edge_id,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Transpose of a dst CSR: for each source node, the CSR positions of its
+ * out-edges in increasing position order.  Asynchronous. */
+EGNN_API int egnn_csr_transpose(int64_t n_nodes, int64_t n_edges, const int32_t* row_ptr,
+                       const int32_t* col_idx, int32_t* src_ptr, int32_t* src_edge,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Checks a caller-supplied CSR: row_ptr[0]=0, non-decreasing, row_ptr[N]=E,
+ * col_idx/row_idx in range and consistent with row_ptr, edge_id in [0,E).
+ * Synchronises `stream`.  EGNN_ERR_INDEX when it is malformed. */
+EGNN_API int egnn_graph_check(int64_t n_nodes, int64_t n_edges, const egnn_graph* g,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- layer ------------------------------------------------------------- */
+
+/* Bytes of per-layer state egnn_layer_fwd stores for egnn_layer_bwd. */
+EGNN_API size_t egnn_saved_size(const egnn_layer_desc* d);
+
+/* Scratch bytes for egnn_layer_fwd (which = EGNN_WS_FWD) or egnn_layer_bwd
+ * (EGNN_WS_BWD) on a device with `num_sms` SMs (0 = current device). */
+EGNN_API size_t egnn_workspace_size(const egnn_layer_desc* d, int which, int num_sms);
+
+/* E_GCL.forward (egnn_clean.py:95-103): h_out (N,H), x_out (N,3).
+ * edge_attr may be NULL iff d->edge_attr_dim == 0.  `saved` (may be NULL in
+ * inference) receives egnn_saved_size(d) bytes for the backward. */
+EGNN_API int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, const egnn_layer_params* p,
+                   const float* h, const float* x, const float* edge_attr,
+                   float* h_out, float* x_out, void* saved,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward of E_GCL given dL/dh_out, dL/dx_out: writes dL/dh, dL/dx and every
+ * parameter gradient.  Deterministic (no atomics): two calls on the same
+ * inputs give bit-identical outputs. */
+EGNN_API int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, const egnn_layer_params* p,
+                   const float* h, const float* x, const float* edge_attr, const void* saved,
+                   const float* grad_h_out, const float* grad_x_out,
+                   float* grad_h, float* grad_x, const egnn_layer_grads* gp,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- node linear (embedding_in / embedding_out, egnn_clean.py:133-134) --- */
+
+/* y (M,O) = x (M,K) W^T + b  (b may be NULL). */
+EGNN_API int egnn_linear_fwd(int64_t m, int32_t k, int32_t o, const float* x, const float* w,
+                    const float* b, float* y, void* stream);
+
+/* Scratch bytes for egnn_linear_bwd. */
+EGNN_API size_t egnn_linear_workspace_size(int64_t m, int32_t k, int32_t o);
+
+/* dx = dy W (may be NULL to skip), dW = dy^T x, db = sum_rows dy (may be NULL). */
+EGNN_API int egnn_linear_bwd(int64_t m, int32_t k, int32_t o, const float* x, const float* w,
+                    const float* dy, float* dx, float* dw, float* db,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- diagnostics ------------------------------------------------------- */
+
+/* Copies the calling thread's last error message into buf (NUL-terminated);
+ * returns the message length. */
+EGNN_API size_t egnn_last_error(char* buf, size_t len);
+
+/* Library version, e.g. "egnn_b200 0.1 sm_100a". */
+EGNN_API const char* egnn_version(void);
+
+/* Number of kernel launches this library issued (all threads) since the
+ * last call of egnn_launch_count_reset (for launch accounting). */
+EGNN_API uint64_t egnn_launch_count(void);
+EGNN_API void egnn_launch_count_reset(void);
+
+/* Kernel timer for benchmarks: while enabled, the fused edge kernels
+ * ("edge_fwd", "edge_bwd", "src_pass") are bracketed by CUDA events on their
+ * launching stream.  Enabling or disabling clears the records.
+ * egnn_kernel_time waits for the recorded events and returns the summed
+ * milliseconds and launch count of one kernel name. */
+EGNN_API void egnn_kernel_timing(int enable);
+EGNN_API int egnn_kernel_time(const char* name, double* total_ms, int64_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EGNN_B200_H */

@@ -1,0 +1,98 @@
+// Shared helpers of libegnn_b200: status/error plumbing, launch accounting,
+// activations and bf16 rounding.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stddef.h>
+#include <string>
+
+#include "egnn_b200.h"
+
+namespace egnn {
+
+// ---- error plumbing -------------------------------------------------------
+void set_error(int code, const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+void count_launch(int n = 1);
+
+// While egnn_kernel_timing(1) is on, brackets the kernels launched in its
+// lifetime with CUDA events on `s`, filed under `name`.
+struct TimerScope {
+  TimerScope(const char* name, cudaStream_t s);
+  ~TimerScope();
+  bool active;
+  cudaStream_t stream;
+  size_t index = 0;
+};
+
+#define EGNN_CHECK_CUDA(expr)                                                   \
+  do {                                                                          \
+    cudaError_t _e = (expr);                                                    \
+    if (_e != cudaSuccess)                                                      \
+      return ::egnn::fail(EGNN_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,        \
+                          cudaGetErrorString(_e), __FILE__, __LINE__);          \
+  } while (0)
+
+#define EGNN_CHECK_LAUNCH()                                                     \
+  do {                                                                          \
+    ::egnn::count_launch();                                                     \
+    cudaError_t _e = cudaGetLastError();                                        \
+    if (_e != cudaSuccess)                                                      \
+      return ::egnn::fail(EGNN_ERR_CUDA, "kernel launch failed: %s (%s:%d)",    \
+                          cudaGetErrorString(_e), __FILE__, __LINE__);          \
+  } while (0)
+
+#define EGNN_TRY(expr)                                                          \
+  do {                                                                          \
+    int _s = (expr);                                                            \
+    if (_s != EGNN_OK) return _s;                                               \
+  } while (0)
+
+int num_sms_current();
+// Bit of the current device (for per-device one-time setup flags).
+uint64_t device_bit();
+
+// ---- workspace carving ----------------------------------------------------
+// Sub-buffers are 256-byte aligned so every float4 / TMA access is aligned.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+  size_t size() const { return (off + 255) & ~size_t(255); }
+};
+
+// ---- device math ----------------------------------------------------------
+__device__ __forceinline__ float sigmoidf_(float x) {
+  return 1.0f / (1.0f + __expf(-x));
+}
+
+// SiLU and its derivative from the same sigmoid:
+//   silu(a) = a s,  silu'(a) = s (1 + a (1 - s)),  s = sigmoid(a).
+__device__ __forceinline__ float silu_f(float a) { return a * sigmoidf_(a); }
+
+__device__ __forceinline__ void silu_and_grad(float a, float& y, float& dy) {
+  float s = sigmoidf_(a);
+  y = a * s;
+  dy = s * (1.0f + a * (1.0f - s));
+}
+
+// Round-to-nearest-even to the bf16 grid, kept in a float register.
+__device__ __forceinline__ float bf16r(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+template <bool BF>
+__device__ __forceinline__ float maybe_bf(float v) {
+  if constexpr (BF) return bf16r(v); else return v;
+}
+
+}  // namespace egnn

@@ -1,0 +1,76 @@
+// Fused EGNN edge kernels (SIMT FFMA path): argument blocks and launchers.
+#pragma once
+
+#include "common.cuh"
+
+namespace egnn {
+
+// Fields shared by the forward and backward edge kernels.
+struct EdgeCommon {
+  int64_t N = 0, E = 0;
+  const int32_t* row_ptr = nullptr;
+  const int32_t* col_idx = nullptr;
+  const int32_t* row_idx = nullptr;
+  const int32_t* edge_id = nullptr;
+  const float4* xp = nullptr;    // (N) coordinates padded to 16 bytes
+  const float* PQ = nullptr;     // (N, 2H): P = h Wa^T + b1 | Q = h Wb^T
+  const float* wr = nullptr;     // (H) radial column of edge_mlp.0
+  const float* We = nullptr;     // (H, d) edge_attr columns of edge_mlp.0
+  const float* attr = nullptr;   // (E, d) edge attributes by original edge id
+  int d = 0;
+  const float* W2T = nullptr;    // (H,H) [k][o] = edge_mlp.2.weight[o][k]
+  const float* b2 = nullptr;
+  const float* Wc1T = nullptr;   // (H,H) [k][o] = coord_mlp.0.weight[o][k]
+  const float* bc1 = nullptr;
+  const float* wc2 = nullptr;    // (H) coord_mlp.2.weight
+  int flags = 0;
+  int64_t epc = 0;               // edges per CTA (multiple of the chunk size)
+  float* carry = nullptr;        // (G, 2, H+4) partial rows at CTA range edges
+  int32_t* carry_row = nullptr;  // (G, 2)
+};
+
+struct EdgeFwdArgs : EdgeCommon {
+  const float* x = nullptr;      // (N,3)
+  float* agg = nullptr;          // (N,H) out: sum of messages per row
+  float* x_out = nullptr;        // (N,3) out
+};
+
+struct EdgeBwdArgs : EdgeCommon {
+  const float* W2 = nullptr;     // (H,H) edge_mlp.2.weight (bf16-rounded in bf16 mode)
+  const float* Wc1 = nullptr;    // (H,H) coord_mlp.0.weight (idem)
+  const float* gx_out = nullptr; // (N,3) dL/dx'
+  const float* g_agg = nullptr;  // (N,H) dL/dagg from the node MLP backward
+  float* S_dst = nullptr;        // (N,H) out: sum over each row of dL/da1
+  float* gxd = nullptr;          // (N,3) out: sum over each row of dL/d(x_i - x_j)
+  float* gstore = nullptr;       // (E,H) out: dL/da1 per CSR edge
+  float4* gdstore = nullptr;     // (E) out: dL/d(x_i - x_j) per CSR edge
+  float* part = nullptr;         // (G, part_floats(H,d)) per-CTA weight-gradient partials
+};
+
+// Per-CTA partial layout (floats): gWc1 (H*H) | gW2 (H*H) | gbc1 | gb2 | gwc2 | gwr (H each)
+// | gWe (H*d).
+__host__ __device__ inline int64_t edge_part_floats(int H, int d) {
+  int64_t n = 2LL * H * H + 4LL * H + (int64_t)H * d;
+  return (n + 63) / 64 * 64;
+}
+
+// Launch geometry for a given E: CTA count and edges per CTA.
+struct EdgeGrid { int G; int64_t epc; };
+int edge_grid(int H, bool bwd, bool bf16, int64_t E, int num_sms, EdgeGrid* out);
+int edge_chunk(int H);
+
+int edge_fwd(int H, bool bf16, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s);
+int edge_bwd(int H, bool bf16, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s);
+
+// Source-side pass of the backward: S_src[j] = sum of gstore over the
+// out-edges of j (transpose CSR order), gx[j] = gx_out[j] + gxd[j] - sum gd.
+int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_edge,
+                  const float* gstore, const float4* gdstore, const float* gx_out,
+                  const float* gxd, float* S_src, float* gx, cudaStream_t s);
+
+// Reduce the G per-CTA partials in CTA order and scatter them into the
+// parameter-gradient outputs.
+int edge_part_reduce(int H, int d, int G, const float* part, const egnn_layer_grads* gp,
+                     int64_t ld_w1, cudaStream_t s);
+
+}  // namespace egnn

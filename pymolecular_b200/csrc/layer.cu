@@ -1,0 +1,401 @@
+// C ABI of the EGNN layer: argument checks, workspace layout and the
+// sequence of node GEMMs and fused edge kernels for one E_GCL forward and
+// backward (egnn_clean.py:95-103 and its autograd).
+//
+// Forward:  PQ = h [Wa; Wb]^T + [b1; 0]            node GEMM (N x 2H)
+//           edge_fwd: agg, x'                      fused edge kernel + fix-up
+//           n1 = silu([h, agg] Wn1^T + bn1)        node GEMM
+//           h' = h + n1 Wn2^T + bn2                node GEMM
+// Backward: node-MLP backward (GEMMs), edge_bwd (dst pass, recompute),
+//           src pass through the transpose CSR, then the W1 gradients and
+//           dL/dh by node GEMMs.
+#include <algorithm>
+
+#include "edge_simt.cuh"
+#include "node_gemm.cuh"
+
+namespace egnn {
+namespace {
+
+bool valid_hidden(int H) { return H == 32 || H == 64 || H == 128 || H == 256; }
+
+int check_desc(const egnn_layer_desc* d) {
+  if (!d) return fail(EGNN_ERR_INVALID_ARG, "null layer descriptor");
+  if (d->n_nodes < 0 || d->n_edges < 0 || d->n_nodes >= INT32_MAX || d->n_edges >= INT32_MAX)
+    return fail(EGNN_ERR_INVALID_ARG, "N=%lld / E=%lld out of range", (long long)d->n_nodes,
+                (long long)d->n_edges);
+  if (!valid_hidden(d->hidden))
+    return fail(EGNN_ERR_UNSUPPORTED, "hidden size %d not built (32, 64, 128, 256)", d->hidden);
+  if (d->edge_attr_dim < 0 || d->edge_attr_dim > 16)
+    return fail(EGNN_ERR_UNSUPPORTED, "edge_attr_dim %d not built (0..16)", d->edge_attr_dim);
+  if (d->flags & ~31) return fail(EGNN_ERR_INVALID_ARG, "unknown flag bits 0x%x", d->flags);
+  if (d->flags & EGNN_FLAG_ATTENTION)
+    return fail(EGNN_ERR_UNSUPPORTED, "attention=True is not built in this version");
+  if (d->precision != EGNN_PREC_FP32 && d->precision != EGNN_PREC_BF16)
+    return fail(EGNN_ERR_INVALID_ARG, "unknown precision %d", d->precision);
+  return EGNN_OK;
+}
+
+int resolve_sms(int num_sms) { return num_sms > 0 ? num_sms : num_sms_current(); }
+
+// Upper bound on the edge-kernel CTA count (occupancy is at most 8 CTAs of
+// 256 threads per SM).
+int64_t max_ctas(int64_t E, int H, int num_sms) {
+  const int T = edge_chunk(H);
+  int64_t chunks = std::max<int64_t>(1, (E + T - 1) / T);
+  return std::min<int64_t>(chunks, (int64_t)num_sms * 8);
+}
+
+// Prepared operands shared by the forward and the backward.
+struct Prep {
+  float4* xp; float* bias2; float* W2T; float* Wc1T; float* W2r; float* Wc1r; float* wr; float* We;
+};
+
+Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd) {
+  Prep p{};
+  p.xp = c.take<float4>(std::max<int64_t>(N, 1));
+  p.bias2 = c.take<float>(2 * H);
+  p.W2T = c.take<float>((size_t)H * H);
+  p.Wc1T = c.take<float>((size_t)H * H);
+  p.W2r = bwd ? c.take<float>((size_t)H * H) : nullptr;
+  p.Wc1r = bwd ? c.take<float>((size_t)H * H) : nullptr;
+  p.wr = c.take<float>(H);
+  p.We = c.take<float>((size_t)H * std::max(d, 1));
+  return p;
+}
+
+__global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_layer_params p,
+                            const float* x, Prep o) {
+  const int64_t HH = (int64_t)H * H;
+  const int64_t total = N + 2 * H + 4 * HH + H + (int64_t)H * d;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t t = idx;
+    if (t < N) { o.xp[t] = make_float4(x[t * 3], x[t * 3 + 1], x[t * 3 + 2], 0.f); continue; }
+    t -= N;
+    if (t < 2 * H) { o.bias2[t] = t < H ? p.edge_b1[t] : 0.f; continue; }
+    t -= 2 * H;
+    if (t < 4 * HH) {
+      const int which = (int)(t / HH);
+      const int64_t r = t % HH, k = r / H, n = r % H;   // (k, n) of a [k][n] matrix
+      float v;
+      switch (which) {
+        case 0: v = p.edge_w2[n * H + k]; if (o.W2T) o.W2T[r] = bf ? bf16r(v) : v; break;
+        case 1: v = p.coord_w1[n * H + k]; if (o.Wc1T) o.Wc1T[r] = bf ? bf16r(v) : v; break;
+        case 2: v = p.edge_w2[r]; if (o.W2r) o.W2r[r] = bf ? bf16r(v) : v; break;
+        default: v = p.coord_w1[r]; if (o.Wc1r) o.Wc1r[r] = bf ? bf16r(v) : v; break;
+      }
+      continue;
+    }
+    t -= 4 * HH;
+    if (t < H) { o.wr[t] = p.edge_w1[t * ld1 + 2 * H]; continue; }
+    t -= H;
+    { const int64_t f = t / d, a = t % d; o.We[f * d + a] = p.edge_w1[f * ld1 + 2 * H + 1 + a]; }
+  }
+}
+
+int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_params* p,
+                const float* x, const Prep& o, cudaStream_t s) {
+  const int64_t total = N + 2 * H + 4LL * H * H + H + (int64_t)H * d;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
+  prep_kernel<<<blocks, 256, 0, s>>>(N, H, d, ld1, bf ? 1 : 0, *p, x, o);
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+int gemm_pq(int64_t N, int H, int64_t ld1, bool bf, const float* h, const float* W1,
+            const float* bias2, float* PQ, cudaStream_t s) {
+  GemmArgs g;
+  g.M = N; g.N = 2 * H; g.K = H;
+  g.A = mat(h, H);
+  g.B = mat_rows(W1, ld1, H, W1 + H, ld1); g.b_t = 1;
+  g.bias = bias2;
+  g.C = PQ; g.ldc = 2 * H;
+  g.round_bf16 = bf;
+  return gemm(g, s);
+}
+
+struct FwdWs {
+  Prep prep; float* PQ; float* n1; float* carry; int32_t* carry_row; float* agg_tmp;
+};
+
+FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
+  const int64_t N = d->n_nodes, E = d->n_edges;
+  const int H = d->hidden;
+  FwdWs w;
+  w.prep = carve_prep(c, N, H, d->edge_attr_dim, false);
+  w.PQ = c.take<float>((size_t)std::max<int64_t>(N, 1) * 2 * H);
+  w.n1 = c.take<float>((size_t)std::max<int64_t>(N, 1) * H);
+  const int64_t G = max_ctas(E, H, num_sms);
+  w.carry = c.take<float>((size_t)G * 2 * (H + 4));
+  w.carry_row = c.take<int32_t>((size_t)G * 2);
+  w.agg_tmp = c.take<float>((size_t)std::max<int64_t>(N, 1) * H);   // when no saved buffer
+  return w;
+}
+
+struct BwdWs {
+  Prep prep; float* PQ; float* n1pre; float* n1; float* g_n1pre; float* gh_acc; float* g_agg;
+  float* S_dst; float* S_src; float* gxd; float* gstore; float4* gdstore; float* carry;
+  int32_t* carry_row; float* part; float* wpart;
+};
+
+int64_t wpart_floats(int64_t N, int H) {
+  int64_t a = wgrad_splits(N, H, 2 * H) * (int64_t)H * 2 * H;
+  int64_t b = wgrad_splits(N, H, H) * (int64_t)H * H;
+  int64_t c = colsum_splits(N) * (int64_t)2 * H;
+  return std::max<int64_t>({a, b, c, 1});
+}
+
+BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
+  const int64_t N = std::max<int64_t>(d->n_nodes, 1), E = d->n_edges;
+  const int H = d->hidden;
+  BwdWs w;
+  w.prep = carve_prep(c, N, H, d->edge_attr_dim, true);
+  w.PQ = c.take<float>((size_t)N * 2 * H);
+  w.n1pre = c.take<float>((size_t)N * H);
+  w.n1 = c.take<float>((size_t)N * H);
+  w.g_n1pre = c.take<float>((size_t)N * H);
+  w.gh_acc = c.take<float>((size_t)N * H);
+  w.g_agg = c.take<float>((size_t)N * H);
+  w.S_dst = c.take<float>((size_t)N * H);
+  w.S_src = c.take<float>((size_t)N * H);
+  w.gxd = c.take<float>((size_t)N * 3);
+  w.gstore = c.take<float>((size_t)std::max<int64_t>(E, 1) * H);
+  w.gdstore = c.take<float4>((size_t)std::max<int64_t>(E, 1));
+  const int64_t G = max_ctas(E, H, num_sms);
+  w.carry = c.take<float>((size_t)G * 2 * (H + 4));
+  w.carry_row = c.take<int32_t>((size_t)G * 2);
+  w.part = c.take<float>((size_t)G * edge_part_floats(H, d->edge_attr_dim));
+  w.wpart = c.take<float>((size_t)wpart_floats(N, H));
+  return w;
+}
+
+bool missing_params(const egnn_layer_params* p) {
+  return !p || !p->edge_w1 || !p->edge_b1 || !p->edge_w2 || !p->edge_b2 || !p->node_w1 ||
+         !p->node_b1 || !p->node_w2 || !p->node_b2 || !p->coord_w1 || !p->coord_b1 || !p->coord_w2;
+}
+
+bool missing_graph(const egnn_graph* g, bool bwd, bool attr) {
+  if (!g || !g->row_ptr || !g->col_idx || !g->row_idx) return true;
+  if (attr && !g->edge_id) return true;
+  if (bwd && (!g->src_ptr || !g->src_edge)) return true;
+  return false;
+}
+
+void fill_common(EdgeCommon& a, const egnn_layer_desc* d, const egnn_graph* g, const Prep& pr,
+                 const float* PQ, const float* edge_attr, const egnn_layer_params* p, const EdgeGrid& eg) {
+  a.N = d->n_nodes; a.E = d->n_edges;
+  a.row_ptr = g->row_ptr; a.col_idx = g->col_idx; a.row_idx = g->row_idx; a.edge_id = g->edge_id;
+  a.xp = pr.xp; a.PQ = PQ; a.wr = pr.wr; a.We = pr.We; a.attr = edge_attr; a.d = d->edge_attr_dim;
+  a.W2T = pr.W2T; a.b2 = p->edge_b2; a.Wc1T = pr.Wc1T; a.bc1 = p->coord_b1; a.wc2 = p->coord_w2;
+  a.flags = d->flags; a.epc = eg.epc;
+}
+
+}  // namespace
+}  // namespace egnn
+
+using namespace egnn;
+
+extern "C" size_t egnn_saved_size(const egnn_layer_desc* d) {
+  if (!d) return 0;
+  return (size_t)std::max<int64_t>(d->n_nodes, 1) * d->hidden * sizeof(float);
+}
+
+extern "C" size_t egnn_workspace_size(const egnn_layer_desc* d, int which, int num_sms) {
+  if (!d || check_desc(d) != EGNN_OK) return 0;
+  const int sms = resolve_sms(num_sms);
+  Carver c(nullptr);
+  if (which == EGNN_WS_FWD) carve_fwd(c, d, sms); else carve_bwd(c, d, sms);
+  return c.size();
+}
+
+extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, const egnn_layer_params* p,
+                              const float* h, const float* x, const float* edge_attr, float* h_out,
+                              float* x_out, void* saved, void* ws, size_t ws_bytes, void* stream) {
+  EGNN_TRY(check_desc(d));
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t N = d->n_nodes, E = d->n_edges;
+  const int H = d->hidden, dd = d->edge_attr_dim;
+  const bool bf = d->precision == EGNN_PREC_BF16;
+  if (N == 0) return EGNN_OK;
+  if (missing_params(p) || missing_graph(g, false, dd > 0) || !h || !x || !h_out || !x_out ||
+      (dd > 0 && !edge_attr))
+    return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_fwd: null pointer argument");
+  const int sms = num_sms_current();
+  Carver probe(nullptr);
+  carve_fwd(probe, d, sms);
+  if (!ws || ws_bytes < probe.size())
+    return fail(EGNN_ERR_WORKSPACE, "egnn_layer_fwd: workspace %zu < %zu bytes", ws_bytes, probe.size());
+  Carver c(ws);
+  FwdWs w = carve_fwd(c, d, sms);
+  const int64_t ld1 = 2 * H + 1 + dd;
+  float* agg = saved ? static_cast<float*>(saved) : w.agg_tmp;
+
+  EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
+  EGNN_TRY(gemm_pq(N, H, ld1, bf, h, p->edge_w1, w.prep.bias2, w.PQ, s));
+
+  EdgeGrid eg;
+  EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));
+  EdgeFwdArgs a;
+  fill_common(a, d, g, w.prep, w.PQ, edge_attr, p, eg);
+  a.carry = w.carry; a.carry_row = w.carry_row;
+  a.x = x; a.agg = agg; a.x_out = x_out;
+  EGNN_TRY(edge_fwd(H, bf, a, eg, s));
+
+  GemmArgs n1;
+  n1.M = N; n1.N = H; n1.K = 2 * H;
+  n1.A = mat_cols(h, H, H, agg, H);
+  n1.B = mat(p->node_w1, 2 * H); n1.b_t = 1;
+  n1.bias = p->node_b1; n1.act = ACT_SILU;
+  n1.C = w.n1; n1.ldc = H; n1.round_bf16 = bf;
+  EGNN_TRY(gemm(n1, s));
+
+  GemmArgs n2;
+  n2.M = N; n2.N = H; n2.K = H;
+  n2.A = mat(w.n1, H);
+  n2.B = mat(p->node_w2, H); n2.b_t = 1;
+  n2.bias = p->node_b2;
+  if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = H; }
+  n2.C = h_out; n2.ldc = H; n2.round_bf16 = bf;
+  EGNN_TRY(gemm(n2, s));
+  return EGNN_OK;
+}
+
+extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, const egnn_layer_params* p,
+                              const float* h, const float* x, const float* edge_attr, const void* saved,
+                              const float* gh_out, const float* gx_out, float* grad_h, float* grad_x,
+                              const egnn_layer_grads* gp, void* ws, size_t ws_bytes, void* stream) {
+  EGNN_TRY(check_desc(d));
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t N = d->n_nodes, E = d->n_edges;
+  const int H = d->hidden, dd = d->edge_attr_dim;
+  const bool bf = d->precision == EGNN_PREC_BF16;
+  const bool residual = d->flags & EGNN_FLAG_RESIDUAL;
+  if (missing_params(p) || missing_graph(g, true, dd > 0) || !h || !x || !saved || !gh_out ||
+      !gx_out || !grad_h || !grad_x || !gp || (dd > 0 && !edge_attr))
+    return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_bwd: null pointer argument");
+  if (!gp->edge_w1 || !gp->edge_b1 || !gp->edge_w2 || !gp->edge_b2 || !gp->node_w1 || !gp->node_b1 ||
+      !gp->node_w2 || !gp->node_b2 || !gp->coord_w1 || !gp->coord_b1 || !gp->coord_w2)
+    return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_bwd: null gradient output");
+  const int sms = num_sms_current();
+  Carver probe(nullptr);
+  carve_bwd(probe, d, sms);
+  if (!ws || ws_bytes < probe.size())
+    return fail(EGNN_ERR_WORKSPACE, "egnn_layer_bwd: workspace %zu < %zu bytes", ws_bytes, probe.size());
+  Carver c(ws);
+  BwdWs w = carve_bwd(c, d, sms);
+  const int64_t ld1 = 2 * H + 1 + dd;
+  const float* agg = static_cast<const float*>(saved);
+  if (N == 0) return EGNN_OK;
+
+  EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
+  EGNN_TRY(gemm_pq(N, H, ld1, bf, h, p->edge_w1, w.prep.bias2, w.PQ, s));
+
+  // ---- node MLP backward: h' = [h +] Wn2 silu(Wn1 [h, agg] + bn1) + bn2
+  {
+    GemmArgs n1;
+    n1.M = N; n1.N = H; n1.K = 2 * H;
+    n1.A = mat_cols(h, H, H, agg, H);
+    n1.B = mat(p->node_w1, 2 * H); n1.b_t = 1;
+    n1.bias = p->node_b1; n1.act = ACT_SILU;
+    n1.pre = w.n1pre; n1.ldp = H;
+    n1.C = w.n1; n1.ldc = H; n1.round_bf16 = bf;
+    EGNN_TRY(gemm(n1, s));
+  }
+  EGNN_TRY(wgrad(N, H, H, mat(gh_out, H), mat(w.n1, H), gp->node_w2, H, gp->node_b2, bf, w.wpart, s));
+  {
+    GemmArgs gn;
+    gn.M = N; gn.N = H; gn.K = H;
+    gn.A = mat(gh_out, H);
+    gn.B = mat(p->node_w2, H); gn.b_t = 0;
+    gn.act = ACT_DSILU; gn.aux = w.n1pre; gn.ldaux = H;
+    gn.C = w.g_n1pre; gn.ldc = H; gn.round_bf16 = bf;
+    EGNN_TRY(gemm(gn, s));
+  }
+  EGNN_TRY(wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
+                 gp->node_b1, bf, w.wpart, s));
+  {
+    GemmArgs gh;
+    gh.M = N; gh.N = H; gh.K = H;
+    gh.A = mat(w.g_n1pre, H);
+    gh.B = mat(p->node_w1, 2 * H); gh.b_t = 0;
+    if (residual) { gh.resid = gh_out; gh.ldr = H; }
+    gh.C = w.gh_acc; gh.ldc = H; gh.round_bf16 = bf;
+    EGNN_TRY(gemm(gh, s));
+    GemmArgs ga = gh;
+    ga.B = mat(p->node_w1 + H, 2 * H);
+    ga.resid = nullptr;
+    ga.C = w.g_agg;
+    EGNN_TRY(gemm(ga, s));
+  }
+
+  // ---- edge backward: dst pass, fix-up, partial reduction, src pass
+  EdgeGrid eg;
+  EGNN_TRY(edge_grid(H, true, bf, E, sms, &eg));
+  EdgeBwdArgs a;
+  fill_common(a, d, g, w.prep, w.PQ, edge_attr, p, eg);
+  a.carry = w.carry; a.carry_row = w.carry_row;
+  a.W2 = bf ? w.prep.W2r : p->edge_w2;
+  a.Wc1 = bf ? w.prep.Wc1r : p->coord_w1;
+  a.gx_out = gx_out; a.g_agg = w.g_agg;
+  a.S_dst = w.S_dst; a.gxd = w.gxd; a.gstore = w.gstore; a.gdstore = w.gdstore; a.part = w.part;
+  EGNN_TRY(edge_bwd(H, bf, a, eg, s));
+  EGNN_TRY(edge_part_reduce(H, dd, eg.G, w.part, gp, ld1, s));
+  EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, w.gdstore, gx_out, w.gxd, w.S_src,
+                         grad_x, s));
+
+  // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb ;  dWa, dWb, db1
+  {
+    GemmArgs gh;
+    gh.M = N; gh.N = H; gh.K = 2 * H;
+    gh.A = mat_cols(w.S_dst, H, H, w.S_src, H);
+    gh.B = mat_rows(p->edge_w1, ld1, H, p->edge_w1 + H, ld1); gh.b_t = 0;
+    gh.resid = w.gh_acc; gh.ldr = H;
+    gh.C = grad_h; gh.ldc = H; gh.round_bf16 = bf;
+    EGNN_TRY(gemm(gh, s));
+  }
+  EGNN_TRY(wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart, s));
+  EGNN_TRY(wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, bf, w.wpart, s));
+  return EGNN_OK;
+}
+
+extern "C" int egnn_linear_fwd(int64_t m, int32_t k, int32_t o, const float* x, const float* w,
+                               const float* b, float* y, void* stream) {
+  if (m < 0 || k <= 0 || o <= 0) return fail(EGNN_ERR_INVALID_ARG, "egnn_linear_fwd: bad shape");
+  if (m == 0) return EGNN_OK;
+  if (!x || !w || !y) return fail(EGNN_ERR_INVALID_ARG, "egnn_linear_fwd: null pointer");
+  GemmArgs g;
+  g.M = m; g.N = o; g.K = k;
+  g.A = mat(x, k);
+  g.B = mat(w, k); g.b_t = 1;
+  g.bias = b;
+  g.C = y; g.ldc = o;
+  return gemm(g, (cudaStream_t)stream);
+}
+
+extern "C" size_t egnn_linear_workspace_size(int64_t m, int32_t k, int32_t o) {
+  Carver c(nullptr);
+  c.take<float>((size_t)std::max<int64_t>(
+      {wgrad_splits(m, o, k) * (int64_t)o * k, colsum_splits(m) * (int64_t)o, 1}));
+  return c.size();
+}
+
+extern "C" int egnn_linear_bwd(int64_t m, int32_t k, int32_t o, const float* x, const float* w,
+                               const float* dy, float* dx, float* dw, float* db, void* ws,
+                               size_t ws_bytes, void* stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  if (m < 0 || k <= 0 || o <= 0) return fail(EGNN_ERR_INVALID_ARG, "egnn_linear_bwd: bad shape");
+  if (!x || !w || !dy || !dw) return fail(EGNN_ERR_INVALID_ARG, "egnn_linear_bwd: null pointer");
+  if (!ws || ws_bytes < egnn_linear_workspace_size(m, k, o))
+    return fail(EGNN_ERR_WORKSPACE, "egnn_linear_bwd: workspace too small");
+  float* part = static_cast<float*>(ws);
+  if (dx && m > 0) {
+    GemmArgs g;
+    g.M = m; g.N = k; g.K = o;
+    g.A = mat(dy, o);
+    g.B = mat(w, k); g.b_t = 0;
+    g.C = dx; g.ldc = k;
+    EGNN_TRY(gemm(g, s));
+  }
+  return wgrad(m, o, k, mat(dy, o), mat(x, k), dw, k, db, 0, part, s);
+}

@@ -1,0 +1,76 @@
+// Node-side dense GEMMs of the EGNN layer (embedding, phi_e layer-1
+// projections, node MLP and their gradients).  These run over N rows, an
+// order of magnitude fewer than the E edge rows of the fused edge kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace egnn {
+
+// A logical row-major matrix that may be the concatenation of two buffers,
+// either side by side (split on columns, e.g. cat([h, agg], 1)) or stacked
+// (split on rows).  at(r, c) is element (r, c).
+struct Mat {
+  const float* p0 = nullptr;
+  const float* p1 = nullptr;
+  int64_t ld0 = 0, ld1 = 0;
+  int64_t split = INT64_MAX;   // columns (or rows) < split live in p0
+  int split_rows = 0;
+  __device__ __forceinline__ float at(int64_t r, int64_t c) const {
+    if (split_rows) {
+      return r < split ? p0[r * ld0 + c] : p1[(r - split) * ld1 + c];
+    }
+    return c < split ? p0[r * ld0 + c] : p1[r * ld1 + (c - split)];
+  }
+};
+
+inline Mat mat(const float* p, int64_t ld) { Mat m; m.p0 = p; m.ld0 = ld; return m; }
+inline Mat mat_cols(const float* a, int64_t lda, int64_t ka, const float* b, int64_t ldb) {
+  Mat m; m.p0 = a; m.ld0 = lda; m.p1 = b; m.ld1 = ldb; m.split = ka; return m;
+}
+inline Mat mat_rows(const float* a, int64_t lda, int64_t ra, const float* b, int64_t ldb) {
+  Mat m; m.p0 = a; m.ld0 = lda; m.p1 = b; m.ld1 = ldb; m.split = ra; m.split_rows = 1; return m;
+}
+
+enum { ACT_NONE = 0, ACT_SILU = 1, ACT_DSILU = 2 };
+
+// C (M,N) = epilogue( op(A) (M,K) * op(B) (K,N) ).
+//   a_t: A(m,k) = A.at(k,m) (else A.at(m,k));  b_t: B(k,n) = B.at(n,k) (nn.Linear W).
+// Epilogue: v = acc + bias[n];  pre[m,n] = v (if pre);
+//   act SILU: v = silu(v);  act DSILU: v = v * silu'(aux[m,n]);
+//   v += resid[m,n] (if resid);  C[m,n] = v.
+// Split-K (ksplit > 1): grid.z slices of the K range write raw partial sums
+// to part[z][M][N]; gemm_reduce() then adds the slices in slice order.
+struct GemmArgs {
+  int64_t M = 0, N = 0, K = 0;
+  Mat A, B;
+  int a_t = 0, b_t = 0;
+  float* C = nullptr; int64_t ldc = 0;
+  const float* bias = nullptr;
+  float* pre = nullptr; int64_t ldp = 0;
+  int act = ACT_NONE;
+  const float* aux = nullptr; int64_t ldaux = 0;
+  const float* resid = nullptr; int64_t ldr = 0;
+  int round_bf16 = 0;           // round A and B elements to bf16 (bf16-GEMM mode)
+  int ksplit = 1;
+  float* part = nullptr;
+};
+
+int gemm(const GemmArgs& a, cudaStream_t s);
+
+// Workspace floats gemm() needs for its split-K partials when used as a
+// weight-gradient GEMM with reduction length K.
+int64_t wgrad_splits(int64_t K, int64_t M, int64_t N);
+
+// Weight gradient dW (M,N) = sum_r G[r, m] * X[r, n]  over r in [0,R),
+// plus optional db[m] = sum_r G[r, m].  Deterministic split-K.
+// `part` must hold wgrad_splits(R,M,N) * (M*N + M) floats.
+int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw,
+          float* db, int round_bf16, float* part, cudaStream_t s);
+
+// Column sums db[c] = sum_r G[r,c] (deterministic, 2-level).  part holds
+// colsum_splits(R) * C floats.
+int64_t colsum_splits(int64_t R);
+int colsum(int64_t R, int64_t C, Mat G, float* db, float* part, cudaStream_t s);
+
+}  // namespace egnn

@@ -1,0 +1,117 @@
+"""Host-side checks that need no GPU: the C ABI library loads and exports every
+declared symbol, size queries behave, and the module API mirrors the reference."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+import torch
+from torch import nn
+
+from conftest import ROOT, load_golden
+from pymolecular_b200 import _native as nat
+from pymolecular_b200 import EGNN, E_GCL
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "egnn_b200.h").read_text()
+    return sorted(set(re.findall(r"EGNN_API\s+[\w\s\*]+?\b(egnn_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_abi():
+    syms = declared_symbols()
+    for name in ["egnn_csr_build", "egnn_csr_transpose", "egnn_layer_fwd", "egnn_layer_bwd",
+                 "egnn_workspace_size", "egnn_last_error"]:
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = nat.lib()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(declared_symbols()) == set(nat.EXPORTED)
+
+
+def test_version_and_error_plumbing():
+    lib = nat.lib()
+    assert lib.egnn_version().startswith(b"egnn_b200")
+    assert isinstance(nat.last_error(), str)
+
+
+def test_workspace_sizes_are_host_only_and_monotone():
+    lib = nat.lib()
+    small = nat.LayerDesc(1000, 20000, 128, 0, nat.FLAG_RESIDUAL, nat.PREC_FP32)
+    big = nat.LayerDesc(4000, 80000, 128, 0, nat.FLAG_RESIDUAL, nat.PREC_FP32)
+    for which in (nat.WS_FWD, nat.WS_BWD):
+        a = lib.egnn_workspace_size(C.byref(small), which, 148)
+        b = lib.egnn_workspace_size(C.byref(big), which, 148)
+        assert 0 < a < b
+    # backward keeps one H-vector per edge: at least E*H*4 bytes
+    assert lib.egnn_workspace_size(C.byref(big), nat.WS_BWD, 148) >= 80000 * 128 * 4
+    assert lib.egnn_saved_size(C.byref(small)) == 1000 * 128 * 4
+    assert lib.egnn_csr_workspace_size(1000, 20000) >= 4 * 20000 * 4
+
+
+def test_workspace_size_rejects_unsupported_shapes():
+    lib = nat.lib()
+    for d in [nat.LayerDesc(10, 10, 48, 0, 1, 0),          # hidden not built
+              nat.LayerDesc(10, 10, 64, 17, 1, 0),         # too many edge features
+              nat.LayerDesc(10, 10, 64, 0, 1, 7),          # unknown precision
+              nat.LayerDesc(10, 10, 64, 0, nat.FLAG_ATTENTION, 0)]:
+        assert lib.egnn_workspace_size(C.byref(d), nat.WS_FWD, 148) == 0
+
+
+def test_state_dict_names_and_seeded_init_match_reference():
+    c = load_golden("model_molecules")
+    torch.manual_seed(1)
+    m = EGNN(in_node_nf=5, hidden_nf=32, out_node_nf=1, n_layers=2)
+    sd = m.state_dict()
+    assert list(sd) == list(c["state_dict"])
+    for k, v in sd.items():
+        assert torch.equal(v.double(), c["state_dict"][k]), k
+    # and it loads reference checkpoints as they are
+    m.load_state_dict({k: v.float() for k, v in c["state_dict"].items()})
+
+
+def test_e_gcl_signature_guards():
+    with pytest.raises(NotImplementedError):
+        E_GCL(32, 32, 32, act_fn=nn.ReLU())
+    with pytest.raises(NotImplementedError):
+        E_GCL(16, 32, 32)
+    with pytest.raises(Exception):
+        E_GCL(32, 32, 32, coords_agg="max")
+    with pytest.raises(ValueError):
+        E_GCL(32, 32, 32, precision="fp8")
+
+
+def test_cpu_tensors_are_rejected_not_computed():
+    m = EGNN(in_node_nf=5, hidden_nf=32, out_node_nf=1, n_layers=1)
+    h = torch.zeros(4, 5)
+    x = torch.zeros(4, 3)
+    with pytest.raises(ValueError, match="CUDA"):
+        m(h, x, [torch.tensor([0, 1]), torch.tensor([1, 0])], None)
+
+
+def test_precision_switch():
+    m = EGNN(in_node_nf=5, hidden_nf=32, out_node_nf=1, n_layers=2, precision="bf16")
+    assert m.precision == "bf16"
+    m.precision = "fp32"
+    assert all(m._modules[f"gcl_{i}"].precision == "fp32" for i in range(2))
+
+
+def test_flag_bits_match_header():
+    text = (ROOT / "include" / "egnn_b200.h").read_text()
+    for name, val in [("EGNN_FLAG_RESIDUAL", nat.FLAG_RESIDUAL), ("EGNN_FLAG_ATTENTION", nat.FLAG_ATTENTION),
+                      ("EGNN_FLAG_NORMALIZE", nat.FLAG_NORMALIZE), ("EGNN_FLAG_TANH", nat.FLAG_TANH),
+                      ("EGNN_FLAG_COORDS_SUM", nat.FLAG_COORDS_SUM)]:
+        assert re.search(rf"{name}\s*=\s*{val}\b", text), name
+    assert len(nat.LayerDesc._fields_) == 6 and C.sizeof(nat.LayerDesc) == 32
+    assert C.sizeof(nat.Graph) == 6 * 8
+    assert C.sizeof(nat.LayerParams) == 13 * 8
+
+
+def test_no_oracle_import_in_product():
+    """The product path never imports the CPU oracle (it must fail loudly instead)."""
+    pat = re.compile(r"^\s*(from\s+oracle|import\s+oracle)", re.M)
+    for p in (ROOT / "pymolecular_b200").rglob("*.py"):
+        assert not pat.search(p.read_text()), p

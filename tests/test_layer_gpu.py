@@ -1,0 +1,248 @@
+"""Parity of the CUDA layer (through the C ABI) with the CPU oracle.
+
+Tolerances (max |y - y_ref| / max |y_ref| per tensor, against the fp64 oracle):
+  fp32 mode: 1e-5 on h, x, dL/dh, dL/dx and every parameter gradient;
+  bf16-GEMM mode: 2e-2 on the same tensors.
+CSR construction is compared bit for bit.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_cases, load_golden, rel_err
+from oracle import csr_oracle as CO
+from oracle import egnn_oracle as O
+from pymolecular_b200 import CSR, EGNN, E_GCL
+from pymolecular_b200 import _native as nat
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp32": 1e-5, "bf16": 2e-2}
+
+
+def _layer_from_state(sd, hidden, precision, dev, edges_in_d=0, **flags):
+    layer = E_GCL(hidden, hidden, hidden, edges_in_d=edges_in_d, precision=precision, **flags).to(dev)
+    layer.load_state_dict({k: v.float() for k, v in sd.items()})
+    return layer
+
+
+def _run_layer(layer, h, x, csr, gh, gx, edge_attr=None):
+    h = h.clone().requires_grad_(True)
+    x = x.clone().requires_grad_(True)
+    ho, xo, _ = layer(h, csr, x, edge_attr=edge_attr)
+    torch.autograd.backward([ho, xo], [gh, gx])
+    grads = {k: v.grad.clone() for k, v in layer.named_parameters()}
+    for v in layer.parameters():
+        v.grad = None
+    return ho.detach(), xo.detach(), h.grad, x.grad, grads
+
+
+def _compare_layer(res, ref, tol, what=""):
+    ho, xo, gh, gx, grads = res
+    rh, rx, rgh, rgx, rgrads = ref
+    errs = {"h": rel_err(ho, rh), "x": rel_err(xo, rx), "dh": rel_err(gh, rgh), "dx": rel_err(gx, rgx)}
+    for k, v in rgrads.items():
+        errs[k] = rel_err(grads[k], v if v is not None else torch.zeros_like(grads[k]))
+    bad = {k: e for k, e in errs.items() if not (e <= tol)}
+    assert not bad, f"{what} over tolerance {tol}: {bad}"
+    return errs
+
+
+# ---------------------------------------------------------------------------
+# golden fixtures (reference outputs, fp64)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_golden_fixture_fp32(name, cuda_device):
+    c = load_golden(name)
+    dev = cuda_device
+    if c["kind"] == "layer":
+        flags = dict(c.get("flags", {}))
+        layer = _layer_from_state(c["state_dict"], c["hidden"], "fp32", dev, c["edges_in_d"], **flags)
+        csr = CSR.from_edges(c["row"], c["col"], n_nodes=c["h"].shape[0], device=dev)
+        ea = c["edge_attr"].float().to(dev) if c["edge_attr"] is not None else None
+        res = _run_layer(layer, c["h"].float().to(dev), c["x"].float().to(dev), csr,
+                         c["gh"].float().to(dev), c["gx"].float().to(dev), ea)
+        ref = (c["h_out"], c["x_out"], c["grad_h"], c["grad_x"], c["grads"])
+        _compare_layer(res, ref, TOL["fp32"], name)
+        return
+    model = EGNN(c["in_node_nf"], c["hidden"], c["out_node_nf"], in_edge_nf=c.get("in_edge_nf", 0),
+                 n_layers=c["n_layers"], device=dev)
+    model.load_state_dict({k: v.float() for k, v in c["state_dict"].items()})
+    h = c["h"].float().to(dev).requires_grad_(True)
+    x = c["x"].float().to(dev).requires_grad_(True)
+    ea = c["edge_attr"].float().to(dev) if c.get("edge_attr") is not None else None
+    ho, xo = model(h, x, [c["row"].to(dev), c["col"].to(dev)], ea)
+    if c["kind"] == "model":
+        gp = c["graph_ptr"]
+        gi = torch.repeat_interleave(torch.arange(len(gp) - 1), gp[1:] - gp[:-1]).to(dev)
+        pred = torch.zeros(len(gp) - 1, device=dev).index_add_(0, gi, ho[:, 0])
+        loss = ((pred - c["target"].float().to(dev)) ** 2).mean()
+    else:
+        loss = (ho ** 2).sum() + (xo * torch.linspace(-1, 1, 96, device=dev).view(32, 3)).sum()
+    loss.backward()
+    assert rel_err(loss, c["loss"]) < TOL["fp32"]
+    assert rel_err(ho, c["h_out"]) < TOL["fp32"]
+    assert rel_err(xo, c["x_out"]) < TOL["fp32"]
+    assert rel_err(h.grad, c["grad_h"]) < TOL["fp32"]
+    assert rel_err(x.grad, c["grad_x"]) < TOL["fp32"]
+    for k, v in model.named_parameters():
+        assert rel_err(v.grad if v.grad is not None else torch.zeros_like(v), c["grads"][k]) < TOL["fp32"], k
+
+
+# ---------------------------------------------------------------------------
+# seeded layer sweep against the fp64 oracle
+# ---------------------------------------------------------------------------
+
+def _seeded_layer_case(seed, N, E, H, edges_in_d=0, hub=True, **flags):
+    g = torch.Generator().manual_seed(seed)
+    row = torch.randint(0, N, (E,), generator=g)
+    col = torch.randint(0, N, (E,), generator=g)
+    if hub:
+        row[: E // 3] = 0           # one row much longer than an edge range
+    p = O.init_params(H, H, 1, 1, in_edge_nf=edges_in_d, seed=seed, dtype=torch.float64)
+    p = {k[len("gcl_0."):]: v for k, v in p.items() if k.startswith("gcl_0.")}
+    # larger coord weights than the 0.001 xavier gain so the x path is exercised
+    p["coord_mlp.2.weight"] = p["coord_mlp.2.weight"] * 300.0
+    h = torch.randn(N, H, generator=g, dtype=torch.float64)
+    x = torch.randn(N, 3, generator=g, dtype=torch.float64) * 1.5
+    ea = torch.randn(E, edges_in_d, generator=g, dtype=torch.float64) if edges_in_d else None
+    gh = torch.randn(N, H, generator=g, dtype=torch.float64)
+    gx = torch.randn(N, 3, generator=g, dtype=torch.float64)
+    return row, col, p, h, x, ea, gh, gx
+
+
+LAYER_CASES = [
+    # (H, precision, N, E, edges_in_d, flags)
+    (32, "fp32", 300, 4000, 0, {}),
+    (64, "fp32", 500, 12000, 0, {}),
+    (128, "fp32", 700, 20000, 0, {}),
+    (256, "fp32", 400, 9000, 0, {}),
+    (64, "fp32", 300, 5000, 3, {"normalize": True, "tanh": True}),
+    (128, "fp32", 300, 5000, 0, {"coords_agg": "sum", "residual": False}),
+    (64, "bf16", 500, 12000, 0, {}),
+    (128, "bf16", 700, 20000, 0, {}),
+    (256, "bf16", 400, 9000, 0, {}),
+    (128, "bf16", 300, 5000, 2, {"normalize": True}),
+]
+
+
+@pytest.mark.parametrize("H,precision,N,E,d,flags", LAYER_CASES)
+def test_layer_matches_oracle(H, precision, N, E, d, flags, cuda_device):
+    dev = cuda_device
+    row, col, p, h, x, ea, gh, gx = _seeded_layer_case(H * 7 + E, N, E, H, d, **{})
+    ref = O.layer_grads(p, "", h, row, col, x, gh, gx, ea, **flags)
+    layer = _layer_from_state(p, H, precision, dev, d, **flags)
+    csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
+    res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev),
+                     gx.float().to(dev), ea.float().to(dev) if ea is not None else None)
+    _compare_layer(res, ref, TOL[precision], f"H={H} {precision} {flags}")
+
+
+def test_layer_without_edges(cuda_device):
+    """E = 0: agg = 0, x' = x, only the node MLP acts."""
+    dev = cuda_device
+    N, H = 20, 64
+    row = torch.zeros(0, dtype=torch.int64)
+    col = torch.zeros(0, dtype=torch.int64)
+    _, _, p, h, x, _, gh, gx = _seeded_layer_case(1, N, 10, H)
+    ref = O.layer_grads(p, "", h, row, col, x, gh, gx)
+    layer = _layer_from_state(p, H, "fp32", dev)
+    csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
+    res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev), gx.float().to(dev))
+    _compare_layer(res, ref, TOL["fp32"], "no edges")
+
+
+def test_single_edge_and_isolated_nodes(cuda_device):
+    dev = cuda_device
+    N, H = 9, 32
+    row = torch.tensor([4])
+    col = torch.tensor([7])
+    _, _, p, h, x, _, gh, gx = _seeded_layer_case(2, N, 10, H)
+    ref = O.layer_grads(p, "", h, row, col, x, gh, gx)
+    layer = _layer_from_state(p, H, "fp32", dev)
+    csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
+    res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev), gx.float().to(dev))
+    _compare_layer(res, ref, TOL["fp32"], "single edge")
+
+
+def test_backward_is_deterministic(cuda_device):
+    dev = cuda_device
+    N, E, H = 2000, 60000, 128
+    row, col, p, h, x, _, gh, gx = _seeded_layer_case(9, N, E, H)
+    layer = _layer_from_state(p, H, "fp32", dev)
+    csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
+    args = (h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev), gx.float().to(dev))
+    a = _run_layer(layer, *args)
+    b = _run_layer(layer, *args)
+    for u, v in zip(a[:4], b[:4]):
+        assert torch.equal(u, v)
+    for k in a[4]:
+        assert torch.equal(a[4][k], b[4][k]), k
+
+
+# ---------------------------------------------------------------------------
+# CSR construction and guards
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("N,E", [(1, 0), (10, 1), (97, 1000), (5000, 200000)])
+def test_csr_build_bit_exact(N, E, cuda_device):
+    g = torch.Generator().manual_seed(N + E)
+    row = torch.randint(0, N, (E,), generator=g)
+    col = torch.randint(0, N, (E,), generator=g)
+    csr = CSR.from_edges(row, col, n_nodes=N, device=cuda_device)
+    rp, ci, ri, eid = CO.csr_build(row.numpy(), col.numpy(), N)
+    assert np.array_equal(csr.row_ptr.cpu().numpy(), rp)
+    assert np.array_equal(csr.col_idx.cpu().numpy(), ci)
+    assert np.array_equal(csr.row_idx.cpu().numpy(), ri)
+    assert np.array_equal(csr.edge_id.cpu().numpy(), eid)
+    sp, se = CO.csr_transpose(ci, N)
+    assert np.array_equal(csr.src_ptr.cpu().numpy(), sp)
+    assert np.array_equal(csr.src_edge.cpu().numpy(), se)
+    srt, perm = torch.sort(row, stable=True)
+    assert torch.equal(csr.edge_id.cpu().long(), perm)
+
+
+def test_csr_from_reference_triple(cuda_device):
+    g = torch.Generator().manual_seed(3)
+    N, E = 200, 3000
+    row = torch.randint(0, N, (E,), generator=g)
+    col = torch.randint(0, N, (E,), generator=g)
+    rp, ci, ri, eid = CO.csr_build(row.numpy(), col.numpy(), N)
+    csr = CSR.from_csr(torch.from_numpy(rp), torch.from_numpy(ci), torch.from_numpy(eid), device=cuda_device)
+    assert np.array_equal(csr.row_idx.cpu().numpy(), ri)
+
+
+def test_guards_return_errors_not_faults(cuda_device):
+    dev = cuda_device
+    with pytest.raises(nat.EgnnError) as ei:
+        CSR.from_edges(torch.tensor([0, 1, 2]), torch.tensor([1, 9, 0]), n_nodes=5, device=dev)
+    assert ei.value.status == nat.EGNN_ERR_INDEX
+    with pytest.raises(nat.EgnnError) as ei:
+        CSR.from_edges(torch.tensor([0, -1]), torch.tensor([1, 0]), n_nodes=5, device=dev)
+    assert ei.value.status == nat.EGNN_ERR_INDEX
+    # non-monotone row_ptr
+    with pytest.raises(nat.EgnnError) as ei:
+        CSR.from_csr(torch.tensor([0, 3, 1, 4]), torch.tensor([0, 1, 2, 0]), n_nodes=3, device=dev)
+    assert ei.value.status == nat.EGNN_ERR_INDEX
+    # column out of range in a caller CSR
+    with pytest.raises(nat.EgnnError):
+        CSR.from_csr(torch.tensor([0, 1, 2, 2]), torch.tensor([0, 7]), n_nodes=3, device=dev)
+    # wrong dtype / device
+    layer = E_GCL(32, 32, 32).to(dev)
+    csr = CSR.from_edges(torch.tensor([0, 1]), torch.tensor([1, 0]), n_nodes=2, device=dev)
+    with pytest.raises(TypeError):
+        layer(torch.zeros(2, 32, device=dev, dtype=torch.float64), csr, torch.zeros(2, 3, device=dev))
+    with pytest.raises(ValueError):
+        layer(torch.zeros(2, 32), csr, torch.zeros(2, 3))
+
+
+def test_legacy_edge_list_equals_csr(cuda_device):
+    dev = cuda_device
+    c = load_golden("layer_default_h64")
+    layer = _layer_from_state(c["state_dict"], 64, "fp32", dev)
+    h, x = c["h"].float().to(dev), c["x"].float().to(dev)
+    a = layer(h, [c["row"].to(dev), c["col"].to(dev)], x)
+    csr = CSR.from_edges(c["row"], c["col"], n_nodes=h.shape[0], device=dev)
+    b = layer(h, csr, x)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])

@@ -267,6 +267,10 @@ __device__ __forceinline__ void gather_phase(const EdgeCommon& a, int64_t c0, in
         const float r = dx * dx + dy * dy + dz * dz;
         float inv = 1.f;
         if (normalize) inv = 1.f / (sqrtf(r) + 1e-8f);
+        // A self-loop's d = x_i - x_i adds +g to x_i and -g to the same x_i:
+        // its coordinate gradient is exactly zero, so drop it rather than let
+        // the 1/(|d| + eps) factor of normalize=True blow up the cancellation.
+        const float inv_g = (i == j) ? 0.f : inv;
         const float* Pi = a.PQ + (int64_t)i * 2 * H;
         const float* Qj = a.PQ + (int64_t)j * 2 * H + H;
         int eid = 0;
@@ -277,7 +281,7 @@ __device__ __forceinline__ void gather_phase(const EdgeCommon& a, int64_t c0, in
             dl[e] = make_float4(dx, dy, dz, r);
             const float sc = deg_scale(a.row_ptr, i, a.flags);
             float4* gt = reinterpret_cast<float4*>(sm + off_gt);
-            gt[e] = make_float4(gx_out[i * 3 + 0] * sc, gx_out[i * 3 + 1] * sc, gx_out[i * 3 + 2] * sc, inv);
+            gt[e] = make_float4(gx_out[i * 3 + 0] * sc, gx_out[i * 3 + 1] * sc, gx_out[i * 3 + 2] * sc, inv_g);
           } else {
             dl[e] = make_float4(dx * inv, dy * inv, dz * inv, r);
           }

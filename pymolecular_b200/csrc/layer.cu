@@ -9,6 +9,12 @@
 // Backward: node-MLP backward (GEMMs), edge_bwd (dst pass, recompute),
 //           src pass through the transpose CSR, then the W1 gradients and
 //           dL/dh by node GEMMs.
+// Precision: the node-side GEMMs (N rows) always run in fp32; bf16 mode
+// rounds the operands of the per-edge GEMMs only (phi_e layer 2, phi_x
+// layer 1 and their gradients, E rows), which carry the bulk of the work.
+// Rounding the node-side operands too costs far more accuracy than time:
+// on graphs with high in-degree rows the node MLP input [h, agg] and the
+// projections P, Q lose several percent in their weight gradients.
 #include <algorithm>
 
 #include "edge_simt.cuh"
@@ -103,7 +109,7 @@ int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_
   return EGNN_OK;
 }
 
-int gemm_pq(int64_t N, int H, int64_t ld1, bool bf, const float* h, const float* W1,
+int gemm_pq(int64_t N, int H, int64_t ld1, const float* h, const float* W1,
             const float* bias2, float* PQ, cudaStream_t s) {
   GemmArgs g;
   g.M = N; g.N = 2 * H; g.K = H;
@@ -111,7 +117,7 @@ int gemm_pq(int64_t N, int H, int64_t ld1, bool bf, const float* h, const float*
   g.B = mat_rows(W1, ld1, H, W1 + H, ld1); g.b_t = 1;
   g.bias = bias2;
   g.C = PQ; g.ldc = 2 * H;
-  g.round_bf16 = bf;
+  g.round_bf16 = 0;
   return gemm(g, s);
 }
 
@@ -175,10 +181,13 @@ bool missing_params(const egnn_layer_params* p) {
          !p->node_b1 || !p->node_w2 || !p->node_b2 || !p->coord_w1 || !p->coord_b1 || !p->coord_w2;
 }
 
-bool missing_graph(const egnn_graph* g, bool bwd, bool attr) {
-  if (!g || !g->row_ptr || !g->col_idx || !g->row_idx) return true;
+bool missing_graph(const egnn_graph* g, bool bwd, bool attr, int64_t E) {
+  if (!g || !g->row_ptr) return true;
+  if (bwd && !g->src_ptr) return true;
+  if (E == 0) return false;   // per-edge arrays may be empty
+  if (!g->col_idx || !g->row_idx) return true;
   if (attr && !g->edge_id) return true;
-  if (bwd && (!g->src_ptr || !g->src_edge)) return true;
+  if (bwd && !g->src_edge) return true;
   return false;
 }
 
@@ -218,8 +227,8 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   const int H = d->hidden, dd = d->edge_attr_dim;
   const bool bf = d->precision == EGNN_PREC_BF16;
   if (N == 0) return EGNN_OK;
-  if (missing_params(p) || missing_graph(g, false, dd > 0) || !h || !x || !h_out || !x_out ||
-      (dd > 0 && !edge_attr))
+  if (missing_params(p) || missing_graph(g, false, dd > 0, E) || !h || !x || !h_out || !x_out ||
+      (dd > 0 && E > 0 && !edge_attr))
     return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_fwd: null pointer argument");
   const int sms = num_sms_current();
   Carver probe(nullptr);
@@ -232,7 +241,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   float* agg = saved ? static_cast<float*>(saved) : w.agg_tmp;
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, ld1, bf, h, p->edge_w1, w.prep.bias2, w.PQ, s));
+  EGNN_TRY(gemm_pq(N, H, ld1, h, p->edge_w1, w.prep.bias2, w.PQ, s));
 
   EdgeGrid eg;
   EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));
@@ -247,7 +256,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n1.A = mat_cols(h, H, H, agg, H);
   n1.B = mat(p->node_w1, 2 * H); n1.b_t = 1;
   n1.bias = p->node_b1; n1.act = ACT_SILU;
-  n1.C = w.n1; n1.ldc = H; n1.round_bf16 = bf;
+  n1.C = w.n1; n1.ldc = H;
   EGNN_TRY(gemm(n1, s));
 
   GemmArgs n2;
@@ -256,7 +265,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n2.B = mat(p->node_w2, H); n2.b_t = 1;
   n2.bias = p->node_b2;
   if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = H; }
-  n2.C = h_out; n2.ldc = H; n2.round_bf16 = bf;
+  n2.C = h_out; n2.ldc = H;
   EGNN_TRY(gemm(n2, s));
   return EGNN_OK;
 }
@@ -271,8 +280,8 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   const int H = d->hidden, dd = d->edge_attr_dim;
   const bool bf = d->precision == EGNN_PREC_BF16;
   const bool residual = d->flags & EGNN_FLAG_RESIDUAL;
-  if (missing_params(p) || missing_graph(g, true, dd > 0) || !h || !x || !saved || !gh_out ||
-      !gx_out || !grad_h || !grad_x || !gp || (dd > 0 && !edge_attr))
+  if (missing_params(p) || missing_graph(g, true, dd > 0, E) || !h || !x || !saved || !gh_out ||
+      !gx_out || !grad_h || !grad_x || !gp || (dd > 0 && E > 0 && !edge_attr))
     return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_bwd: null pointer argument");
   if (!gp->edge_w1 || !gp->edge_b1 || !gp->edge_w2 || !gp->edge_b2 || !gp->node_w1 || !gp->node_b1 ||
       !gp->node_w2 || !gp->node_b2 || !gp->coord_w1 || !gp->coord_b1 || !gp->coord_w2)
@@ -289,7 +298,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   if (N == 0) return EGNN_OK;
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, ld1, bf, h, p->edge_w1, w.prep.bias2, w.PQ, s));
+  EGNN_TRY(gemm_pq(N, H, ld1, h, p->edge_w1, w.prep.bias2, w.PQ, s));
 
   // ---- node MLP backward: h' = [h +] Wn2 silu(Wn1 [h, agg] + bn1) + bn2
   {
@@ -299,28 +308,28 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     n1.B = mat(p->node_w1, 2 * H); n1.b_t = 1;
     n1.bias = p->node_b1; n1.act = ACT_SILU;
     n1.pre = w.n1pre; n1.ldp = H;
-    n1.C = w.n1; n1.ldc = H; n1.round_bf16 = bf;
+    n1.C = w.n1; n1.ldc = H;
     EGNN_TRY(gemm(n1, s));
   }
-  EGNN_TRY(wgrad(N, H, H, mat(gh_out, H), mat(w.n1, H), gp->node_w2, H, gp->node_b2, bf, w.wpart, s));
+  EGNN_TRY(wgrad(N, H, H, mat(gh_out, H), mat(w.n1, H), gp->node_w2, H, gp->node_b2, 0, w.wpart, s));
   {
     GemmArgs gn;
     gn.M = N; gn.N = H; gn.K = H;
     gn.A = mat(gh_out, H);
     gn.B = mat(p->node_w2, H); gn.b_t = 0;
     gn.act = ACT_DSILU; gn.aux = w.n1pre; gn.ldaux = H;
-    gn.C = w.g_n1pre; gn.ldc = H; gn.round_bf16 = bf;
+    gn.C = w.g_n1pre; gn.ldc = H;
     EGNN_TRY(gemm(gn, s));
   }
   EGNN_TRY(wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
-                 gp->node_b1, bf, w.wpart, s));
+                 gp->node_b1, 0, w.wpart, s));
   {
     GemmArgs gh;
     gh.M = N; gh.N = H; gh.K = H;
     gh.A = mat(w.g_n1pre, H);
     gh.B = mat(p->node_w1, 2 * H); gh.b_t = 0;
     if (residual) { gh.resid = gh_out; gh.ldr = H; }
-    gh.C = w.gh_acc; gh.ldc = H; gh.round_bf16 = bf;
+    gh.C = w.gh_acc; gh.ldc = H;
     EGNN_TRY(gemm(gh, s));
     GemmArgs ga = gh;
     ga.B = mat(p->node_w1 + H, 2 * H);
@@ -351,11 +360,11 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.A = mat_cols(w.S_dst, H, H, w.S_src, H);
     gh.B = mat_rows(p->edge_w1, ld1, H, p->edge_w1 + H, ld1); gh.b_t = 0;
     gh.resid = w.gh_acc; gh.ldr = H;
-    gh.C = grad_h; gh.ldc = H; gh.round_bf16 = bf;
+    gh.C = grad_h; gh.ldc = H;
     EGNN_TRY(gemm(gh, s));
   }
-  EGNN_TRY(wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart, s));
-  EGNN_TRY(wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, bf, w.wpart, s));
+  EGNN_TRY(wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, 0, w.wpart, s));
+  EGNN_TRY(wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, 0, w.wpart, s));
   return EGNN_OK;
 }
 

@@ -28,6 +28,37 @@ def rel_err(a, b) -> float:
     return num / den
 
 
+def graph_sum(values, graph_ptr):
+    """Deterministic per-graph sum of node values (nodes grouped by graph)."""
+    cs = torch.cat([values.new_zeros(1), values.cumsum(0)])
+    gp = graph_ptr.to(values.device)
+    return cs[gp[1:]] - cs[gp[:-1]]
+
+
+def tolerances(ref, approx, floor, factor):
+    """Per-tensor tolerance: max(floor, factor * error of `approx` against `ref`).
+
+    `approx` is the reference algorithm computed at the precision under test
+    (the fp32 oracle, or the rounding-exact bf16 model), so each tensor's bar
+    is never tighter than what that precision can reach on it.
+    """
+    return {k: max(floor, factor * rel_err(approx[k], ref[k])) for k in ref}
+
+
+def as_dict(res):
+    """(h, x, dh, dx, {grads}) -> flat dict."""
+    out = {"h": res[0], "x": res[1], "dh": res[2], "dx": res[3]}
+    out.update({k: (v if v is not None else torch.zeros(1)) for k, v in res[4].items()})
+    return out
+
+
+def check_tensors(got, ref, tol, what=""):
+    errs = {k: rel_err(got[k], ref[k]) for k in ref}
+    bad = {k: (errs[k], tol[k]) for k in ref if not errs[k] <= tol[k]}
+    assert not bad, f"{what}: (error, tolerance) over bar: {bad}"
+    return errs
+
+
 def golden_cases():
     return sorted(p.stem for p in GOLDEN.glob("*.pt"))
 

@@ -1,16 +1,23 @@
 """Parity of the CUDA layer (through the C ABI) with the CPU oracle.
 
-Tolerances (max |y - y_ref| / max |y_ref| per tensor, against the fp64 oracle):
-  fp32 mode: 1e-5 on h, x, dL/dh, dL/dx and every parameter gradient;
-  bf16-GEMM mode: 2e-2 on the same tensors.
+Error = max |y - y_ref| / max |y_ref| per tensor, against the fp64 oracle,
+on h, x, dL/dh, dL/dx and every parameter gradient.
+  fp32 mode: <= max(1e-5, 3 x the error of the reference algorithm run in
+    fp32 on the same inputs).  Where the reference's own fp32 result is
+    further than 1e-5 from fp64 (ill-conditioned gradients), no fp32
+    implementation can promise 1e-5.
+  bf16-GEMM mode: <= max(2e-2, 3 x the error of the rounding-exact bf16
+    model, oracle/egnn_emulation.py), and within 5e-3 of that model on
+    every tensor it computes to better than 5e-3 itself.
 CSR construction is compared bit for bit.
 """
 import numpy as np
 import pytest
 import torch
 
-from conftest import golden_cases, load_golden, rel_err
+from conftest import as_dict, check_tensors, golden_cases, load_golden, rel_err, tolerances
 from oracle import csr_oracle as CO
+from oracle import egnn_emulation as EM
 from oracle import egnn_oracle as O
 from pymolecular_b200 import CSR, EGNN, E_GCL
 from pymolecular_b200 import _native as nat
@@ -37,15 +44,12 @@ def _run_layer(layer, h, x, csr, gh, gx, edge_attr=None):
     return ho.detach(), xo.detach(), h.grad, x.grad, grads
 
 
-def _compare_layer(res, ref, tol, what=""):
-    ho, xo, gh, gx, grads = res
-    rh, rx, rgh, rgx, rgrads = ref
-    errs = {"h": rel_err(ho, rh), "x": rel_err(xo, rx), "dh": rel_err(gh, rgh), "dx": rel_err(gx, rgx)}
-    for k, v in rgrads.items():
-        errs[k] = rel_err(grads[k], v if v is not None else torch.zeros_like(grads[k]))
-    bad = {k: e for k, e in errs.items() if not (e <= tol)}
-    assert not bad, f"{what} over tolerance {tol}: {bad}"
-    return errs
+def _fp32_tol(p, h, row, col, x, gh, gx, ea, ref, flags):
+    """Per-tensor fp32 bar: max(1e-5, 3 x the fp32 reference's own error)."""
+    p32 = {k: v.float() for k, v in p.items()}
+    r32 = O.layer_grads(p32, "", h.float(), row, col, x.float(), gh.float(), gx.float(),
+                        ea.float() if ea is not None else None, **flags)
+    return tolerances(as_dict(ref), as_dict(r32), 1e-5, 3.0)
 
 
 # ---------------------------------------------------------------------------
@@ -64,7 +68,9 @@ def test_golden_fixture_fp32(name, cuda_device):
         res = _run_layer(layer, c["h"].float().to(dev), c["x"].float().to(dev), csr,
                          c["gh"].float().to(dev), c["gx"].float().to(dev), ea)
         ref = (c["h_out"], c["x_out"], c["grad_h"], c["grad_x"], c["grads"])
-        _compare_layer(res, ref, TOL["fp32"], name)
+        tol = _fp32_tol(c["state_dict"], c["h"], c["row"], c["col"], c["x"], c["gh"], c["gx"],
+                        c["edge_attr"], ref, flags)
+        check_tensors(as_dict(res), as_dict(ref), tol, name)
         return
     model = EGNN(c["in_node_nf"], c["hidden"], c["out_node_nf"], in_edge_nf=c.get("in_edge_nf", 0),
                  n_layers=c["n_layers"], device=dev)
@@ -73,21 +79,32 @@ def test_golden_fixture_fp32(name, cuda_device):
     x = c["x"].float().to(dev).requires_grad_(True)
     ea = c["edge_attr"].float().to(dev) if c.get("edge_attr") is not None else None
     ho, xo = model(h, x, [c["row"].to(dev), c["col"].to(dev)], ea)
-    if c["kind"] == "model":
-        gp = c["graph_ptr"]
-        gi = torch.repeat_interleave(torch.arange(len(gp) - 1), gp[1:] - gp[:-1]).to(dev)
-        pred = torch.zeros(len(gp) - 1, device=dev).index_add_(0, gi, ho[:, 0])
-        loss = ((pred - c["target"].float().to(dev)) ** 2).mean()
-    else:
-        loss = (ho ** 2).sum() + (xo * torch.linspace(-1, 1, 96, device=dev).view(32, 3)).sum()
+    loss = _golden_loss(c, ho, xo)
     loss.backward()
-    assert rel_err(loss, c["loss"]) < TOL["fp32"]
-    assert rel_err(ho, c["h_out"]) < TOL["fp32"]
-    assert rel_err(xo, c["x_out"]) < TOL["fp32"]
-    assert rel_err(h.grad, c["grad_h"]) < TOL["fp32"]
-    assert rel_err(x.grad, c["grad_x"]) < TOL["fp32"]
-    for k, v in model.named_parameters():
-        assert rel_err(v.grad if v.grad is not None else torch.zeros_like(v), c["grads"][k]) < TOL["fp32"], k
+    got = {"loss": loss, "h": ho, "x": xo, "dh": h.grad, "dx": x.grad}
+    got.update({k: (v.grad if v.grad is not None else torch.zeros_like(v)) for k, v in model.named_parameters()})
+    ref = {"loss": c["loss"], "h": c["h_out"], "x": c["x_out"], "dh": c["grad_h"], "dx": c["grad_x"]}
+    ref.update(c["grads"])
+    # the reference algorithm in fp32 on the same inputs sets the achievable bar
+    p32 = {k: v.float().clone().requires_grad_(True) for k, v in c["state_dict"].items()}
+    h32 = c["h"].float().clone().requires_grad_(True)
+    x32 = c["x"].float().clone().requires_grad_(True)
+    ho32, xo32 = O.egnn(p32, h32, x32, c["row"], c["col"],
+                        c["edge_attr"].float() if c.get("edge_attr") is not None else None)
+    l32 = _golden_loss(c, ho32, xo32)
+    l32.backward()
+    r32 = {"loss": l32, "h": ho32, "x": xo32, "dh": h32.grad, "dx": x32.grad}
+    r32.update({k: (v.grad if v.grad is not None else torch.zeros_like(v)) for k, v in p32.items()})
+    check_tensors(got, ref, tolerances(ref, r32, 1e-5, 3.0), name)
+
+
+def _golden_loss(c, ho, xo):
+    if c["kind"] == "model":
+        from conftest import graph_sum
+        pred = graph_sum(ho[:, 0], c["graph_ptr"])
+        return ((pred - c["target"].to(pred.dtype).to(pred.device)) ** 2).mean()
+    w = torch.linspace(-1, 1, 96, dtype=xo.dtype, device=xo.device).view(32, 3)
+    return (ho ** 2).sum() + (xo * w).sum()
 
 
 # ---------------------------------------------------------------------------
@@ -130,13 +147,22 @@ LAYER_CASES = [
 @pytest.mark.parametrize("H,precision,N,E,d,flags", LAYER_CASES)
 def test_layer_matches_oracle(H, precision, N, E, d, flags, cuda_device):
     dev = cuda_device
-    row, col, p, h, x, ea, gh, gx = _seeded_layer_case(H * 7 + E, N, E, H, d, **{})
+    row, col, p, h, x, ea, gh, gx = _seeded_layer_case(H * 7 + E, N, E, H, d, hub=True)
     ref = O.layer_grads(p, "", h, row, col, x, gh, gx, ea, **flags)
     layer = _layer_from_state(p, H, precision, dev, d, **flags)
     csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
     res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev),
                      gx.float().to(dev), ea.float().to(dev) if ea is not None else None)
-    _compare_layer(res, ref, TOL[precision], f"H={H} {precision} {flags}")
+    got, refd = as_dict(res), as_dict(ref)
+    what = f"H={H} {precision} d={d} {flags}"
+    if precision == "fp32":
+        check_tensors(got, refd, _fp32_tol(p, h, row, col, x, gh, gx, ea, ref, flags), what)
+        return
+    emu = as_dict(EM.layer_fwd_bwd(p, h, row, col, x, gh, gx, ea, precision="bf16", **flags))
+    emu_err = {k: rel_err(emu[k], refd[k]) for k in refd}
+    check_tensors(got, refd, tolerances(refd, emu, TOL["bf16"], 3.0), what + " vs fp64")
+    tight = {k: (5e-3 if emu_err[k] < 5e-3 else float("inf")) for k in refd}
+    check_tensors(got, emu, tight, what + " vs rounding-exact bf16 model")
 
 
 def test_layer_without_edges(cuda_device):
@@ -150,7 +176,7 @@ def test_layer_without_edges(cuda_device):
     layer = _layer_from_state(p, H, "fp32", dev)
     csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
     res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev), gx.float().to(dev))
-    _compare_layer(res, ref, TOL["fp32"], "no edges")
+    check_tensors(as_dict(res), as_dict(ref), _fp32_tol(p, h, row, col, x, gh, gx, None, ref, {}), "no edges")
 
 
 def test_single_edge_and_isolated_nodes(cuda_device):
@@ -163,7 +189,7 @@ def test_single_edge_and_isolated_nodes(cuda_device):
     layer = _layer_from_state(p, H, "fp32", dev)
     csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
     res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev), gx.float().to(dev))
-    _compare_layer(res, ref, TOL["fp32"], "single edge")
+    check_tensors(as_dict(res), as_dict(ref), _fp32_tol(p, h, row, col, x, gh, gx, None, ref, {}), "single edge")
 
 
 def test_backward_is_deterministic(cuda_device):

@@ -175,6 +175,31 @@ EGNN_API int egnn_linear_bwd(int64_t m, int32_t k, int32_t o, const float* x, co
                     const float* dy, float* dx, float* dw, float* db,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the scratch array compiled into the library for
+ * egnn_linear_bwd_static (4 MiB; each GPU that loads the library holds one
+ * copy of it until the process exits). */
+#define EGNN_LINEAR_BWD_STATIC_SCRATCH_BYTES ((size_t)4 << 20)
+
+/* egnn_linear_bwd for callers that cannot allocate device memory.
+ * No counterpart in the reference: it exists for host code that must not
+ * call cudaMalloc, e.g. code that runs while a stream is being captured
+ * (allocation is forbidden there), or a plugin living inside a framework
+ * that owns every device allocation and hands out no workspace.  Same
+ * inputs, outputs and results as egnn_linear_bwd; its scratch is a fixed
+ * device array inside the library instead of a caller workspace, and it
+ * calls no cudaMalloc, cudaFree or allocating library routine.
+ * - Shapes whose egnn_linear_workspace_size(m, k, o) exceeds
+ *   EGNN_LINEAR_BWD_STATIC_SCRATCH_BYTES are rejected with
+ *   EGNN_ERR_WORKSPACE before anything is launched.
+ * - The first call on each device looks up the array's device address with
+ *   that device current; make that first call before any stream capture.
+ * - All calls on a device share the one array and it keeps the previous
+ *   call's contents (this entry point writes every scratch word before it
+ *   reads it, so nothing needs clearing).  Calls whose GPU work overlaps,
+ *   on different streams or threads, race on it: order them on one stream. */
+EGNN_API int egnn_linear_bwd_static(int64_t m, int32_t k, int32_t o, const float* x, const float* w,
+                                    const float* dy, float* dx, float* dw, float* db, void* stream);
+
 /* ---- diagnostics ------------------------------------------------------- */
 
 /* Copies the calling thread's last error message into buf (NUL-terminated);

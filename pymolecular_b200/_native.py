@@ -31,6 +31,8 @@ PREC_BF16 = 1
 WS_FWD = 0
 WS_BWD = 1
 
+LINEAR_BWD_STATIC_SCRATCH_BYTES = 4 << 20   # EGNN_LINEAR_BWD_STATIC_SCRATCH_BYTES
+
 VP = C.c_void_p
 
 
@@ -85,6 +87,7 @@ _SIGNATURES = {
     "egnn_linear_workspace_size": (C.c_size_t, [C.c_int64, C.c_int32, C.c_int32]),
     "egnn_linear_bwd": (C.c_int, [C.c_int64, C.c_int32, C.c_int32, VP, VP, VP, VP, VP, VP, VP,
                                   C.c_size_t, VP]),
+    "egnn_linear_bwd_static": (C.c_int, [C.c_int64, C.c_int32, C.c_int32, VP, VP, VP, VP, VP, VP, VP]),
     "egnn_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
     "egnn_version": (C.c_char_p, []),
     "egnn_launch_count": (C.c_uint64, []),

@@ -206,6 +206,12 @@ EGNN_API int egnn_linear_bwd_static(int64_t m, int32_t k, int32_t o, const float
  * returns the message length. */
 EGNN_API size_t egnn_last_error(char* buf, size_t len);
 
+/* Synchronises `stream` and reports whether a tensor-core edge kernel gave
+ * up on a bounded wait since the last call (EGNN_ERR_CUDA, counter reset)
+ * or not (EGNN_OK).  A kernel that gives up skips its remaining work, frees
+ * its tensor memory and returns, so the context stays usable. */
+EGNN_API int egnn_device_status(void* stream);
+
 /* Library version, e.g. "egnn_b200 0.1 sm_100a". */
 EGNN_API const char* egnn_version(void);
 

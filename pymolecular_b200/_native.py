@@ -90,6 +90,7 @@ _SIGNATURES = {
     "egnn_linear_bwd_static": (C.c_int, [C.c_int64, C.c_int32, C.c_int32, VP, VP, VP, VP, VP, VP, VP]),
     "egnn_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
     "egnn_version": (C.c_char_p, []),
+    "egnn_device_status": (C.c_int, [VP]),
     "egnn_launch_count": (C.c_uint64, []),
     "egnn_launch_count_reset": (None, []),
     "egnn_kernel_timing": (None, [C.c_int]),

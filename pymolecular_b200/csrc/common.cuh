@@ -85,6 +85,17 @@ __device__ __forceinline__ void silu_and_grad(float a, float& y, float& dy) {
   dy = s * (1.0f + a * (1.0f - s));
 }
 
+// Fast variants for the bf16 tensor-core path: approximate exp and divide
+// (two MUFU operations, relative error ~1e-7), whose results are rounded to
+// bf16 or fp16 downstream anyway.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_fast(float a) { return a * sigmoid_fast(a); }
+__device__ __forceinline__ void silu_grad_fast(float a, float& y, float& dy) {
+  const float s = sigmoid_fast(a);
+  y = a * s;
+  dy = s * (1.0f + a * (1.0f - s));
+}
+
 // Round-to-nearest-even to the bf16 grid, kept in a float register.
 __device__ __forceinline__ float bf16r(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));

@@ -930,6 +930,13 @@ int edge_fwd(int H, bool bf16, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStre
   return fail(EGNN_ERR_UNSUPPORTED, "hidden size %d not built (32, 64, 128, 256)", H);
 }
 
+int edge_fixup_fwd(int H, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
+  edge_fixup_kernel<false><<<g.G - 1, 128, 0, s>>>(H, a.E, g.G, g.epc, a.row_ptr, a.row_idx, a.carry, a.flags,
+                                                   a.x, a.agg, a.x_out);
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
 int edge_bwd(int H, bool bf16, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
 #define EGNN_BWD(HH) \
   if (H == HH) return bf16 ? launch_bwd<HH, true>(a, g, s) : launch_bwd<HH, false>(a, g, s);

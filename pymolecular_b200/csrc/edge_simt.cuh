@@ -23,6 +23,8 @@ struct EdgeCommon {
   const float* Wc1T = nullptr;   // (H,H) [k][o] = coord_mlp.0.weight[o][k]
   const float* bc1 = nullptr;
   const float* wc2 = nullptr;    // (H) coord_mlp.2.weight
+  const float* W2_src = nullptr; // (H,H) edge_mlp.2.weight as given (fp32, [out][in])
+  const float* Wc1_src = nullptr;// (H,H) coord_mlp.0.weight as given
   int flags = 0;
   int64_t epc = 0;               // edges per CTA (multiple of the chunk size)
   float* carry = nullptr;        // (G, 2, H+4) partial rows at CTA range edges
@@ -60,6 +62,9 @@ int edge_grid(int H, bool bwd, bool bf16, int64_t E, int num_sms, EdgeGrid* out)
 int edge_chunk(int H);
 
 int edge_fwd(int H, bool bf16, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s);
+
+// Boundary fix-up of the forward: rows cut by a CTA range boundary.
+int edge_fixup_fwd(int H, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s);
 int edge_bwd(int H, bool bf16, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s);
 
 // Source-side pass of the backward: S_src[j] = sum of gstore over the

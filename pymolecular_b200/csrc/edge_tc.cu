@@ -1,0 +1,876 @@
+// Fused EGNN edge kernels on the 5th-generation tensor cores (tcgen05, bf16
+// operands, fp32 accumulation in TMEM), for bf16-GEMM mode with H = 128.
+//
+// Same per-edge math and work split as the SIMT kernels (edge_simt.cu): each
+// CTA owns an equal contiguous range of CSR edges, processed in chunks of 128
+// edges.  Inside a chunk thread t owns edge t, which is also row t of every
+// MMA tile and lane t of TMEM:
+//
+//   forward  u1 = silu(P_i + Q_j + w_r r)        CUDA cores -> bf16 tile U
+//            a2 = U W2^T                          tcgen05 -> TMEM
+//            m  = silu(a2 + b2)                   -> bf16 tile M, fp32 staging
+//            c1 = M Wc1^T                         tcgen05 -> TMEM
+//            phi = wc2 . silu(c1 + bc1)           per thread
+//            agg, x' : row walk over the staging (as in the SIMT kernel)
+//   backward recompute a2, m, c1 as above, then
+//            g_c1 = gphi wc2 silu'(c1)             -> bf16 tile G
+//            dWc1 += G^T M   (TMEM, persists over the CTA's chunks)
+//            g_m  = G Wc1 + g_agg[i]              tcgen05 + CUDA cores
+//            g_a2 = g_m silu'(a2)                 -> tile G
+//            dW2  += G^T U   (TMEM, persistent)
+//            g_a1 = (G W2) silu'(a1)              -> global, one H-vector per edge
+// The weight tiles live in shared memory for the whole kernel; one copy of
+// each serves the forward product (K-major B) and the data-gradient product
+// (MN-major B).  The row sums of g_a1 and of the coordinate gradients are
+// taken by row_pass_kernel (dst side) and the source pass (src side).
+#include <algorithm>
+#include <climits>
+
+#include "edge_simt.cuh"
+#include "edge_tc.cuh"
+#include "tc.cuh"
+
+namespace egnn {
+
+// Number of tensor-core waits that ran out (a kernel that gives up sets it,
+// skips its remaining work, frees its TMEM and returns).
+__device__ int g_tc_wait_timeouts = 0;
+
+namespace {
+
+using namespace tc;
+
+constexpr int kM = 128;     // edges per chunk = threads per CTA = TMEM lanes
+
+// Every MMA is M = 128 (edge rows, or output features for the weight
+// gradients), which ties this path to H = 128.
+template <int H>
+struct TC {
+  static_assert(H == 128, "tensor-core path built for H = 128");
+  static constexpr int TILE = kM * H * 2;   // [128 x H] bf16 tile
+  static constexpr int WT = H * H * 2;      // [H x H] bf16 weight tile
+  static constexpr int LDS = H + 4;         // fp32 staging row stride (floats)
+  static constexpr int LDD = H + 8;         // fp16 staging row stride (halves)
+  static constexpr uint32_t IDESC_FWD = make_idesc_bf16(kM, H, 0, 0);    // A K-major, B K-major
+  static constexpr uint32_t IDESC_DGRAD = make_idesc_bf16(kM, H, 0, 1);  // B = W, MN-major
+  static constexpr uint32_t IDESC_WGRAD = make_idesc_bf16(H, H, 1, 1);   // A = G^T, B = X, both MN-major
+};
+
+// Load an (H x H) fp32 nn.Linear weight into an SW128 bf16 tile (rows = out).
+template <int H>
+__device__ void load_weight_tile(char* tile, const float* __restrict__ W) {
+  for (int idx = threadIdx.x; idx < H * H / 8; idx += blockDim.x) {
+    const int o = idx / (H / 8), c8 = (idx % (H / 8)) * 8;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(W + o * H + c8));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(W + o * H + c8 + 4));
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    st_row8_bf16(tile, H, o, c8, v);
+  }
+}
+
+// K-major operand descriptor of K-step kk (16 columns) of a tile with `rows` rows.
+__device__ __forceinline__ uint64_t desc_k(const char* tile, int rows, int kk) {
+  return make_desc(smem_u32(tile) + (kk >> 2) * rows * 128 + (kk & 3) * 32, 16, 1024);
+}
+// MN-major operand descriptor of K-step kk (16 rows) of a tile with `rows` rows.
+__device__ __forceinline__ uint64_t desc_mn(const char* tile, int rows, int kk) {
+  return make_desc(smem_u32(tile) + kk * 2048, rows * 128, 1024);
+}
+
+// Thread-uniform bounded wait on the chunk barrier; false on timeout, after
+// one more bounded wait for the MMAs still in flight.
+__device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase) {
+  const bool ok = mbar_wait(bar, phase);
+  const int bad = __syncthreads_or(!ok);
+  if (bad) {
+    if (threadIdx.x == 0) {
+      atomicAdd(&g_tc_wait_timeouts, 1);
+      mbar_wait(bar, phase);
+    }
+    __syncthreads();
+    return false;
+  }
+  phase ^= 1;
+  fence_after_sync();
+  return true;
+}
+
+// Operand writes (generic proxy) and TMEM reads done -> tensor core may go.
+__device__ __forceinline__ void handoff_to_mma() {
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+}
+
+// Sum over the warp's 32 lanes of x[c]; lane l returns the sum for c = l.
+__device__ __forceinline__ float warp_colsum32(float (&x)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const bool up = lane & off;
+      const float send = up ? x[i] : x[i + off];
+      const float keep = up ? x[i + off] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return x[0];
+}
+
+__device__ __forceinline__ float scale_of(const int32_t* row_ptr, int r, int flags) {
+  if (flags & EGNN_FLAG_COORDS_SUM) return 1.f;
+  return 1.f / (float)max(row_ptr[r + 1] - row_ptr[r], 1);
+}
+
+// ---- thread geometry -------------------------------------------------------------
+// 512 threads: warp w covers TMEM lanes 32*(w%4)..+31 (edge rows) and the
+// 32-column slice 32*(w/4)..+31 of those rows.
+struct Geo {
+  int tid, warp, lane, q, cg, e, col0;
+  uint32_t lane_base;
+  __device__ Geo() {
+    tid = threadIdx.x;
+    warp = tid >> 5;
+    lane = tid & 31;
+    q = warp & 3;
+    cg = warp >> 2;
+    e = q * 32 + lane;
+    col0 = cg * 32;
+    lane_base = (uint32_t)(q * 32) << 16;
+  }
+};
+constexpr int kNT = 512;
+
+__device__ __forceinline__ void st_row32_bf16(char* tile, int row, int col0, const float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 32; k += 8) st_row8_bf16(tile, kM, row, col0 + k, v + k);
+}
+
+// ---- forward ----------------------------------------------------------------------
+template <int H>
+struct FwdLayout {
+  static constexpr size_t W2 = 0;
+  static constexpr size_t WC1 = W2 + TC<H>::WT;
+  static constexpr size_t U = WC1 + TC<H>::WT;
+  static constexpr size_t M = U + TC<H>::TILE;
+  static constexpr size_t MLO = M + TC<H>::TILE;       // bf16(m - bf16(m))
+  static constexpr size_t S = MLO + TC<H>::TILE;       // 0/1 segment matrix [slot][edge]
+  static constexpr size_t VEC = S + TC<H>::TILE;       // wr, b2, bc1, wc2
+  static constexpr size_t PART = VEC + 4 * H * 4;      // float[4][128]
+  static constexpr size_t DL = PART + 4 * kM * 4;      // float4[128]: dn.xyz, r
+  static constexpr size_t SEGX = DL + kM * 16;         // float4[128]: coordinate sums per segment
+  static constexpr size_t PHI = SEGX + kM * 16;        // float[128]
+  static constexpr size_t ROWL = PHI + kM * 4;         // int[128]
+  static constexpr size_t SEGROW = ROWL + kM * 4;      // int[129]
+  static constexpr size_t SEGSTART = SEGROW + (kM + 4) * 4;
+  static constexpr size_t OPEN = SEGSTART + (kM + 4) * 4;   // float[H + 4]
+  static constexpr size_t MISC = OPEN + (H + 4) * 4;   // ints: nseg, open_row, prev_row, warp counts[4]
+  static constexpr size_t BAR = MISC + 64;
+  static constexpr size_t END = BAR + 16;
+  static constexpr size_t BYTES = END + 1024;
+};
+
+template <int H>
+__global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
+  using C = TC<H>;
+  using L = FwdLayout<H>;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* W2t = sm + L::W2;
+  char* Wc1t = sm + L::WC1;
+  char* Ut = sm + L::U;
+  char* Mt = sm + L::M;
+  char* Mlo = sm + L::MLO;
+  char* St = sm + L::S;
+  float* s_wr = reinterpret_cast<float*>(sm + L::VEC);
+  float* s_b2 = s_wr + H;
+  float* s_bc1 = s_b2 + H;
+  float* s_wc2 = s_bc1 + H;
+  float* part = reinterpret_cast<float*>(sm + L::PART);
+  float4* dl = reinterpret_cast<float4*>(sm + L::DL);
+  float4* segx = reinterpret_cast<float4*>(sm + L::SEGX);
+  float* phi = reinterpret_cast<float*>(sm + L::PHI);
+  int* rowl = reinterpret_cast<int*>(sm + L::ROWL);
+  int* segrow = reinterpret_cast<int*>(sm + L::SEGROW);
+  int* segstart = reinterpret_cast<int*>(sm + L::SEGSTART);
+  float* open = reinterpret_cast<float*>(sm + L::OPEN);
+  int* misc = reinterpret_cast<int*>(sm + L::MISC);   // [0] nseg [1] open_row [2] prev_row [4..7] warp counts
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
+
+  const Geo g;
+  constexpr uint32_t NCOL = 2 * H;   // D0 | DAGG
+  if (g.warp == 0) tmem_alloc(tmem_base_s, NCOL);
+  if (g.tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  load_weight_tile<H>(W2t, a.W2_src);
+  load_weight_tile<H>(Wc1t, a.Wc1_src);
+  for (int c = g.tid; c < H; c += kNT) {
+    s_wr[c] = a.wr[c]; s_b2[c] = a.b2[c]; s_bc1[c] = a.bc1[c]; s_wc2[c] = a.wc2[c];
+  }
+  const int cta = blockIdx.x, G = gridDim.x;
+  const int64_t eb = std::min<int64_t>(a.E, (int64_t)cta * a.epc);
+  const int64_t ee = std::min<int64_t>(a.E, eb + a.epc);
+  const int N = (int)a.N;
+  const int end_row = (cta == G - 1) ? N : a.row_idx[ee];
+  if (g.tid == 0) {
+    misc[1] = -1;                                      // open_row
+    misc[2] = (cta == 0) ? -1 : a.row_idx[eb] - 1;     // last row seen
+    a.carry_row[cta * 2] = -1;
+    a.carry_row[cta * 2 + 1] = -1;
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+  const uint32_t tD0 = tmem, tAGG = tmem + H;
+  uint32_t phase = 0;
+  const bool normalize = a.flags & EGNN_FLAG_NORMALIZE;
+  const bool tanh_ = a.flags & EGNN_FLAG_TANH;
+  bool ok = true;
+
+  // Write the 32-column slice of a finished row (and its coordinates when cg == 0).
+  auto put_row = [&](int r, const float (&v)[32], float4 cx, bool zero) {
+    const bool before = a.row_ptr[r] < eb;
+    if (!before) {
+      float* dst = a.agg + (int64_t)r * H + g.col0;
+#pragma unroll
+      for (int k = 0; k < 32; k += 4)
+        *reinterpret_cast<float4*>(dst + k) = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                                   : make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+      if (g.cg == 0) {
+        const float sc = scale_of(a.row_ptr, r, a.flags);
+        const float c3[3] = {cx.x, cx.y, cx.z};
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+          a.x_out[(int64_t)r * 3 + d] = a.x[(int64_t)r * 3 + d] + (zero ? 0.f : c3[d] * sc);
+      }
+    } else {
+      float* dst = a.carry + ((int64_t)cta * 2 + 0) * (H + 4);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) dst[g.col0 + k] = v[k];
+      if (g.cg == 0) {
+        dst[H] = cx.x; dst[H + 1] = cx.y; dst[H + 2] = cx.z;
+        a.carry_row[cta * 2] = r;
+      }
+    }
+  };
+  const float zero32[32] = {};
+
+#pragma unroll 1
+  for (int64_t c0 = eb; c0 < ee && ok; c0 += kM) {
+    const int n = (int)std::min<int64_t>(kM, ee - c0);
+    const bool valid = g.e < n;
+    // ---- gather: u1 slice of edge e; zero the segment matrix
+    {
+      float u[32];
+      if (valid) {
+        const int64_t k = c0 + g.e;
+        const int i = a.row_idx[k], j = a.col_idx[k];
+        const float4 xi = a.xp[i], xj = a.xp[j];
+        const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
+        const float r = dx * dx + dy * dy + dz * dz;
+        if (g.cg == 0) {
+          const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
+          rowl[g.e] = i;
+          dl[g.e] = make_float4(dx * inv, dy * inv, dz * inv, r);
+        }
+        const float* Pi = a.PQ + (int64_t)i * 2 * H + g.col0;
+        const float* Qj = a.PQ + (int64_t)j * 2 * H + H + g.col0;
+#pragma unroll
+        for (int q4 = 0; q4 < 32; q4 += 4) {
+          const float4 p = *reinterpret_cast<const float4*>(Pi + q4);
+          const float4 qv = *reinterpret_cast<const float4*>(Qj + q4);
+          u[q4 + 0] = silu_fast(fmaf(s_wr[g.col0 + q4 + 0], r, p.x + qv.x));
+          u[q4 + 1] = silu_fast(fmaf(s_wr[g.col0 + q4 + 1], r, p.y + qv.y));
+          u[q4 + 2] = silu_fast(fmaf(s_wr[g.col0 + q4 + 2], r, p.z + qv.z));
+          u[q4 + 3] = silu_fast(fmaf(s_wr[g.col0 + q4 + 3], r, p.w + qv.w));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) u[q] = 0.f;
+        if (g.cg == 0) {
+          rowl[g.e] = INT_MAX;
+          dl[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      st_row32_bf16(Ut, g.e, g.col0, u);
+      uint4* sz = reinterpret_cast<uint4*>(St);
+#pragma unroll
+      for (int k = 0; k < C::TILE / 16 / kNT; ++k) sz[g.tid + k * kNT] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncthreads();
+    // ---- segments of the chunk (runs of equal destination rows)
+    if (g.cg == 0) {
+      const int r = rowl[g.e];
+      const bool flag = valid && (g.e == 0 || rowl[g.e - 1] != r);
+      const unsigned mask = __ballot_sync(0xffffffffu, flag);
+      if (g.lane == 0) misc[4 + g.q] = __popc(mask);
+      asm volatile("bar.sync 1, 128;" ::: "memory");   // warps 0..3 only
+      int before = __popc(mask & ((1u << g.lane) - 1u)) + (flag ? 1 : 0);
+      for (int w = 0; w < g.q; ++w) before += misc[4 + w];
+      const int seg = before - 1;   // segment of this edge
+      if (flag) {
+        segrow[seg] = r;
+        segstart[seg] = g.e;
+      }
+      if (valid) {
+        const __nv_bfloat16 one = __float2bfloat16_rn(1.f);
+        *reinterpret_cast<__nv_bfloat16*>(St + sw128_offset(seg, g.e, kM)) = one;
+      }
+      if (g.e == kM - 1) {
+        const int total = misc[4] + misc[5] + misc[6] + misc[7];
+        misc[0] = total;
+        segstart[total] = n;
+      }
+    }
+    handoff_to_mma();
+    if (g.tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2t, H, kk), C::IDESC_FWD, kk > 0);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma(bar, phase))) break;
+
+    // ---- m = silu(a2 + b2) -> tiles M (bf16) and MLO (bf16 residual)
+    {
+      float v[32], lo[32];
+      tmem_ld32(tD0 + g.lane_base + g.col0, v);
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        const float m = silu_fast(v[q] + s_b2[g.col0 + q]);
+        v[q] = m;
+        lo[q] = m - __bfloat162float(__float2bfloat16_rn(m));
+      }
+      st_row32_bf16(Mt, g.e, g.col0, v);
+      st_row32_bf16(Mlo, g.e, g.col0, lo);
+    }
+    handoff_to_mma();
+    if (g.tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Mt, kM, kk), desc_k(Wc1t, H, kk), C::IDESC_FWD, kk > 0);
+      // agg rows of the chunk: S (slots x edges) times M and MLO (edges x features)
+#pragma unroll
+      for (int kk = 0; kk < kM / 16; ++kk)
+        mma_bf16(tAGG, desc_k(St, kM, kk), desc_mn(Mt, kM, kk), C::IDESC_DGRAD, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < kM / 16; ++kk)
+        mma_bf16(tAGG, desc_k(St, kM, kk), desc_mn(Mlo, kM, kk), C::IDESC_DGRAD, 1u);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma(bar, phase))) break;
+
+    // ---- phi = wc2 . silu(c1 + bc1), four column slices per edge
+    {
+      float v[32];
+      tmem_ld32(tD0 + g.lane_base + g.col0, v);
+      float p = 0.f;
+#pragma unroll
+      for (int q = 0; q < 32; ++q) p = fmaf(silu_fast(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
+      part[g.cg * kM + g.e] = p;
+    }
+    __syncthreads();
+    if (g.cg == 0) {
+      const float p = part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e];
+      phi[g.e] = valid ? (tanh_ ? tanhf(p) : p) : 0.f;
+    }
+    __syncthreads();
+    const int nseg = misc[0];
+    if (g.tid < nseg) {
+      const int s = g.tid;
+      float sx = 0.f, sy = 0.f, sz = 0.f;
+      for (int e2 = segstart[s]; e2 < segstart[s + 1]; ++e2) {
+        const float4 d = dl[e2];
+        const float f = phi[e2];
+        sx = fmaf(d.x, f, sx); sy = fmaf(d.y, f, sy); sz = fmaf(d.z, f, sz);
+      }
+      segx[s] = make_float4(sx, sy, sz, 0.f);
+    }
+    __syncthreads();
+    // ---- finish the chunk's rows: slot s = edge lane of this thread
+    {
+      const int s = g.e;
+      const int open_row = misc[1];
+      const int prev = misc[2];
+      float v[32];
+      tmem_ld32(tAGG + g.lane_base + g.col0, v);   // every warp takes part in the TMEM load
+      if (s < nseg) {
+        const int r = segrow[s];
+        const int pr = (s == 0) ? prev : segrow[s - 1];
+        for (int rr = pr + 1; rr < r; ++rr) put_row(rr, zero32, make_float4(0.f, 0.f, 0.f, 0.f), true);
+        float4 cx = segx[s];
+        if (s == 0 && r == open_row) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] += open[g.col0 + k];
+          cx.x += open[H]; cx.y += open[H + 1]; cx.z += open[H + 2];
+        }
+        const bool complete = (s < nseg - 1) || (a.row_ptr[r + 1] <= c0 + n);
+        if (complete) {
+          put_row(r, v, cx, false);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) open[g.col0 + k] = v[k];
+          if (g.cg == 0) { open[H] = cx.x; open[H + 1] = cx.y; open[H + 2] = cx.z; }
+        }
+      }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (g.tid == 0) {
+      const int r = segrow[nseg - 1];
+      misc[2] = r;
+      misc[1] = (a.row_ptr[r + 1] <= c0 + n) ? -1 : r;
+    }
+    __syncthreads();
+  }
+  // ---- end of the CTA range: open row -> carry slot, trailing empty rows
+  if (ok) {
+    const int open_row = misc[1];
+    const int last = misc[2];
+    if (open_row >= 0) {
+      const int slot = (a.row_ptr[open_row] < eb) ? 0 : 1;
+      if (g.e == 0) {
+        float* dst = a.carry + ((int64_t)cta * 2 + slot) * (H + 4);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) dst[g.col0 + k] = open[g.col0 + k];
+        if (g.cg == 0) {
+          dst[H] = open[H]; dst[H + 1] = open[H + 1]; dst[H + 2] = open[H + 2];
+          a.carry_row[cta * 2 + slot] = open_row;
+        }
+      }
+    }
+    for (int rr = last + 1 + g.e; rr < end_row; rr += kM) put_row(rr, zero32, make_float4(0.f, 0.f, 0.f, 0.f), true);
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (g.warp == 0) tmem_dealloc(tmem, NCOL);
+}
+
+// ---- backward (dst pass) ---------------------------------------------------------------
+template <int H>
+struct BwdLayout {
+  static constexpr size_t W2 = 0;
+  static constexpr size_t WC1 = W2 + TC<H>::WT;
+  static constexpr size_t U = WC1 + TC<H>::WT;
+  static constexpr size_t M = U + TC<H>::TILE;
+  static constexpr size_t G = M + TC<H>::TILE;
+  static constexpr size_t D2 = G + TC<H>::TILE;                       // fp16 [128][LDD]
+  static constexpr size_t VEC = D2 + (size_t)kM * TC<H>::LDD * 2;    // wr, b2, bc1, wc2
+  static constexpr size_t PART = VEC + 4 * H * 4;                     // float[4][128]
+  static constexpr size_t DL = PART + 4 * kM * 4;                     // float4[128]: d.xyz, r
+  static constexpr size_t GT = DL + kM * 16;                          // float4[128]: g_trans.xyz, inv
+  static constexpr size_t PHI = GT + kM * 16;                         // float2[128]: phi, gphi'
+  static constexpr size_t ROWI = PHI + kM * 8;                        // int[128]
+  static constexpr size_t BAR = ROWI + kM * 4;
+  static constexpr size_t END = BAR + 16;
+  static constexpr size_t BYTES = END + 1024;
+};
+
+template <int H>
+__global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
+  using C = TC<H>;
+  using L = BwdLayout<H>;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* W2t = sm + L::W2;
+  char* Wc1t = sm + L::WC1;
+  char* Ut = sm + L::U;
+  char* Mt = sm + L::M;
+  char* Gt = sm + L::G;
+  __half* d2s = reinterpret_cast<__half*>(sm + L::D2);
+  float* s_wr = reinterpret_cast<float*>(sm + L::VEC);
+  float* s_b2 = s_wr + H;
+  float* s_bc1 = s_b2 + H;
+  float* s_wc2 = s_bc1 + H;
+  float* part = reinterpret_cast<float*>(sm + L::PART);
+  float4* dl = reinterpret_cast<float4*>(sm + L::DL);
+  float4* gtr = reinterpret_cast<float4*>(sm + L::GT);
+  float2* phis = reinterpret_cast<float2*>(sm + L::PHI);
+  int* rowi = reinterpret_cast<int*>(sm + L::ROWI);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
+
+  const Geo g;
+  constexpr uint32_t NCOL = 4 * H;   // D0 | s1 | dWc1 | dW2
+  if (g.warp == 0) tmem_alloc(tmem_base_s, NCOL);
+  if (g.tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  load_weight_tile<H>(W2t, a.W2_src);
+  load_weight_tile<H>(Wc1t, a.Wc1_src);
+  for (int c = g.tid; c < H; c += kNT) {
+    s_wr[c] = a.wr[c]; s_b2[c] = a.b2[c]; s_bc1[c] = a.bc1[c]; s_wc2[c] = a.wc2[c];
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+  const uint32_t tD0 = tmem, tS1 = tmem + H, tWC1 = tmem + 2 * H, tW2 = tmem + 3 * H;
+  uint32_t phase = 0;
+
+  const int cta = blockIdx.x;
+  const int64_t eb = std::min<int64_t>(a.E, (int64_t)cta * a.epc);
+  const int64_t ee = std::min<int64_t>(a.E, eb + a.epc);
+  const bool normalize = a.flags & EGNN_FLAG_NORMALIZE;
+  const bool tanh_ = a.flags & EGNN_FLAG_TANH;
+
+  // per-lane column partials over the warp's 32 rows: column col0 + lane
+  float r_bc1 = 0.f, r_b2 = 0.f, r_wc2 = 0.f, r_wr = 0.f;
+  bool ok = true;
+  bool first = true;
+
+#pragma unroll 1
+  for (int64_t c0 = eb; c0 < ee && ok; c0 += kM) {
+    const int n = (int)std::min<int64_t>(kM, ee - c0);
+    const bool valid = g.e < n;
+    // ---- gather: u1 slice (tile U), s1 = silu'(a1) slice (TMEM), geometry
+    {
+      float u[32], s1v[32];
+      if (valid) {
+        const int64_t k = c0 + g.e;
+        const int i = a.row_idx[k], j = a.col_idx[k];
+        const float4 xi = a.xp[i], xj = a.xp[j];
+        const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
+        const float r = dx * dx + dy * dy + dz * dz;
+        if (g.cg == 0) {
+          const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
+          const float inv_g = (i == j) ? 0.f : inv;   // self-loop: zero coordinate gradient
+          const float sc = scale_of(a.row_ptr, i, a.flags);
+          rowi[g.e] = i;
+          dl[g.e] = make_float4(dx, dy, dz, r);
+          gtr[g.e] = make_float4(a.gx_out[(int64_t)i * 3] * sc, a.gx_out[(int64_t)i * 3 + 1] * sc,
+                                 a.gx_out[(int64_t)i * 3 + 2] * sc, inv_g);
+        }
+        const float* Pi = a.PQ + (int64_t)i * 2 * H + g.col0;
+        const float* Qj = a.PQ + (int64_t)j * 2 * H + H + g.col0;
+#pragma unroll
+        for (int q4 = 0; q4 < 32; q4 += 4) {
+          const float4 p = *reinterpret_cast<const float4*>(Pi + q4);
+          const float4 qv = *reinterpret_cast<const float4*>(Qj + q4);
+          const float pv[4] = {p.x + qv.x, p.y + qv.y, p.z + qv.z, p.w + qv.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            silu_grad_fast(fmaf(s_wr[g.col0 + q4 + t], r, pv[t]), u[q4 + t], s1v[q4 + t]);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) { u[q] = 0.f; s1v[q] = 0.f; }
+        if (g.cg == 0) {
+          rowi[g.e] = 0;
+          dl[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
+          gtr[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      st_row32_bf16(Ut, g.e, g.col0, u);
+      tmem_st32(tS1 + g.lane_base + g.col0, s1v);
+    }
+    handoff_to_mma();
+    if (g.tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2t, H, kk), C::IDESC_FWD, kk > 0);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma(bar, phase))) break;
+
+    // ---- m = silu(a2 + b2) -> tile M ; silu'(a2) -> fp16 staging
+    {
+      float v[32];
+      tmem_ld32(tD0 + g.lane_base + g.col0, v);
+      __half2* drow = reinterpret_cast<__half2*>(d2s + g.e * C::LDD + g.col0);
+#pragma unroll
+      for (int q = 0; q < 32; q += 2) {
+        float y0, d0, y1, d1;
+        silu_grad_fast(v[q] + s_b2[g.col0 + q], y0, d0);
+        silu_grad_fast(v[q + 1] + s_b2[g.col0 + q + 1], y1, d1);
+        v[q] = y0; v[q + 1] = y1;
+        drow[q / 2] = __floats2half2_rn(d0, d1);
+      }
+      st_row32_bf16(Mt, g.e, g.col0, v);
+    }
+    handoff_to_mma();
+    if (g.tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Mt, kM, kk), desc_k(Wc1t, H, kk), C::IDESC_FWD, kk > 0);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma(bar, phase))) break;
+
+    // ---- phi and its gradient (row sums across the four column slices)
+    {
+      float v[32];
+      tmem_ld32(tD0 + g.lane_base + g.col0, v);
+      float p = 0.f;
+#pragma unroll
+      for (int q = 0; q < 32; ++q) p = fmaf(silu_fast(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
+      part[g.cg * kM + g.e] = p;
+    }
+    __syncthreads();
+    if (g.cg == 0) {
+      const float p = part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e];
+      const float4 d = dl[g.e], gt = gtr[g.e];
+      const float ph = tanh_ ? tanhf(p) : p;
+      float gp = gt.x * d.x + gt.y * d.y + gt.z * d.z;
+      if (normalize) gp *= gt.w;
+      if (tanh_) gp *= (1.f - ph * ph);
+      phis[g.e] = valid ? make_float2(ph, gp) : make_float2(0.f, 0.f);
+    }
+    __syncthreads();
+    // ---- g_c1 = gphi' wc2 silu'(c1) -> tile G ; column sums
+    {
+      const float gp = phis[g.e].y;
+      float v[32], gc[32];
+      tmem_ld32(tD0 + g.lane_base + g.col0, v);
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        float y, dy;
+        silu_grad_fast(v[q] + s_bc1[g.col0 + q], y, dy);
+        gc[q] = gp * s_wc2[g.col0 + q] * dy;
+        v[q] = gp * y;
+      }
+      st_row32_bf16(Gt, g.e, g.col0, gc);
+      r_bc1 += warp_colsum32(gc);
+      r_wc2 += warp_colsum32(v);
+    }
+    handoff_to_mma();
+    if (g.tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kM / 16; ++kk)
+        mma_bf16(tWC1, desc_mn(Gt, kM, kk), desc_mn(Mt, kM, kk), C::IDESC_WGRAD, (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Gt, kM, kk), desc_mn(Wc1t, H, kk), C::IDESC_DGRAD, kk > 0);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma(bar, phase))) break;
+
+    // ---- g_a2 = (g_m + g_agg[i]) silu'(a2) -> tile G ; column sums
+    {
+      float v[32];
+      tmem_ld32(tD0 + g.lane_base + g.col0, v);
+      const __half2* drow = reinterpret_cast<const __half2*>(d2s + g.e * C::LDD + g.col0);
+      const float* ga = a.g_agg + (int64_t)rowi[g.e] * H + g.col0;
+#pragma unroll
+      for (int q = 0; q < 32; q += 4) {
+        float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) g4 = *reinterpret_cast<const float4*>(ga + q);
+        const float2 d01 = __half22float2(drow[q / 2]);
+        const float2 d23 = __half22float2(drow[q / 2 + 1]);
+        v[q] = valid ? (v[q] + g4.x) * d01.x : 0.f;
+        v[q + 1] = valid ? (v[q + 1] + g4.y) * d01.y : 0.f;
+        v[q + 2] = valid ? (v[q + 2] + g4.z) * d23.x : 0.f;
+        v[q + 3] = valid ? (v[q + 3] + g4.w) * d23.y : 0.f;
+      }
+      st_row32_bf16(Gt, g.e, g.col0, v);
+      r_b2 += warp_colsum32(v);
+    }
+    handoff_to_mma();
+    if (g.tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kM / 16; ++kk)
+        mma_bf16(tW2, desc_mn(Gt, kM, kk), desc_mn(Ut, kM, kk), C::IDESC_WGRAD, (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Gt, kM, kk), desc_mn(W2t, H, kk), C::IDESC_DGRAD, kk > 0);
+      mma_commit(bar);
+    }
+    first = false;
+    if (!(ok = wait_mma(bar, phase))) break;
+
+    // ---- g_a1 = g_u1 silu'(a1) -> global ; d-gradient
+    {
+      const float4 d = dl[g.e];
+      float v[32], sv[32];
+      tmem_ld32(tD0 + g.lane_base + g.col0, v);
+      tmem_ld32(tS1 + g.lane_base + g.col0, sv);
+      float pr = 0.f;
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        v[q] = valid ? v[q] * sv[q] : 0.f;
+        pr = fmaf(v[q], s_wr[g.col0 + q], pr);
+      }
+      if (valid) {
+        float* dst = a.gstore + (c0 + g.e) * H + g.col0;
+#pragma unroll
+        for (int q = 0; q < 32; q += 4)
+          *reinterpret_cast<float4*>(dst + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+      }
+      part[g.cg * kM + g.e] = pr;
+#pragma unroll
+      for (int q = 0; q < 32; ++q) v[q] *= d.w;
+      r_wr += warp_colsum32(v);
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (g.cg == 0 && valid) {
+      const float gr = part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e];
+      const float4 d = dl[g.e], gt = gtr[g.e];
+      const float f = phis[g.e].x * gt.w;
+      a.gdstore[c0 + g.e] = make_float4(gt.x * f + 2.f * gr * d.x, gt.y * f + 2.f * gr * d.y,
+                                        gt.z * f + 2.f * gr * d.z, 0.f);
+    }
+    __syncthreads();
+  }
+
+  // ---- per-CTA partials: dWc1, dW2 rows from TMEM; column sums over the row quarters
+  const int PF = (int)edge_part_floats(H, 0);
+  float* out = a.part + (int64_t)cta * PF;
+  if (ok) {
+    if (first) {
+      for (int c = g.tid; c < 2 * H * H; c += kNT) out[c] = 0.f;
+    } else {
+      float v[32];
+      tmem_ld32(tWC1 + g.lane_base + g.col0, v);
+#pragma unroll
+      for (int q = 0; q < 32; q += 4)
+        *reinterpret_cast<float4*>(out + g.e * H + g.col0 + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+      tmem_ld32(tW2 + g.lane_base + g.col0, v);
+#pragma unroll
+      for (int q = 0; q < 32; q += 4)
+        *reinterpret_cast<float4*>(out + H * H + g.e * H + g.col0 + q) =
+            make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(Ut);   // [4 quarters][4 vectors][H]
+  {
+    const int c = g.col0 + g.lane;
+    red[(g.q * 4 + 0) * H + c] = r_bc1;
+    red[(g.q * 4 + 1) * H + c] = r_b2;
+    red[(g.q * 4 + 2) * H + c] = r_wc2;
+    red[(g.q * 4 + 3) * H + c] = r_wr;
+  }
+  __syncthreads();
+  for (int idx = g.tid; idx < 4 * H; idx += kNT) {
+    const int v = idx / H, c = idx % H;
+    out[2 * H * H + v * H + c] = red[(0 * 4 + v) * H + c] + red[(1 * 4 + v) * H + c] +
+                                 red[(2 * 4 + v) * H + c] + red[(3 * 4 + v) * H + c];
+  }
+  __syncthreads();
+  if (g.warp == 0) tmem_dealloc(tmem, NCOL);
+}
+
+// ---- dst row pass: S_dst[i] = sum of g_a1 over row i, gxd[i] = sum of d-gradients ----
+template <int H>
+__global__ void row_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr, const float* __restrict__ gstore,
+                                const float4* __restrict__ gdstore, float* __restrict__ S_dst,
+                                float* __restrict__ gxd) {
+  constexpr int CC = H / 32;
+  const int lane = threadIdx.x % 32;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (r >= N) return;
+  float s[CC];
+#pragma unroll
+  for (int c = 0; c < CC; ++c) s[c] = 0.f;
+  float gs = 0.f;
+  const int kb = row_ptr[r], ke = row_ptr[r + 1];
+  for (int k = kb; k < ke; ++k) {
+#pragma unroll
+    for (int c = 0; c < CC; ++c) s[c] += gstore[(int64_t)k * H + lane + 32 * c];
+    if (lane < 3) {
+      const float4 g = gdstore[k];
+      gs += (lane == 0) ? g.x : (lane == 1 ? g.y : g.z);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < CC; ++c) S_dst[r * H + lane + 32 * c] = s[c];
+  if (lane < 3) gxd[r * 3 + lane] = gs;
+}
+
+template <int H>
+int launch_fwd_tc(const EdgeFwdArgs& a, int G, cudaStream_t s) {
+  constexpr size_t bytes = FwdLayout<H>::BYTES;
+  static uint64_t attr_set = 0;
+  const uint64_t bit = device_bit();
+  if (!(attr_set & bit)) {
+    EGNN_CHECK_CUDA(cudaFuncSetAttribute(edge_fwd_tc_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)bytes));
+    attr_set |= bit;
+  }
+  {
+    TimerScope ts("edge_fwd", s);
+    edge_fwd_tc_kernel<H><<<G, kNT, bytes, s>>>(a);
+  }
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+template <int H>
+int launch_bwd_tc(const EdgeBwdArgs& a, int G, cudaStream_t s) {
+  constexpr size_t bytes = BwdLayout<H>::BYTES;
+  static uint64_t attr_set = 0;
+  const uint64_t bit = device_bit();
+  if (!(attr_set & bit)) {
+    EGNN_CHECK_CUDA(cudaFuncSetAttribute(edge_bwd_tc_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)bytes));
+    attr_set |= bit;
+  }
+  {
+    TimerScope ts("edge_bwd", s);
+    edge_bwd_tc_kernel<H><<<G, kNT, bytes, s>>>(a);
+  }
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+}  // namespace
+
+bool edge_tc_supported(int H, int d, int flags, int precision) {
+  (void)flags;
+  return precision == EGNN_PREC_BF16 && H == 128 && d == 0;
+}
+
+EdgeGrid edge_tc_grid(int64_t E, int num_sms) {
+  const int64_t chunks = std::max<int64_t>(1, (E + kM - 1) / kM);
+  int64_t G = std::min<int64_t>(num_sms, chunks);
+  const int64_t epc = (chunks + G - 1) / G * kM;
+  G = std::max<int64_t>(1, (E + epc - 1) / epc);
+  return EdgeGrid{(int)G, epc};
+}
+
+int edge_fwd_tc(int H, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
+  if (H != 128) return fail(EGNN_ERR_UNSUPPORTED, "tensor-core edge path built for H = 128");
+  EGNN_TRY(launch_fwd_tc<128>(a, g.G, s));
+  if (g.G > 1) EGNN_TRY(edge_fixup_fwd(H, a, g, s));
+  return EGNN_OK;
+}
+
+int edge_bwd_tc(int H, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
+  if (H != 128) return fail(EGNN_ERR_UNSUPPORTED, "tensor-core edge path built for H = 128");
+  EGNN_TRY(launch_bwd_tc<128>(a, g.G, s));
+  if (a.N > 0) {
+    const int warps = 8;
+    const unsigned blocks = (unsigned)((a.N + warps - 1) / warps);
+    TimerScope ts("row_pass", s);
+    row_pass_kernel<128><<<blocks, warps * 32, 0, s>>>(a.N, a.row_ptr, a.gstore, a.gdstore, a.S_dst, a.gxd);
+  }
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+}  // namespace egnn
+
+extern "C" int egnn_device_status(void* stream) {
+  using namespace egnn;
+  cudaStream_t s = (cudaStream_t)stream;
+  EGNN_CHECK_CUDA(cudaStreamSynchronize(s));
+  int n = 0;
+  EGNN_CHECK_CUDA(cudaMemcpyFromSymbol(&n, g_tc_wait_timeouts, sizeof(int)));
+  if (n != 0) {
+    const int zero = 0;
+    EGNN_CHECK_CUDA(cudaMemcpyToSymbol(g_tc_wait_timeouts, &zero, sizeof(int)));
+    return fail(EGNN_ERR_CUDA, "%d tensor-core wait(s) in the edge kernels timed out; results are invalid", n);
+  }
+  return EGNN_OK;
+}

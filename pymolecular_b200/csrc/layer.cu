@@ -18,6 +18,7 @@
 #include <algorithm>
 
 #include "edge_simt.cuh"
+#include "edge_tc.cuh"
 #include "node_gemm.cuh"
 
 namespace egnn {
@@ -197,6 +198,7 @@ void fill_common(EdgeCommon& a, const egnn_layer_desc* d, const egnn_graph* g, c
   a.row_ptr = g->row_ptr; a.col_idx = g->col_idx; a.row_idx = g->row_idx; a.edge_id = g->edge_id;
   a.xp = pr.xp; a.PQ = PQ; a.wr = pr.wr; a.We = pr.We; a.attr = edge_attr; a.d = d->edge_attr_dim;
   a.W2T = pr.W2T; a.b2 = p->edge_b2; a.Wc1T = pr.Wc1T; a.bc1 = p->coord_b1; a.wc2 = p->coord_w2;
+  a.W2_src = p->edge_w2; a.Wc1_src = p->coord_w1;
   a.flags = d->flags; a.epc = eg.epc;
 }
 
@@ -243,13 +245,16 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
   EGNN_TRY(gemm_pq(N, H, ld1, h, p->edge_w1, w.prep.bias2, w.PQ, s));
 
+  const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
   EdgeGrid eg;
-  EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));
+  if (tc) eg = edge_tc_grid(E, sms);
+  else EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));
   EdgeFwdArgs a;
   fill_common(a, d, g, w.prep, w.PQ, edge_attr, p, eg);
   a.carry = w.carry; a.carry_row = w.carry_row;
   a.x = x; a.agg = agg; a.x_out = x_out;
-  EGNN_TRY(edge_fwd(H, bf, a, eg, s));
+  if (tc) EGNN_TRY(edge_fwd_tc(H, a, eg, s));
+  else EGNN_TRY(edge_fwd(H, bf, a, eg, s));
 
   GemmArgs n1;
   n1.M = N; n1.N = H; n1.K = 2 * H;
@@ -339,8 +344,10 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   }
 
   // ---- edge backward: dst pass, fix-up, partial reduction, src pass
+  const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
   EdgeGrid eg;
-  EGNN_TRY(edge_grid(H, true, bf, E, sms, &eg));
+  if (tc) eg = edge_tc_grid(E, sms);
+  else EGNN_TRY(edge_grid(H, true, bf, E, sms, &eg));
   EdgeBwdArgs a;
   fill_common(a, d, g, w.prep, w.PQ, edge_attr, p, eg);
   a.carry = w.carry; a.carry_row = w.carry_row;
@@ -348,7 +355,8 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   a.Wc1 = bf ? w.prep.Wc1r : p->coord_w1;
   a.gx_out = gx_out; a.g_agg = w.g_agg;
   a.S_dst = w.S_dst; a.gxd = w.gxd; a.gstore = w.gstore; a.gdstore = w.gdstore; a.part = w.part;
-  EGNN_TRY(edge_bwd(H, bf, a, eg, s));
+  if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
+  else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
   EGNN_TRY(edge_part_reduce(H, dd, eg.G, w.part, gp, ld1, s));
   EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, w.gdstore, gx_out, w.gxd, w.S_src,
                          grad_x, s));

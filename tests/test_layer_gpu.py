@@ -141,6 +141,10 @@ LAYER_CASES = [
     (128, "bf16", 700, 20000, 0, {}),
     (256, "bf16", 400, 9000, 0, {}),
     (128, "bf16", 300, 5000, 2, {"normalize": True}),
+    # tensor-core path (bf16, H = 128, no edge attributes)
+    (128, "bf16", 100, 90, 0, {}),
+    (128, "bf16", 2000, 60000, 0, {"normalize": True, "tanh": True, "coords_agg": "sum"}),
+    (128, "bf16", 3000, 100000, 0, {"residual": False}),
 ]
 
 
@@ -192,11 +196,12 @@ def test_single_edge_and_isolated_nodes(cuda_device):
     check_tensors(as_dict(res), as_dict(ref), _fp32_tol(p, h, row, col, x, gh, gx, None, ref, {}), "single edge")
 
 
-def test_backward_is_deterministic(cuda_device):
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_backward_is_deterministic(precision, cuda_device):
     dev = cuda_device
     N, E, H = 2000, 60000, 128
     row, col, p, h, x, _, gh, gx = _seeded_layer_case(9, N, E, H)
-    layer = _layer_from_state(p, H, "fp32", dev)
+    layer = _layer_from_state(p, H, precision, dev)
     csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
     args = (h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev), gx.float().to(dev))
     a = _run_layer(layer, *args)
@@ -205,6 +210,7 @@ def test_backward_is_deterministic(cuda_device):
         assert torch.equal(u, v)
     for k in a[4]:
         assert torch.equal(a[4][k], b[4][k]), k
+    assert nat.lib().egnn_device_status(nat.stream_ptr()) == nat.EGNN_OK, nat.last_error()
 
 
 # ---------------------------------------------------------------------------

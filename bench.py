@@ -35,6 +35,7 @@ def parse():
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--precision", default=None, help="override the config's GEMM precision")
     ap.add_argument("--n-graphs", type=int, default=None, help="shrink the batch (profiling runs)")
+    ap.add_argument("--n-nodes", type=int, default=None, help="config 5: node count (default 2^20)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -195,70 +196,140 @@ def run_reference(args):
 # B200 arm
 # ---------------------------------------------------------------------------
 
+class Problem:
+    """One rank's share of the workload and its training step.
+
+    Data-parallel configs (1-4): the rank steps its own seeded batch of graphs
+    (weak scaling) and gradients are averaged with one NCCL all-reduce.
+    Config 5 on N > 1 GPUs: the single graph is split into Morton-ordered node
+    ranges with a halo exchange before every layer (strong scaling) and the
+    gradients are summed.
+    """
+
+    def __init__(self, args, world, rank, dev):
+        import torch
+        from pymolecular_b200 import CSR, EGNN, parallel
+        from pymolecular_b200.datasets import CONFIGS, make_workload
+        self.torch, self.parallel, self.CSR = torch, parallel, CSR
+        self.dev, self.world, self.rank = dev, world, rank
+        self.mc = mc = CONFIGS[args.config]
+        self.precision = args.precision or mc.precision
+        self.halo = args.config == 5 and world > 1
+        if self.halo:
+            b = make_workload(5, seed=0, n_nodes=args.n_nodes)
+            self.plan = parallel.build_halo_plan(b.row, b.col, b.n_nodes, rank, world).to(dev)
+            lo, hi = self.plan.own_lo, self.plan.own_hi
+            self.h_host, self.x_host = b.h[lo:hi].contiguous(), b.x[lo:hi].contiguous()
+            self.row_host, self.col_host = self.plan.row, self.plan.col
+            self.n_nodes_csr = self.plan.n_local
+            self.edges_job = b.n_edges
+            self.graphs_job = 1
+            self.target = b.target
+            self.scaling = "strong"
+        else:
+            b = make_workload(args.config, seed=rank, n_graphs=args.n_graphs, n_nodes=args.n_nodes)
+            self.h_host, self.x_host = b.h, b.x
+            self.row_host, self.col_host = b.row, b.col
+            self.n_nodes_csr = b.n_nodes
+            self.edges_job = b.n_edges * world
+            self.graphs_job = b.n_graphs * world
+            self.graph_ptr = b.graph_ptr
+            self.target = b.target
+            self.scaling = "weak"
+        self.batch = b
+        self.edges_rank = int(self.row_host.numel())
+        self.nodes_rank = int(self.h_host.shape[0])
+        torch.manual_seed(0)
+        self.model = EGNN(mc.in_node_nf, mc.hidden_nf, mc.out_node_nf, n_layers=mc.n_layers, device=dev,
+                          precision=self.precision)
+        self.params = list(self.model.parameters())
+        self.opt = torch.optim.SGD(self.params, lr=1e-4)
+        self.sync_grads = parallel.GradAllReduce(self.params, average=not self.halo)
+        self.csr = CSR.from_edges(self.row_host, self.col_host, n_nodes=self.n_nodes_csr, device=dev)
+        self.h = self.h_host.to(dev)
+        self.x = self.x_host.to(dev)
+        self.tgt = self.target.to(dev)
+        if not self.halo:
+            self.gp = self.graph_ptr.to(dev)
+
+    def loss(self, h_out, gp=None, tgt=None):
+        torch = self.torch
+        tgt = self.tgt if tgt is None else tgt
+        if self.halo:
+            pred = self.parallel.global_sum(h_out[:, 0].sum())
+            return ((pred - tgt[0]) ** 2)
+        gp = self.gp if gp is None else gp
+        cs = torch.cat([h_out.new_zeros(1), h_out[:, 0].cumsum(0)])
+        pred = cs[gp[1:]] - cs[gp[:-1]]
+        return ((pred - tgt) ** 2).mean()
+
+    def forward(self, h, x, csr):
+        if self.halo:
+            return self.parallel.partitioned_forward(self.model, h, x, csr, self.plan)
+        return self.model(h, x, csr)
+
+    def step(self):
+        self.opt.zero_grad(set_to_none=True)
+        ho, _ = self.forward(self.h, self.x, self.csr)
+        loss = self.loss(ho)
+        loss.backward()
+        self.sync_grads()
+        self.opt.step()
+        return loss
+
+    def host_buffers(self):
+        bufs = {"h": self.h_host.pin_memory(), "x": self.x_host.pin_memory(),
+                "row": self.row_host.pin_memory(), "col": self.col_host.pin_memory(),
+                "tgt": self.target.pin_memory()}
+        if not self.halo:
+            bufs["gp"] = self.graph_ptr.pin_memory()
+        return bufs
+
+    def e2e_step(self, host, loss_host):
+        """Public-API step from pinned host tensors: H2D copies, CSR built on the
+        device from the edge list, forward, loss, backward, update, loss D2H."""
+        d = {k: v.to(self.dev, non_blocking=True) for k, v in host.items()}
+        csr = self.CSR.from_edges(d["row"], d["col"], n_nodes=self.n_nodes_csr, device=self.dev)
+        self.opt.zero_grad(set_to_none=True)
+        ho, _ = self.forward(d["h"], d["x"], csr)
+        loss = self.loss(ho, d.get("gp"), d["tgt"])
+        loss.backward()
+        self.sync_grads()
+        self.opt.step()
+        loss_host.copy_(loss.detach().reshape(1), non_blocking=True)
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
-    from pymolecular_b200 import CSR, EGNN, _native
-    from pymolecular_b200.datasets import CONFIGS, make_workload
+    from pymolecular_b200 import _native
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-    mc = CONFIGS[args.config]
-    precision = args.precision or mc.precision
-
-    b = make_workload(args.config, seed=rank, n_graphs=args.n_graphs)
-    torch.manual_seed(0)
-    model = EGNN(mc.in_node_nf, mc.hidden_nf, mc.out_node_nf, n_layers=mc.n_layers, device=dev,
-                 precision=precision)
-    params = list(model.parameters())
-    opt = torch.optim.SGD(params, lr=1e-4)
-    csr = CSR.from_edges(b.row, b.col, n_nodes=b.n_nodes, device=dev)
-    h = b.h.to(dev)
-    x = b.x.to(dev)
-    gi = b.graph_index().to(dev)
-    tgt = b.target.to(dev)
-    G = b.n_graphs
-
-    def allreduce():
-        if world == 1:
-            return
-        grads = [p.grad if p.grad is not None else torch.zeros_like(p) for p in params]
-        flat = torch.cat([g.reshape(-1) for g in grads])
-        dist.all_reduce(flat)
-        flat.div_(world)
-        off = 0
-        for p, g in zip(params, grads):
-            n = g.numel()
-            p.grad = flat[off:off + n].view_as(g)
-            off += n
-
-    def step(hh, xx, cc, gg, tt):
-        opt.zero_grad(set_to_none=True)
-        ho, _ = model(hh, xx, cc)
-        pred = torch.zeros(G, device=dev).index_add_(0, gg, ho[:, 0])
-        loss = ((pred - tt) ** 2).mean()
-        loss.backward()
-        allreduce()
-        opt.step()
-        return loss
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    prob = Problem(args, world, rank, dev)
+    mc = prob.mc
 
     if args.profile:
-        step(h, x, csr, gi, tgt)
+        prob.step()
         torch.cuda.synchronize()
         for _ in range(args.steps):
-            step(h, x, csr, gi, tgt)
+            prob.step()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
         return 0
 
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
     clocks = ClockSampler(local)
     clocks.start()
-    for _ in range(max(args.warmup, 3)):
-        step(h, x, csr, gi, tgt)
+    warmup = max(args.warmup, 3)
+    for _ in range(warmup):
+        prob.step()
     torch.cuda.synchronize()
 
     # ---- device-resident timed region (L2 flushed between steps, untimed)
@@ -271,7 +342,7 @@ def run_b200(args):
     for k in range(args.steps):
         flush.fill_(float(k))
         starts[k].record()
-        step(h, x, csr, gi, tgt)
+        prob.step()
         ends[k].record()
     torch.cuda.synchronize()
     launches = int(_native.lib().egnn_launch_count())
@@ -282,41 +353,27 @@ def run_b200(args):
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    ms_per_step = ms_max / args.steps
+    ms_per_step = float(t.item()) / args.steps
 
     # ---- live kernel timing of the fused edge kernels (separate pass)
     _native.lib().egnn_kernel_timing(1)
     kt_steps = min(args.steps, 5)
     for k in range(kt_steps):
         flush.fill_(float(k))
-        step(h, x, csr, gi, tgt)
+        prob.step()
     torch.cuda.synchronize()
-    ktimes = {n: _native.kernel_time(n) for n in ("edge_bwd", "edge_fwd", "src_pass")}
+    ktimes = {n: _native.kernel_time(n) for n in ("edge_bwd", "edge_fwd", "src_pass", "row_pass")}
     _native.lib().egnn_kernel_timing(0)
+    status = _native.lib().egnn_device_status(_native.stream_ptr())
 
     # ---- end to end through the public API from pinned host buffers
     e2e = None
     if not args.no_e2e:
-        host = {"h": b.h.pin_memory(), "x": b.x.pin_memory(), "row": b.row.pin_memory(),
-                "col": b.col.pin_memory(), "gi": b.graph_index().pin_memory(), "tgt": b.target.pin_memory()}
+        host = prob.host_buffers()
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
-
-        def e2e_step():
-            d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
-            opt.zero_grad(set_to_none=True)
-            ho, _ = model(d["h"], d["x"], [d["row"], d["col"]])   # CSR built on the device
-            pred = torch.zeros(G, device=dev).index_add_(0, d["gi"], ho[:, 0])
-            loss = ((pred - d["tgt"]) ** 2).mean()
-            loss.backward()
-            allreduce()
-            opt.step()
-            loss_host.copy_(loss.detach().reshape(1), non_blocking=True)
-            return loss
-
         for _ in range(2):
-            e2e_step()
+            prob.e2e_step(host, loss_host)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -324,18 +381,18 @@ def run_b200(args):
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            e2e_step()
+            prob.e2e_step(host, loss_host)
         e1.record()
         torch.cuda.synchronize()
         te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = float(te.item()) / args.steps
-        e2e = {"value": world * mc.n_layers * b.n_edges / (e2e_ms * 1e-3), "unit": "layer-edges/s",
+        e2e = {"value": mc.n_layers * prob.edges_job / (e2e_ms * 1e-3), "unit": "layer-edges/s",
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-               "molecules_per_s": world * G / (e2e_ms * 1e-3),
-               "path": "EGNN.forward(h, x, [row, col]) from pinned host tensors; CSR built on device "
-                       "each step; loss copied back"}
+               "molecules_per_s": prob.graphs_job / (e2e_ms * 1e-3),
+               "path": "EGNN.forward(h, x, [row, col]) from pinned host tensors, CSR built on the device "
+                       "each step, loss copied back"}
 
     peak_vram = torch.cuda.max_memory_allocated(dev) / 2**30
 
@@ -345,11 +402,10 @@ def run_b200(args):
         bwd_ms, bwd_n = ktimes["edge_bwd"]
         fwd_ms, fwd_n = ktimes["edge_fwd"]
         per_launch_ms = bwd_ms / max(bwd_n, 1)
-        edges_per_launch = b.n_edges
-        flops_launch = 8.0 * H * H * edges_per_launch        # dgrad + wgrad of 2 HxH GEMMs per edge
+        flops_launch = 8.0 * H * H * prob.edges_rank   # dgrad + wgrad of the two H x H edge GEMMs
         achieved = flops_launch / (per_launch_ms * 1e-3) / 1e12
-        peak = peaks["bf16_tflops_sustained"] if precision == "bf16" else peaks["bf16_tflops_sustained"]
-        step_flops = model_flops(mc, b.n_nodes, b.n_edges)
+        peak = peaks["bf16_tflops_sustained"]
+        step_flops = model_flops(mc, prob.nodes_rank, prob.edges_rank) * world
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
@@ -360,17 +416,19 @@ def run_b200(args):
                              f"oracle restatement of egnn_clean.EGNN, median of 3 steps"}
         line = {
             "metric": "egnn_train_layer_edges_per_s",
-            "value": world * mc.n_layers * b.n_edges / (ms_per_step * 1e-3),
+            "value": mc.n_layers * prob.edges_job / (ms_per_step * 1e-3),
             "unit": "layer-edges/s",
-            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": precision, "data": "synthetic (seeded generators, random init)",
-            "config": {"workload": f"config{args.config}", "graphs_per_gpu": G, "nodes_per_gpu": b.n_nodes,
-                       "edges_per_gpu": b.n_edges, "layers": mc.n_layers, "hidden": mc.hidden_nf,
-                       "precision": precision, "l2": "flushed between timed steps (252 MB write)",
-                       "parallelism": f"dp{world}", "optimizer": "SGD"},
-            "molecules_per_s": world * G / (ms_per_step * 1e-3),
-            "model_tflops": step_flops * world / (ms_per_step * 1e-3) / 1e12,
+            "n_gpus": world, "steps": args.steps, "warmup": warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": prob.scaling,
+            "vs_baseline": None, "dtype": prob.precision,
+            "data": "synthetic (seeded generators, random init)",
+            "config": {"workload": f"config{args.config}", "graphs_per_gpu": prob.graphs_job // world,
+                       "nodes_per_gpu": prob.nodes_rank, "edges_per_gpu": prob.edges_rank,
+                       "layers": mc.n_layers, "hidden": H, "precision": prob.precision,
+                       "l2": "flushed between timed steps (252 MB write)",
+                       "parallelism": ("nodepart" if prob.halo else "dp") + str(world), "optimizer": "SGD"},
+            "molecules_per_s": prob.graphs_job / (ms_per_step * 1e-3),
+            "model_tflops": step_flops / (ms_per_step * 1e-3) / 1e12,
             "e2e": e2e,
             "gpu_launches": launches,
             "roofline": {"kernel": "edge_bwd", "bound": "tensor", "achieved": achieved,
@@ -379,10 +437,12 @@ def run_b200(args):
                          "traffic": None, "per_launch_ms": per_launch_ms, "launches": bwd_n,
                          "flops_per_launch": flops_launch,
                          "edge_fwd_per_launch_ms": fwd_ms / max(fwd_n, 1),
-                         "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1)},
+                         "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1),
+                         "row_pass_per_launch_ms": ktimes["row_pass"][0] / max(ktimes["row_pass"][1], 1)},
             "cpu_baseline": cpu,
             "clocks": clk,
             "peak_vram_gb": peak_vram,
+            "device_status": "ok" if status == 0 else _native.last_error(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:

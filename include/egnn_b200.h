@@ -137,7 +137,9 @@ EGNN_API int egnn_graph_check(int64_t n_nodes, int64_t n_edges, const egnn_graph
 
 /* ---- layer ------------------------------------------------------------- */
 
-/* Bytes of per-layer state egnn_layer_fwd stores for egnn_layer_bwd. */
+/* Bytes of per-layer state egnn_layer_fwd stores for egnn_layer_bwd: per
+ * node, agg (H), the projections P and Q (2H) and the node-MLP hidden layer
+ * before and after SiLU (2H), all float32.  No per-edge state is kept. */
 EGNN_API size_t egnn_saved_size(const egnn_layer_desc* d);
 
 /* Scratch bytes for egnn_layer_fwd (which = EGNN_WS_FWD) or egnn_layer_bwd

@@ -56,6 +56,7 @@ int64_t max_ctas(int64_t E, int H, int num_sms) {
 // Prepared operands shared by the forward and the backward.
 struct Prep {
   float4* xp; float* bias2; float* W2T; float* Wc1T; float* W2r; float* Wc1r; float* wr; float* We;
+  float* WPQ;   // (2H, H): rows of edge_mlp.0 restricted to the h_i and h_j columns, contiguous
 };
 
 Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd) {
@@ -68,16 +69,23 @@ Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd) {
   p.Wc1r = bwd ? c.take<float>((size_t)H * H) : nullptr;
   p.wr = c.take<float>(H);
   p.We = c.take<float>((size_t)H * std::max(d, 1));
+  p.WPQ = c.take<float>((size_t)2 * H * H);
   return p;
 }
 
 __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_layer_params p,
                             const float* x, Prep o) {
   const int64_t HH = (int64_t)H * H;
-  const int64_t total = N + 2 * H + 4 * HH + H + (int64_t)H * d;
+  const int64_t total = N + 2 * H + 4 * HH + H + (int64_t)H * d + 2 * HH;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     int64_t t = idx;
+    if (t < 2 * HH) {
+      const int64_t r = t / H, c = t % H;   // WPQ[r][c]: r < H -> Wa, else Wb
+      o.WPQ[t] = r < H ? p.edge_w1[r * ld1 + c] : p.edge_w1[(r - H) * ld1 + H + c];
+      continue;
+    }
+    t -= 2 * HH;
     if (t < N) { o.xp[t] = make_float4(x[t * 3], x[t * 3 + 1], x[t * 3 + 2], 0.f); continue; }
     t -= N;
     if (t < 2 * H) { o.bias2[t] = t < H ? p.edge_b1[t] : 0.f; continue; }
@@ -103,27 +111,43 @@ __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_l
 
 int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_params* p,
                 const float* x, const Prep& o, cudaStream_t s) {
-  const int64_t total = N + 2 * H + 4LL * H * H + H + (int64_t)H * d;
+  const int64_t total = N + 2 * H + 6LL * H * H + H + (int64_t)H * d;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
   prep_kernel<<<blocks, 256, 0, s>>>(N, H, d, ld1, bf ? 1 : 0, *p, x, o);
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
 
-int gemm_pq(int64_t N, int H, int64_t ld1, const float* h, const float* W1,
-            const float* bias2, float* PQ, cudaStream_t s) {
+int gemm_pq(int64_t N, int H, const float* h, const float* WPQ, const float* bias2, float* PQ,
+            cudaStream_t s) {
   GemmArgs g;
   g.M = N; g.N = 2 * H; g.K = H;
   g.A = mat(h, H);
-  g.B = mat_rows(W1, ld1, H, W1 + H, ld1); g.b_t = 1;
+  g.B = mat(WPQ, H); g.b_t = 1;
   g.bias = bias2;
   g.C = PQ; g.ldc = 2 * H;
   g.round_bf16 = 0;
   return gemm(g, s);
 }
 
+// Per-layer state the forward keeps for the backward (all per node):
+// agg (N,H) | PQ (N,2H) | n1pre (N,H) | n1 (N,H).
+struct Saved {
+  float* agg; float* PQ; float* n1pre; float* n1;
+};
+
+Saved carve_saved(Carver& c, int64_t N, int H) {
+  Saved v;
+  const size_t n = (size_t)std::max<int64_t>(N, 1);
+  v.agg = c.take<float>(n * H);
+  v.PQ = c.take<float>(n * 2 * H);
+  v.n1pre = c.take<float>(n * H);
+  v.n1 = c.take<float>(n * H);
+  return v;
+}
+
 struct FwdWs {
-  Prep prep; float* PQ; float* n1; float* carry; int32_t* carry_row; float* agg_tmp;
+  Prep prep; float* carry; int32_t* carry_row; char* saved_tmp;
 };
 
 FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
@@ -131,24 +155,24 @@ FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int H = d->hidden;
   FwdWs w;
   w.prep = carve_prep(c, N, H, d->edge_attr_dim, false);
-  w.PQ = c.take<float>((size_t)std::max<int64_t>(N, 1) * 2 * H);
-  w.n1 = c.take<float>((size_t)std::max<int64_t>(N, 1) * H);
   const int64_t G = max_ctas(E, H, num_sms);
   w.carry = c.take<float>((size_t)G * 2 * (H + 4));
   w.carry_row = c.take<int32_t>((size_t)G * 2);
-  w.agg_tmp = c.take<float>((size_t)std::max<int64_t>(N, 1) * H);   // when no saved buffer
+  Carver probe(nullptr);
+  carve_saved(probe, N, H);
+  w.saved_tmp = c.take<char>(probe.size());   // used when the caller keeps no state
   return w;
 }
 
 struct BwdWs {
-  Prep prep; float* PQ; float* n1pre; float* n1; float* g_n1pre; float* gh_acc; float* g_agg;
+  Prep prep; float* g_n1pre; float* gh_acc; float* g_agg;
   float* S_dst; float* S_src; float* gxd; float* gstore; float4* gdstore; float* carry;
   int32_t* carry_row; float* part; float* wpart;
 };
 
 int64_t wpart_floats(int64_t N, int H) {
-  int64_t a = wgrad_splits(N, H, 2 * H) * (int64_t)H * 2 * H;
-  int64_t b = wgrad_splits(N, H, H) * (int64_t)H * H;
+  int64_t a = wgrad_splits(N, H, 2 * H) * ((int64_t)H * 2 * H + H);
+  int64_t b = wgrad_splits(N, H, H) * ((int64_t)H * H + H);
   int64_t c = colsum_splits(N) * (int64_t)2 * H;
   return std::max<int64_t>({a, b, c, 1});
 }
@@ -158,9 +182,6 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int H = d->hidden;
   BwdWs w;
   w.prep = carve_prep(c, N, H, d->edge_attr_dim, true);
-  w.PQ = c.take<float>((size_t)N * 2 * H);
-  w.n1pre = c.take<float>((size_t)N * H);
-  w.n1 = c.take<float>((size_t)N * H);
   w.g_n1pre = c.take<float>((size_t)N * H);
   w.gh_acc = c.take<float>((size_t)N * H);
   w.g_agg = c.take<float>((size_t)N * H);
@@ -209,7 +230,9 @@ using namespace egnn;
 
 extern "C" size_t egnn_saved_size(const egnn_layer_desc* d) {
   if (!d) return 0;
-  return (size_t)std::max<int64_t>(d->n_nodes, 1) * d->hidden * sizeof(float);
+  Carver c(nullptr);
+  carve_saved(c, d->n_nodes, d->hidden);
+  return c.size();
 }
 
 extern "C" size_t egnn_workspace_size(const egnn_layer_desc* d, int which, int num_sms) {
@@ -240,17 +263,19 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   Carver c(ws);
   FwdWs w = carve_fwd(c, d, sms);
   const int64_t ld1 = 2 * H + 1 + dd;
-  float* agg = saved ? static_cast<float*>(saved) : w.agg_tmp;
+  Carver sc(saved ? saved : static_cast<void*>(w.saved_tmp));
+  const Saved sv = carve_saved(sc, N, H);
+  float* agg = sv.agg;
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, ld1, h, p->edge_w1, w.prep.bias2, w.PQ, s));
+  EGNN_TRY(gemm_pq(N, H, h, w.prep.WPQ, w.prep.bias2, sv.PQ, s));
 
   const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
   EdgeGrid eg;
   if (tc) eg = edge_tc_grid(E, sms);
   else EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));
   EdgeFwdArgs a;
-  fill_common(a, d, g, w.prep, w.PQ, edge_attr, p, eg);
+  fill_common(a, d, g, w.prep, sv.PQ, edge_attr, p, eg);
   a.carry = w.carry; a.carry_row = w.carry_row;
   a.x = x; a.agg = agg; a.x_out = x_out;
   if (tc) EGNN_TRY(edge_fwd_tc(H, a, eg, s));
@@ -261,12 +286,13 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n1.A = mat_cols(h, H, H, agg, H);
   n1.B = mat(p->node_w1, 2 * H); n1.b_t = 1;
   n1.bias = p->node_b1; n1.act = ACT_SILU;
-  n1.C = w.n1; n1.ldc = H;
+  n1.pre = sv.n1pre; n1.ldp = H;
+  n1.C = sv.n1; n1.ldc = H;
   EGNN_TRY(gemm(n1, s));
 
   GemmArgs n2;
   n2.M = N; n2.N = H; n2.K = H;
-  n2.A = mat(w.n1, H);
+  n2.A = mat(sv.n1, H);
   n2.B = mat(p->node_w2, H); n2.b_t = 1;
   n2.bias = p->node_b2;
   if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = H; }
@@ -299,30 +325,21 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   Carver c(ws);
   BwdWs w = carve_bwd(c, d, sms);
   const int64_t ld1 = 2 * H + 1 + dd;
-  const float* agg = static_cast<const float*>(saved);
+  Carver sc(const_cast<void*>(saved));
+  const Saved sv = carve_saved(sc, N, H);
+  const float* agg = sv.agg;
   if (N == 0) return EGNN_OK;
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, ld1, h, p->edge_w1, w.prep.bias2, w.PQ, s));
 
   // ---- node MLP backward: h' = [h +] Wn2 silu(Wn1 [h, agg] + bn1) + bn2
-  {
-    GemmArgs n1;
-    n1.M = N; n1.N = H; n1.K = 2 * H;
-    n1.A = mat_cols(h, H, H, agg, H);
-    n1.B = mat(p->node_w1, 2 * H); n1.b_t = 1;
-    n1.bias = p->node_b1; n1.act = ACT_SILU;
-    n1.pre = w.n1pre; n1.ldp = H;
-    n1.C = w.n1; n1.ldc = H;
-    EGNN_TRY(gemm(n1, s));
-  }
-  EGNN_TRY(wgrad(N, H, H, mat(gh_out, H), mat(w.n1, H), gp->node_w2, H, gp->node_b2, 0, w.wpart, s));
+  EGNN_TRY(wgrad(N, H, H, mat(gh_out, H), mat(sv.n1, H), gp->node_w2, H, gp->node_b2, 0, w.wpart, s));
   {
     GemmArgs gn;
     gn.M = N; gn.N = H; gn.K = H;
     gn.A = mat(gh_out, H);
     gn.B = mat(p->node_w2, H); gn.b_t = 0;
-    gn.act = ACT_DSILU; gn.aux = w.n1pre; gn.ldaux = H;
+    gn.act = ACT_DSILU; gn.aux = sv.n1pre; gn.ldaux = H;
     gn.C = w.g_n1pre; gn.ldc = H;
     EGNN_TRY(gemm(gn, s));
   }
@@ -349,7 +366,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   if (tc) eg = edge_tc_grid(E, sms);
   else EGNN_TRY(edge_grid(H, true, bf, E, sms, &eg));
   EdgeBwdArgs a;
-  fill_common(a, d, g, w.prep, w.PQ, edge_attr, p, eg);
+  fill_common(a, d, g, w.prep, sv.PQ, edge_attr, p, eg);
   a.carry = w.carry; a.carry_row = w.carry_row;
   a.W2 = bf ? w.prep.W2r : p->edge_w2;
   a.Wc1 = bf ? w.prep.Wc1r : p->coord_w1;
@@ -366,7 +383,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     GemmArgs gh;
     gh.M = N; gh.N = H; gh.K = 2 * H;
     gh.A = mat_cols(w.S_dst, H, H, w.S_src, H);
-    gh.B = mat_rows(p->edge_w1, ld1, H, p->edge_w1 + H, ld1); gh.b_t = 0;
+    gh.B = mat(w.prep.WPQ, H); gh.b_t = 0;
     gh.resid = w.gh_acc; gh.ldr = H;
     gh.C = grad_h; gh.ldc = H;
     EGNN_TRY(gemm(gh, s));
@@ -393,7 +410,7 @@ extern "C" int egnn_linear_fwd(int64_t m, int32_t k, int32_t o, const float* x, 
 extern "C" size_t egnn_linear_workspace_size(int64_t m, int32_t k, int32_t o) {
   Carver c(nullptr);
   c.take<float>((size_t)std::max<int64_t>(
-      {wgrad_splits(m, o, k) * (int64_t)o * k, colsum_splits(m) * (int64_t)o, 1}));
+      {wgrad_splits(m, o, k) * ((int64_t)o * k + o), colsum_splits(m) * (int64_t)o, 1}));
   return c.size();
 }
 

@@ -118,6 +118,14 @@ __global__ void __launch_bounds__(NT) gemm_kernel(GemmArgs a) {
 __global__ void gemm_reduce_kernel(GemmArgs a) {
   Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.C, a.ldc};
   const int64_t total = a.M * a.N;
+  if (a.db && a.db_part) {
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < a.M;
+         m += (int64_t)gridDim.x * blockDim.x) {
+      float v = 0.f;
+      for (int z = 0; z < a.ksplit; ++z) v += a.db_part[(int64_t)z * a.M + m];
+      a.db[m] = v;
+    }
+  }
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     float v = 0.f;
@@ -143,16 +151,200 @@ __global__ void colsum_reduce_kernel(int64_t C, int S, const float* part, float*
   out[c] = s;
 }
 
+
+// ---- register-tiled path -------------------------------------------------------
+// BM x 128 output tile (BM = 128 or 64), K in slices of 8 through a double
+// buffer, 256 threads each owning (BM/16) x 8 outputs.  Used when K is a
+// multiple of 8 and the operands allow 16-byte loads (checked by gemm()).
+template <int BM, int A_T, int B_T>
+__global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
+  constexpr int BN2 = 128, BK2 = 8, TM = BM / 16;
+  __shared__ __align__(16) float As[2][BK2][BM + 4];
+  __shared__ __align__(16) float Bs[2][BK2][BN2 + 4];
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN2;
+  int64_t kbeg = 0, kend = a.K;
+  if (a.ksplit > 1) {
+    int64_t kc = (a.K + a.ksplit - 1) / a.ksplit;
+    kc = (kc + BK2 - 1) / BK2 * BK2;
+    kbeg = (int64_t)blockIdx.z * kc;
+    kend = min(a.K, kbeg + kc);
+  }
+  // A slice: BM x 8 floats, B slice: 8 x 128 floats; one float4 each per
+  // thread (A with BM = 64 uses half of the threads).
+  float4 ra = make_float4(0.f, 0.f, 0.f, 0.f), rb = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto load = [&](int64_t k0) {
+    ra = make_float4(0.f, 0.f, 0.f, 0.f);
+    rb = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (A_T == 0) {          // A(m, k) row-major: row m = tid/2, k = 4*(tid%2)
+      const int64_t m = m0 + tid / 2, k = k0 + (tid % 2) * 4;
+      if (tid / 2 < BM && m < a.M && k < kend) {
+        const float* p = k < a.A.split ? a.A.p0 + m * a.A.ld0 + k : a.A.p1 + m * a.A.ld1 + (k - a.A.split);
+        ra = *reinterpret_cast<const float4*>(p);
+      }
+    } else {                 // A(m, k) = G[k][m]: k = tid/32, m = 4*(tid%32)
+      const int64_t k = k0 + tid / 32, m = m0 + (tid % 32) * 4;
+      if ((tid % 32) * 4 < BM && m < a.M && k < kend)
+        ra = *reinterpret_cast<const float4*>(a.A.p0 + k * a.A.ld0 + m);
+    }
+    if (B_T == 1) {          // B(k, n) = W[n][k]: row n = tid/2, k = 4*(tid%2)
+      const int64_t n = n0 + tid / 2, k = k0 + (tid % 2) * 4;
+      if (n < a.N && k < kend) {
+        const float* p = (a.B.split_rows && n >= a.B.split) ? a.B.p1 + (n - a.B.split) * a.B.ld1 + k
+                                                             : a.B.p0 + n * a.B.ld0 + k;
+        rb = *reinterpret_cast<const float4*>(p);
+      }
+    } else {                 // B(k, n) = X[k][n] (columns may be split): k = tid/32, n = 4*(tid%32)
+      const int64_t k = k0 + tid / 32, n = n0 + (tid % 32) * 4;
+      if (n < a.N && k < kend) {
+        const float* p = n < a.B.split ? a.B.p0 + k * a.B.ld0 + n : a.B.p1 + k * a.B.ld1 + (n - a.B.split);
+        rb = *reinterpret_cast<const float4*>(p);
+      }
+    }
+  };
+  auto store = [&](int buf) {
+    if (a.round_bf16) {
+      ra = make_float4(bf16r(ra.x), bf16r(ra.y), bf16r(ra.z), bf16r(ra.w));
+      rb = make_float4(bf16r(rb.x), bf16r(rb.y), bf16r(rb.z), bf16r(rb.w));
+    }
+    if (A_T == 0) {
+      if (tid / 2 < BM) {
+        const int ml = tid / 2, kl = (tid % 2) * 4;
+        As[buf][kl + 0][ml] = ra.x; As[buf][kl + 1][ml] = ra.y;
+        As[buf][kl + 2][ml] = ra.z; As[buf][kl + 3][ml] = ra.w;
+      }
+    } else if ((tid % 32) * 4 < BM) {
+      *reinterpret_cast<float4*>(&As[buf][tid / 32][(tid % 32) * 4]) = ra;
+    }
+    if (B_T == 1) {
+      const int nl = tid / 2, kl = (tid % 2) * 4;
+      Bs[buf][kl + 0][nl] = rb.x; Bs[buf][kl + 1][nl] = rb.y;
+      Bs[buf][kl + 2][nl] = rb.z; Bs[buf][kl + 3][nl] = rb.w;
+    } else {
+      *reinterpret_cast<float4*>(&Bs[buf][tid / 32][(tid % 32) * 4]) = rb;
+    }
+  };
+
+  float acc[TM][8];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  // db[m] = sum_k A(m, k): taken by the tx == 0 threads of the first column tile
+  const bool do_db = A_T == 1 && a.db != nullptr && blockIdx.x == 0 && tx == 0;
+  float dbacc[TM];
+#pragma unroll
+  for (int i = 0; i < TM; ++i) dbacc[i] = 0.f;
+
+  int buf = 0;
+  if (kbeg < kend) {
+    load(kbeg);
+    store(0);
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int64_t k0 = kbeg; k0 < kend; k0 += BK2) {
+    const bool more = k0 + BK2 < kend;
+    if (more) load(k0 + BK2);
+#pragma unroll
+    for (int k = 0; k < BK2; ++k) {
+      float av[TM], bv[8];
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
+      bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+      bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+      if constexpr (TM == 8) {
+        const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
+        av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+      }
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      if (do_db) {
+#pragma unroll
+        for (int i = 0; i < TM; ++i) dbacc[i] += av[i];
+      }
+    }
+    if (more) store(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+  }
+
+  if (do_db) {
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+      if (m >= a.M) continue;
+      if (a.ksplit > 1) a.db_part[(int64_t)blockIdx.z * a.M + m] = dbacc[i];
+      else a.db[m] = dbacc[i];
+    }
+  }
+  Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.C, a.ldc};
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (m >= a.M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      if (n >= a.N) continue;
+      if (a.ksplit > 1) a.part[(int64_t)blockIdx.z * a.M * a.N + m * a.N + n] = acc[i][j];
+      else e.apply(m, n, acc[i][j]);
+    }
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Whether the register-tiled kernel can take these operands.
+bool tiled_ok(const GemmArgs& a) {
+  // 16-byte loads along k need K % 8 == 0; row-wise loads (A^T, B) take any K.
+  if ((a.a_t == 0 || a.b_t == 1) && a.K % 8 != 0) return false;
+  const Mat& A = a.A;
+  const Mat& B = a.B;
+  if (a.a_t == 0) {
+    if (A.split_rows || !aligned16(A.p0) || A.ld0 % 4) return false;
+    if (A.p1 && (!aligned16(A.p1) || A.ld1 % 4 || A.split % 8)) return false;
+  } else {
+    if (A.p1 || !aligned16(A.p0) || A.ld0 % 4 || a.M % 4) return false;
+  }
+  if (a.b_t == 1) {
+    if (!aligned16(B.p0) || B.ld0 % 4) return false;
+    if (B.p1 && (!B.split_rows || !aligned16(B.p1) || B.ld1 % 4)) return false;
+  } else {
+    if (B.split_rows || !aligned16(B.p0) || B.ld0 % 4 || a.N % 4) return false;
+    if (B.p1 && (!aligned16(B.p1) || B.ld1 % 4 || B.split % 4)) return false;
+  }
+  return true;
+}
+
+template <int BM>
+void launch_tiled(const GemmArgs& a, dim3 grid, cudaStream_t s) {
+  if (a.a_t == 0 && a.b_t == 1) gemm_tiled_kernel<BM, 0, 1><<<grid, 256, 0, s>>>(a);
+  else if (a.a_t == 0 && a.b_t == 0) gemm_tiled_kernel<BM, 0, 0><<<grid, 256, 0, s>>>(a);
+  else if (a.a_t == 1 && a.b_t == 0) gemm_tiled_kernel<BM, 1, 0><<<grid, 256, 0, s>>>(a);
+  else gemm_tiled_kernel<BM, 1, 1><<<grid, 256, 0, s>>>(a);
+}
+
 }  // namespace
 
 int gemm(const GemmArgs& a, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return EGNN_OK;
-  dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM),
-            (unsigned)(a.ksplit > 1 ? a.ksplit : 1));
-  if (a.K <= 0 && a.ksplit <= 1) {
-    // empty reduction: the epilogue still runs on zeros
+  const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
+  if (tiled_ok(a)) {
+    const int64_t tiles128 = ((a.M + 127) / 128) * ((a.N + 127) / 128) * z;
+    if (tiles128 >= 148) {
+      launch_tiled<128>(a, dim3((unsigned)((a.N + 127) / 128), (unsigned)((a.M + 127) / 128), z), s);
+    } else {
+      launch_tiled<64>(a, dim3((unsigned)((a.N + 127) / 128), (unsigned)((a.M + 63) / 64), z), s);
+    }
+  } else {
+    dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), z);
+    gemm_kernel<<<grid, NT, 0, s>>>(a);
   }
-  gemm_kernel<<<grid, NT, 0, s>>>(a);
   EGNN_CHECK_LAUNCH();
   if (a.ksplit > 1) {
     int64_t total = a.M * a.N;
@@ -164,9 +356,9 @@ int gemm(const GemmArgs& a, cudaStream_t s) {
 }
 
 int64_t wgrad_splits(int64_t K, int64_t M, int64_t N) {
-  int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  int64_t want = (2 * 148 + tiles - 1) / tiles;          // about two waves of CTAs
-  int64_t by_len = std::max<int64_t>(1, K / 128);         // at least 128 rows per slice
+  int64_t tiles = ((M + 63) / 64) * ((N + 127) / 128);
+  int64_t want = (148 + tiles - 1) / tiles;               // about one wave of CTAs
+  int64_t by_len = std::max<int64_t>(1, K / 256);         // at least 256 rows per slice
   return std::max<int64_t>(1, std::min<int64_t>({want, by_len, 64}));
 }
 
@@ -181,8 +373,13 @@ int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw
   a.ksplit = (int)wgrad_splits(R, M, N);
   a.part = part;
   if (a.ksplit == 1) a.part = nullptr;
+  const bool fused_db = db && tiled_ok(a);
+  if (fused_db) {
+    a.db = db;
+    a.db_part = a.ksplit > 1 ? part + (int64_t)a.ksplit * M * N : nullptr;
+  }
   EGNN_TRY(gemm(a, s));
-  if (db) EGNN_TRY(colsum(R, M, G, db, part, s));
+  if (db && !fused_db) EGNN_TRY(colsum(R, M, G, db, part, s));
   return EGNN_OK;
 }
 

@@ -54,6 +54,10 @@ struct GemmArgs {
   int round_bf16 = 0;           // round A and B elements to bf16 (bf16-GEMM mode)
   int ksplit = 1;
   float* part = nullptr;
+  // Weight-gradient GEMMs (a_t = 1) may also produce db[m] = sum_k A(m, k);
+  // with split-K the slices go to db_part[z][M] first.
+  float* db = nullptr;
+  float* db_part = nullptr;
 };
 
 int gemm(const GemmArgs& a, cudaStream_t s);
@@ -64,7 +68,8 @@ int64_t wgrad_splits(int64_t K, int64_t M, int64_t N);
 
 // Weight gradient dW (M,N) = sum_r G[r, m] * X[r, n]  over r in [0,R),
 // plus optional db[m] = sum_r G[r, m].  Deterministic split-K.
-// `part` must hold wgrad_splits(R,M,N) * (M*N + M) floats.
+// `part` must hold wgrad_splits(R,M,N) * (M*N + M) floats (and at least
+// colsum_splits(R) * M).
 int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw,
           float* db, int round_bf16, float* part, cudaStream_t s);
 

@@ -1,0 +1,284 @@
+"""Multi-GPU training for the EGNN layer: one process per GPU.
+
+Two decompositions:
+
+* Graph-batch data parallelism (batches of independent graphs): every rank
+  steps its own graphs; gradients are summed with one all-reduce of a flat
+  fp32 buffer (NCCL over NVLink on GPUs, gloo in the CPU tests).
+  ``partition_graphs`` balances graphs over ranks by edges + nodes
+  (longest-processing-time greedy) when a fixed global batch is split.
+
+* Node-range partitioning of one giant graph: nodes are ordered along a
+  Morton curve and each rank owns a contiguous range and the CSR rows of its
+  nodes.  Before every layer the rank fetches the rows of h and x of its
+  "halo" (source nodes of its edges owned by other ranks); in the backward
+  the gradients of those halo rows are returned to their owners and added
+  there in fixed rank order (deterministic).  ``HaloPlan`` builds the
+  exchange lists once; ``halo_exchange`` is the autograd-aware exchange.
+
+The reference (models/EGNN/egnn_clean.py) is single-process; this module is
+the multi-GPU layer the benchmark configurations ask for.
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import List, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+# ---------------------------------------------------------------------------
+# data parallel
+# ---------------------------------------------------------------------------
+
+def partition_graphs(n_nodes: Sequence[int], n_edges: Sequence[int], world: int) -> List[List[int]]:
+    """Assign graphs to ranks, balancing sum(E + N) (greedy LPT).
+
+    Deterministic: graphs are taken by decreasing cost (ties by index) and
+    each goes to the least-loaded rank (ties by rank).  Each rank's list is
+    returned in increasing graph order.
+    """
+    cost = [int(e) + int(n) for n, e in zip(n_nodes, n_edges)]
+    order = sorted(range(len(cost)), key=lambda g: (-cost[g], g))
+    load = [0] * world
+    parts: List[List[int]] = [[] for _ in range(world)]
+    for g in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        parts[r].append(g)
+        load[r] += cost[g]
+    return [sorted(p) for p in parts]
+
+
+class GradAllReduce:
+    """Sum (or average) the gradients of `params` over the process group.
+
+    The gradients are packed into one flat fp32 buffer, reduced with a single
+    all_reduce and unpacked; parameters without a gradient contribute zeros,
+    so every rank issues the same collective in the same order.
+    """
+
+    def __init__(self, params, average: bool = True, group=None):
+        self.params = [p for p in params]
+        self.average = average
+        self.group = group
+        n = sum(p.numel() for p in self.params)
+        dev = self.params[0].device if self.params else torch.device("cpu")
+        self.flat = torch.zeros(n, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return
+        off = 0
+        for p in self.params:
+            n = p.numel()
+            if p.grad is None:
+                self.flat[off:off + n].zero_()
+            else:
+                self.flat[off:off + n].copy_(p.grad.reshape(-1))
+            off += n
+        dist.all_reduce(self.flat, group=self.group)
+        if self.average:
+            self.flat.div_(dist.get_world_size(self.group))
+        off = 0
+        for p in self.params:
+            n = p.numel()
+            view = self.flat[off:off + n].view_as(p)
+            if p.grad is None:
+                p.grad = view.clone()
+            else:
+                p.grad.copy_(view)
+            off += n
+
+
+# ---------------------------------------------------------------------------
+# node-range partitioning with halo exchange
+# ---------------------------------------------------------------------------
+
+def node_ranges(n_nodes: int, world: int) -> List[int]:
+    """Contiguous, near-equal node ranges: rank r owns [b[r], b[r+1])."""
+    return [(n_nodes * r) // world for r in range(world + 1)]
+
+
+@dataclasses.dataclass
+class HaloPlan:
+    """Exchange lists of one rank for a node-range partition.
+
+    own_lo, own_hi: owned global node range.
+    halo: (n_halo,) global ids of the non-owned source nodes, grouped by owner
+          rank in increasing rank order, increasing id inside a group;
+          local index of halo k is n_own + k.
+    recv_counts[p]: how many halo rows come from rank p.
+    send_idx[p]: local (owned) row indices this rank sends to rank p.
+    row, col: the local edge list (destination local ids in [0, n_own),
+          source local ids in [0, n_own + n_halo)).
+    """
+
+    rank: int
+    world: int
+    own_lo: int
+    own_hi: int
+    halo: torch.Tensor
+    recv_counts: List[int]
+    send_idx: List[torch.Tensor]
+    row: torch.Tensor
+    col: torch.Tensor
+
+    @property
+    def n_own(self) -> int:
+        return self.own_hi - self.own_lo
+
+    @property
+    def n_local(self) -> int:
+        return self.n_own + int(self.halo.numel())
+
+    @property
+    def send_counts(self) -> List[int]:
+        return [int(t.numel()) for t in self.send_idx]
+
+    def to(self, device) -> "HaloPlan":
+        """Keep the send lists on `device` (they index device rows every layer)."""
+        self.send_idx = [t.to(device) for t in self.send_idx]
+        return self
+
+
+def local_edges(row: torch.Tensor, col: torch.Tensor, lo: int, hi: int):
+    """Edges whose destination lies in [lo, hi), and their halo sources."""
+    keep = (row >= lo) & (row < hi)
+    r, c = row[keep], col[keep]
+    outside = (c < lo) | (c >= hi)
+    halo = torch.unique(c[outside])   # sorted ascending -> grouped by owner rank
+    return r, c, halo
+
+
+def build_halo_plan(row: torch.Tensor, col: torch.Tensor, n_nodes: int, rank: int, world: int,
+                    group=None) -> HaloPlan:
+    """Exchange plan for `rank`; every rank calls it (one all_to_all of counts
+    and one of index lists).  `row`/`col` are the global edge list (CPU)."""
+    b = node_ranges(n_nodes, world)
+    lo, hi = b[rank], b[rank + 1]
+    r, c, halo = local_edges(row, col, lo, hi)
+    owner = torch.bucketize(halo, torch.tensor(b[1:-1], dtype=halo.dtype), right=True)
+    recv_counts = [int((owner == p).sum()) for p in range(world)]
+    # local ids: owned -> id - lo ; halo -> n_own + position in `halo`
+    n_own = hi - lo
+    pos = torch.searchsorted(halo, c)
+    c_local = torch.where((c >= lo) & (c < hi), c - lo, n_own + pos)
+    r_local = r - lo
+    # tell every owner which of its nodes this rank needs
+    send_idx = _exchange_requests(halo, recv_counts, b, rank, world, group)
+    return HaloPlan(rank, world, lo, hi, halo, recv_counts, send_idx, r_local.long(), c_local.long())
+
+
+def _exchange_requests(halo, recv_counts, b, rank, world, group):
+    if world == 1:
+        return [torch.zeros(0, dtype=torch.long)]
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" \
+        else torch.device("cpu")
+    counts_out = torch.tensor(recv_counts, dtype=torch.long, device=dev)
+    counts_in = torch.empty_like(counts_out)
+    dist.all_to_all_single(counts_in, counts_out, group=group)
+    reqs = halo.to(dev)
+    got = torch.empty(int(counts_in.sum()), dtype=torch.long, device=dev)
+    dist.all_to_all_single(got, reqs, output_split_sizes=counts_in.tolist(),
+                           input_split_sizes=recv_counts, group=group)
+    got = got.cpu() - b[rank]
+    out, off = [], 0
+    for p in range(world):
+        n = int(counts_in[p])
+        out.append(got[off:off + n].clone())
+        off += n
+    return out
+
+
+class _HaloExchange(torch.autograd.Function):
+    """[h_own] -> [h_own; h_halo] with h_halo fetched from the owners.
+
+    Backward: the gradient rows of the halo are sent back and added to the
+    owners' rows, summed in increasing source-rank order."""
+
+    @staticmethod
+    def forward(ctx, h_own, plan: HaloPlan, group):
+        ctx.plan, ctx.group = plan, group
+        send = [h_own[idx] if idx.device == h_own.device else h_own[idx.to(h_own.device)]
+                for idx in plan.send_idx]
+        recv = _all_to_all_rows(send, plan.recv_counts, h_own, group)
+        return torch.cat([h_own, recv], dim=0)
+
+    @staticmethod
+    def backward(ctx, g):
+        plan, group = ctx.plan, ctx.group
+        g = g.contiguous()
+        g_own = g[:plan.n_own].clone()
+        g_halo = g[plan.n_own:]
+        # rows destined to each owner, in the order the owner sent them
+        send, off = [], 0
+        for p in range(plan.world):
+            n = plan.recv_counts[p]
+            send.append(g_halo[off:off + n])
+            off += n
+        back = _all_to_all_rows(send, plan.send_counts, g_own, group)
+        off = 0
+        for p in range(plan.world):
+            n = plan.send_counts[p]
+            if n:
+                g_own.index_add_(0, plan.send_idx[p].to(g.device, non_blocking=True), back[off:off + n])
+            off += n
+        return g_own, None, None
+
+
+def _all_to_all_rows(send: List[torch.Tensor], recv_counts: List[int], like: torch.Tensor, group):
+    """Row all-to-all: send[p] goes to rank p; returns rows from ranks 0..P-1 concatenated."""
+    world = len(send)
+    width = like.shape[1:]
+    if world == 1:
+        return like.new_zeros((0, *width))
+    out = like.new_empty((sum(recv_counts), *width))
+    inp = torch.cat([s.reshape(-1, *width) for s in send], dim=0) if send else like.new_zeros((0, *width))
+    dist.all_to_all_single(out, inp.contiguous(), output_split_sizes=recv_counts,
+                           input_split_sizes=[int(s.shape[0]) for s in send], group=group)
+    return out
+
+
+def halo_exchange(h_own: torch.Tensor, plan: HaloPlan, group=None) -> torch.Tensor:
+    """Autograd-aware halo fetch: returns (n_own + n_halo, F) rows."""
+    if plan.world == 1:
+        return h_own
+    return _HaloExchange.apply(h_own, plan, group)
+
+
+__all__ = ["partition_graphs", "GradAllReduce", "node_ranges", "HaloPlan", "build_halo_plan",
+           "halo_exchange", "local_edges"]
+
+
+def partitioned_forward(model, h_own: torch.Tensor, x_own: torch.Tensor, csr_local, plan: HaloPlan,
+                        group=None):
+    """EGNN.forward (egnn_clean.py:141-146) on one rank of a node partition.
+
+    embedding_in on the owned rows; before every layer the halo rows of h
+    and x are fetched; each layer runs on the local graph (owned rows plus
+    halo rows, edges into owned rows only) and keeps its owned rows;
+    embedding_out on the owned rows.  Returns (h_out_own, x_out_own)."""
+    from .egnn import linear
+    n_own = plan.n_own
+    h = linear(h_own, model.embedding_in)
+    x = x_own
+    for i in range(model.n_layers):
+        h_loc = halo_exchange(h, plan, group)
+        x_loc = halo_exchange(x, plan, group)
+        h_loc, x_loc, _ = model._modules["gcl_%d" % i](h_loc, csr_local, x_loc)
+        h, x = h_loc[:n_own], x_loc[:n_own]
+    return linear(h.contiguous(), model.embedding_out), x
+
+
+def global_sum(t: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of `t` over all ranks in the forward; the gradient flows to the
+    local term only (each rank back-propagates its own share)."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return t
+    tot = t.detach().clone()
+    dist.all_reduce(tot, group=group)
+    return t + (tot - t.detach())
+
+
+__all__ += ["partitioned_forward", "global_sum"]

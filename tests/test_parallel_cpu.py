@@ -1,0 +1,157 @@
+"""Multi-process logic on CPU ranks (gloo, world_size 2): graph partitioning,
+gradient all-reduce, and the node-range halo exchange checked end to end
+against the single-process oracle."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import egnn_oracle as O
+from pymolecular_b200 import parallel as P
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _run(world, fn, *args):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, q, args)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for ok, msg in results:
+        assert ok, msg
+    return results
+
+
+def _entry(rank, world, port, fn, q, args):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        fn(rank, world, *args)
+        dist.barrier()
+        q.put((True, ""))
+    except Exception as exc:  # report to the parent instead of hanging it
+        import traceback
+        q.put((False, f"rank {rank}: {exc}\n{traceback.format_exc()}"))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_partition_graphs_balanced_and_deterministic():
+    g = torch.Generator().manual_seed(0)
+    n = torch.randint(9, 30, (512,), generator=g).tolist()
+    e = [k * (k - 1) for k in n]
+    parts = P.partition_graphs(n, e, 8)
+    assert sorted(sum(parts, [])) == list(range(512))
+    loads = [sum(n[i] + e[i] for i in p) for p in parts]
+    assert max(loads) / min(loads) < 1.01
+    assert parts == P.partition_graphs(n, e, 8)
+
+
+def test_node_ranges_cover():
+    b = P.node_ranges(1000, 3)
+    assert b[0] == 0 and b[-1] == 1000 and all(b[i] <= b[i + 1] for i in range(3))
+
+
+def _grad_allreduce_worker(rank, world):
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(4, 3)
+    x = torch.full((2, 4), float(rank + 1))
+    lin(x).sum().backward()
+    expect = torch.full((3, 4), 2.0 * (1 + 2) / 2)   # mean over ranks of 2*(rank+1)
+    P.GradAllReduce(lin.parameters())()
+    assert torch.allclose(lin.weight.grad, expect)
+    assert torch.allclose(lin.bias.grad, torch.full((3,), 2.0))
+
+
+def test_grad_allreduce_two_ranks():
+    _run(2, _grad_allreduce_worker)
+
+
+def _graph(seed, n=160, k=6):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.rand(n, 3, generator=g, dtype=torch.float64) * 10
+    d = torch.cdist(x, x) + torch.eye(n, dtype=torch.float64) * 1e9
+    nbr = d.topk(k, largest=False).indices       # k nearest sources per destination
+    row = torch.arange(n).repeat_interleave(k)
+    col = nbr.reshape(-1)
+    h = torch.randn(n, 16, generator=g, dtype=torch.float64)
+    wh = torch.randn(n, 16, generator=g, dtype=torch.float64)
+    wx = torch.randn(n, 3, generator=g, dtype=torch.float64)
+    return row, col, x, h, wh, wx
+
+
+def _halo_worker(rank, world, seed):
+    row, col, x, h, wh, wx = _graph(seed)
+    n = x.shape[0]
+    params = O.init_params(16, 16, 1, 1, seed=seed, dtype=torch.float64)
+    lp = {k[len("gcl_0."):]: v for k, v in params.items() if k.startswith("gcl_0.")}
+    lp["coord_mlp.2.weight"] = lp["coord_mlp.2.weight"] * 300.0
+    plan = P.build_halo_plan(row, col, n, rank, world)
+    lo, hi = plan.own_lo, plan.own_hi
+    leaf = {k: v.clone().requires_grad_(True) for k, v in lp.items()}
+    h_own = h[lo:hi].clone().requires_grad_(True)
+    x_own = x[lo:hi].clone().requires_grad_(True)
+    h_loc = P.halo_exchange(h_own, plan)
+    x_loc = P.halo_exchange(x_own, plan)
+    ho, xo = O.e_gcl(leaf, "", h_loc, plan.row, plan.col, x_loc)
+    loss = (ho[:plan.n_own] * wh[lo:hi]).sum() + (xo[:plan.n_own] * wx[lo:hi]).sum()
+    loss.backward()
+    grads = torch.cat([leaf[k].grad.reshape(-1) for k in sorted(leaf)])
+    dist.all_reduce(grads)
+    # single-process reference on the whole graph
+    leaf2 = {k: v.clone().requires_grad_(True) for k, v in lp.items()}
+    hh = h.clone().requires_grad_(True)
+    xx = x.clone().requires_grad_(True)
+    ho2, xo2 = O.e_gcl(leaf2, "", hh, row, col, xx)
+    ((ho2 * wh).sum() + (xo2 * wx).sum()).backward()
+    ref = torch.cat([leaf2[k].grad.reshape(-1) for k in sorted(leaf2)])
+    assert torch.allclose(ho[:plan.n_own], ho2[lo:hi], atol=1e-12, rtol=0)
+    assert torch.allclose(xo[:plan.n_own], xo2[lo:hi], atol=1e-12, rtol=0)
+    assert torch.allclose(grads, ref, atol=1e-10, rtol=1e-10)
+    assert torch.allclose(h_own.grad, hh.grad[lo:hi], atol=1e-10, rtol=1e-10)
+    assert torch.allclose(x_own.grad, xx.grad[lo:hi], atol=1e-10, rtol=1e-10)
+    assert plan.n_local > plan.n_own   # the partition really cuts edges
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_halo_exchange_matches_single_process(world):
+    _run(world, _halo_worker, 7)
+
+
+def _global_sum_worker(rank, world):
+    t = torch.tensor([float(rank + 1)], requires_grad=True)
+    s = P.global_sum(t)
+    assert float(s) == sum(range(1, world + 1))
+    (s * 3.0).sum().backward()
+    assert float(t.grad) == 3.0
+
+
+def test_global_sum_gradient_stays_local():
+    _run(2, _global_sum_worker)
+
+
+def test_halo_plan_lists():
+    row, col, *_ = _graph(3, n=90, k=4)
+    # single-process plan views for two ranks built without a process group
+    b = P.node_ranges(90, 2)
+    r, c, halo = P.local_edges(row, col, b[0], b[1])
+    assert torch.all((r >= b[0]) & (r < b[1]))
+    assert torch.all((halo >= b[1]))
+    assert torch.equal(halo, torch.unique(halo))

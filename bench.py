@@ -122,6 +122,18 @@ class ClockSampler:
                 "power_w_max": max(r[2] for r in rows)}
 
 
+def ncu_traffic(config: int, kernel: str, edges: int):
+    """DRAM bytes per launch measured by ncu for this kernel and workload
+    (profiles/ncu_traffic.json), scaled to `edges` edges per launch; None if
+    no capture covers it."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    try:
+        rec = json.loads(p.read_text())[f"config{config}"][kernel]
+    except (OSError, KeyError, ValueError):
+        return None
+    return rec["bytes_per_launch"] * edges / rec["edges_per_launch"]
+
+
 def model_flops(cfg, n_nodes, n_edges):
     """Credited (algorithmic) flops of one training step, factored EGNN count.
 
@@ -434,7 +446,10 @@ def run_b200(args):
             "roofline": {"kernel": "edge_bwd", "bound": "tensor", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peaks['source']} bf16 sustained",
-                         "traffic": None, "per_launch_ms": per_launch_ms, "launches": bwd_n,
+                         "traffic": (ncu_traffic(args.config, "edge_bwd", prob.edges_rank)
+                                     if prob.precision == "bf16" and H == 128 else None),
+                         "traffic_unit": "bytes per launch (ncu capture)",
+                         "per_launch_ms": per_launch_ms, "launches": bwd_n,
                          "flops_per_launch": flops_launch,
                          "edge_fwd_per_launch_ms": fwd_ms / max(fwd_n, 1),
                          "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1),

@@ -280,8 +280,14 @@ class Problem:
             return self.parallel.partitioned_forward(self.model, h, x, csr, self.plan)
         return self.model(h, x, csr)
 
+    def zero_grad(self):
+        if self.world > 1:
+            self.sync_grads.zero_grad()
+        else:
+            self.opt.zero_grad(set_to_none=True)
+
     def step(self):
-        self.opt.zero_grad(set_to_none=True)
+        self.zero_grad()
         ho, _ = self.forward(self.h, self.x, self.csr)
         loss = self.loss(ho)
         loss.backward()
@@ -302,7 +308,7 @@ class Problem:
         device from the edge list, forward, loss, backward, update, loss D2H."""
         d = {k: v.to(self.dev, non_blocking=True) for k, v in host.items()}
         csr = self.CSR.from_edges(d["row"], d["col"], n_nodes=self.n_nodes_csr, device=self.dev)
-        self.opt.zero_grad(set_to_none=True)
+        self.zero_grad()
         ho, _ = self.forward(d["h"], d["x"], csr)
         loss = self.loss(ho, d.get("gp"), d["tgt"])
         loss.backward()

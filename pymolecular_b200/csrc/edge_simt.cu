@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeBwdArgs a) {
 #pragma unroll
       for (int g = 0; g < C::NG; ++g) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (e < n) v = *reinterpret_cast<const float4*>(a.g_agg + (int64_t)rowl[e] * H + C::col(g, 0));
+        if (e < n) v = *reinterpret_cast<const float4*>(a.g_agg + (int64_t)rowl[e] * (a.ld_gagg ? a.ld_gagg : H) + C::col(g, 0));
         acc[m][g * 4 + 0] = v.x; acc[m][g * 4 + 1] = v.y;
         acc[m][g * 4 + 2] = v.z; acc[m][g * 4 + 3] = v.w;
       }

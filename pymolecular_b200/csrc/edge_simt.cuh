@@ -41,7 +41,8 @@ struct EdgeBwdArgs : EdgeCommon {
   const float* W2 = nullptr;     // (H,H) edge_mlp.2.weight (bf16-rounded in bf16 mode)
   const float* Wc1 = nullptr;    // (H,H) coord_mlp.0.weight (idem)
   const float* gx_out = nullptr; // (N,3) dL/dx'
-  const float* g_agg = nullptr;  // (N,H) dL/dagg from the node MLP backward
+  const float* g_agg = nullptr;  // (N, ld_gagg) dL/dagg from the node MLP backward
+  int64_t ld_gagg = 0;           // row stride of g_agg (H when 0)
   float* S_dst = nullptr;        // (N,H) out: sum over each row of dL/da1
   float* gxd = nullptr;          // (N,3) out: sum over each row of dL/d(x_i - x_j)
   float* gstore = nullptr;       // (E,H) out: dL/da1 per CSR edge

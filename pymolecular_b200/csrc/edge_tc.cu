@@ -659,7 +659,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       float v[32];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
       const __half2* drow = reinterpret_cast<const __half2*>(d2s + g.e * C::LDD + g.col0);
-      const float* ga = a.g_agg + (int64_t)rowi[g.e] * H + g.col0;
+      const float* ga = a.g_agg + (int64_t)rowi[g.e] * (a.ld_gagg ? a.ld_gagg : H) + g.col0;
 #pragma unroll
       for (int q = 0; q < 32; q += 4) {
         float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);

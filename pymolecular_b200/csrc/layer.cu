@@ -165,7 +165,7 @@ FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
 }
 
 struct BwdWs {
-  Prep prep; float* g_n1pre; float* gh_acc; float* g_agg;
+  Prep prep; float* g_n1pre; float* ghg;   // ghg: (N, 2H) = [dL/dh from the node MLP | dL/dagg]
   float* S_dst; float* S_src; float* gxd; float* gstore; float4* gdstore; float* carry;
   int32_t* carry_row; float* part; float* wpart;
 };
@@ -183,8 +183,7 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   BwdWs w;
   w.prep = carve_prep(c, N, H, d->edge_attr_dim, true);
   w.g_n1pre = c.take<float>((size_t)N * H);
-  w.gh_acc = c.take<float>((size_t)N * H);
-  w.g_agg = c.take<float>((size_t)N * H);
+  w.ghg = c.take<float>((size_t)N * 2 * H);
   w.S_dst = c.take<float>((size_t)N * H);
   w.S_src = c.take<float>((size_t)N * H);
   w.gxd = c.take<float>((size_t)N * 3);
@@ -346,18 +345,14 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
                  gp->node_b1, 0, w.wpart, s));
   {
+    // [dL/dh (MLP path) + residual | dL/dagg] = g_n1pre Wn1, one N x 2H product
     GemmArgs gh;
-    gh.M = N; gh.N = H; gh.K = H;
+    gh.M = N; gh.N = 2 * H; gh.K = H;
     gh.A = mat(w.g_n1pre, H);
     gh.B = mat(p->node_w1, 2 * H); gh.b_t = 0;
-    if (residual) { gh.resid = gh_out; gh.ldr = H; }
-    gh.C = w.gh_acc; gh.ldc = H;
+    if (residual) { gh.resid = gh_out; gh.ldr = H; gh.resid_cols = H; }
+    gh.C = w.ghg; gh.ldc = 2 * H;
     EGNN_TRY(gemm(gh, s));
-    GemmArgs ga = gh;
-    ga.B = mat(p->node_w1 + H, 2 * H);
-    ga.resid = nullptr;
-    ga.C = w.g_agg;
-    EGNN_TRY(gemm(ga, s));
   }
 
   // ---- edge backward: dst pass, fix-up, partial reduction, src pass
@@ -370,7 +365,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   a.carry = w.carry; a.carry_row = w.carry_row;
   a.W2 = bf ? w.prep.W2r : p->edge_w2;
   a.Wc1 = bf ? w.prep.Wc1r : p->coord_w1;
-  a.gx_out = gx_out; a.g_agg = w.g_agg;
+  a.gx_out = gx_out; a.g_agg = w.ghg + H; a.ld_gagg = 2 * H;
   a.S_dst = w.S_dst; a.gxd = w.gxd; a.gstore = w.gstore; a.gdstore = w.gdstore; a.part = w.part;
   if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
   else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
@@ -384,7 +379,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.M = N; gh.N = H; gh.K = 2 * H;
     gh.A = mat_cols(w.S_dst, H, H, w.S_src, H);
     gh.B = mat(w.prep.WPQ, H); gh.b_t = 0;
-    gh.resid = w.gh_acc; gh.ldr = H;
+    gh.resid = w.ghg; gh.ldr = 2 * H;
     gh.C = grad_h; gh.ldc = H;
     EGNN_TRY(gemm(gh, s));
   }

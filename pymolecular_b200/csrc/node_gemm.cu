@@ -15,7 +15,7 @@ constexpr int BM = 64, BN = 64, BK = 16, NT = 256;
 
 struct Epi {
   const float* bias; float* pre; int64_t ldp; int act;
-  const float* aux; int64_t ldaux; const float* resid; int64_t ldr;
+  const float* aux; int64_t ldaux; const float* resid; int64_t ldr; int64_t resid_cols;
   float* C; int64_t ldc;
   __device__ __forceinline__ void apply(int64_t m, int64_t n, float v) const {
     if (bias) v += bias[n];
@@ -27,7 +27,7 @@ struct Epi {
       silu_and_grad(aux[m * ldaux + n], y, dy);
       v *= dy;
     }
-    if (resid) v += resid[m * ldr + n];
+    if (resid && n < resid_cols) v += resid[m * ldr + n];
     C[m * ldc + n] = v;
   }
 };
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(NT) gemm_kernel(GemmArgs a) {
     }
     return;
   }
-  Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.C, a.ldc};
+  Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.resid_cols, a.C, a.ldc};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     int64_t m = m0 + ty * 4 + i;
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(NT) gemm_kernel(GemmArgs a) {
 }
 
 __global__ void gemm_reduce_kernel(GemmArgs a) {
-  Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.C, a.ldc};
+  Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.resid_cols, a.C, a.ldc};
   const int64_t total = a.M * a.N;
   if (a.db && a.db_part) {
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < a.M;
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
       else a.db[m] = dbacc[i];
     }
   }
-  Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.C, a.ldc};
+  Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.resid_cols, a.C, a.ldc};
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
     const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));

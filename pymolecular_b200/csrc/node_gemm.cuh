@@ -51,6 +51,7 @@ struct GemmArgs {
   int act = ACT_NONE;
   const float* aux = nullptr; int64_t ldaux = 0;
   const float* resid = nullptr; int64_t ldr = 0;
+  int64_t resid_cols = INT64_MAX;   // the residual is added to columns n < resid_cols only
   int round_bf16 = 0;           // round A and B elements to bf16 (bf16-GEMM mode)
   int ksplit = 1;
   float* part = nullptr;

@@ -53,9 +53,11 @@ def partition_graphs(n_nodes: Sequence[int], n_edges: Sequence[int], world: int)
 class GradAllReduce:
     """Sum (or average) the gradients of `params` over the process group.
 
-    The gradients are packed into one flat fp32 buffer, reduced with a single
-    all_reduce and unpacked; parameters without a gradient contribute zeros,
-    so every rank issues the same collective in the same order.
+    All gradients live in one flat fp32 buffer: ``zero_grad()`` clears it and
+    makes every ``p.grad`` a view of it, so the backward accumulates straight
+    into the buffer and the reduction is one all_reduce with no packing.
+    Gradients that arrive as separate tensors are copied in first.  Every rank
+    issues the same collective in the same order.
     """
 
     def __init__(self, params, average: bool = True, group=None):
@@ -65,30 +67,28 @@ class GradAllReduce:
         n = sum(p.numel() for p in self.params)
         dev = self.params[0].device if self.params else torch.device("cpu")
         self.flat = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.views, off = [], 0
+        for p in self.params:
+            self.views.append(self.flat[off:off + p.numel()].view_as(p))
+            off += p.numel()
+
+    def zero_grad(self):
+        self.flat.zero_()
+        for p, v in zip(self.params, self.views):
+            p.grad = v
 
     def __call__(self):
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return
-        off = 0
-        for p in self.params:
-            n = p.numel()
+        for p, v in zip(self.params, self.views):
             if p.grad is None:
-                self.flat[off:off + n].zero_()
-            else:
-                self.flat[off:off + n].copy_(p.grad.reshape(-1))
-            off += n
+                v.zero_()
+            elif p.grad.data_ptr() != v.data_ptr():
+                v.copy_(p.grad)
+            p.grad = v
         dist.all_reduce(self.flat, group=self.group)
         if self.average:
             self.flat.div_(dist.get_world_size(self.group))
-        off = 0
-        for p in self.params:
-            n = p.numel()
-            view = self.flat[off:off + n].view_as(p)
-            if p.grad is None:
-                p.grad = view.clone()
-            else:
-                p.grad.copy_(view)
-            off += n
 
 
 # ---------------------------------------------------------------------------

@@ -72,12 +72,19 @@ def test_node_ranges_cover():
 def _grad_allreduce_worker(rank, world):
     torch.manual_seed(0)
     lin = torch.nn.Linear(4, 3)
-    x = torch.full((2, 4), float(rank + 1))
-    lin(x).sum().backward()
-    expect = torch.full((3, 4), 2.0 * (1 + 2) / 2)   # mean over ranks of 2*(rank+1)
-    P.GradAllReduce(lin.parameters())()
-    assert torch.allclose(lin.weight.grad, expect)
-    assert torch.allclose(lin.bias.grad, torch.full((3,), 2.0))
+    sync = P.GradAllReduce(lin.parameters())
+    for bound in (False, True):   # gradients as fresh tensors, then as views of the flat buffer
+        if bound:
+            sync.zero_grad()
+        else:
+            lin.zero_grad(set_to_none=True)
+        x = torch.full((2, 4), float(rank + 1))
+        lin(x).sum().backward()
+        expect = torch.full((3, 4), 2.0 * (1 + 2) / 2)   # mean over ranks of 2*(rank+1)
+        sync()
+        assert torch.allclose(lin.weight.grad, expect)
+        assert torch.allclose(lin.bias.grad, torch.full((3,), 2.0))
+        assert lin.weight.grad.data_ptr() == sync.views[0].data_ptr()
 
 
 def test_grad_allreduce_two_ranks():

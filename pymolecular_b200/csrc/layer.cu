@@ -57,6 +57,11 @@ int64_t max_ctas(int64_t E, int H, int num_sms) {
 struct Prep {
   float4* xp; float* bias2; float* W2T; float* Wc1T; float* W2r; float* Wc1r; float* wr; float* We;
   float* WPQ;   // (2H, H): rows of edge_mlp.0 restricted to the h_i and h_j columns, contiguous
+  // forward only: transposed weights (in x out), so that the forward node
+  // GEMMs read their weight operand k-major like the backward ones
+  float* Wn2T;  // (H, H):  node_mlp.2.weight^T
+  float* Wn1T;  // (2H, H): node_mlp.0.weight^T
+  float* WPQT;  // (H, 2H): WPQ^T
 };
 
 Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd) {
@@ -70,16 +75,39 @@ Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd) {
   p.wr = c.take<float>(H);
   p.We = c.take<float>((size_t)H * std::max(d, 1));
   p.WPQ = c.take<float>((size_t)2 * H * H);
+  p.Wn2T = bwd ? nullptr : c.take<float>((size_t)H * H);
+  p.Wn1T = bwd ? nullptr : c.take<float>((size_t)2 * H * H);
+  p.WPQT = bwd ? nullptr : c.take<float>((size_t)2 * H * H);
   return p;
 }
+
+__host__ __device__ inline int64_t prep_transposes(const Prep& o, int H) { return o.Wn2T ? 5LL * H * H : 0; }
 
 __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_layer_params p,
                             const float* x, Prep o) {
   const int64_t HH = (int64_t)H * H;
-  const int64_t total = N + 2 * H + 4 * HH + H + (int64_t)H * d + 2 * HH;
+  const int64_t total = N + 2 * H + 4 * HH + H + (int64_t)H * d + 2 * HH + prep_transposes(o, H);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     int64_t t = idx;
+    if (o.Wn2T) {
+      if (t < HH) {   // Wn2T[n][k] = node_w2[k][n]
+        o.Wn2T[t] = p.node_w2[(t % H) * H + t / H];
+        continue;
+      }
+      t -= HH;
+      if (t < 2 * HH) {   // Wn1T[n][k] = node_w1[k][n], node_w1 is (H, 2H)
+        o.Wn1T[t] = p.node_w1[(t % H) * 2 * H + t / H];
+        continue;
+      }
+      t -= 2 * HH;
+      if (t < 2 * HH) {   // WPQT[n][k] = WPQ[k][n], n < H, k < 2H
+        const int64_t n = t / (2 * H), k = t % (2 * H);
+        o.WPQT[t] = k < H ? p.edge_w1[k * ld1 + n] : p.edge_w1[(k - H) * ld1 + H + n];
+        continue;
+      }
+      t -= 2 * HH;
+    }
     if (t < 2 * HH) {
       const int64_t r = t / H, c = t % H;   // WPQ[r][c]: r < H -> Wa, else Wb
       o.WPQ[t] = r < H ? p.edge_w1[r * ld1 + c] : p.edge_w1[(r - H) * ld1 + H + c];
@@ -111,19 +139,19 @@ __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_l
 
 int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_params* p,
                 const float* x, const Prep& o, cudaStream_t s) {
-  const int64_t total = N + 2 * H + 6LL * H * H + H + (int64_t)H * d;
+  const int64_t total = N + 2 * H + 6LL * H * H + H + (int64_t)H * d + prep_transposes(o, H);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
   prep_kernel<<<blocks, 256, 0, s>>>(N, H, d, ld1, bf ? 1 : 0, *p, x, o);
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
 
-int gemm_pq(int64_t N, int H, const float* h, const float* WPQ, const float* bias2, float* PQ,
+int gemm_pq(int64_t N, int H, const float* h, const float* WPQT, const float* bias2, float* PQ,
             cudaStream_t s) {
   GemmArgs g;
   g.M = N; g.N = 2 * H; g.K = H;
   g.A = mat(h, H);
-  g.B = mat(WPQ, H); g.b_t = 1;
+  g.B = mat(WPQT, 2 * H); g.b_t = 0;
   g.bias = bias2;
   g.C = PQ; g.ldc = 2 * H;
   g.round_bf16 = 0;
@@ -267,7 +295,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   float* agg = sv.agg;
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, h, w.prep.WPQ, w.prep.bias2, sv.PQ, s));
+  EGNN_TRY(gemm_pq(N, H, h, w.prep.WPQT, w.prep.bias2, sv.PQ, s));
 
   const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
   EdgeGrid eg;
@@ -283,7 +311,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   GemmArgs n1;
   n1.M = N; n1.N = H; n1.K = 2 * H;
   n1.A = mat_cols(h, H, H, agg, H);
-  n1.B = mat(p->node_w1, 2 * H); n1.b_t = 1;
+  n1.B = mat(w.prep.Wn1T, H); n1.b_t = 0;
   n1.bias = p->node_b1; n1.act = ACT_SILU;
   n1.pre = sv.n1pre; n1.ldp = H;
   n1.C = sv.n1; n1.ldc = H;
@@ -292,7 +320,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   GemmArgs n2;
   n2.M = N; n2.N = H; n2.K = H;
   n2.A = mat(sv.n1, H);
-  n2.B = mat(p->node_w2, H); n2.b_t = 1;
+  n2.B = mat(w.prep.Wn2T, H); n2.b_t = 0;
   n2.bias = p->node_b2;
   if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = H; }
   n2.C = h_out; n2.ldc = H;

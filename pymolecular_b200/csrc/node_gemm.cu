@@ -1,8 +1,9 @@
-// Node-side SIMT GEMMs (fp32 FFMA, optional bf16 rounding of the inputs).
+// Node-side SIMT GEMMs (fp32 FFMA).
 //
-// 64x64 output tile per 256-thread CTA, K staged through shared memory in
-// slices of 16, 4x4 outputs per thread.  Deterministic: every output is one
-// thread's fixed-order sum; split-K partial slices are added in slice order.
+// The tiled kernel (below) takes every operand layout the layer uses; a
+// plain 64x64-tile kernel covers the rest (bf16-rounded inputs, K not a
+// multiple of 4, unaligned operands).  Deterministic: every output is one thread's
+// fixed-order sum; split-K partial slices are added in slice order.
 #include <algorithm>
 
 #include "node_gemm.cuh"
@@ -128,8 +129,17 @@ __global__ void gemm_reduce_kernel(GemmArgs a) {
   }
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
+    // slices loaded eight at a time (independent loads), added in slice order
     float v = 0.f;
-    for (int z = 0; z < a.ksplit; ++z) v += a.part[(int64_t)z * total + idx];
+    int z = 0;
+    for (; z + 8 <= a.ksplit; z += 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = a.part[(int64_t)(z + u) * total + idx];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v += t[u];
+    }
+    for (; z < a.ksplit; ++z) v += a.part[(int64_t)z * total + idx];
     e.apply(idx / a.N, idx % a.N, v);
   }
 }
@@ -152,78 +162,130 @@ __global__ void colsum_reduce_kernel(int64_t C, int S, const float* part, float*
 }
 
 
-// ---- register-tiled path -------------------------------------------------------
-// BM x 128 output tile (BM = 128 or 64), K in slices of 8 through a double
-// buffer, 256 threads each owning (BM/16) x 8 outputs.  Used when K is a
-// multiple of 8 and the operands allow 16-byte loads (checked by gemm()).
-template <int BM, int A_T, int B_T>
-__global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
-  constexpr int BN2 = 128, BK2 = 8, TM = BM / 16;
-  __shared__ __align__(16) float As[2][BK2][BM + 4];
-  __shared__ __align__(16) float Bs[2][BK2][BN2 + 4];
-  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
-  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN2;
+// ---- tiled path ------------------------------------------------------------------
+// C (M x N) = A B for every operand layout the layer uses.  Tile 64 x 128
+// per 256-thread CTA; thread (tx, ty) owns rows ty*4 + {0..3} and columns
+// tx*4 + {0..3}, 64 + tx*4 + {0..3}.  K runs in slices of 16 through a double
+// buffer in shared memory, stored k-major: As[k][m], Bs[k][n], so every step
+// of the inner product is an outer product of two register fragments read
+// with 16-byte loads.
+//   k-major operands in global memory (A^T of a weight gradient, B = X[k][n])
+//   are copied with cp.async; row-major ones (A[m][k], B = W[n][k]) are read
+//   four k at a time into registers one slice ahead and stored transposed.
+// 256 threads form a 16 x 16 grid in which every half-warp is a 4 x 4 block,
+// so each fragment load touches 4 distinct 16-byte words per half-warp.
+__device__ __forceinline__ uint32_t sptr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// Zero-filling 16-byte asynchronous copy: nothing is read when `ok` is false.
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sptr(dst)), "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+__device__ __forceinline__ const float* mat_ptr(const Mat& A, int64_t r, int64_t c) {
+  if (A.split_rows) return r < A.split ? A.p0 + r * A.ld0 + c : A.p1 + (r - A.split) * A.ld1 + c;
+  return c < A.split ? A.p0 + r * A.ld0 + c : A.p1 + r * A.ld1 + (c - A.split);
+}
+
+__device__ __forceinline__ void thread_grid(int& tx, int& ty) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  ty = (warp >> 2) * 8 + (lane >> 2);
+  tx = (warp & 3) * 4 + (lane & 3);
+}
+
+// 64 x 128 tiles (TM = 4): on B200 the 128 x 128 tile (TM = 8) measured no
+// faster on these shapes (K = 128..256) and quantises worse over 148 SMs.
+constexpr int TBN = 128, TBK = 16, TTM = 4;
+
+template <int BM>
+constexpr size_t tiled_smem_bytes() {
+  return (size_t)2 * TBK * ((BM + 4) + (TBN + 4)) * sizeof(float);
+}
+
+// One operand slice: ROWS rows (m or n) x 16 k into s[k][row] (leading
+// dimension ROWS + 4).  KMAJ: element (row, k) at X[k][row] (cp.async);
+// otherwise at X[row][k] (register staging, transposed store).
+template <int ROWS, int KMAJ>
+struct Slice {
+  static constexpr int LD = ROWS + 4;
+  static constexpr int Q = ROWS * TBK / 4 / 256;   // 16-byte words per thread
+  float4 r[KMAJ ? 1 : Q];
+  __device__ __forceinline__ void fetch(float* s, const Mat& X, int64_t r0, int64_t rows, int64_t k0,
+                                        int64_t kend) {
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const int c = threadIdx.x + 256 * q;
+      if (KMAJ) {   // word c: k = c / (ROWS / 4), rows 4 (c % (ROWS / 4)) .. + 3
+        const int kl = c / (ROWS / 4), rl = (c % (ROWS / 4)) * 4;
+        const int64_t rr = r0 + rl, k = k0 + kl;
+        const bool ok = rr < rows && k < kend;   // rows % 4 == 0: a word is wholly in or out
+        cp_async16(s + kl * LD + rl, ok ? mat_ptr(X, k, rr) : X.p0, ok);
+      } else {      // word c: row c % ROWS, k 4 (c / ROWS) .. + 3 (a warp reads 32 rows)
+        const int rl = c % ROWS, kl = (c / ROWS) * 4;
+        const int64_t rr = r0 + rl, k = k0 + kl;
+        if (rr < rows && k + 3 < kend) {
+          r[q] = *reinterpret_cast<const float4*>(mat_ptr(X, rr, k));
+        } else {
+          float t[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) t[u] = (rr < rows && k + u < kend) ? *mat_ptr(X, rr, k + u) : 0.f;
+          r[q] = make_float4(t[0], t[1], t[2], t[3]);
+        }
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float* s) const {
+    if (KMAJ) return;
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const int c = threadIdx.x + 256 * q;
+      const int rl = c % ROWS, kl = (c / ROWS) * 4;
+      s[(kl + 0) * LD + rl] = r[q].x;
+      s[(kl + 1) * LD + rl] = r[q].y;
+      s[(kl + 2) * LD + rl] = r[q].z;
+      s[(kl + 3) * LD + rl] = r[q].w;
+    }
+  }
+};
+
+__device__ __forceinline__ float4 epi_act(float4 v, int act, const float* aux) {
+  if (act == ACT_SILU) {
+    v = make_float4(silu_f(v.x), silu_f(v.y), silu_f(v.z), silu_f(v.w));
+  } else if (act == ACT_DSILU) {
+    const float4 z = *reinterpret_cast<const float4*>(aux);
+    float y, d;
+    silu_and_grad(z.x, y, d); v.x *= d;
+    silu_and_grad(z.y, y, d); v.y *= d;
+    silu_and_grad(z.z, y, d); v.z *= d;
+    silu_and_grad(z.w, y, d); v.w *= d;
+  }
+  return v;
+}
+
+template <int TM, int A_T, int B_T>
+__global__ void __launch_bounds__(256, 2) gemm_tiled_kernel(GemmArgs a) {
+  static_assert(TM == 4, "fragment loads below cover 4 rows per thread");
+  constexpr int BM = 16 * TM, LDA = BM + 4, LDB = TBN + 4;
+  constexpr int SA = TBK * LDA, SB = TBK * LDB;
+  extern __shared__ __align__(16) float tsm[];
+  float* As = tsm;
+  float* Bs = tsm + 2 * SA;
+  int tx, ty;
+  thread_grid(tx, ty);
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * TBN;
   int64_t kbeg = 0, kend = a.K;
   if (a.ksplit > 1) {
     int64_t kc = (a.K + a.ksplit - 1) / a.ksplit;
-    kc = (kc + BK2 - 1) / BK2 * BK2;
-    kbeg = (int64_t)blockIdx.z * kc;
+    kc = (kc + TBK - 1) / TBK * TBK;
+    kbeg = min(a.K, (int64_t)blockIdx.z * kc);
     kend = min(a.K, kbeg + kc);
   }
-  // A slice: BM x 8 floats, B slice: 8 x 128 floats; one float4 each per
-  // thread (A with BM = 64 uses half of the threads).
-  float4 ra = make_float4(0.f, 0.f, 0.f, 0.f), rb = make_float4(0.f, 0.f, 0.f, 0.f);
-  auto load = [&](int64_t k0) {
-    ra = make_float4(0.f, 0.f, 0.f, 0.f);
-    rb = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (A_T == 0) {          // A(m, k) row-major: row m = tid/2, k = 4*(tid%2)
-      const int64_t m = m0 + tid / 2, k = k0 + (tid % 2) * 4;
-      if (tid / 2 < BM && m < a.M && k < kend) {
-        const float* p = k < a.A.split ? a.A.p0 + m * a.A.ld0 + k : a.A.p1 + m * a.A.ld1 + (k - a.A.split);
-        ra = *reinterpret_cast<const float4*>(p);
-      }
-    } else {                 // A(m, k) = G[k][m]: k = tid/32, m = 4*(tid%32)
-      const int64_t k = k0 + tid / 32, m = m0 + (tid % 32) * 4;
-      if ((tid % 32) * 4 < BM && m < a.M && k < kend)
-        ra = *reinterpret_cast<const float4*>(a.A.p0 + k * a.A.ld0 + m);
-    }
-    if (B_T == 1) {          // B(k, n) = W[n][k]: row n = tid/2, k = 4*(tid%2)
-      const int64_t n = n0 + tid / 2, k = k0 + (tid % 2) * 4;
-      if (n < a.N && k < kend) {
-        const float* p = (a.B.split_rows && n >= a.B.split) ? a.B.p1 + (n - a.B.split) * a.B.ld1 + k
-                                                             : a.B.p0 + n * a.B.ld0 + k;
-        rb = *reinterpret_cast<const float4*>(p);
-      }
-    } else {                 // B(k, n) = X[k][n] (columns may be split): k = tid/32, n = 4*(tid%32)
-      const int64_t k = k0 + tid / 32, n = n0 + (tid % 32) * 4;
-      if (n < a.N && k < kend) {
-        const float* p = n < a.B.split ? a.B.p0 + k * a.B.ld0 + n : a.B.p1 + k * a.B.ld1 + (n - a.B.split);
-        rb = *reinterpret_cast<const float4*>(p);
-      }
-    }
-  };
-  auto store = [&](int buf) {
-    if (a.round_bf16) {
-      ra = make_float4(bf16r(ra.x), bf16r(ra.y), bf16r(ra.z), bf16r(ra.w));
-      rb = make_float4(bf16r(rb.x), bf16r(rb.y), bf16r(rb.z), bf16r(rb.w));
-    }
-    if (A_T == 0) {
-      if (tid / 2 < BM) {
-        const int ml = tid / 2, kl = (tid % 2) * 4;
-        As[buf][kl + 0][ml] = ra.x; As[buf][kl + 1][ml] = ra.y;
-        As[buf][kl + 2][ml] = ra.z; As[buf][kl + 3][ml] = ra.w;
-      }
-    } else if ((tid % 32) * 4 < BM) {
-      *reinterpret_cast<float4*>(&As[buf][tid / 32][(tid % 32) * 4]) = ra;
-    }
-    if (B_T == 1) {
-      const int nl = tid / 2, kl = (tid % 2) * 4;
-      Bs[buf][kl + 0][nl] = rb.x; Bs[buf][kl + 1][nl] = rb.y;
-      Bs[buf][kl + 2][nl] = rb.z; Bs[buf][kl + 3][nl] = rb.w;
-    } else {
-      *reinterpret_cast<float4*>(&Bs[buf][tid / 32][(tid % 32) * 4]) = rb;
-    }
-  };
+  const int64_t nk = (kend - kbeg + TBK - 1) / TBK;
+  Slice<BM, A_T> sa;
+  Slice<TBN, 1 - B_T> sb;
 
   float acc[TM][8];
 #pragma unroll
@@ -236,29 +298,35 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
 #pragma unroll
   for (int i = 0; i < TM; ++i) dbacc[i] = 0.f;
 
-  int buf = 0;
-  if (kbeg < kend) {
-    load(kbeg);
-    store(0);
+  if (nk > 0) {
+    sa.fetch(As, a.A, m0, a.M, kbeg, kend);
+    sb.fetch(Bs, a.B, n0, a.N, kbeg, kend);
+    cp_async_commit();
+    sa.store(As);
+    sb.store(Bs);
+    cp_async_wait_all();
   }
   __syncthreads();
 #pragma unroll 1
-  for (int64_t k0 = kbeg; k0 < kend; k0 += BK2) {
-    const bool more = k0 + BK2 < kend;
-    if (more) load(k0 + BK2);
+  for (int64_t kt = 0; kt < nk; ++kt) {
+    const int cur = (int)(kt & 1);
+    const bool more = kt + 1 < nk;
+    if (more) {   // next slice: copies in flight / loads in registers during the compute
+      sa.fetch(As + (cur ^ 1) * SA, a.A, m0, a.M, kbeg + (kt + 1) * TBK, kend);
+      sb.fetch(Bs + (cur ^ 1) * SB, a.B, n0, a.N, kbeg + (kt + 1) * TBK, kend);
+      cp_async_commit();
+    }
+    const float* as = As + cur * SA + ty * 4;
+    const float* bs = Bs + cur * SB + tx * 4;
 #pragma unroll
-    for (int k = 0; k < BK2; ++k) {
+    for (int k = 0; k < TBK; ++k) {
       float av[TM], bv[8];
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(bs + k * LDB);
+      const float4 b1 = *reinterpret_cast<const float4*>(bs + k * LDB + 64);
       bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
       bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      const float4 a0 = *reinterpret_cast<const float4*>(as + k * LDA);
       av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
-      if constexpr (TM == 8) {
-        const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
-        av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
-      }
 #pragma unroll
       for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -268,15 +336,19 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
         for (int i = 0; i < TM; ++i) dbacc[i] += av[i];
       }
     }
-    if (more) store(buf ^ 1);
+    if (more) {
+      sa.store(As + (cur ^ 1) * SA);
+      sb.store(Bs + (cur ^ 1) * SB);
+      cp_async_wait_all();
+    }
     __syncthreads();
-    buf ^= 1;
   }
 
+  auto row_of = [&](int i) { return m0 + ty * 4 + i; };
   if (do_db) {
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
-      const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+      const int64_t m = row_of(i);
       if (m >= a.M) continue;
       if (a.ksplit > 1) a.db_part[(int64_t)blockIdx.z * a.M + m] = dbacc[i];
       else a.db[m] = dbacc[i];
@@ -285,63 +357,111 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
   Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.resid_cols, a.C, a.ldc};
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
-    const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    const int64_t m = row_of(i);
     if (m >= a.M) continue;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int64_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
-      if (n >= a.N) continue;
-      if (a.ksplit > 1) a.part[(int64_t)blockIdx.z * a.M * a.N + m * a.N + n] = acc[i][j];
-      else e.apply(m, n, acc[i][j]);
+    for (int jj = 0; jj < 2; ++jj) {
+      const int64_t n = n0 + jj * 64 + tx * 4;
+      const float* v4 = &acc[i][jj * 4];
+      if (a.ksplit > 1) {
+        float* dst = a.part + (int64_t)blockIdx.z * a.M * a.N + m * a.N + n;
+        if (n + 3 < a.N) {   // N % 4 == 0 on the split-K path
+          *reinterpret_cast<float4*>(dst) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            if (n + t < a.N) dst[t] = v4[t];
+        }
+      } else if (a.vec && n + 3 < a.N) {
+        float4 v = make_float4(v4[0], v4[1], v4[2], v4[3]);
+        if (a.bias) {
+          const float4 b = *reinterpret_cast<const float4*>(a.bias + n);
+          v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
+        }
+        if (a.pre) *reinterpret_cast<float4*>(a.pre + m * a.ldp + n) = v;
+        v = epi_act(v, a.act, a.aux + m * a.ldaux + n);
+        if (a.resid && n < a.resid_cols) {
+          const float4 r = *reinterpret_cast<const float4*>(a.resid + m * a.ldr + n);
+          v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+        }
+        *reinterpret_cast<float4*>(a.C + m * a.ldc + n) = v;
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (n + t < a.N) e.apply(m, n + t, v4[t]);
+      }
     }
   }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Whether the register-tiled kernel can take these operands.
-bool tiled_ok(const GemmArgs& a) {
-  // 16-byte loads along k need K % 8 == 0; row-wise loads (A^T, B) take any K.
-  if ((a.a_t == 0 || a.b_t == 1) && a.K % 8 != 0) return false;
-  const Mat& A = a.A;
-  const Mat& B = a.B;
-  if (a.a_t == 0) {
-    if (A.split_rows || !aligned16(A.p0) || A.ld0 % 4) return false;
-    if (A.p1 && (!aligned16(A.p1) || A.ld1 % 4 || A.split % 8)) return false;
-  } else {
-    if (A.p1 || !aligned16(A.p0) || A.ld0 % 4 || a.M % 4) return false;
-  }
-  if (a.b_t == 1) {
-    if (!aligned16(B.p0) || B.ld0 % 4) return false;
-    if (B.p1 && (!B.split_rows || !aligned16(B.p1) || B.ld1 % 4)) return false;
-  } else {
-    if (B.split_rows || !aligned16(B.p0) || B.ld0 % 4 || a.N % 4) return false;
-    if (B.p1 && (!aligned16(B.p1) || B.ld1 % 4 || B.split % 4)) return false;
-  }
+// A k-major operand (copied 16 bytes at a time): aligned rows, no row split,
+// a column split on a 4-element boundary, and a row count that is a multiple
+// of 4.  A row-major operand (read as float4 along k): aligned rows, K % 4 == 0,
+// a column split on a 4-element boundary.
+bool kmajor_ok(const Mat& X, int64_t rows) {
+  if (X.split_rows || rows % 4 || !aligned16(X.p0) || X.ld0 % 4) return false;
+  if (X.p1 && (!aligned16(X.p1) || X.ld1 % 4 || X.split % 4)) return false;
+  return true;
+}
+bool rowmajor_ok(const Mat& X, int64_t K) {
+  if (K % 4 || !aligned16(X.p0) || X.ld0 % 4) return false;
+  if (X.p1 && (!aligned16(X.p1) || X.ld1 % 4 || X.split % 4)) return false;
   return true;
 }
 
-template <int BM>
-void launch_tiled(const GemmArgs& a, dim3 grid, cudaStream_t s) {
-  if (a.a_t == 0 && a.b_t == 1) gemm_tiled_kernel<BM, 0, 1><<<grid, 256, 0, s>>>(a);
-  else if (a.a_t == 0 && a.b_t == 0) gemm_tiled_kernel<BM, 0, 0><<<grid, 256, 0, s>>>(a);
-  else if (a.a_t == 1 && a.b_t == 0) gemm_tiled_kernel<BM, 1, 0><<<grid, 256, 0, s>>>(a);
-  else gemm_tiled_kernel<BM, 1, 1><<<grid, 256, 0, s>>>(a);
+bool tiled_ok(const GemmArgs& a) {
+  if (a.round_bf16) return false;
+  if (a.a_t == 1 ? !kmajor_ok(a.A, a.M) : (a.A.split_rows || !rowmajor_ok(a.A, a.K))) return false;
+  if (a.b_t == 0 ? !kmajor_ok(a.B, a.N) : !rowmajor_ok(a.B, a.K)) return false;
+  if (a.ksplit > 1 && a.N % 4) return false;
+  return true;
+}
+
+// Whether the epilogue may move four columns at a time.
+int vec_epilogue(const GemmArgs& a) {
+  if (a.N % 4 || a.ldc % 4 || !aligned16(a.C)) return 0;
+  if (a.bias && !aligned16(a.bias)) return 0;
+  if (a.pre && (a.ldp % 4 || !aligned16(a.pre))) return 0;
+  if (a.act == ACT_DSILU && (a.ldaux % 4 || !aligned16(a.aux))) return 0;
+  if (a.resid && (a.ldr % 4 || !aligned16(a.resid) || (a.resid_cols != INT64_MAX && a.resid_cols % 4))) return 0;
+  return 1;
+}
+
+template <int TM, int A_T, int B_T>
+int launch_tiled_t(const GemmArgs& a, cudaStream_t s) {
+  static uint64_t attr_set = 0;
+  constexpr size_t bytes = tiled_smem_bytes<16 * TM>();
+  const uint64_t bit = device_bit();
+  if (!(attr_set & bit)) {
+    EGNN_CHECK_CUDA(cudaFuncSetAttribute(gemm_tiled_kernel<TM, A_T, B_T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    attr_set |= bit;
+  }
+  const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
+  const dim3 grid((unsigned)((a.N + TBN - 1) / TBN), (unsigned)((a.M + 16 * TM - 1) / (16 * TM)), z);
+  gemm_tiled_kernel<TM, A_T, B_T><<<grid, 256, bytes, s>>>(a);
+  return EGNN_OK;
+}
+
+int launch_tiled(const GemmArgs& a, cudaStream_t s) {
+  if (a.a_t == 0 && a.b_t == 0) return launch_tiled_t<TTM, 0, 0>(a, s);
+  if (a.a_t == 0 && a.b_t == 1) return launch_tiled_t<TTM, 0, 1>(a, s);
+  if (a.a_t == 1 && a.b_t == 0) return launch_tiled_t<TTM, 1, 0>(a, s);
+  return launch_tiled_t<TTM, 1, 1>(a, s);
 }
 
 }  // namespace
 
-int gemm(const GemmArgs& a, cudaStream_t s) {
-  if (a.M <= 0 || a.N <= 0) return EGNN_OK;
-  const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
+int gemm(const GemmArgs& a_in, cudaStream_t s) {
+  if (a_in.M <= 0 || a_in.N <= 0) return EGNN_OK;
+  GemmArgs a = a_in;
+  a.vec = vec_epilogue(a);
   if (tiled_ok(a)) {
-    const int64_t tiles128 = ((a.M + 127) / 128) * ((a.N + 127) / 128) * z;
-    if (tiles128 >= 148) {
-      launch_tiled<128>(a, dim3((unsigned)((a.N + 127) / 128), (unsigned)((a.M + 127) / 128), z), s);
-    } else {
-      launch_tiled<64>(a, dim3((unsigned)((a.N + 127) / 128), (unsigned)((a.M + 63) / 64), z), s);
-    }
+    EGNN_TRY(launch_tiled(a, s));
   } else {
+    const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
     dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), z);
     gemm_kernel<<<grid, NT, 0, s>>>(a);
   }
@@ -358,7 +478,7 @@ int gemm(const GemmArgs& a, cudaStream_t s) {
 int64_t wgrad_splits(int64_t K, int64_t M, int64_t N) {
   int64_t tiles = ((M + 63) / 64) * ((N + 127) / 128);
   int64_t want = (148 + tiles - 1) / tiles;               // about one wave of CTAs
-  int64_t by_len = std::max<int64_t>(1, K / 256);         // at least 256 rows per slice
+  int64_t by_len = std::max<int64_t>(1, K / 128);         // at least 128 rows per slice
   return std::max<int64_t>(1, std::min<int64_t>({want, by_len, 64}));
 }
 

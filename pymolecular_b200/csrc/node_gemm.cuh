@@ -59,6 +59,7 @@ struct GemmArgs {
   // with split-K the slices go to db_part[z][M] first.
   float* db = nullptr;
   float* db_part = nullptr;
+  int vec = 0;   // set by gemm(): the epilogue may move four columns at a time
 };
 
 int gemm(const GemmArgs& a, cudaStream_t s);

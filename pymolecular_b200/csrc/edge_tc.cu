@@ -49,7 +49,6 @@ struct TC {
   static_assert(H == 128, "tensor-core path built for H = 128");
   static constexpr int TILE = kM * H * 2;   // [128 x H] bf16 tile
   static constexpr int WT = H * H * 2;      // [H x H] bf16 weight tile
-  static constexpr int LDS = H + 4;         // fp32 staging row stride (floats)
   static constexpr int LDD = H + 8;         // fp16 staging row stride (halves)
   static constexpr uint32_t IDESC_FWD = make_idesc_bf16(kM, H, 0, 0);    // A K-major, B K-major
   static constexpr uint32_t IDESC_DGRAD = make_idesc_bf16(kM, H, 0, 1);  // B = W, MN-major
@@ -143,6 +142,61 @@ struct Geo {
 };
 constexpr int kNT = 512;
 
+// fp32 row staging [128 edges][H features] in shared memory, in 16-byte
+// words; word w of row e lives at w ^ (e & 31).  A warp then moves one whole
+// row per instruction (lane = word), and a thread that owns a row reads its
+// 32-column slice with each quarter-warp on 8 distinct bank groups.
+__device__ __forceinline__ int stage_word(int e, int w) { return e * 32 + (w ^ (e & 31)); }
+
+// a1 = P_i + Q_j + w_r r for the chunk's edges, one warp per edge and four
+// features per lane (the P and Q rows are read whole), into the staging.
+// Invalid edges (e >= n) stage zeros.
+__device__ __forceinline__ void gather_a1(float4* stage, const float* __restrict__ PQ, const int* rows,
+                                          const int* cols, const float4* geo, const float* s_wr, int n,
+                                          int warp, int lane) {
+  constexpr int H = 128;
+  const float4 wr4 = *reinterpret_cast<const float4*>(s_wr + 4 * lane);
+#pragma unroll
+  for (int b = 0; b < 8; b += 4) {
+    float4 p[4], q[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int e = warp * 8 + b + t;
+      if (e < n) {
+        p[t] = __ldg(reinterpret_cast<const float4*>(PQ + (int64_t)rows[e] * 2 * H) + lane);
+        q[t] = __ldg(reinterpret_cast<const float4*>(PQ + (int64_t)cols[e] * 2 * H + H) + lane);
+      } else {
+        p[t] = q[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int e = warp * 8 + b + t;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < n) {
+        const float r = geo[e].w;
+        a = make_float4(fmaf(wr4.x, r, p[t].x + q[t].x), fmaf(wr4.y, r, p[t].y + q[t].y),
+                        fmaf(wr4.z, r, p[t].z + q[t].z), fmaf(wr4.w, r, p[t].w + q[t].w));
+      }
+      stage[stage_word(e, lane)] = a;
+    }
+  }
+}
+
+// The 32-column slice col0..col0+31 of staged row e.
+__device__ __forceinline__ void stage_read32(const float4* stage, int e, int col0, float (&v)[32]) {
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const float4 t = stage[stage_word(e, col0 / 4 + w)];
+    v[4 * w] = t.x; v[4 * w + 1] = t.y; v[4 * w + 2] = t.z; v[4 * w + 3] = t.w;
+  }
+}
+__device__ __forceinline__ void stage_write32(float4* stage, int e, int col0, const float (&v)[32]) {
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    stage[stage_word(e, col0 / 4 + w)] = make_float4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
+}
+
 __device__ __forceinline__ void st_row32_bf16(char* tile, int row, int col0, const float (&v)[32]) {
 #pragma unroll
   for (int k = 0; k < 32; k += 8) st_row8_bf16(tile, kM, row, col0 + k, v + k);
@@ -163,7 +217,8 @@ struct FwdLayout {
   static constexpr size_t SEGX = DL + kM * 16;         // float4[128]: coordinate sums per segment
   static constexpr size_t PHI = SEGX + kM * 16;        // float[128]
   static constexpr size_t ROWL = PHI + kM * 4;         // int[128]
-  static constexpr size_t SEGROW = ROWL + kM * 4;      // int[129]
+  static constexpr size_t COLL = ROWL + kM * 4;        // int[128]
+  static constexpr size_t SEGROW = COLL + kM * 4;      // int[129]
   static constexpr size_t SEGSTART = SEGROW + (kM + 4) * 4;
   static constexpr size_t OPEN = SEGSTART + (kM + 4) * 4;   // float[H + 4]
   static constexpr size_t MISC = OPEN + (H + 4) * 4;   // ints: nseg, open_row, prev_row, warp counts[4]
@@ -193,6 +248,8 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   float4* segx = reinterpret_cast<float4*>(sm + L::SEGX);
   float* phi = reinterpret_cast<float*>(sm + L::PHI);
   int* rowl = reinterpret_cast<int*>(sm + L::ROWL);
+  int* coll = reinterpret_cast<int*>(sm + L::COLL);
+  float4* stage = reinterpret_cast<float4*>(Mt);   // a1 staging over the M | MLO tiles (64 KB)
   int* segrow = reinterpret_cast<int*>(sm + L::SEGROW);
   int* segstart = reinterpret_cast<int*>(sm + L::SEGSTART);
   float* open = reinterpret_cast<float*>(sm + L::OPEN);
@@ -266,45 +323,40 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   for (int64_t c0 = eb; c0 < ee && ok; c0 += kM) {
     const int n = (int)std::min<int64_t>(kM, ee - c0);
     const bool valid = g.e < n;
-    // ---- gather: u1 slice of edge e; zero the segment matrix
-    {
-      float u[32];
+    // ---- per-edge geometry (column slice 0); zero the segment matrix
+    if (g.cg == 0) {
       if (valid) {
         const int64_t k = c0 + g.e;
         const int i = a.row_idx[k], j = a.col_idx[k];
         const float4 xi = a.xp[i], xj = a.xp[j];
         const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
         const float r = dx * dx + dy * dy + dz * dz;
-        if (g.cg == 0) {
-          const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
-          rowl[g.e] = i;
-          dl[g.e] = make_float4(dx * inv, dy * inv, dz * inv, r);
-        }
-        const float* Pi = a.PQ + (int64_t)i * 2 * H + g.col0;
-        const float* Qj = a.PQ + (int64_t)j * 2 * H + H + g.col0;
-#pragma unroll
-        for (int q4 = 0; q4 < 32; q4 += 4) {
-          const float4 p = *reinterpret_cast<const float4*>(Pi + q4);
-          const float4 qv = *reinterpret_cast<const float4*>(Qj + q4);
-          u[q4 + 0] = silu_fast(fmaf(s_wr[g.col0 + q4 + 0], r, p.x + qv.x));
-          u[q4 + 1] = silu_fast(fmaf(s_wr[g.col0 + q4 + 1], r, p.y + qv.y));
-          u[q4 + 2] = silu_fast(fmaf(s_wr[g.col0 + q4 + 2], r, p.z + qv.z));
-          u[q4 + 3] = silu_fast(fmaf(s_wr[g.col0 + q4 + 3], r, p.w + qv.w));
-        }
+        const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
+        rowl[g.e] = i;
+        coll[g.e] = j;
+        dl[g.e] = make_float4(dx * inv, dy * inv, dz * inv, r);
       } else {
-#pragma unroll
-        for (int q = 0; q < 32; ++q) u[q] = 0.f;
-        if (g.cg == 0) {
-          rowl[g.e] = INT_MAX;
-          dl[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        rowl[g.e] = INT_MAX;
+        coll[g.e] = 0;
+        dl[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      st_row32_bf16(Ut, g.e, g.col0, u);
+    }
+    {
       uint4* sz = reinterpret_cast<uint4*>(St);
 #pragma unroll
       for (int k = 0; k < C::TILE / 16 / kNT; ++k) sz[g.tid + k * kNT] = make_uint4(0u, 0u, 0u, 0u);
     }
     __syncthreads();
+    // ---- a1 rows (coalesced), then u1 = silu(a1) slice of edge e -> tile U
+    gather_a1(stage, a.PQ, rowl, coll, dl, s_wr, n, g.warp, g.lane);
+    __syncthreads();
+    {
+      float u[32];
+      stage_read32(stage, g.e, g.col0, u);
+#pragma unroll
+      for (int q = 0; q < 32; ++q) u[q] = silu_fast(u[q]);
+      st_row32_bf16(Ut, g.e, g.col0, u);
+    }
     // ---- segments of the chunk (runs of equal destination rows)
     if (g.cg == 0) {
       const int r = rowl[g.e];
@@ -468,7 +520,8 @@ struct BwdLayout {
   static constexpr size_t GT = DL + kM * 16;                          // float4[128]: g_trans.xyz, inv
   static constexpr size_t PHI = GT + kM * 16;                         // float2[128]: phi, gphi'
   static constexpr size_t ROWI = PHI + kM * 8;                        // int[128]
-  static constexpr size_t BAR = ROWI + kM * 4;
+  static constexpr size_t COLI = ROWI + kM * 4;                       // int[128]
+  static constexpr size_t BAR = COLI + kM * 4;
   static constexpr size_t END = BAR + 16;
   static constexpr size_t BYTES = END + 1024;
 };
@@ -494,6 +547,8 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   float4* gtr = reinterpret_cast<float4*>(sm + L::GT);
   float2* phis = reinterpret_cast<float2*>(sm + L::PHI);
   int* rowi = reinterpret_cast<int*>(sm + L::ROWI);
+  int* coli = reinterpret_cast<int*>(sm + L::COLI);
+  float4* stage = reinterpret_cast<float4*>(Mt);   // fp32 row staging over the M | G tiles (64 KB)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
 
@@ -532,43 +587,40 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   for (int64_t c0 = eb; c0 < ee && ok; c0 += kM) {
     const int n = (int)std::min<int64_t>(kM, ee - c0);
     const bool valid = g.e < n;
-    // ---- gather: u1 slice (tile U), s1 = silu'(a1) slice (TMEM), geometry
-    {
-      float u[32], s1v[32];
+    // ---- per-edge geometry (column slice 0)
+    if (g.cg == 0) {
       if (valid) {
         const int64_t k = c0 + g.e;
         const int i = a.row_idx[k], j = a.col_idx[k];
         const float4 xi = a.xp[i], xj = a.xp[j];
         const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
         const float r = dx * dx + dy * dy + dz * dz;
-        if (g.cg == 0) {
-          const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
-          const float inv_g = (i == j) ? 0.f : inv;   // self-loop: zero coordinate gradient
-          const float sc = scale_of(a.row_ptr, i, a.flags);
-          rowi[g.e] = i;
-          dl[g.e] = make_float4(dx, dy, dz, r);
-          gtr[g.e] = make_float4(a.gx_out[(int64_t)i * 3] * sc, a.gx_out[(int64_t)i * 3 + 1] * sc,
-                                 a.gx_out[(int64_t)i * 3 + 2] * sc, inv_g);
-        }
-        const float* Pi = a.PQ + (int64_t)i * 2 * H + g.col0;
-        const float* Qj = a.PQ + (int64_t)j * 2 * H + H + g.col0;
-#pragma unroll
-        for (int q4 = 0; q4 < 32; q4 += 4) {
-          const float4 p = *reinterpret_cast<const float4*>(Pi + q4);
-          const float4 qv = *reinterpret_cast<const float4*>(Qj + q4);
-          const float pv[4] = {p.x + qv.x, p.y + qv.y, p.z + qv.z, p.w + qv.w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t)
-            silu_grad_fast(fmaf(s_wr[g.col0 + q4 + t], r, pv[t]), u[q4 + t], s1v[q4 + t]);
-        }
+        const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
+        const float inv_g = (i == j) ? 0.f : inv;   // self-loop: zero coordinate gradient
+        const float sc = scale_of(a.row_ptr, i, a.flags);
+        rowi[g.e] = i;
+        coli[g.e] = j;
+        dl[g.e] = make_float4(dx, dy, dz, r);
+        gtr[g.e] = make_float4(a.gx_out[(int64_t)i * 3] * sc, a.gx_out[(int64_t)i * 3 + 1] * sc,
+                               a.gx_out[(int64_t)i * 3 + 2] * sc, inv_g);
       } else {
+        rowi[g.e] = 0;
+        coli[g.e] = 0;
+        dl[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        gtr[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    __syncthreads();
+    // ---- a1 rows (coalesced); u1 slice -> tile U, s1 = silu'(a1) slice -> TMEM
+    gather_a1(stage, a.PQ, rowi, coli, dl, s_wr, n, g.warp, g.lane);
+    __syncthreads();
+    {
+      float u[32], s1v[32];
+      stage_read32(stage, g.e, g.col0, u);
 #pragma unroll
-        for (int q = 0; q < 32; ++q) { u[q] = 0.f; s1v[q] = 0.f; }
-        if (g.cg == 0) {
-          rowi[g.e] = 0;
-          dl[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
-          gtr[g.e] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+      for (int q = 0; q < 32; ++q) {
+        silu_grad_fast(u[q], u[q], s1v[q]);
+        if (!valid) { u[q] = 0.f; s1v[q] = 0.f; }
       }
       st_row32_bf16(Ut, g.e, g.col0, u);
       tmem_st32(tS1 + g.lane_base + g.col0, s1v);
@@ -699,12 +751,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
         v[q] = valid ? v[q] * sv[q] : 0.f;
         pr = fmaf(v[q], s_wr[g.col0 + q], pr);
       }
-      if (valid) {
-        float* dst = a.gstore + (c0 + g.e) * H + g.col0;
-#pragma unroll
-        for (int q = 0; q < 32; q += 4)
-          *reinterpret_cast<float4*>(dst + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-      }
+      stage_write32(stage, g.e, g.col0, v);   // the M and G tiles are free again here
       part[g.cg * kM + g.e] = pr;
 #pragma unroll
       for (int q = 0; q < 32; ++q) v[q] *= d.w;
@@ -718,6 +765,12 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       const float f = phis[g.e].x * gt.w;
       a.gdstore[c0 + g.e] = make_float4(gt.x * f + 2.f * gr * d.x, gt.y * f + 2.f * gr * d.y,
                                         gt.z * f + 2.f * gr * d.z, 0.f);
+    }
+    // g_a1 rows of the chunk to global memory, one warp per edge row
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const int e = g.warp * 8 + t;
+      if (e < n) reinterpret_cast<float4*>(a.gstore + (c0 + e) * H)[g.lane] = stage[stage_word(e, g.lane)];
     }
     __syncthreads();
   }

@@ -28,6 +28,7 @@
 
 #include "edge_simt.cuh"
 #include "edge_tc.cuh"
+#include "node_tc.cuh"
 #include "tc.cuh"
 
 namespace egnn {
@@ -923,7 +924,10 @@ extern "C" int egnn_device_status(void* stream) {
   if (n != 0) {
     const int zero = 0;
     EGNN_CHECK_CUDA(cudaMemcpyToSymbol(g_tc_wait_timeouts, &zero, sizeof(int)));
-    return fail(EGNN_ERR_CUDA, "%d tensor-core wait(s) in the edge kernels timed out; results are invalid", n);
+  }
+  n += node_tc_take_timeouts();
+  if (n != 0) {
+    return fail(EGNN_ERR_CUDA, "%d tensor-core wait(s) timed out; results are invalid", n);
   }
   return EGNN_OK;
 }

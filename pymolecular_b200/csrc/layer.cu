@@ -9,17 +9,20 @@
 // Backward: node-MLP backward (GEMMs), edge_bwd (dst pass, recompute),
 //           src pass through the transpose CSR, then the W1 gradients and
 //           dL/dh by node GEMMs.
-// Precision: the node-side GEMMs (N rows) always run in fp32; bf16 mode
-// rounds the operands of the per-edge GEMMs only (phi_e layer 2, phi_x
-// layer 1 and their gradients, E rows), which carry the bulk of the work.
-// Rounding the node-side operands too costs far more accuracy than time:
-// on graphs with high in-degree rows the node MLP input [h, agg] and the
-// projections P, Q lose several percent in their weight gradients.
+// Precision: fp32 mode runs every GEMM in fp32 FFMA.  bf16 mode rounds the
+// operands of the per-edge GEMMs (phi_e layer 2, phi_x layer 1 and their
+// gradients, E rows) to bf16, and runs the node-side GEMMs (N rows) on the
+// tensor cores with each fp32 operand split into two bf16 parts (about 16
+// bits of precision).  Plain bf16 node-side operands would cost far more
+// accuracy than time: on graphs with high in-degree rows the node MLP input
+// [h, agg] and the projections P, Q lose several percent in their weight
+// gradients.
 #include <algorithm>
 
 #include "edge_simt.cuh"
 #include "edge_tc.cuh"
 #include "node_gemm.cuh"
+#include "node_tc.cuh"
 
 namespace egnn {
 namespace {
@@ -146,7 +149,16 @@ int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_
   return EGNN_OK;
 }
 
-int gemm_pq(int64_t N, int H, const float* h, const float* WPQT, const float* bias2, float* PQ,
+// Node GEMMs: fp32 FFMA in fp32 mode, split-bf16 tensor cores in bf16 mode.
+int node_gemm(const GemmArgs& g, bool bf, cudaStream_t s) {
+  return (bf && gemm_tc_ok(g)) ? gemm_tc(g, s) : gemm(g, s);
+}
+int node_wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw, float* db, bool bf,
+               float* part, cudaStream_t s) {
+  return bf ? wgrad_tc(R, M, N, G, X, dW, lddw, db, part, s) : wgrad(R, M, N, G, X, dW, lddw, db, 0, part, s);
+}
+
+int gemm_pq(int64_t N, int H, const float* h, const float* WPQT, const float* bias2, float* PQ, bool bf,
             cudaStream_t s) {
   GemmArgs g;
   g.M = N; g.N = 2 * H; g.K = H;
@@ -155,7 +167,7 @@ int gemm_pq(int64_t N, int H, const float* h, const float* WPQT, const float* bi
   g.bias = bias2;
   g.C = PQ; g.ldc = 2 * H;
   g.round_bf16 = 0;
-  return gemm(g, s);
+  return node_gemm(g, bf, s);
 }
 
 // Per-layer state the forward keeps for the backward (all per node):
@@ -295,7 +307,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   float* agg = sv.agg;
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, h, w.prep.WPQT, w.prep.bias2, sv.PQ, s));
+  EGNN_TRY(gemm_pq(N, H, h, w.prep.WPQT, w.prep.bias2, sv.PQ, bf, s));
 
   const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
   EdgeGrid eg;
@@ -315,7 +327,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n1.bias = p->node_b1; n1.act = ACT_SILU;
   n1.pre = sv.n1pre; n1.ldp = H;
   n1.C = sv.n1; n1.ldc = H;
-  EGNN_TRY(gemm(n1, s));
+  EGNN_TRY(node_gemm(n1, bf, s));
 
   GemmArgs n2;
   n2.M = N; n2.N = H; n2.K = H;
@@ -324,7 +336,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n2.bias = p->node_b2;
   if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = H; }
   n2.C = h_out; n2.ldc = H;
-  EGNN_TRY(gemm(n2, s));
+  EGNN_TRY(node_gemm(n2, bf, s));
   return EGNN_OK;
 }
 
@@ -360,7 +372,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
 
   // ---- node MLP backward: h' = [h +] Wn2 silu(Wn1 [h, agg] + bn1) + bn2
-  EGNN_TRY(wgrad(N, H, H, mat(gh_out, H), mat(sv.n1, H), gp->node_w2, H, gp->node_b2, 0, w.wpart, s));
+  EGNN_TRY(node_wgrad(N, H, H, mat(gh_out, H), mat(sv.n1, H), gp->node_w2, H, gp->node_b2, bf, w.wpart, s));
   {
     GemmArgs gn;
     gn.M = N; gn.N = H; gn.K = H;
@@ -368,10 +380,10 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gn.B = mat(p->node_w2, H); gn.b_t = 0;
     gn.act = ACT_DSILU; gn.aux = sv.n1pre; gn.ldaux = H;
     gn.C = w.g_n1pre; gn.ldc = H;
-    EGNN_TRY(gemm(gn, s));
+    EGNN_TRY(node_gemm(gn, bf, s));
   }
-  EGNN_TRY(wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
-                 gp->node_b1, 0, w.wpart, s));
+  EGNN_TRY(node_wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
+                      gp->node_b1, bf, w.wpart, s));
   {
     // [dL/dh (MLP path) + residual | dL/dagg] = g_n1pre Wn1, one N x 2H product
     GemmArgs gh;
@@ -380,7 +392,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.B = mat(p->node_w1, 2 * H); gh.b_t = 0;
     if (residual) { gh.resid = gh_out; gh.ldr = H; gh.resid_cols = H; }
     gh.C = w.ghg; gh.ldc = 2 * H;
-    EGNN_TRY(gemm(gh, s));
+    EGNN_TRY(node_gemm(gh, bf, s));
   }
 
   // ---- edge backward: dst pass, fix-up, partial reduction, src pass
@@ -409,10 +421,10 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.B = mat(w.prep.WPQ, H); gh.b_t = 0;
     gh.resid = w.ghg; gh.ldr = 2 * H;
     gh.C = grad_h; gh.ldc = H;
-    EGNN_TRY(gemm(gh, s));
+    EGNN_TRY(node_gemm(gh, bf, s));
   }
-  EGNN_TRY(wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, 0, w.wpart, s));
-  EGNN_TRY(wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, 0, w.wpart, s));
+  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart, s));
+  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, bf, w.wpart, s));
   return EGNN_OK;
 }
 

@@ -466,12 +466,17 @@ int gemm(const GemmArgs& a_in, cudaStream_t s) {
     gemm_kernel<<<grid, NT, 0, s>>>(a);
   }
   EGNN_CHECK_LAUNCH();
-  if (a.ksplit > 1) {
-    int64_t total = a.M * a.N;
-    int blocks = (int)std::min<int64_t>((total + 255) / 256, 4096);
-    gemm_reduce_kernel<<<blocks, 256, 0, s>>>(a);
-    EGNN_CHECK_LAUNCH();
-  }
+  if (a.ksplit > 1) EGNN_TRY(gemm_reduce(a, s));
+  return EGNN_OK;
+}
+
+int gemm_reduce(const GemmArgs& a_in, cudaStream_t s) {
+  GemmArgs a = a_in;
+  a.vec = 0;
+  const int64_t total = a.M * a.N;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
+  gemm_reduce_kernel<<<blocks, 256, 0, s>>>(a);
+  EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
 

@@ -64,6 +64,10 @@ struct GemmArgs {
 
 int gemm(const GemmArgs& a, cudaStream_t s);
 
+// The ordered split-K reduction (and epilogue) of a GEMM whose ksplit > 1
+// partial slices sit in a.part (and db slices in a.db_part).
+int gemm_reduce(const GemmArgs& a, cudaStream_t s);
+
 // Workspace floats gemm() needs for its split-K partials when used as a
 // weight-gradient GEMM with reduction length K.
 int64_t wgrad_splits(int64_t K, int64_t M, int64_t N);

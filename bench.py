@@ -39,6 +39,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="time eager steps instead of replays of the captured training step")
     ap.add_argument("--profile", action="store_true",
                     help="profiler target: 1 warm-up + --steps steps, no side passes, no JSON")
     return ap.parse_args()
@@ -346,9 +348,25 @@ def run_b200(args):
     clocks = ClockSampler(local)
     clocks.start()
     warmup = max(args.warmup, 3)
-    for _ in range(warmup):
+    for _ in range(warmup - 1):
         prob.step()
     torch.cuda.synchronize()
+    _native.lib().egnn_launch_count_reset()
+    prob.step()                      # last warm-up step: count this library's launches per step
+    torch.cuda.synchronize()
+    launches_per_step = int(_native.lib().egnn_launch_count())
+
+    # The timed steps replay the whole training step (forward, backward, the
+    # gradient all-reduce, SGD update) captured once as a CUDA graph; the
+    # node-partitioned config (host-sized halo exchanges) runs eagerly.
+    graphed = None
+    run_step = prob.step
+    if not args.no_graphs and not prob.halo:
+        from pymolecular_b200.graphs import GraphedStep
+        graphed = GraphedStep(prob.step, warmup=1)
+        run_step = graphed.replay
+        run_step()                   # one untimed replay
+        torch.cuda.synchronize()
 
     # ---- device-resident timed region (L2 flushed between steps, untimed)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -356,14 +374,13 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    _native.lib().egnn_launch_count_reset()
     for k in range(args.steps):
         flush.fill_(float(k))
         starts[k].record()
-        prob.step()
+        run_step()
         ends[k].record()
     torch.cuda.synchronize()
-    launches = int(_native.lib().egnn_launch_count())
+    launches = launches_per_step * args.steps
     if world > 1:
         dist.barrier()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
@@ -444,7 +461,8 @@ def run_b200(args):
                        "nodes_per_gpu": prob.nodes_rank, "edges_per_gpu": prob.edges_rank,
                        "layers": mc.n_layers, "hidden": H, "precision": prob.precision,
                        "l2": "flushed between timed steps (252 MB write)",
-                       "parallelism": ("nodepart" if prob.halo else "dp") + str(world), "optimizer": "SGD"},
+                       "parallelism": ("nodepart" if prob.halo else "dp") + str(world), "optimizer": "SGD",
+                       "cuda_graph": graphed is not None},
             "molecules_per_s": prob.graphs_job / (ms_per_step * 1e-3),
             "model_tflops": step_flops / (ms_per_step * 1e-3) / 1e12,
             "e2e": e2e,
@@ -466,6 +484,8 @@ def run_b200(args):
             "device_status": "ok" if status == 0 else _native.last_error(),
         }
         print(json.dumps(line), flush=True)
+    if graphed is not None:
+        graphed.release()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -96,6 +96,24 @@ __device__ __forceinline__ void silu_grad_fast(float a, float& y, float& dy) {
   dy = s * (1.0f + a * (1.0f - s));
 }
 
+// Per-edge activations of the bf16 tensor-core edge kernels: one MUFU
+// operation per sigmoid, sigmoid(x) = 1/2 + tanh(x/2)/2 with the hardware's
+// tanh.approx (relative error about 2^-11, a quarter of bf16's half-unit;
+// these values are rounded to bf16 or fp16, or summed in fp32 over many
+// edges, downstream).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sigmoid_edge(float x) { return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f); }
+__device__ __forceinline__ float silu_edge(float a) { return a * sigmoid_edge(a); }
+__device__ __forceinline__ void silu_grad_edge(float a, float& y, float& dy) {
+  const float s = sigmoid_edge(a);
+  y = a * s;
+  dy = s * (1.0f + a * (1.0f - s));
+}
+
 // Round-to-nearest-even to the bf16 grid, kept in a float register.
 __device__ __forceinline__ float bf16r(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));

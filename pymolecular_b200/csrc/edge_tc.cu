@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       float u[32];
       stage_read32(stage, g.e, g.col0, u);
 #pragma unroll
-      for (int q = 0; q < 32; ++q) u[q] = silu_fast(u[q]);
+      for (int q = 0; q < 32; ++q) u[q] = silu_edge(u[q]);
       st_row32_bf16(Ut, g.e, g.col0, u);
     }
     // ---- segments of the chunk (runs of equal destination rows)
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
 #pragma unroll
       for (int q = 0; q < 32; ++q) {
-        const float m = silu_fast(v[q] + s_b2[g.col0 + q]);
+        const float m = silu_edge(v[q] + s_b2[g.col0 + q]);
         v[q] = m;
         lo[q] = m - __bfloat162float(__float2bfloat16_rn(m));
       }
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
       float p = 0.f;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) p = fmaf(silu_fast(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
+      for (int q = 0; q < 32; ++q) p = fmaf(silu_edge(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
       part[g.cg * kM + g.e] = p;
     }
     __syncthreads();
@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       stage_read32(stage, g.e, g.col0, u);
 #pragma unroll
       for (int q = 0; q < 32; ++q) {
-        silu_grad_fast(u[q], u[q], s1v[q]);
+        silu_grad_edge(u[q], u[q], s1v[q]);
         if (!valid) { u[q] = 0.f; s1v[q] = 0.f; }
       }
       st_row32_bf16(Ut, g.e, g.col0, u);
@@ -643,8 +643,8 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
 #pragma unroll
       for (int q = 0; q < 32; q += 2) {
         float y0, d0, y1, d1;
-        silu_grad_fast(v[q] + s_b2[g.col0 + q], y0, d0);
-        silu_grad_fast(v[q + 1] + s_b2[g.col0 + q + 1], y1, d1);
+        silu_grad_edge(v[q] + s_b2[g.col0 + q], y0, d0);
+        silu_grad_edge(v[q + 1] + s_b2[g.col0 + q + 1], y1, d1);
         v[q] = y0; v[q + 1] = y1;
         drow[q / 2] = __floats2half2_rn(d0, d1);
       }
@@ -665,7 +665,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
       float p = 0.f;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) p = fmaf(silu_fast(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
+      for (int q = 0; q < 32; ++q) p = fmaf(silu_edge(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
       part[g.cg * kM + g.e] = p;
     }
     __syncthreads();
@@ -687,7 +687,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
 #pragma unroll
       for (int q = 0; q < 32; ++q) {
         float y, dy;
-        silu_grad_fast(v[q] + s_bc1[g.col0 + q], y, dy);
+        silu_grad_edge(v[q] + s_bc1[g.col0 + q], y, dy);
         gc[q] = gp * s_wc2[g.col0 + q] * dy;
         v[q] = gp * y;
       }

@@ -769,26 +769,50 @@ __global__ void src_pass_kernel(int64_t N, const int32_t* __restrict__ src_ptr,
                                 const float4* __restrict__ gdstore, const float* __restrict__ gx_out,
                                 const float* __restrict__ gxd, float* __restrict__ S_src,
                                 float* __restrict__ gx) {
-  constexpr int CC = H / 32;
+  // One warp per source node; lane owns the H / 32 consecutive features
+  // lane*VW .. +VW-1.  Edge rows are fetched four at a time (indices first),
+  // and added in increasing CSR-position order as before.
+  constexpr int VW = H / 32;
   const int lane = threadIdx.x % 32;
   const int64_t j = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (j >= N) return;
-  float s[CC];
+  float s[VW];
 #pragma unroll
-  for (int c = 0; c < CC; ++c) s[c] = 0.f;
+  for (int c = 0; c < VW; ++c) s[c] = 0.f;
   float gs = 0.f;
   const int kb = src_ptr[j], ke = src_ptr[j + 1];
-  for (int k = kb; k < ke; ++k) {
-    const int64_t p = src_edge[k];
+  int k = kb;
+  for (; k + 4 <= ke; k += 4) {
+    int64_t p[4];
 #pragma unroll
-    for (int c = 0; c < CC; ++c) s[c] += gstore[p * H + lane + 32 * c];
+    for (int u = 0; u < 4; ++u) p[u] = src_edge[k + u];
+    float v[4][VW];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) load_row_slice<H>(gstore + p[u] * H, lane, v[u]);
+    float4 g[4];
+    if (lane < 3) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) g[u] = gdstore[p[u]];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+      for (int c = 0; c < VW; ++c) s[c] += v[u][c];
+      if (lane < 3) gs += (lane == 0) ? g[u].x : (lane == 1 ? g[u].y : g[u].z);
+    }
+  }
+  for (; k < ke; ++k) {
+    const int64_t p = src_edge[k];
+    float v[VW];
+    load_row_slice<H>(gstore + p * H, lane, v);
+#pragma unroll
+    for (int c = 0; c < VW; ++c) s[c] += v[c];
     if (lane < 3) {
       const float4 g = gdstore[p];
       gs += (lane == 0) ? g.x : (lane == 1 ? g.y : g.z);
     }
   }
-#pragma unroll
-  for (int c = 0; c < CC; ++c) S_src[j * H + lane + 32 * c] = s[c];
+  store_row_slice<H>(S_src + j * H, lane, s);
   if (lane < 3) gx[j * 3 + lane] = gx_out[j * 3 + lane] + gxd[j * 3 + lane] - gs;
 }
 
@@ -797,8 +821,17 @@ __global__ void part_reduce_kernel(int H, int d, int G, int64_t PF, const float*
   const int64_t total = 2LL * H * H + 4LL * H + (int64_t)H * d;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
+    // CTA partials loaded eight at a time (independent loads), added in CTA order
     float s = 0.f;
-    for (int c = 0; c < G; ++c) s += part[(int64_t)c * PF + idx];
+    int c = 0;
+    for (; c + 8 <= G; c += 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = part[(int64_t)(c + u) * PF + idx];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += t[u];
+    }
+    for (; c < G; ++c) s += part[(int64_t)c * PF + idx];
     const int64_t HH = (int64_t)H * H;
     if (idx < HH) {
       gp.coord_w1[idx] = s;
@@ -837,6 +870,7 @@ int launch_fwd(const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
   }
   EGNN_CHECK_LAUNCH();
   if (g.G > 1) {
+    TimerScope ts_fix("edge_fixup", s);
     edge_fixup_kernel<false><<<g.G - 1, 128, 0, s>>>(H, a.E, g.G, g.epc, a.row_ptr, a.row_idx, a.carry,
                                                      a.flags, a.x, a.agg, a.x_out);
     EGNN_CHECK_LAUNCH();
@@ -862,6 +896,7 @@ int launch_bwd(const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
   }
   EGNN_CHECK_LAUNCH();
   if (g.G > 1) {
+    TimerScope ts_fix("edge_fixup", s);
     edge_fixup_kernel<true><<<g.G - 1, 128, 0, s>>>(H, a.E, g.G, g.epc, a.row_ptr, a.row_idx, a.carry,
                                                     a.flags, nullptr, a.S_dst, a.gxd);
     EGNN_CHECK_LAUNCH();
@@ -931,6 +966,7 @@ int edge_fwd(int H, bool bf16, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStre
 }
 
 int edge_fixup_fwd(int H, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
+  TimerScope ts_fix("edge_fixup", s);
   edge_fixup_kernel<false><<<g.G - 1, 128, 0, s>>>(H, a.E, g.G, g.epc, a.row_ptr, a.row_idx, a.carry, a.flags,
                                                    a.x, a.agg, a.x_out);
   EGNN_CHECK_LAUNCH();
@@ -968,6 +1004,7 @@ int edge_part_reduce(int H, int d, int G, const float* part, const egnn_layer_gr
                      int64_t ld_w1, cudaStream_t s) {
   const int64_t total = 2LL * H * H + 4LL * H + (int64_t)H * d;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+  TimerScope ts("part_reduce", s);
   part_reduce_kernel<<<blocks, 256, 0, s>>>(H, d, G, edge_part_floats(H, d), part, *gp, ld_w1);
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;

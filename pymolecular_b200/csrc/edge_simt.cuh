@@ -5,6 +5,39 @@
 
 namespace egnn {
 
+// A warp reads / writes one H-float row with lane owning the H / 32
+// consecutive features lane * (H / 32) .. (rows are H-float aligned).
+template <int H>
+__device__ __forceinline__ void load_row_slice(const float* row, int lane, float (&v)[H / 32]) {
+  constexpr int VW = H / 32;
+  const float* p = row + lane * VW;
+  if constexpr (VW % 4 == 0) {
+#pragma unroll
+    for (int w = 0; w < VW; w += 4) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(p + w));
+      v[w] = a.x; v[w + 1] = a.y; v[w + 2] = a.z; v[w + 3] = a.w;
+    }
+  } else if constexpr (VW == 2) {
+    const float2 a = __ldg(reinterpret_cast<const float2*>(p));
+    v[0] = a.x; v[1] = a.y;
+  } else {
+    v[0] = __ldg(p);
+  }
+}
+template <int H>
+__device__ __forceinline__ void store_row_slice(float* row, int lane, const float (&v)[H / 32]) {
+  constexpr int VW = H / 32;
+  float* p = row + lane * VW;
+  if constexpr (VW % 4 == 0) {
+#pragma unroll
+    for (int w = 0; w < VW; w += 4) *reinterpret_cast<float4*>(p + w) = make_float4(v[w], v[w + 1], v[w + 2], v[w + 3]);
+  } else if constexpr (VW == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  } else {
+    p[0] = v[0];
+  }
+}
+
 // Fields shared by the forward and backward edge kernels.
 struct EdgeCommon {
   int64_t N = 0, E = 0;

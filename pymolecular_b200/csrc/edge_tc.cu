@@ -820,25 +820,45 @@ template <int H>
 __global__ void row_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr, const float* __restrict__ gstore,
                                 const float4* __restrict__ gdstore, float* __restrict__ S_dst,
                                 float* __restrict__ gxd) {
-  constexpr int CC = H / 32;
+  // One warp per destination row, lane owning H / 32 consecutive features;
+  // four edge rows in flight, added in CSR order.
+  constexpr int VW = H / 32;
   const int lane = threadIdx.x % 32;
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (r >= N) return;
-  float s[CC];
+  float s[VW];
 #pragma unroll
-  for (int c = 0; c < CC; ++c) s[c] = 0.f;
+  for (int c = 0; c < VW; ++c) s[c] = 0.f;
   float gs = 0.f;
   const int kb = row_ptr[r], ke = row_ptr[r + 1];
-  for (int k = kb; k < ke; ++k) {
+  int k = kb;
+  for (; k + 4 <= ke; k += 4) {
+    float v[4][VW];
 #pragma unroll
-    for (int c = 0; c < CC; ++c) s[c] += gstore[(int64_t)k * H + lane + 32 * c];
+    for (int u = 0; u < 4; ++u) load_row_slice<H>(gstore + (int64_t)(k + u) * H, lane, v[u]);
+    float4 g[4];
+    if (lane < 3) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) g[u] = gdstore[k + u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+      for (int c = 0; c < VW; ++c) s[c] += v[u][c];
+      if (lane < 3) gs += (lane == 0) ? g[u].x : (lane == 1 ? g[u].y : g[u].z);
+    }
+  }
+  for (; k < ke; ++k) {
+    float v[VW];
+    load_row_slice<H>(gstore + (int64_t)k * H, lane, v);
+#pragma unroll
+    for (int c = 0; c < VW; ++c) s[c] += v[c];
     if (lane < 3) {
       const float4 g = gdstore[k];
       gs += (lane == 0) ? g.x : (lane == 1 ? g.y : g.z);
     }
   }
-#pragma unroll
-  for (int c = 0; c < CC; ++c) S_dst[r * H + lane + 32 * c] = s[c];
+  store_row_slice<H>(S_dst + r * H, lane, s);
   if (lane < 3) gxd[r * 3 + lane] = gs;
 }
 

@@ -18,6 +18,7 @@
 // [h, agg] and the projections P, Q lose several percent in their weight
 // gradients.
 #include <algorithm>
+#include <mutex>
 
 #include "edge_simt.cuh"
 #include "edge_tc.cuh"
@@ -144,6 +145,7 @@ int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_
                 const float* x, const Prep& o, cudaStream_t s) {
   const int64_t total = N + 2 * H + 6LL * H * H + H + (int64_t)H * d + prep_transposes(o, H);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
+  TimerScope ts("prep", s);
   prep_kernel<<<blocks, 256, 0, s>>>(N, H, d, ld1, bf ? 1 : 0, *p, x, o);
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
@@ -208,6 +210,7 @@ struct BwdWs {
   Prep prep; float* g_n1pre; float* ghg;   // ghg: (N, 2H) = [dL/dh from the node MLP | dL/dagg]
   float* S_dst; float* S_src; float* gxd; float* gstore; float4* gdstore; float* carry;
   int32_t* carry_row; float* part; float* wpart;
+  float* wpart_aux;   // split-K scratch of the weight gradients run on the side stream
 };
 
 int64_t wpart_floats(int64_t N, int H) {
@@ -234,8 +237,52 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   w.carry_row = c.take<int32_t>((size_t)G * 2);
   w.part = c.take<float>((size_t)G * edge_part_floats(H, d->edge_attr_dim));
   w.wpart = c.take<float>((size_t)wpart_floats(N, H));
+  w.wpart_aux = c.take<float>((size_t)wpart_floats(N, H));
   return w;
 }
+
+// ---- side stream ------------------------------------------------------------------
+// The backward forks work that no later kernel of the layer needs (the node-MLP
+// and W1 weight gradients) onto a per-device side stream, so that it fills SMs
+// the edge kernels leave free and overlaps the main chain's latency.  Fork and
+// join are event waits, which stream capture records as graph edges; the
+// stream and events are created on the first call, outside any capture.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev[4] = {};
+};
+
+int side_stream(SideStream** out) {
+  static std::mutex mu;
+  static SideStream per_dev[64];
+  int dev = 0;
+  EGNN_CHECK_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  SideStream& ss = per_dev[dev & 63];
+  if (!ss.stream) {
+    EGNN_CHECK_CUDA(cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking));
+    for (auto& e : ss.ev) EGNN_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  *out = &ss;
+  return EGNN_OK;
+}
+
+// `to` waits for everything issued on `from` so far.
+int stream_fork(cudaStream_t from, cudaStream_t to, cudaEvent_t ev) {
+  EGNN_CHECK_CUDA(cudaEventRecord(ev, from));
+  EGNN_CHECK_CUDA(cudaStreamWaitEvent(to, ev, 0));
+  return EGNN_OK;
+}
+
+// Joins the side stream back into the main one when it goes out of scope
+// (also on an early error return, so no capture is left forked).
+struct SideJoin {
+  cudaStream_t main_s;
+  SideStream* side;
+  ~SideJoin() {
+    if (cudaEventRecord(side->ev[3], side->stream) == cudaSuccess) cudaStreamWaitEvent(main_s, side->ev[3], 0);
+  }
+};
 
 bool missing_params(const egnn_layer_params* p) {
   return !p || !p->edge_w1 || !p->edge_b1 || !p->edge_w2 || !p->edge_b2 || !p->node_w1 ||
@@ -370,9 +417,15 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   if (N == 0) return EGNN_OK;
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
+  SideStream* side = nullptr;
+  EGNN_TRY(side_stream(&side));
+  const cudaStream_t s2 = side->stream;
+  SideJoin join{s, side};
 
   // ---- node MLP backward: h' = [h +] Wn2 silu(Wn1 [h, agg] + bn1) + bn2
-  EGNN_TRY(node_wgrad(N, H, H, mat(gh_out, H), mat(sv.n1, H), gp->node_w2, H, gp->node_b2, bf, w.wpart, s));
+  // dW_n2, db_n2 on the side stream (inputs ready at entry)
+  EGNN_TRY(stream_fork(s, s2, side->ev[0]));
+  EGNN_TRY(node_wgrad(N, H, H, mat(gh_out, H), mat(sv.n1, H), gp->node_w2, H, gp->node_b2, bf, w.wpart_aux, s2));
   {
     GemmArgs gn;
     gn.M = N; gn.N = H; gn.K = H;
@@ -382,8 +435,10 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gn.C = w.g_n1pre; gn.ldc = H;
     EGNN_TRY(node_gemm(gn, bf, s));
   }
+  // dW_n1, db_n1 on the side stream once g_n1pre exists
+  EGNN_TRY(stream_fork(s, s2, side->ev[1]));
   EGNN_TRY(node_wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
-                      gp->node_b1, bf, w.wpart, s));
+                      gp->node_b1, bf, w.wpart_aux, s2));
   {
     // [dL/dh (MLP path) + residual | dL/dagg] = g_n1pre Wn1, one N x 2H product
     GemmArgs gh;
@@ -413,7 +468,9 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, w.gdstore, gx_out, w.gxd, w.S_src,
                          grad_x, s));
 
-  // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb ;  dWa, dWb, db1
+  // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb ;  dWa, db1 on the side stream, dWb here
+  EGNN_TRY(stream_fork(s, s2, side->ev[2]));
+  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart_aux, s2));
   {
     GemmArgs gh;
     gh.M = N; gh.N = H; gh.K = 2 * H;
@@ -423,7 +480,6 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.C = grad_h; gh.ldc = H;
     EGNN_TRY(node_gemm(gh, bf, s));
   }
-  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart, s));
   EGNN_TRY(node_wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, bf, w.wpart, s));
   return EGNN_OK;
 }

@@ -458,12 +458,15 @@ int gemm(const GemmArgs& a_in, cudaStream_t s) {
   if (a_in.M <= 0 || a_in.N <= 0) return EGNN_OK;
   GemmArgs a = a_in;
   a.vec = vec_epilogue(a);
-  if (tiled_ok(a)) {
-    EGNN_TRY(launch_tiled(a, s));
-  } else {
-    const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
-    dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), z);
-    gemm_kernel<<<grid, NT, 0, s>>>(a);
+  {
+    TimerScope ts("node_gemm", s);
+    if (tiled_ok(a)) {
+      EGNN_TRY(launch_tiled(a, s));
+    } else {
+      const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
+      dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), z);
+      gemm_kernel<<<grid, NT, 0, s>>>(a);
+    }
   }
   EGNN_CHECK_LAUNCH();
   if (a.ksplit > 1) EGNN_TRY(gemm_reduce(a, s));
@@ -475,6 +478,7 @@ int gemm_reduce(const GemmArgs& a_in, cudaStream_t s) {
   a.vec = 0;
   const int64_t total = a.M * a.N;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
+  TimerScope ts("gemm_reduce", s);
   gemm_reduce_kernel<<<blocks, 256, 0, s>>>(a);
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
@@ -518,6 +522,7 @@ int colsum(int64_t R, int64_t C, Mat G, float* db, float* part, cudaStream_t s) 
   int64_t rows_per = (R + S - 1) / S;
   if (R == 0) rows_per = 1;
   dim3 grid((unsigned)((C + 127) / 128), (unsigned)S);
+  TimerScope ts("node_gemm", s);
   colsum_partial_kernel<<<grid, 128, 0, s>>>(R, C, G, rows_per, part);
   EGNN_CHECK_LAUNCH();
   colsum_reduce_kernel<<<(unsigned)((C + 127) / 128), 128, 0, s>>>(C, (int)S, part, db);

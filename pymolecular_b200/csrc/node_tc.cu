@@ -398,6 +398,7 @@ int launch_t(const GemmArgs& a, cudaStream_t s) {
   }
   const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
   const dim3 grid((unsigned)((a.N + BNT - 1) / BNT), (unsigned)((a.M + BMT - 1) / BMT), z);
+  TimerScope ts("node_gemm", s);
   gemm_tc_kernel<A_T, B_T, BNT><<<grid, NTH, bytes, s>>>(a);
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;

@@ -7,10 +7,13 @@ the shared object is missing or fails to load, every call raises
 from __future__ import annotations
 
 import ctypes as C
+import os
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libegnn_b200.so"
+# The in-tree build; PYMOLECULAR_B200_LIB points at another build of the same
+# library (same C ABI) instead.
+LIB_PATH = Path(os.environ.get("PYMOLECULAR_B200_LIB") or Path(__file__).resolve().parent / "libegnn_b200.so")
 
 EGNN_OK = 0
 EGNN_ERR_INVALID_ARG = 1

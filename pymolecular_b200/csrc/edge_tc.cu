@@ -151,17 +151,18 @@ __device__ __forceinline__ int stage_word(int e, int w) { return e * 32 + (w ^ (
 
 // a1 = P_i + Q_j + w_r r for the chunk's edges, one warp per edge and four
 // features per lane (the P and Q rows are read whole), into the staging.
-// Invalid edges (e >= n) stage zeros.
+// Invalid edges (e >= n) stage zeros.  GB edges' rows are in flight at once.
+template <int GB>
 __device__ __forceinline__ void gather_a1(float4* stage, const float* __restrict__ PQ, const int* rows,
                                           const int* cols, const float4* geo, const float* s_wr, int n,
                                           int warp, int lane) {
   constexpr int H = 128;
   const float4 wr4 = *reinterpret_cast<const float4*>(s_wr + 4 * lane);
 #pragma unroll
-  for (int b = 0; b < 8; b += 4) {
-    float4 p[4], q[4];
+  for (int b = 0; b < 8; b += GB) {
+    float4 p[GB], q[GB];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+    for (int t = 0; t < GB; ++t) {
       const int e = warp * 8 + b + t;
       if (e < n) {
         p[t] = __ldg(reinterpret_cast<const float4*>(PQ + (int64_t)rows[e] * 2 * H) + lane);
@@ -171,7 +172,7 @@ __device__ __forceinline__ void gather_a1(float4* stage, const float* __restrict
       }
     }
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+    for (int t = 0; t < GB; ++t) {
       const int e = warp * 8 + b + t;
       float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
       if (e < n) {
@@ -216,10 +217,14 @@ struct FwdLayout {
   static constexpr size_t PART = VEC + 4 * H * 4;      // float[4][128]
   static constexpr size_t DL = PART + 4 * kM * 4;      // float4[128]: dn.xyz, r
   static constexpr size_t SEGX = DL + kM * 16;         // float4[128]: coordinate sums per segment
-  static constexpr size_t PHI = SEGX + kM * 16;        // float[128]
+  static constexpr size_t NXI = SEGX + kM * 16;        // float4[128]: next chunk's x_i (prefetch)
+  static constexpr size_t NXJ = NXI + kM * 16;         // float4[128]: next chunk's x_j
+  static constexpr size_t PHI = NXJ + kM * 16;         // float[128]
   static constexpr size_t ROWL = PHI + kM * 4;         // int[128]
   static constexpr size_t COLL = ROWL + kM * 4;        // int[128]
-  static constexpr size_t SEGROW = COLL + kM * 4;      // int[129]
+  static constexpr size_t NROW = COLL + kM * 4;        // int[128]: next chunk's destination ids
+  static constexpr size_t NCOL = NROW + kM * 4;        // int[128]: next chunk's source ids
+  static constexpr size_t SEGROW = NCOL + kM * 4;      // int[129]
   static constexpr size_t SEGSTART = SEGROW + (kM + 4) * 4;
   static constexpr size_t OPEN = SEGSTART + (kM + 4) * 4;   // float[H + 4]
   static constexpr size_t MISC = OPEN + (H + 4) * 4;   // ints: nseg, open_row, prev_row, warp counts[4]
@@ -250,6 +255,10 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   float* phi = reinterpret_cast<float*>(sm + L::PHI);
   int* rowl = reinterpret_cast<int*>(sm + L::ROWL);
   int* coll = reinterpret_cast<int*>(sm + L::COLL);
+  int* nrow = reinterpret_cast<int*>(sm + L::NROW);
+  int* ncol = reinterpret_cast<int*>(sm + L::NCOL);
+  float4* nxi = reinterpret_cast<float4*>(sm + L::NXI);
+  float4* nxj = reinterpret_cast<float4*>(sm + L::NXJ);
   float4* stage = reinterpret_cast<float4*>(Mt);   // a1 staging over the M | MLO tiles (64 KB)
   int* segrow = reinterpret_cast<int*>(sm + L::SEGROW);
   int* segstart = reinterpret_cast<int*>(sm + L::SEGSTART);
@@ -320,16 +329,28 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   };
   const float zero32[32] = {};
 
+  // The next chunk's edge ids and coordinates are prefetched with cp.async by
+  // the threads of column slice 1 while this chunk's MMAs and activations run
+  // (ids after the first MMA is issued, coordinates once they have landed).
+  bool pref = false;
 #pragma unroll 1
   for (int64_t c0 = eb; c0 < ee && ok; c0 += kM) {
     const int n = (int)std::min<int64_t>(kM, ee - c0);
     const bool valid = g.e < n;
+    const int64_t c1 = c0 + kM;
+    const int n_next = (int)std::max<int64_t>(0, std::min<int64_t>(kM, ee - c1));
+    const bool prefetcher = g.cg == 1 && g.e < n_next;
     // ---- per-edge geometry (column slice 0); zero the segment matrix
     if (g.cg == 0) {
       if (valid) {
-        const int64_t k = c0 + g.e;
-        const int i = a.row_idx[k], j = a.col_idx[k];
-        const float4 xi = a.xp[i], xj = a.xp[j];
+        int i, j;
+        float4 xi, xj;
+        if (pref) {
+          i = nrow[g.e]; j = ncol[g.e]; xi = nxi[g.e]; xj = nxj[g.e];
+        } else {
+          const int64_t k = c0 + g.e;
+          i = a.row_idx[k]; j = a.col_idx[k]; xi = a.xp[i]; xj = a.xp[j];
+        }
         const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
         const float r = dx * dx + dy * dy + dz * dz;
         const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
@@ -349,7 +370,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
     }
     __syncthreads();
     // ---- a1 rows (coalesced), then u1 = silu(a1) slice of edge e -> tile U
-    gather_a1(stage, a.PQ, rowl, coll, dl, s_wr, n, g.warp, g.lane);
+    gather_a1<4>(stage, a.PQ, rowl, coll, dl, s_wr, n, g.warp, g.lane);
     __syncthreads();
     {
       float u[32];
@@ -389,7 +410,18 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
         mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2t, H, kk), C::IDESC_FWD, kk > 0);
       mma_commit(bar);
     }
+    if (prefetcher) {
+      cp_async4(&nrow[g.e], a.row_idx + c1 + g.e);
+      cp_async4(&ncol[g.e], a.col_idx + c1 + g.e);
+      cp_async_commit_group();
+    }
     if (!(ok = wait_mma(bar, phase))) break;
+    if (prefetcher) {
+      cp_async_wait_all_groups();
+      cp_async16_ca(&nxi[g.e], a.xp + nrow[g.e]);
+      cp_async16_ca(&nxj[g.e], a.xp + ncol[g.e]);
+      cp_async_commit_group();
+    }
 
     // ---- m = silu(a2 + b2) -> tiles M (bf16) and MLO (bf16 residual)
     {
@@ -474,6 +506,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
         }
       }
     }
+    if (prefetcher) cp_async_wait_all_groups();
     fence_before_sync();
     __syncthreads();
     if (g.tid == 0) {
@@ -482,7 +515,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       misc[1] = (a.row_ptr[r + 1] <= c0 + n) ? -1 : r;
     }
     __syncthreads();
+    pref = n_next > 0;
   }
+  cp_async_wait_all_groups();   // nothing in flight when the CTA leaves (also after a timeout)
   // ---- end of the CTA range: open row -> carry slot, trailing empty rows
   if (ok) {
     const int open_row = misc[1];
@@ -522,7 +557,14 @@ struct BwdLayout {
   static constexpr size_t PHI = GT + kM * 16;                         // float2[128]: phi, gphi'
   static constexpr size_t ROWI = PHI + kM * 8;                        // int[128]
   static constexpr size_t COLI = ROWI + kM * 4;                       // int[128]
-  static constexpr size_t BAR = COLI + kM * 4;
+  // next chunk's prefetched inputs: ids, row_ptr[i], row_ptr[i + 1], x_i, x_j, dL/dx'_i
+  static constexpr size_t NROW = COLI + kM * 4;                       // int[128]
+  static constexpr size_t NCOL = NROW + kM * 4;                       // int[128]
+  static constexpr size_t NRP = NCOL + kM * 4;                        // int[128][2]
+  static constexpr size_t NXI = NRP + kM * 8;                         // float4[128]
+  static constexpr size_t NXJ = NXI + kM * 16;                        // float4[128]
+  static constexpr size_t NGX = NXJ + kM * 16;                        // float4[128] (xyz)
+  static constexpr size_t BAR = NGX + kM * 16;
   static constexpr size_t END = BAR + 16;
   static constexpr size_t BYTES = END + 1024;
 };
@@ -549,6 +591,12 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   float2* phis = reinterpret_cast<float2*>(sm + L::PHI);
   int* rowi = reinterpret_cast<int*>(sm + L::ROWI);
   int* coli = reinterpret_cast<int*>(sm + L::COLI);
+  int* nrow = reinterpret_cast<int*>(sm + L::NROW);
+  int* ncol = reinterpret_cast<int*>(sm + L::NCOL);
+  int* nrp = reinterpret_cast<int*>(sm + L::NRP);
+  float4* nxi = reinterpret_cast<float4*>(sm + L::NXI);
+  float4* nxj = reinterpret_cast<float4*>(sm + L::NXJ);
+  float4* ngx = reinterpret_cast<float4*>(sm + L::NGX);
   float4* stage = reinterpret_cast<float4*>(Mt);   // fp32 row staging over the M | G tiles (64 KB)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
@@ -584,26 +632,39 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   bool ok = true;
   bool first = true;
 
+  // The next chunk's per-edge inputs are prefetched with cp.async by the
+  // threads of column slice 1 while this chunk's MMAs and activations run.
+  bool pref = false;
 #pragma unroll 1
   for (int64_t c0 = eb; c0 < ee && ok; c0 += kM) {
     const int n = (int)std::min<int64_t>(kM, ee - c0);
     const bool valid = g.e < n;
+    const int64_t c1 = c0 + kM;
+    const int n_next = (int)std::max<int64_t>(0, std::min<int64_t>(kM, ee - c1));
+    const bool prefetcher = g.cg == 1 && g.e < n_next;
     // ---- per-edge geometry (column slice 0)
     if (g.cg == 0) {
       if (valid) {
-        const int64_t k = c0 + g.e;
-        const int i = a.row_idx[k], j = a.col_idx[k];
-        const float4 xi = a.xp[i], xj = a.xp[j];
+        int i, j, rp0, rp1;
+        float4 xi, xj, gxi;
+        if (pref) {
+          i = nrow[g.e]; j = ncol[g.e]; rp0 = nrp[2 * g.e]; rp1 = nrp[2 * g.e + 1];
+          xi = nxi[g.e]; xj = nxj[g.e]; gxi = ngx[g.e];
+        } else {
+          const int64_t k = c0 + g.e;
+          i = a.row_idx[k]; j = a.col_idx[k]; rp0 = a.row_ptr[i]; rp1 = a.row_ptr[i + 1];
+          xi = a.xp[i]; xj = a.xp[j];
+          gxi = make_float4(a.gx_out[(int64_t)i * 3], a.gx_out[(int64_t)i * 3 + 1], a.gx_out[(int64_t)i * 3 + 2], 0.f);
+        }
         const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
         const float r = dx * dx + dy * dy + dz * dz;
         const float inv = normalize ? 1.f / (sqrtf(r) + 1e-8f) : 1.f;
         const float inv_g = (i == j) ? 0.f : inv;   // self-loop: zero coordinate gradient
-        const float sc = scale_of(a.row_ptr, i, a.flags);
+        const float sc = (a.flags & EGNN_FLAG_COORDS_SUM) ? 1.f : 1.f / (float)max(rp1 - rp0, 1);
         rowi[g.e] = i;
         coli[g.e] = j;
         dl[g.e] = make_float4(dx, dy, dz, r);
-        gtr[g.e] = make_float4(a.gx_out[(int64_t)i * 3] * sc, a.gx_out[(int64_t)i * 3 + 1] * sc,
-                               a.gx_out[(int64_t)i * 3 + 2] * sc, inv_g);
+        gtr[g.e] = make_float4(gxi.x * sc, gxi.y * sc, gxi.z * sc, inv_g);
       } else {
         rowi[g.e] = 0;
         coli[g.e] = 0;
@@ -613,7 +674,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
     }
     __syncthreads();
     // ---- a1 rows (coalesced); u1 slice -> tile U, s1 = silu'(a1) slice -> TMEM
-    gather_a1(stage, a.PQ, rowi, coli, dl, s_wr, n, g.warp, g.lane);
+    gather_a1<4>(stage, a.PQ, rowi, coli, dl, s_wr, n, g.warp, g.lane);
     __syncthreads();
     {
       float u[32], s1v[32];
@@ -633,7 +694,24 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
         mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2t, H, kk), C::IDESC_FWD, kk > 0);
       mma_commit(bar);
     }
+    if (prefetcher) {
+      cp_async4(&nrow[g.e], a.row_idx + c1 + g.e);
+      cp_async4(&ncol[g.e], a.col_idx + c1 + g.e);
+      cp_async_commit_group();
+    }
     if (!(ok = wait_mma(bar, phase))) break;
+    if (prefetcher) {
+      cp_async_wait_all_groups();
+      const int i = nrow[g.e], j = ncol[g.e];
+      cp_async16_ca(&nxi[g.e], a.xp + i);
+      cp_async16_ca(&nxj[g.e], a.xp + j);
+      cp_async4(&nrp[2 * g.e], a.row_ptr + i);
+      cp_async4(&nrp[2 * g.e + 1], a.row_ptr + i + 1);
+      cp_async4(reinterpret_cast<float*>(&ngx[g.e]), a.gx_out + (int64_t)i * 3);
+      cp_async4(reinterpret_cast<float*>(&ngx[g.e]) + 1, a.gx_out + (int64_t)i * 3 + 1);
+      cp_async4(reinterpret_cast<float*>(&ngx[g.e]) + 2, a.gx_out + (int64_t)i * 3 + 2);
+      cp_async_commit_group();
+    }
 
     // ---- m = silu(a2 + b2) -> tile M ; silu'(a2) -> fp16 staging
     {
@@ -773,8 +851,11 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       const int e = g.warp * 8 + t;
       if (e < n) reinterpret_cast<float4*>(a.gstore + (c0 + e) * H)[g.lane] = stage[stage_word(e, g.lane)];
     }
+    if (prefetcher) cp_async_wait_all_groups();
     __syncthreads();
+    pref = n_next > 0;
   }
+  cp_async_wait_all_groups();   // nothing in flight when the CTA leaves (also after a timeout)
 
   // ---- per-CTA partials: dWc1, dW2 rows from TMEM; column sums over the row quarters
   const int PF = (int)edge_part_floats(H, 0);

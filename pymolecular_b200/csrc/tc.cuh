@@ -108,6 +108,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// ---- cp.async (4- and 16-byte, per-thread groups) ---------------------------
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16_ca(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all_groups() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // ---- TMEM -------------------------------------------------------------------
 // Allocation: one full warp; the base address is written to *dst (shared).
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {

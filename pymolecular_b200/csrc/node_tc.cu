@@ -166,60 +166,6 @@ __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t ph) {
   return !__syncthreads_or(!ok);
 }
 
-// Epilogue of the 16 consecutive columns nb..nb+15 of row m.  When all of
-// them are in range and 16-byte aligned, every operand load of the 16
-// columns is issued before any is used.  (bf16 mode only: the activations
-// use the fast exponential and division.)
-__device__ __forceinline__ void epilogue16(const GemmArgs& a, int64_t m, int64_t nb, const float* v) {
-  if (a.vec && nb + 15 < a.N) {
-    float4 bb[4], aux[4], rs[4];
-    const bool rsd = a.resid && nb < a.resid_cols;   // resid_cols % 16 == 0 on this path
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      bb[g] = a.bias ? *reinterpret_cast<const float4*>(a.bias + nb + 4 * g) : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (a.act == ACT_DSILU) aux[g] = *reinterpret_cast<const float4*>(a.aux + m * a.ldaux + nb + 4 * g);
-      if (rsd) rs[g] = *reinterpret_cast<const float4*>(a.resid + m * a.ldr + nb + 4 * g);
-    }
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      float y[4] = {v[4 * g] + bb[g].x, v[4 * g + 1] + bb[g].y, v[4 * g + 2] + bb[g].z, v[4 * g + 3] + bb[g].w};
-      if (a.pre) *reinterpret_cast<float4*>(a.pre + m * a.ldp + nb + 4 * g) = make_float4(y[0], y[1], y[2], y[3]);
-      if (a.act == ACT_SILU) {
-#pragma unroll
-        for (int t = 0; t < 4; ++t) y[t] = silu_fast(y[t]);
-      } else if (a.act == ACT_DSILU) {
-        const float z[4] = {aux[g].x, aux[g].y, aux[g].z, aux[g].w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          float yy, d;
-          silu_grad_fast(z[t], yy, d);
-          y[t] *= d;
-        }
-      }
-      if (rsd) { y[0] += rs[g].x; y[1] += rs[g].y; y[2] += rs[g].z; y[3] += rs[g].w; }
-      *reinterpret_cast<float4*>(a.C + m * a.ldc + nb + 4 * g) = make_float4(y[0], y[1], y[2], y[3]);
-    }
-    return;
-  }
-#pragma unroll
-  for (int u = 0; u < 16; ++u) {
-    const int64_t n = nb + u;
-    if (n >= a.N) continue;
-    float y = v[u];
-    if (a.bias) y += a.bias[n];
-    if (a.pre) a.pre[m * a.ldp + n] = y;
-    if (a.act == ACT_SILU) {
-      y = silu_fast(y);
-    } else if (a.act == ACT_DSILU) {
-      float yy, d;
-      silu_grad_fast(a.aux[m * a.ldaux + n], yy, d);
-      y *= d;
-    }
-    if (a.resid && n < a.resid_cols) y += a.resid[m * a.ldr + n];
-    a.C[m * a.ldc + n] = y;
-  }
-}
-
 template <int A_T, int B_T, int BNT>
 __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
   using S = TcShape<BNT>;
@@ -340,39 +286,96 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
     }
   }
 
-  // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. (rows) and the
-  // column quarter (w / 4) BNT / 4 .. + BNT / 4
-  constexpr int NCW = BNT / 4;   // 32 or 16 columns per warp
-  const int q = warp & 3, h = warp >> 2;
-  const int64_t m = m0 + q * 32 + lane;
-  const int64_t nb = n0 + h * NCW;
-  float v[NCW];
-  if constexpr (NCW == 32) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
-  else tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
-  if (nkc == 0) {   // empty K slice of a split: the accumulator was never written
+  // ---- epilogue.  1: warp w moves TMEM lanes 32 (w % 4) .. (rows), column
+  // quarter w / 4, into an fp32 staging tile over the (idle) raw ring.
+  constexpr int NCW = BNT / 4;       // 32 or 16 columns per warp
+  constexpr int LDO = BNT + 4;       // staging row stride: 33 or 17 16-byte words (odd)
+  float* ostage = reinterpret_cast<float*>(sm + S::OFF_RAW);
+  {
+    const int q = warp & 3, h = warp >> 2;
+    float v[NCW];
+    if constexpr (NCW == 32) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
+    else tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
+    if (nkc == 0) {   // empty K slice of a split: the accumulator was never written
 #pragma unroll
-    for (int t = 0; t < NCW; ++t) v[t] = 0.f;
-  }
-  if (m < a.M && nb < a.N) {
-    if (a.ksplit > 1) {
-      float* dst = a.part + (int64_t)blockIdx.z * a.M * a.N + m * a.N + nb;
-      if (nb + NCW - 1 < a.N) {
-#pragma unroll
-        for (int t = 0; t < NCW; t += 4)
-          *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
-      } else {
-#pragma unroll
-        for (int t = 0; t < NCW; ++t)
-          if (nb + t < a.N) dst[t] = v[t];
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < NCW; c += 16) epilogue16(a, m, nb + c, v + c);
+      for (int t = 0; t < NCW; ++t) v[t] = 0.f;
     }
+    float* dst = ostage + (q * 32 + lane) * LDO + h * NCW;
+#pragma unroll
+    for (int t = 0; t < NCW; t += 4) *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
   }
   fence_before_sync();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, BNT);
+  // 2: whole rows out.  Thread -> (row, 4-column word), consecutive threads on
+  // consecutive words of a row, so every global access of a warp is one
+  // contiguous run; UR rows per thread have their operand loads in flight together.
+  constexpr int G4 = BNT / 4, RPP = NTH / G4, UR = 4;
+  const int cw = tid % G4, rr = tid / G4;
+  const int64_t n = n0 + 4 * cw;
+  const bool nin = n < a.N, nvec = a.vec && n + 3 < a.N;
+  float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (a.ksplit <= 1 && a.bias && nvec) bb = *reinterpret_cast<const float4*>(a.bias + n);
+#pragma unroll 1
+  for (int rb = 0; rb < BMT; rb += RPP * UR) {
+    float4 acc[UR], aux[UR], rs[UR];
+    int64_t mr[UR];
+#pragma unroll
+    for (int u = 0; u < UR; ++u) {
+      const int row = rb + u * RPP + rr;
+      mr[u] = m0 + row;
+      acc[u] = *reinterpret_cast<const float4*>(ostage + row * LDO + 4 * cw);
+      const bool live = nvec && mr[u] < a.M && a.ksplit <= 1;
+      if (live && a.act == ACT_DSILU) aux[u] = *reinterpret_cast<const float4*>(a.aux + mr[u] * a.ldaux + n);
+      if (live && a.resid && n < a.resid_cols) rs[u] = *reinterpret_cast<const float4*>(a.resid + mr[u] * a.ldr + n);
+    }
+#pragma unroll
+    for (int u = 0; u < UR; ++u) {
+      const int64_t m = mr[u];
+      if (m >= a.M || !nin) continue;
+      if (a.ksplit > 1) {   // raw split-K slice (N % 4 == 0 on this path)
+        *reinterpret_cast<float4*>(a.part + (int64_t)blockIdx.z * a.M * a.N + m * a.N + n) = acc[u];
+        continue;
+      }
+      if (nvec) {
+        float y[4] = {acc[u].x + bb.x, acc[u].y + bb.y, acc[u].z + bb.z, acc[u].w + bb.w};
+        if (a.pre) *reinterpret_cast<float4*>(a.pre + m * a.ldp + n) = make_float4(y[0], y[1], y[2], y[3]);
+        if (a.act == ACT_SILU) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) y[t] = silu_fast(y[t]);
+        } else if (a.act == ACT_DSILU) {
+          const float z[4] = {aux[u].x, aux[u].y, aux[u].z, aux[u].w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            float yy, d;
+            silu_grad_fast(z[t], yy, d);
+            y[t] *= d;
+          }
+        }
+        if (a.resid && n < a.resid_cols) { y[0] += rs[u].x; y[1] += rs[u].y; y[2] += rs[u].z; y[3] += rs[u].w; }
+        *reinterpret_cast<float4*>(a.C + m * a.ldc + n) = make_float4(y[0], y[1], y[2], y[3]);
+      } else {
+        const float yv[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int64_t nn = n + t;
+          if (nn >= a.N) continue;
+          float y = yv[t];
+          if (a.bias) y += a.bias[nn];
+          if (a.pre) a.pre[m * a.ldp + nn] = y;
+          if (a.act == ACT_SILU) {
+            y = silu_fast(y);
+          } else if (a.act == ACT_DSILU) {
+            float yy, d;
+            silu_grad_fast(a.aux[m * a.ldaux + nn], yy, d);
+            y *= d;
+          }
+          if (a.resid && nn < a.resid_cols) y += a.resid[m * a.ldr + nn];
+          a.C[m * a.ldc + nn] = y;
+        }
+      }
+    }
+  }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -185,6 +185,48 @@ __device__ __forceinline__ void gather_a1(float4* stage, const float* __restrict
   }
 }
 
+// Forward variant: u1 = silu(a1) rounded to bf16 straight into row e of the
+// SW128 tile U (lane = features 4 lane .. + 3, one 8-byte store); invalid
+// edges get zero rows.  Same arithmetic and rounding as staging a1 first.
+template <int GB>
+__device__ __forceinline__ void gather_u(char* Ut, const float* __restrict__ PQ, const int* rows, const int* cols,
+                                         const float4* geo, const float* s_wr, int n, int warp, int lane) {
+  constexpr int H = 128;
+  const float4 wr4 = *reinterpret_cast<const float4*>(s_wr + 4 * lane);
+#pragma unroll
+  for (int b = 0; b < 8; b += GB) {
+    float4 p[GB], q[GB];
+#pragma unroll
+    for (int t = 0; t < GB; ++t) {
+      const int e = warp * 8 + b + t;
+      if (e < n) {
+        p[t] = __ldg(reinterpret_cast<const float4*>(PQ + (int64_t)rows[e] * 2 * H) + lane);
+        q[t] = __ldg(reinterpret_cast<const float4*>(PQ + (int64_t)cols[e] * 2 * H + H) + lane);
+      } else {
+        p[t] = q[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < GB; ++t) {
+      const int e = warp * 8 + b + t;
+      float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
+      if (e < n) {
+        const float r = geo[e].w;
+        u0 = silu_edge(fmaf(wr4.x, r, p[t].x + q[t].x));
+        u1 = silu_edge(fmaf(wr4.y, r, p[t].y + q[t].y));
+        u2 = silu_edge(fmaf(wr4.z, r, p[t].z + q[t].z));
+        u3 = silu_edge(fmaf(wr4.w, r, p[t].w + q[t].w));
+      }
+      const __nv_bfloat162 h01 = __floats2bfloat162_rn(u0, u1);
+      const __nv_bfloat162 h23 = __floats2bfloat162_rn(u2, u3);
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t*>(&h01);
+      w.y = *reinterpret_cast<const uint32_t*>(&h23);
+      *reinterpret_cast<uint2*>(Ut + sw128_offset(e, 4 * lane, kM)) = w;
+    }
+  }
+}
+
 // The 32-column slice col0..col0+31 of staged row e.
 __device__ __forceinline__ void stage_read32(const float4* stage, int e, int col0, float (&v)[32]) {
 #pragma unroll
@@ -259,7 +301,6 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   int* ncol = reinterpret_cast<int*>(sm + L::NCOL);
   float4* nxi = reinterpret_cast<float4*>(sm + L::NXI);
   float4* nxj = reinterpret_cast<float4*>(sm + L::NXJ);
-  float4* stage = reinterpret_cast<float4*>(Mt);   // a1 staging over the M | MLO tiles (64 KB)
   int* segrow = reinterpret_cast<int*>(sm + L::SEGROW);
   int* segstart = reinterpret_cast<int*>(sm + L::SEGSTART);
   float* open = reinterpret_cast<float*>(sm + L::OPEN);
@@ -369,16 +410,8 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       for (int k = 0; k < C::TILE / 16 / kNT; ++k) sz[g.tid + k * kNT] = make_uint4(0u, 0u, 0u, 0u);
     }
     __syncthreads();
-    // ---- a1 rows (coalesced), then u1 = silu(a1) slice of edge e -> tile U
-    gather_a1<4>(stage, a.PQ, rowl, coll, dl, s_wr, n, g.warp, g.lane);
-    __syncthreads();
-    {
-      float u[32];
-      stage_read32(stage, g.e, g.col0, u);
-#pragma unroll
-      for (int q = 0; q < 32; ++q) u[q] = silu_edge(u[q]);
-      st_row32_bf16(Ut, g.e, g.col0, u);
-    }
+    // ---- u1 = silu(a1) rows -> tile U (coalesced P / Q rows, one warp per edge)
+    gather_u<4>(Ut, a.PQ, rowl, coll, dl, s_wr, n, g.warp, g.lane);
     // ---- segments of the chunk (runs of equal destination rows)
     if (g.cg == 0) {
       const int r = rowl[g.e];

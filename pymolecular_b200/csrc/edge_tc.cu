@@ -119,11 +119,6 @@ __device__ __forceinline__ float warp_colsum32(float (&x)[32]) {
   return x[0];
 }
 
-__device__ __forceinline__ float scale_of(const int32_t* row_ptr, int r, int flags) {
-  if (flags & EGNN_FLAG_COORDS_SUM) return 1.f;
-  return 1.f / (float)max(row_ptr[r + 1] - row_ptr[r], 1);
-}
-
 // ---- thread geometry -------------------------------------------------------------
 // 512 threads: warp w covers TMEM lanes 32*(w%4)..+31 (edge rows) and the
 // 32-column slice 32*(w/4)..+31 of those rows.
@@ -268,7 +263,9 @@ struct FwdLayout {
   static constexpr size_t NCOL = NROW + kM * 4;        // int[128]: next chunk's source ids
   static constexpr size_t SEGROW = NCOL + kM * 4;      // int[129]
   static constexpr size_t SEGSTART = SEGROW + (kM + 4) * 4;
-  static constexpr size_t OPEN = SEGSTART + (kM + 4) * 4;   // float[H + 4]
+  static constexpr size_t SEGRP = SEGSTART + (kM + 4) * 4;   // int[128][2]: row_ptr[r], row_ptr[r + 1] of segment rows
+  static constexpr size_t XLI = SEGRP + kM * 8;        // float4[128]: x_i of each edge
+  static constexpr size_t OPEN = XLI + kM * 16;        // float[H + 4]
   static constexpr size_t MISC = OPEN + (H + 4) * 4;   // ints: nseg, open_row, prev_row, warp counts[4]
   static constexpr size_t BAR = MISC + 64;
   static constexpr size_t END = BAR + 16;
@@ -303,6 +300,8 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   float4* nxj = reinterpret_cast<float4*>(sm + L::NXJ);
   int* segrow = reinterpret_cast<int*>(sm + L::SEGROW);
   int* segstart = reinterpret_cast<int*>(sm + L::SEGSTART);
+  int* segrp = reinterpret_cast<int*>(sm + L::SEGRP);
+  float4* xli = reinterpret_cast<float4*>(sm + L::XLI);
   float* open = reinterpret_cast<float*>(sm + L::OPEN);
   int* misc = reinterpret_cast<int*>(sm + L::MISC);   // [0] nseg [1] open_row [2] prev_row [4..7] warp counts
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
@@ -343,8 +342,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   bool ok = true;
 
   // Write the 32-column slice of a finished row (and its coordinates when cg == 0).
-  auto put_row = [&](int r, const float (&v)[32], float4 cx, bool zero) {
-    const bool before = a.row_ptr[r] < eb;
+  // rp0, rp1 = row_ptr[r], row_ptr[r + 1]; xr = x_r (xyz)
+  auto put_row = [&](int r, const float (&v)[32], float4 cx, bool zero, int rp0, int rp1, float4 xr) {
+    const bool before = rp0 < eb;
     if (!before) {
       float* dst = a.agg + (int64_t)r * H + g.col0;
 #pragma unroll
@@ -352,11 +352,10 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
         *reinterpret_cast<float4*>(dst + k) = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
                                                    : make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
       if (g.cg == 0) {
-        const float sc = scale_of(a.row_ptr, r, a.flags);
-        const float c3[3] = {cx.x, cx.y, cx.z};
+        const float sc = (a.flags & EGNN_FLAG_COORDS_SUM) ? 1.f : 1.f / (float)max(rp1 - rp0, 1);
+        const float c3[3] = {cx.x, cx.y, cx.z}, x3[3] = {xr.x, xr.y, xr.z};
 #pragma unroll
-        for (int d = 0; d < 3; ++d)
-          a.x_out[(int64_t)r * 3 + d] = a.x[(int64_t)r * 3 + d] + (zero ? 0.f : c3[d] * sc);
+        for (int d = 0; d < 3; ++d) a.x_out[(int64_t)r * 3 + d] = x3[d] + (zero ? 0.f : c3[d] * sc);
       }
     } else {
       float* dst = a.carry + ((int64_t)cta * 2 + 0) * (H + 4);
@@ -369,6 +368,10 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
     }
   };
   const float zero32[32] = {};
+  // a row with no edges in this chunk: its row pointers and coordinates from memory
+  auto put_empty_row = [&](int r) {
+    put_row(r, zero32, make_float4(0.f, 0.f, 0.f, 0.f), true, a.row_ptr[r], a.row_ptr[r + 1], a.xp[r]);
+  };
 
   // The next chunk's edge ids and coordinates are prefetched with cp.async by
   // the threads of column slice 1 while this chunk's MMAs and activations run
@@ -398,6 +401,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
         rowl[g.e] = i;
         coll[g.e] = j;
         dl[g.e] = make_float4(dx * inv, dy * inv, dz * inv, r);
+        xli[g.e] = xi;
       } else {
         rowl[g.e] = INT_MAX;
         coll[g.e] = 0;
@@ -425,6 +429,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       if (flag) {
         segrow[seg] = r;
         segstart[seg] = g.e;
+        cp_async4(&segrp[2 * seg], a.row_ptr + r);     // needed by the row flush
+        cp_async4(&segrp[2 * seg + 1], a.row_ptr + r + 1);
+        cp_async_commit_group();
       }
       if (valid) {
         const __nv_bfloat16 one = __float2bfloat16_rn(1.f);
@@ -494,6 +501,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       for (int q = 0; q < 32; ++q) p = fmaf(silu_edge(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
       part[g.cg * kM + g.e] = p;
     }
+    if (g.cg == 0) cp_async_wait_all_groups();   // segment heads: row pointers landed
     __syncthreads();
     if (g.cg == 0) {
       const float p = part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e];
@@ -522,16 +530,17 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       if (s < nseg) {
         const int r = segrow[s];
         const int pr = (s == 0) ? prev : segrow[s - 1];
-        for (int rr = pr + 1; rr < r; ++rr) put_row(rr, zero32, make_float4(0.f, 0.f, 0.f, 0.f), true);
+        for (int rr = pr + 1; rr < r; ++rr) put_empty_row(rr);
         float4 cx = segx[s];
         if (s == 0 && r == open_row) {
 #pragma unroll
           for (int k = 0; k < 32; ++k) v[k] += open[g.col0 + k];
           cx.x += open[H]; cx.y += open[H + 1]; cx.z += open[H + 2];
         }
-        const bool complete = (s < nseg - 1) || (a.row_ptr[r + 1] <= c0 + n);
+        const int rp0 = segrp[2 * s], rp1 = segrp[2 * s + 1];
+        const bool complete = (s < nseg - 1) || (rp1 <= c0 + n);
         if (complete) {
-          put_row(r, v, cx, false);
+          put_row(r, v, cx, false, rp0, rp1, xli[segstart[s]]);
         } else {
 #pragma unroll
           for (int k = 0; k < 32; ++k) open[g.col0 + k] = v[k];
@@ -545,7 +554,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
     if (g.tid == 0) {
       const int r = segrow[nseg - 1];
       misc[2] = r;
-      misc[1] = (a.row_ptr[r + 1] <= c0 + n) ? -1 : r;
+      misc[1] = (segrp[2 * (nseg - 1) + 1] <= c0 + n) ? -1 : r;
     }
     __syncthreads();
     pref = n_next > 0;
@@ -567,7 +576,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
         }
       }
     }
-    for (int rr = last + 1 + g.e; rr < end_row; rr += kM) put_row(rr, zero32, make_float4(0.f, 0.f, 0.f, 0.f), true);
+    for (int rr = last + 1 + g.e; rr < end_row; rr += kM) put_empty_row(rr);
   }
   fence_before_sync();
   __syncthreads();

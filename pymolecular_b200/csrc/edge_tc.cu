@@ -825,6 +825,14 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
         mma_bf16(tD0, desc_k(Gt, kM, kk), desc_mn(Wc1t, H, kk), C::IDESC_DGRAD, kk > 0);
       mma_commit(bar);
     }
+    // g_agg[i] slice of edge e: loads issued before the wait, used after it
+    float4 gagg[8];
+    {
+      const float* ga = a.g_agg + (int64_t)rowi[g.e] * (a.ld_gagg ? a.ld_gagg : H) + g.col0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        gagg[q] = valid ? *reinterpret_cast<const float4*>(ga + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (!(ok = wait_mma(bar, phase))) break;
 
     // ---- g_a2 = (g_m + g_agg[i]) silu'(a2) -> tile G ; column sums
@@ -832,11 +840,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       float v[32];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
       const __half2* drow = reinterpret_cast<const __half2*>(d2s + g.e * C::LDD + g.col0);
-      const float* ga = a.g_agg + (int64_t)rowi[g.e] * (a.ld_gagg ? a.ld_gagg : H) + g.col0;
 #pragma unroll
       for (int q = 0; q < 32; q += 4) {
-        float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) g4 = *reinterpret_cast<const float4*>(ga + q);
+        const float4 g4 = gagg[q / 4];
         const float2 d01 = __half22float2(drow[q / 2]);
         const float2 d23 = __half22float2(drow[q / 2 + 1]);
         v[q] = valid ? (v[q] + g4.x) * d01.x : 0.f;

@@ -99,8 +99,12 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     gr = g_a1 @ wr
     self_loop = (row == col).to(d)
     gdl = g_trans * (phi * inv * (1 - self_loop))[:, None] + 2 * gr[:, None] * dlt
-    S_dst = segment_sum(g_a1, row, N)
-    S_src = segment_sum(g_a1, col, N)
+    # the tensor-core path (bf16, H = 128, no edge attributes) stores g_a1 in
+    # bf16 for the dst / src row sums (edge_tc.cu backward); fp32 elsewhere
+    tc_path = on and H == 128 and (edge_attr is None or edge_attr.shape[1] == 0)
+    g_a1s = _bf(g_a1, tc_path)
+    S_dst = segment_sum(g_a1s, row, N)
+    S_src = segment_sum(g_a1s, col, N)
     grad_x = gx + segment_sum(gdl, row, N) - segment_sum(gdl, col, N)
     grad_h = gh_acc + S_dst @ Wa + S_src @ Wb
     gW1 = torch.zeros_like(W1)

@@ -763,9 +763,9 @@ __global__ void edge_fixup_kernel(int H, int64_t E, int G, int64_t epc, const in
 }
 
 // ---- source pass -----------------------------------------------------------------
-template <int H>
+template <int H, typename T>
 __global__ void src_pass_kernel(int64_t N, const int32_t* __restrict__ src_ptr,
-                                const int32_t* __restrict__ src_edge, const float* __restrict__ gstore,
+                                const int32_t* __restrict__ src_edge, const T* __restrict__ gstore,
                                 const float4* __restrict__ gdstore, const float* __restrict__ gx_out,
                                 const float* __restrict__ gxd, float* __restrict__ S_src,
                                 float* __restrict__ gx) {
@@ -982,18 +982,22 @@ int edge_bwd(int H, bool bf16, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStre
 }
 
 int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_edge,
-                  const float* gstore, const float4* gdstore, const float* gx_out,
+                  const void* gstore, bool bf16_rows, const float4* gdstore, const float* gx_out,
                   const float* gxd, float* S_src, float* gx, cudaStream_t s) {
-  if (N == 0) return EGNN_OK;
+  if (N <= 0) return EGNN_OK;
   const int warps = 8;
   const unsigned blocks = (unsigned)((N + warps - 1) / warps);
-#define EGNN_SRC(HH)                                                                              \
-  if (H == HH) {                                                                                  \
-    TimerScope ts("src_pass", s);                                                                 \
-    src_pass_kernel<HH><<<blocks, warps * 32, 0, s>>>(N, src_ptr, src_edge, gstore, gdstore,      \
-                                                     gx_out, gxd, S_src, gx);                     \
-    EGNN_CHECK_LAUNCH();                                                                          \
-    return EGNN_OK;                                                                               \
+#define EGNN_SRC(HH)                                                                               \
+  if (H == HH) {                                                                                   \
+    TimerScope ts("src_pass", s);                                                                  \
+    if (bf16_rows)                                                                                 \
+      src_pass_kernel<HH, __nv_bfloat16><<<blocks, warps * 32, 0, s>>>(                            \
+          N, src_ptr, src_edge, static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, gxd, S_src, gx); \
+    else                                                                                           \
+      src_pass_kernel<HH, float><<<blocks, warps * 32, 0, s>>>(                                    \
+          N, src_ptr, src_edge, static_cast<const float*>(gstore), gdstore, gx_out, gxd, S_src, gx);         \
+    EGNN_CHECK_LAUNCH();                                                                           \
+    return EGNN_OK;                                                                                \
   }
   EGNN_SRC(32) EGNN_SRC(64) EGNN_SRC(128) EGNN_SRC(256)
 #undef EGNN_SRC

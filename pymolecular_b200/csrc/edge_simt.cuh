@@ -24,6 +24,36 @@ __device__ __forceinline__ void load_row_slice(const float* row, int lane, float
     v[0] = __ldg(p);
   }
 }
+// The same slice of a bf16 row (the tensor-core backward stores dL/da1 in bf16).
+template <int H>
+__device__ __forceinline__ void load_row_slice(const __nv_bfloat16* row, int lane, float (&v)[H / 32]) {
+  constexpr int VW = H / 32;
+  const __nv_bfloat16* p = row + lane * VW;
+  if constexpr (VW % 8 == 0) {
+#pragma unroll
+    for (int w = 0; w < VW; w += 8) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + w));
+      const uint32_t x[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x[t]));
+        v[w + 2 * t] = f.x; v[w + 2 * t + 1] = f.y;
+      }
+    }
+  } else if constexpr (VW == 4) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+  } else if constexpr (VW == 2) {
+    const unsigned int u = __ldg(reinterpret_cast<const unsigned int*>(p));
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+    v[0] = f.x; v[1] = f.y;
+  } else {
+    v[0] = __bfloat162float(p[0]);
+  }
+}
+
 template <int H>
 __device__ __forceinline__ void store_row_slice(float* row, int lane, const float (&v)[H / 32]) {
   constexpr int VW = H / 32;
@@ -78,7 +108,7 @@ struct EdgeBwdArgs : EdgeCommon {
   int64_t ld_gagg = 0;           // row stride of g_agg (H when 0)
   float* S_dst = nullptr;        // (N,H) out: sum over each row of dL/da1
   float* gxd = nullptr;          // (N,3) out: sum over each row of dL/d(x_i - x_j)
-  float* gstore = nullptr;       // (E,H) out: dL/da1 per CSR edge
+  float* gstore = nullptr;       // (E,H) out: dL/da1 per CSR edge (bf16 rows on the tensor-core path)
   float4* gdstore = nullptr;     // (E) out: dL/d(x_i - x_j) per CSR edge
   float* part = nullptr;         // (G, part_floats(H,d)) per-CTA weight-gradient partials
 };
@@ -103,8 +133,9 @@ int edge_bwd(int H, bool bf16, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStre
 
 // Source-side pass of the backward: S_src[j] = sum of gstore over the
 // out-edges of j (transpose CSR order), gx[j] = gx_out[j] + gxd[j] - sum gd.
+// gstore holds fp32 rows, or bf16 rows when `bf16_rows` (tensor-core path).
 int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_edge,
-                  const float* gstore, const float4* gdstore, const float* gx_out,
+                  const void* gstore, bool bf16_rows, const float4* gdstore, const float* gx_out,
                   const float* gxd, float* S_src, float* gx, cudaStream_t s);
 
 // Reduce the G per-CTA partials in CTA order and scatter them into the

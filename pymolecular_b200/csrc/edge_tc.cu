@@ -18,7 +18,7 @@
 //            g_m  = G Wc1 + g_agg[i]              tcgen05 + CUDA cores
 //            g_a2 = g_m silu'(a2)                 -> tile G
 //            dW2  += G^T U   (TMEM, persistent)
-//            g_a1 = (G W2) silu'(a1)              -> global, one H-vector per edge
+//            g_a1 = (G W2) silu'(a1)              -> global, one bf16 H-vector per edge
 // The weight tiles live in shared memory for the whole kernel; one copy of
 // each serves the forward product (K-major B) and the data-gradient product
 // (MN-major B).  The row sums of g_a1 and of the coordinate gradients are
@@ -893,11 +893,20 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       a.gdstore[c0 + g.e] = make_float4(gt.x * f + 2.f * gr * d.x, gt.y * f + 2.f * gr * d.y,
                                         gt.z * f + 2.f * gr * d.z, 0.f);
     }
-    // g_a1 rows of the chunk to global memory, one warp per edge row
+    // g_a1 rows of the chunk to global memory as bf16 (the operand of the
+    // dst / src row sums), one warp per edge row, 8 bytes per lane
+    __nv_bfloat16* gst = reinterpret_cast<__nv_bfloat16*>(a.gstore);
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
       const int e = g.warp * 8 + t;
-      if (e < n) reinterpret_cast<float4*>(a.gstore + (c0 + e) * H)[g.lane] = stage[stage_word(e, g.lane)];
+      if (e < n) {
+        const float4 w = stage[stage_word(e, g.lane)];
+        const __nv_bfloat162 h01 = __floats2bfloat162_rn(w.x, w.y), h23 = __floats2bfloat162_rn(w.z, w.w);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&h01);
+        u.y = *reinterpret_cast<const uint32_t*>(&h23);
+        reinterpret_cast<uint2*>(gst + (c0 + e) * H)[g.lane] = u;
+      }
     }
     if (prefetcher) cp_async_wait_all_groups();
     __syncthreads();
@@ -946,7 +955,8 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
 
 // ---- dst row pass: S_dst[i] = sum of g_a1 over row i, gxd[i] = sum of d-gradients ----
 template <int H>
-__global__ void row_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr, const float* __restrict__ gstore,
+__global__ void row_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
+                                const __nv_bfloat16* __restrict__ gstore,
                                 const float4* __restrict__ gdstore, float* __restrict__ S_dst,
                                 float* __restrict__ gxd) {
   // One warp per destination row, lane owning H / 32 consecutive features;
@@ -1056,7 +1066,8 @@ int edge_bwd_tc(int H, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s) 
     const int warps = 8;
     const unsigned blocks = (unsigned)((a.N + warps - 1) / warps);
     TimerScope ts("row_pass", s);
-    row_pass_kernel<128><<<blocks, warps * 32, 0, s>>>(a.N, a.row_ptr, a.gstore, a.gdstore, a.S_dst, a.gxd);
+    row_pass_kernel<128><<<blocks, warps * 32, 0, s>>>(a.N, a.row_ptr, reinterpret_cast<const __nv_bfloat16*>(a.gstore),
+                                                       a.gdstore, a.S_dst, a.gxd);
   }
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;

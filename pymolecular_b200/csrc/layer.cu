@@ -465,7 +465,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
   else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
   EGNN_TRY(edge_part_reduce(H, dd, eg.G, w.part, gp, ld1, s));
-  EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, w.gdstore, gx_out, w.gxd, w.S_src,
+  EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, tc, w.gdstore, gx_out, w.gxd, w.S_src,
                          grad_x, s));
 
   // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb ;  dWa, db1 on the side stream, dWb here

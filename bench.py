@@ -295,7 +295,10 @@ class Problem:
         loss.backward()
         self.sync_grads()
         self.opt.step()
-        return loss
+        # detached: a captured step must not keep its autograd graph alive
+        # past the capture (later eager steps would then accumulate into
+        # nodes that belong to the capture stream)
+        return loss.detach()
 
     def host_buffers(self):
         bufs = {"h": self.h_host.pin_memory(), "x": self.x_host.pin_memory(),

@@ -27,7 +27,7 @@ def _silu(a):
 
 
 def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", residual=True,
-                  normalize=False, tanh=False, coords_agg="mean"):
+                  attention=False, normalize=False, tanh=False, coords_agg="mean"):
     """(h', x', dL/dh, dL/dx, {param: grad}) with the kernels' rounding points."""
     on = precision == "bf16"
     d = torch.float64
@@ -56,6 +56,12 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     u1 = _bf(u1, on)
     a2 = u1 @ _bf(W2, on).t() + b2
     m, d2 = _silu(a2)
+    if attention:
+        # gate in full precision on the ungated message (egnn_clean.py:55-57)
+        n = m
+        wa, ba = p["att_mlp.0.weight"][0], p["att_mlp.0.bias"]
+        at = torch.sigmoid(n @ wa + ba)
+        m = n * at[:, None]
     mb = _bf(m, on)
     c1 = mb @ _bf(Wc1, on).t() + bc1
     v, dv = _silu(c1)
@@ -91,6 +97,11 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     gc1b = _bf(g_c1, on)
     g["coord_mlp.0.weight"] = gc1b.t() @ mb
     g_m = gc1b @ _bf(Wc1, on) + g_agg[row]
+    if attention:
+        gs = (g_m * n).sum(1) * at * (1 - at)
+        g["att_mlp.0.weight"] = (gs[:, None] * n).sum(0)[None, :]
+        g["att_mlp.0.bias"] = gs.sum(0, keepdim=True)
+        g_m = g_m * at[:, None] + gs[:, None] * wa
     g_a2 = g_m * d2
     g["edge_mlp.2.bias"] = g_a2.sum(0)
     ga2b = _bf(g_a2, on)
@@ -99,9 +110,10 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     gr = g_a1 @ wr
     self_loop = (row == col).to(d)
     gdl = g_trans * (phi * inv * (1 - self_loop))[:, None] + 2 * gr[:, None] * dlt
-    # the tensor-core path (bf16, H = 128, no edge attributes) stores g_a1 in
-    # bf16 for the dst / src row sums (edge_tc.cu backward); fp32 elsewhere
-    tc_path = on and H == 128 and (edge_attr is None or edge_attr.shape[1] == 0)
+    # the tensor-core path (bf16, H = 128, no edge attributes, no attention)
+    # stores g_a1 in bf16 for the dst / src row sums (edge_tc.cu backward);
+    # fp32 elsewhere
+    tc_path = on and H == 128 and (edge_attr is None or edge_attr.shape[1] == 0) and not attention
     g_a1s = _bf(g_a1, tc_path)
     S_dst = segment_sum(g_a1s, row, N)
     S_src = segment_sum(g_a1s, col, N)

@@ -5,6 +5,7 @@
 //   d = x_i - x_j, r = |d|^2                                   coord2radial :84-93
 //   a1 = W1 [h_i, h_j, r, attr] + b1 ; u1 = silu(a1)            edge_mlp.0   :22-24
 //   a2 = W2 u1 + b2 ; m = silu(a2)                              edge_mlp.2   :25-26
+//   [attention] m <- m sigmoid(wa . m + ba)                     att_mlp      :44-47, :55-57
 //   c1 = Wc1 m + bc1 ; phi = wc2 . silu(c1) [tanh]              coord_mlp    :36-42
 //   agg_i = sum_e m_e ; x'_i = x_i + mean/sum_e d_e phi_e       :62, :74-81
 // W1 [h_i, h_j] is factored into per-node projections P = h Wa^T + b1 and
@@ -138,6 +139,34 @@ __device__ __forceinline__ float row_sum(float v) {
   return v;
 }
 
+// ---- attention gate (egnn_clean.py:44-47, 55-57) --------------------------------
+// m <- m * at with at = sigmoid(wa . m + ba) per edge; the dot runs over the
+// TXN threads of an edge row, so every one of them gets at[m].
+template <class C>
+__device__ __forceinline__ void att_gate(float (&acc)[C::TM][C::NC], const float* __restrict__ wa, float ba,
+                                         float (&at)[C::TM]) {
+  float w[C::NC];
+#pragma unroll
+  for (int g = 0; g < C::NG; ++g)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) w[g * 4 + q] = __ldg(wa + C::col(g, q));
+#pragma unroll
+  for (int m = 0; m < C::TM; ++m) {
+    float p = 0.f;
+#pragma unroll
+    for (int c = 0; c < C::NC; ++c) p = fmaf(acc[m][c], w[c], p);
+    at[m] = sigmoidf_(row_sum<C>(p) + ba);
+#pragma unroll
+    for (int c = 0; c < C::NC; ++c) acc[m][c] *= at[m];
+  }
+}
+
+// Per-CTA attention scratch of the backward (floats): ungated messages of the
+// chunk as float4 [TM][NG][NT] (each thread reads back what it wrote) | gwa
+// sums [TY][H] | gba sums [TY] (one owner thread per slot, so no atomics).
+template <class C>
+constexpr int64_t att_scratch_floats() { return (int64_t)C::T * C::H + (int64_t)C::TY * (C::H + 1); }
+
 // ---- per-chunk weight-gradient product ------------------------------------
 // Pw[o][k] += sum_{e<T} GT[o][e] * XT[k][e].  Thread (ot, kt) owns rows
 // o = ot + 16 a and columns k = kt + 16 b.
@@ -227,7 +256,8 @@ struct BwdSmem {
   static constexpr size_t phi = gd + 4 * (size_t)C::T;              // float[T]
   static constexpr size_t rowl = phi + C::T;                        // int[T]
   static constexpr size_t attr = rowl + C::T;                       // float[T][kMaxAttr]
-  static constexpr size_t total_floats = attr + (size_t)C::T * kMaxAttr;
+  static constexpr size_t att = attr + (size_t)C::T * kMaxAttr;     // float[T]: attention gate
+  static constexpr size_t total_floats = att + C::T;
   static constexpr size_t bytes = total_floats * 4;
 };
 
@@ -402,6 +432,10 @@ __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeFwdArgs a) {
     for (int m = 0; m < C::TM; ++m)
 #pragma unroll
       for (int c = 0; c < C::NC; ++c) acc[m][c] = silu_f(acc[m][c]);
+    if (a.flags & EGNN_FLAG_ATTENTION) {
+      float at[C::TM];
+      att_gate<C>(acc, a.wa, __ldg(a.ba), at);
+    }
     store_T<C, false>(mT, acc);
     if constexpr (BF) store_T<C, true>(uT, acc);
     __syncthreads();
@@ -469,6 +503,7 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeBwdArgs a) {
   float* phi = sm + S::phi;
   const int* rowl = reinterpret_cast<const int*>(sm + S::rowl);
   const float* attr_s = sm + S::attr;
+  float* att_s = sm + S::att;
 
   const int tid = threadIdx.x, ty = tid / C::TXN, tx = tid % C::TXN;
   const int cta = blockIdx.x, G = gridDim.x;
@@ -481,6 +516,19 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeBwdArgs a) {
   float* pW2 = part + H * H;
   zero_wgrad<C>(pWc1);
   zero_wgrad<C>(pW2);
+
+  const bool att = a.flags & EGNN_FLAG_ATTENTION;
+  float* const scr = att ? a.att_scr + (int64_t)cta * att_scratch_floats<C>() : nullptr;
+  float4* const att_n = reinterpret_cast<float4*>(scr);
+  float* const att_wa = att ? scr + C::T * H : nullptr;
+  float* const att_ba = att ? att_wa + C::TY * H : nullptr;
+  if (att) {
+#pragma unroll
+    for (int g = 0; g < C::NG; ++g)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) att_wa[ty * H + C::col(g, q)] = 0.f;
+    if (tx == 0) att_ba[ty] = 0.f;
+  }
 
   int cur = (cta == 0) ? 0 : a.row_idx[eb];
   const int end_row = (cta == G - 1) ? N : a.row_idx[ee];
@@ -548,6 +596,21 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeBwdArgs a) {
         acc[m][c] = y;
         aux[m][c] = dy;
       }
+    if (att) {
+      // park the ungated messages for the gate's backward, then gate
+#pragma unroll
+      for (int m = 0; m < C::TM; ++m)
+#pragma unroll
+        for (int g = 0; g < C::NG; ++g)
+          att_n[(m * C::NG + g) * C::NT + tid] =
+              make_float4(acc[m][g * 4 + 0], acc[m][g * 4 + 1], acc[m][g * 4 + 2], acc[m][g * 4 + 3]);
+      float at[C::TM];
+      att_gate<C>(acc, a.wa, __ldg(a.ba), at);
+      if (tx == 0) {
+#pragma unroll
+        for (int m = 0; m < C::TM; ++m) att_s[ty * C::TM + m] = at[m];
+      }
+    }
     store_T<C, BF>(mT, acc);
     store_T<C, false>(d2T, aux);
     __syncthreads();
@@ -618,6 +681,33 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeBwdArgs a) {
       }
     }
     chunk_gemm<C>(acc, gT, a.Wc1, Bs);
+    if (att) {
+      // g_m is dL/d(n at): dL/dn = g_m at + gs wa with gs = (g_m . n) at (1 - at);
+      // gwa += gs n, gba += gs
+#pragma unroll
+      for (int m = 0; m < C::TM; ++m) {
+        const float at = att_s[ty * C::TM + m];
+        float nv[C::NC];
+#pragma unroll
+        for (int g = 0; g < C::NG; ++g) {
+          const float4 t = att_n[(m * C::NG + g) * C::NT + tid];
+          nv[g * 4 + 0] = t.x; nv[g * 4 + 1] = t.y; nv[g * 4 + 2] = t.z; nv[g * 4 + 3] = t.w;
+        }
+        float dot = 0.f;
+#pragma unroll
+        for (int c = 0; c < C::NC; ++c) dot = fmaf(acc[m][c], nv[c], dot);
+        const float gs = row_sum<C>(dot) * at * (1.f - at);
+#pragma unroll
+        for (int g = 0; g < C::NG; ++g)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int c = g * 4 + q, f = C::col(g, q);
+            att_wa[ty * H + f] = fmaf(gs, nv[c], att_wa[ty * H + f]);
+            acc[m][c] = fmaf(acc[m][c], at, gs * __ldg(a.wa + f));
+          }
+        if (tx == 0) att_ba[ty] += gs;
+      }
+    }
 #pragma unroll
     for (int m = 0; m < C::TM; ++m)
 #pragma unroll
@@ -729,6 +819,19 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeBwdArgs a) {
     for (int t = 0; t < kMaxAttr; ++t)
       if (t < a.d) part[2 * H * H + 4 * H + tid * a.d + t] = gwe[t];
   }
+  if (att) {   // the barriers above order every thread's scratch updates
+    const int64_t off = edge_part_att(H, a.d);
+    for (int f = tid; f < H; f += C::NT) {
+      float sacc = 0.f;
+      for (int y = 0; y < C::TY; ++y) sacc += att_wa[y * H + f];
+      part[off + f] = sacc;
+    }
+    if (tid == 0) {
+      float sacc = 0.f;
+      for (int y = 0; y < C::TY; ++y) sacc += att_ba[y];
+      part[off + H] = sacc;
+    }
+  }
 }
 
 // ---- boundary fix-up -----------------------------------------------------------
@@ -816,9 +919,9 @@ __global__ void src_pass_kernel(int64_t N, const int32_t* __restrict__ src_ptr,
   if (lane < 3) gx[j * 3 + lane] = gx_out[j * 3 + lane] + gxd[j * 3 + lane] - gs;
 }
 
-__global__ void part_reduce_kernel(int H, int d, int G, int64_t PF, const float* part,
+__global__ void part_reduce_kernel(int H, int d, int att, int G, int64_t PF, const float* part,
                                    egnn_layer_grads gp, int64_t ld_w1) {
-  const int64_t total = 2LL * H * H + 4LL * H + (int64_t)H * d;
+  const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     // CTA partials loaded eight at a time (independent loads), added in CTA order
@@ -843,10 +946,14 @@ __global__ void part_reduce_kernel(int H, int d, int G, int64_t PF, const float*
       else if (v < 2 * H) gp.edge_b2[v - H] = s;
       else if (v < 3 * H) gp.coord_w2[v - 2 * H] = s;
       else if (v < 4 * H) gp.edge_w1[(v - 3 * H) * ld_w1 + 2 * H] = s;
-      else {
+      else if (v < 4 * H + (int64_t)H * d) {
         const int64_t w = v - 4 * H;
         const int64_t f = w / d, t = w % d;
         gp.edge_w1[f * ld_w1 + 2 * H + 1 + t] = s;
+      } else {
+        const int64_t w = v - 4 * H - (int64_t)H * d;
+        if (w < H) gp.att_w[w] = s;
+        else gp.att_b[0] = s;
       }
     }
   }
@@ -930,6 +1037,15 @@ int occupancy(bool bwd, int* out) {
 
 int edge_chunk(int H) { return H >= 256 ? 32 : 64; }
 
+int64_t edge_att_scratch_floats(int H) {
+  switch (H) {
+    case 32: return att_scratch_floats<Cfg<32>>();
+    case 64: return att_scratch_floats<Cfg<64>>();
+    case 128: return att_scratch_floats<Cfg<128>>();
+    default: return att_scratch_floats<Cfg<256>>();
+  }
+}
+
 int edge_grid(int H, bool bwd, bool bf16, int64_t E, int num_sms, EdgeGrid* out) {
   int occ = 1;
   // Occupancy is fixed by shared memory; cache per (H, bwd, bf16).
@@ -1004,12 +1120,12 @@ int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_e
   return fail(EGNN_ERR_UNSUPPORTED, "hidden size %d not built", H);
 }
 
-int edge_part_reduce(int H, int d, int G, const float* part, const egnn_layer_grads* gp,
+int edge_part_reduce(int H, int d, bool att, int G, const float* part, const egnn_layer_grads* gp,
                      int64_t ld_w1, cudaStream_t s) {
-  const int64_t total = 2LL * H * H + 4LL * H + (int64_t)H * d;
+  const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
   TimerScope ts("part_reduce", s);
-  part_reduce_kernel<<<blocks, 256, 0, s>>>(H, d, G, edge_part_floats(H, d), part, *gp, ld_w1);
+  part_reduce_kernel<<<blocks, 256, 0, s>>>(H, d, att ? 1 : 0, G, edge_part_floats(H, d), part, *gp, ld_w1);
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

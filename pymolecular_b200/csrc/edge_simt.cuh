@@ -88,6 +88,8 @@ struct EdgeCommon {
   const float* wc2 = nullptr;    // (H) coord_mlp.2.weight
   const float* W2_src = nullptr; // (H,H) edge_mlp.2.weight as given (fp32, [out][in])
   const float* Wc1_src = nullptr;// (H,H) coord_mlp.0.weight as given
+  const float* wa = nullptr;     // (H) att_mlp.0.weight (attention only)
+  const float* ba = nullptr;     // (1) att_mlp.0.bias (attention only)
   int flags = 0;
   int64_t epc = 0;               // edges per CTA (multiple of the chunk size)
   float* carry = nullptr;        // (G, 2, H+4) partial rows at CTA range edges
@@ -111,14 +113,21 @@ struct EdgeBwdArgs : EdgeCommon {
   float* gstore = nullptr;       // (E,H) out: dL/da1 per CSR edge (bf16 rows on the tensor-core path)
   float4* gdstore = nullptr;     // (E) out: dL/d(x_i - x_j) per CSR edge
   float* part = nullptr;         // (G, part_floats(H,d)) per-CTA weight-gradient partials
+  float* att_scr = nullptr;      // (G, edge_att_scratch_floats(H)) attention only: each CTA's
+                                 // ungated messages of the current chunk and its gate-gradient sums
 };
 
 // Per-CTA partial layout (floats): gWc1 (H*H) | gW2 (H*H) | gbc1 | gb2 | gwc2 | gwr (H each)
-// | gWe (H*d).
+// | gWe (H*d) | gwa (H) | gba (1); the last two only carry values with attention.
+__host__ __device__ inline int64_t edge_part_att(int H, int d) { return 2LL * H * H + 4LL * H + (int64_t)H * d; }
 __host__ __device__ inline int64_t edge_part_floats(int H, int d) {
-  int64_t n = 2LL * H * H + 4LL * H + (int64_t)H * d;
+  int64_t n = edge_part_att(H, d) + H + 1;
   return (n + 63) / 64 * 64;
 }
+
+// Per-CTA attention scratch of the SIMT backward (floats): the chunk's
+// ungated messages (T x H) | gwa partial sums (TY x H) | gba partial sums (TY).
+int64_t edge_att_scratch_floats(int H);
 
 // Launch geometry for a given E: CTA count and edges per CTA.
 struct EdgeGrid { int G; int64_t epc; };
@@ -140,7 +149,7 @@ int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_e
 
 // Reduce the G per-CTA partials in CTA order and scatter them into the
 // parameter-gradient outputs.
-int edge_part_reduce(int H, int d, int G, const float* part, const egnn_layer_grads* gp,
+int edge_part_reduce(int H, int d, bool att, int G, const float* part, const egnn_layer_grads* gp,
                      int64_t ld_w1, cudaStream_t s);
 
 }  // namespace egnn

@@ -1040,8 +1040,8 @@ int launch_bwd_tc(const EdgeBwdArgs& a, int G, cudaStream_t s) {
 }  // namespace
 
 bool edge_tc_supported(int H, int d, int flags, int precision) {
-  (void)flags;
-  return precision == EGNN_PREC_BF16 && H == 128 && d == 0;
+  // the attention gate runs on the SIMT kernels only
+  return precision == EGNN_PREC_BF16 && H == 128 && d == 0 && !(flags & EGNN_FLAG_ATTENTION);
 }
 
 EdgeGrid edge_tc_grid(int64_t E, int num_sms) {

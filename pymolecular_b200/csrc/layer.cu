@@ -40,8 +40,6 @@ int check_desc(const egnn_layer_desc* d) {
   if (d->edge_attr_dim < 0 || d->edge_attr_dim > 16)
     return fail(EGNN_ERR_UNSUPPORTED, "edge_attr_dim %d not built (0..16)", d->edge_attr_dim);
   if (d->flags & ~31) return fail(EGNN_ERR_INVALID_ARG, "unknown flag bits 0x%x", d->flags);
-  if (d->flags & EGNN_FLAG_ATTENTION)
-    return fail(EGNN_ERR_UNSUPPORTED, "attention=True is not built in this version");
   if (d->precision != EGNN_PREC_FP32 && d->precision != EGNN_PREC_BF16)
     return fail(EGNN_ERR_INVALID_ARG, "unknown precision %d", d->precision);
   return EGNN_OK;
@@ -211,6 +209,7 @@ struct BwdWs {
   float* S_dst; float* S_src; float* gxd; float* gstore; float4* gdstore; float* carry;
   int32_t* carry_row; float* part; float* wpart;
   float* wpart_aux;   // split-K scratch of the weight gradients run on the side stream
+  float* att_scr;     // attention only: per-CTA scratch of the SIMT edge backward
 };
 
 int64_t wpart_floats(int64_t N, int H) {
@@ -238,6 +237,7 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   w.part = c.take<float>((size_t)G * edge_part_floats(H, d->edge_attr_dim));
   w.wpart = c.take<float>((size_t)wpart_floats(N, H));
   w.wpart_aux = c.take<float>((size_t)wpart_floats(N, H));
+  w.att_scr = (d->flags & EGNN_FLAG_ATTENTION) ? c.take<float>((size_t)(G * edge_att_scratch_floats(H))) : nullptr;
   return w;
 }
 
@@ -284,9 +284,10 @@ struct SideJoin {
   }
 };
 
-bool missing_params(const egnn_layer_params* p) {
+bool missing_params(const egnn_layer_params* p, int flags) {
   return !p || !p->edge_w1 || !p->edge_b1 || !p->edge_w2 || !p->edge_b2 || !p->node_w1 ||
-         !p->node_b1 || !p->node_w2 || !p->node_b2 || !p->coord_w1 || !p->coord_b1 || !p->coord_w2;
+         !p->node_b1 || !p->node_w2 || !p->node_b2 || !p->coord_w1 || !p->coord_b1 || !p->coord_w2 ||
+         ((flags & EGNN_FLAG_ATTENTION) && (!p->att_w || !p->att_b));
 }
 
 bool missing_graph(const egnn_graph* g, bool bwd, bool attr, int64_t E) {
@@ -306,6 +307,7 @@ void fill_common(EdgeCommon& a, const egnn_layer_desc* d, const egnn_graph* g, c
   a.xp = pr.xp; a.PQ = PQ; a.wr = pr.wr; a.We = pr.We; a.attr = edge_attr; a.d = d->edge_attr_dim;
   a.W2T = pr.W2T; a.b2 = p->edge_b2; a.Wc1T = pr.Wc1T; a.bc1 = p->coord_b1; a.wc2 = p->coord_w2;
   a.W2_src = p->edge_w2; a.Wc1_src = p->coord_w1;
+  a.wa = p->att_w; a.ba = p->att_b;
   a.flags = d->flags; a.epc = eg.epc;
 }
 
@@ -338,7 +340,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   const int H = d->hidden, dd = d->edge_attr_dim;
   const bool bf = d->precision == EGNN_PREC_BF16;
   if (N == 0) return EGNN_OK;
-  if (missing_params(p) || missing_graph(g, false, dd > 0, E) || !h || !x || !h_out || !x_out ||
+  if (missing_params(p, d->flags) || missing_graph(g, false, dd > 0, E) || !h || !x || !h_out || !x_out ||
       (dd > 0 && E > 0 && !edge_attr))
     return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_fwd: null pointer argument");
   const int sms = num_sms_current();
@@ -397,11 +399,12 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   const int H = d->hidden, dd = d->edge_attr_dim;
   const bool bf = d->precision == EGNN_PREC_BF16;
   const bool residual = d->flags & EGNN_FLAG_RESIDUAL;
-  if (missing_params(p) || missing_graph(g, true, dd > 0, E) || !h || !x || !saved || !gh_out ||
+  if (missing_params(p, d->flags) || missing_graph(g, true, dd > 0, E) || !h || !x || !saved || !gh_out ||
       !gx_out || !grad_h || !grad_x || !gp || (dd > 0 && E > 0 && !edge_attr))
     return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_bwd: null pointer argument");
   if (!gp->edge_w1 || !gp->edge_b1 || !gp->edge_w2 || !gp->edge_b2 || !gp->node_w1 || !gp->node_b1 ||
-      !gp->node_w2 || !gp->node_b2 || !gp->coord_w1 || !gp->coord_b1 || !gp->coord_w2)
+      !gp->node_w2 || !gp->node_b2 || !gp->coord_w1 || !gp->coord_b1 || !gp->coord_w2 ||
+      ((d->flags & EGNN_FLAG_ATTENTION) && (!gp->att_w || !gp->att_b)))
     return fail(EGNN_ERR_INVALID_ARG, "egnn_layer_bwd: null gradient output");
   const int sms = num_sms_current();
   Carver probe(nullptr);
@@ -462,9 +465,10 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   a.Wc1 = bf ? w.prep.Wc1r : p->coord_w1;
   a.gx_out = gx_out; a.g_agg = w.ghg + H; a.ld_gagg = 2 * H;
   a.S_dst = w.S_dst; a.gxd = w.gxd; a.gstore = w.gstore; a.gdstore = w.gdstore; a.part = w.part;
+  a.att_scr = w.att_scr;
   if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
   else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
-  EGNN_TRY(edge_part_reduce(H, dd, eg.G, w.part, gp, ld1, s));
+  EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, s));
   EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, tc, w.gdstore, gx_out, w.gxd, w.S_src,
                          grad_x, s));
 

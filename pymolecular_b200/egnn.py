@@ -22,7 +22,7 @@ ways.  One extra keyword, ``precision='fp32' | 'bf16'``, selects fp32 GEMMs
 Differences that raise instead of silently diverging:
 ``act_fn`` other than SiLU, ``input_nf != output_nf != hidden_nf`` in
 ``E_GCL``, ``node_attr`` (the reference node_mlp width ignores it,
-egnn_clean.py:29 vs :63-64), ``attention=True`` (not built yet), CPU tensors.
+egnn_clean.py:29 vs :63-64), CPU tensors.
 """
 from __future__ import annotations
 
@@ -38,8 +38,7 @@ from .csr import CSR, as_csr
 _PARAM_ORDER = ["edge_mlp.0.weight", "edge_mlp.0.bias", "edge_mlp.2.weight", "edge_mlp.2.bias",
                 "node_mlp.0.weight", "node_mlp.0.bias", "node_mlp.2.weight", "node_mlp.2.bias",
                 "coord_mlp.0.weight", "coord_mlp.0.bias", "coord_mlp.2.weight"]
-_STRUCT_FIELDS = ["edge_w1", "edge_b1", "edge_w2", "edge_b2", "node_w1", "node_b1", "node_w2",
-                  "node_b2", "coord_w1", "coord_b1", "coord_w2"]
+_ATT_ORDER = ["att_mlp.0.weight", "att_mlp.0.bias"]   # appended when attention=True
 
 _PRECISIONS = {"fp32": nat.PREC_FP32, "bf16": nat.PREC_BF16}
 
@@ -50,6 +49,13 @@ def _check_tensor(t: torch.Tensor, name: str) -> torch.Tensor:
     if t.dtype != torch.float32:
         raise TypeError(f"{name} must be float32, got {t.dtype}")
     return t.contiguous()
+
+
+def _ptrs(tensors):
+    """Device pointers in egnn_layer_params field order; the att_* fields stay
+    NULL when the layer has no attention gate."""
+    ptrs = [nat.ptr(t) for t in tensors]
+    return ptrs + [None] * (len(_PARAM_ORDER) + len(_ATT_ORDER) - len(ptrs))
 
 
 class _LayerFn(torch.autograd.Function):
@@ -67,7 +73,7 @@ class _LayerFn(torch.autograd.Function):
                             device=h.device)
         ws_bytes = lib.egnn_workspace_size(C.byref(desc), nat.WS_FWD, 0)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=h.device)
-        p = nat.LayerParams(*[nat.ptr(t) for t in params], None, None)
+        p = nat.LayerParams(*_ptrs(params))
         nat.check(lib.egnn_layer_fwd(C.byref(desc), C.byref(csr.struct()), C.byref(p), nat.ptr(h),
                                      nat.ptr(x), nat.ptr(edge_attr), nat.ptr(h_out), nat.ptr(x_out),
                                      nat.ptr(saved), nat.ptr(ws), ws_bytes, nat.stream_ptr()),
@@ -96,8 +102,8 @@ class _LayerFn(torch.autograd.Function):
         grads = [torch.empty_like(t) for t in params]
         ws_bytes = lib.egnn_workspace_size(C.byref(desc), nat.WS_BWD, 0)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=h.device)
-        p = nat.LayerParams(*[nat.ptr(t) for t in params], None, None)
-        gp = nat.LayerGrads(*[nat.ptr(t) for t in grads], None, None)
+        p = nat.LayerParams(*_ptrs(params))
+        gp = nat.LayerGrads(*_ptrs(grads))
         nat.check(lib.egnn_layer_bwd(C.byref(desc), C.byref(csr.struct()), C.byref(p), nat.ptr(h),
                                      nat.ptr(x), nat.ptr(edge_attr), nat.ptr(saved), nat.ptr(gh),
                                      nat.ptr(gx), nat.ptr(grad_h), nat.ptr(grad_x), C.byref(gp),
@@ -202,14 +208,12 @@ class E_GCL(nn.Module):
 
     def _params(self):
         sd = dict(self.named_parameters())
-        return [sd[k] for k in _PARAM_ORDER]
+        return [sd[k] for k in _PARAM_ORDER + (_ATT_ORDER if self.attention else [])]
 
     def forward(self, h, edge_index, coord, edge_attr=None, node_attr=None):
         if node_attr is not None:
             raise NotImplementedError("node_attr is not supported (the reference node_mlp input "
                                       "width does not include it, egnn_clean.py:29, 63-64)")
-        if self.attention:
-            raise NotImplementedError("attention=True is not built in this version")
         h = _check_tensor(h, "h")
         coord = _check_tensor(coord, "coord")
         if coord.dim() != 2 or coord.shape[1] != 3:

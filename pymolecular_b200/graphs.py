@@ -20,7 +20,8 @@ import torch
 
 
 class GraphedStep:
-    """Capture `step` (a callable returning the loss tensor) as a CUDA graph.
+    """Capture `step` (a callable returning the loss tensor, detached so that
+    no autograd graph outlives the capture) as a CUDA graph.
 
     `warmup` eager calls run first on a side stream (they perform the
     library's one-time per-device set-up and let the allocator settle), then

@@ -1,6 +1,6 @@
 """Generates the golden fixtures in this directory from the REFERENCE itself.
 
-    python tests/golden/make_golden.py /path/to/PyMolecular
+    python tests/golden/make_golden.py /path/to/PyMolecular [case ...]
 
 Imports ``models/EGNN/egnn_clean.py`` from the reference checkout, runs its
 ``EGNN`` / ``E_GCL`` in float64 on seeded inputs, backpropagates a seeded
@@ -32,11 +32,11 @@ def _grads(module):
             for k, v in module.named_parameters()}
 
 
-def case_model(ref, name, seed, n_graphs, n_min, n_max, hidden, layers):
+def case_model(ref, name, seed, n_graphs, n_min, n_max, hidden, layers, **flags):
     """Whole EGNN: embedding_in, L x E_GCL, embedding_out; graph-sum MSE loss."""
     b = molecules(n_graphs, seed=seed, n_min=n_min, n_max=n_max)
     torch.manual_seed(seed)
-    model = ref.EGNN(in_node_nf=5, hidden_nf=hidden, out_node_nf=1, n_layers=layers).double()
+    model = ref.EGNN(in_node_nf=5, hidden_nf=hidden, out_node_nf=1, n_layers=layers, **flags).double()
     h0, x0 = b.h.double(), b.x.double().requires_grad_(True)
     h0.requires_grad_(True)
     ho, xo = model(h0, x0, [b.row, b.col], None)
@@ -44,7 +44,7 @@ def case_model(ref, name, seed, n_graphs, n_min, n_max, hidden, layers):
     pred = torch.zeros(b.n_graphs, dtype=torch.float64).index_add_(0, gi, ho[:, 0])
     loss = ((pred - b.target.double()) ** 2).mean()
     loss.backward()
-    return dict(kind="model", hidden=hidden, n_layers=layers, in_node_nf=5, out_node_nf=1,
+    return dict(kind="model", hidden=hidden, n_layers=layers, in_node_nf=5, out_node_nf=1, flags=flags,
                 h=b.h.double(), x=b.x.double(), row=b.row, col=b.col, graph_ptr=b.graph_ptr,
                 target=b.target.double(), state_dict={k: v.clone() for k, v in model.state_dict().items()},
                 h_out=ho.detach(), x_out=xo.detach(), loss=loss.detach(), grads=_grads(model),
@@ -116,6 +116,12 @@ CASES = {
     "layer_noresidual_h32": lambda r: case_layer(r, "layer_noresidual_h32", 4, 30, 90, 32,
                                                  residual=False),
     "reference_demo": case_reference_demo,
+    "layer_attention_h64": lambda r: case_layer(r, "layer_attention_h64", 5, 48, 200, 64, attention=True),
+    "layer_attention_flags_h32": lambda r: case_layer(r, "layer_attention_flags_h32", 6, 40, 150, 32,
+                                                      edges_in_d=3, attention=True, normalize=True,
+                                                      tanh=True, coords_agg="sum"),
+    "model_attention_molecules": lambda r: case_model(r, "model_attention_molecules", 7, 5, 3, 7, 32, 2,
+                                                      attention=True),
 }
 
 
@@ -124,7 +130,9 @@ def main():
     if root is None or not (root / "models" / "EGNN" / "egnn_clean.py").exists():
         raise SystemExit("usage: make_golden.py <reference checkout>")
     ref = load_reference(root)
-    for name, fn in CASES.items():
+    names = sys.argv[2:] or list(CASES)   # optionally only the named cases
+    for name in names:
+        fn = CASES[name]
         data = fn(ref)
         data["name"] = name
         torch.save(data, HERE / f"{name}.pt")

@@ -58,8 +58,32 @@ def test_workspace_size_rejects_unsupported_shapes():
     for d in [nat.LayerDesc(10, 10, 48, 0, 1, 0),          # hidden not built
               nat.LayerDesc(10, 10, 64, 17, 1, 0),         # too many edge features
               nat.LayerDesc(10, 10, 64, 0, 1, 7),          # unknown precision
-              nat.LayerDesc(10, 10, 64, 0, nat.FLAG_ATTENTION, 0)]:
+              nat.LayerDesc(10, 10, 64, 0, 64, 0)]:        # unknown flag bit
         assert lib.egnn_workspace_size(C.byref(d), nat.WS_FWD, 148) == 0
+
+
+def test_attention_workspace_holds_gate_scratch():
+    """attention=True is built: its backward workspace adds the per-CTA scratch
+    of the gate (ungated messages of a chunk and the gate-gradient sums)."""
+    lib = nat.lib()
+    plain = nat.LayerDesc(1000, 50000, 128, 0, 1, 0)
+    att = nat.LayerDesc(1000, 50000, 128, 0, 1 | nat.FLAG_ATTENTION, 0)
+    assert lib.egnn_workspace_size(C.byref(att), nat.WS_FWD, 148) == \
+        lib.egnn_workspace_size(C.byref(plain), nat.WS_FWD, 148)
+    extra = lib.egnn_workspace_size(C.byref(att), nat.WS_BWD, 148) - \
+        lib.egnn_workspace_size(C.byref(plain), nat.WS_BWD, 148)
+    # at most 148 x 8 CTAs, each with 64 x 128 + 16 x 129 floats
+    assert 0 < extra <= 148 * 8 * (64 * 128 + 16 * 129) * 4 + 256
+
+
+def test_attention_state_dict_matches_reference():
+    c = load_golden("model_attention_molecules")
+    torch.manual_seed(7)
+    m = EGNN(in_node_nf=5, hidden_nf=32, out_node_nf=1, n_layers=2, attention=True)
+    sd = m.state_dict()
+    assert list(sd) == list(c["state_dict"])
+    for k, v in sd.items():
+        assert torch.equal(v.double(), c["state_dict"][k]), k
 
 
 def test_state_dict_names_and_seeded_init_match_reference():

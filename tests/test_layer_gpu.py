@@ -72,8 +72,9 @@ def test_golden_fixture_fp32(name, cuda_device):
                         c["edge_attr"], ref, flags)
         check_tensors(as_dict(res), as_dict(ref), tol, name)
         return
+    flags = dict(c.get("flags", {}))
     model = EGNN(c["in_node_nf"], c["hidden"], c["out_node_nf"], in_edge_nf=c.get("in_edge_nf", 0),
-                 n_layers=c["n_layers"], device=dev)
+                 n_layers=c["n_layers"], device=dev, **flags)
     model.load_state_dict({k: v.float() for k, v in c["state_dict"].items()})
     h = c["h"].float().to(dev).requires_grad_(True)
     x = c["x"].float().to(dev).requires_grad_(True)
@@ -90,7 +91,7 @@ def test_golden_fixture_fp32(name, cuda_device):
     h32 = c["h"].float().clone().requires_grad_(True)
     x32 = c["x"].float().clone().requires_grad_(True)
     ho32, xo32 = O.egnn(p32, h32, x32, c["row"], c["col"],
-                        c["edge_attr"].float() if c.get("edge_attr") is not None else None)
+                        c["edge_attr"].float() if c.get("edge_attr") is not None else None, **flags)
     l32 = _golden_loss(c, ho32, xo32)
     l32.backward()
     r32 = {"loss": l32, "h": ho32, "x": xo32, "dh": h32.grad, "dx": x32.grad}
@@ -111,13 +112,13 @@ def _golden_loss(c, ho, xo):
 # seeded layer sweep against the fp64 oracle
 # ---------------------------------------------------------------------------
 
-def _seeded_layer_case(seed, N, E, H, edges_in_d=0, hub=True, **flags):
+def _seeded_layer_case(seed, N, E, H, edges_in_d=0, hub=True, attention=False):
     g = torch.Generator().manual_seed(seed)
     row = torch.randint(0, N, (E,), generator=g)
     col = torch.randint(0, N, (E,), generator=g)
     if hub:
         row[: E // 3] = 0           # one row much longer than an edge range
-    p = O.init_params(H, H, 1, 1, in_edge_nf=edges_in_d, seed=seed, dtype=torch.float64)
+    p = O.init_params(H, H, 1, 1, in_edge_nf=edges_in_d, attention=attention, seed=seed, dtype=torch.float64)
     p = {k[len("gcl_0."):]: v for k, v in p.items() if k.startswith("gcl_0.")}
     # larger coord weights than the 0.001 xavier gain so the x path is exercised
     p["coord_mlp.2.weight"] = p["coord_mlp.2.weight"] * 300.0
@@ -141,6 +142,13 @@ LAYER_CASES = [
     (128, "bf16", 700, 20000, 0, {}),
     (256, "bf16", 400, 9000, 0, {}),
     (128, "bf16", 300, 5000, 2, {"normalize": True}),
+    # attention gate (SIMT path for every H and precision)
+    (32, "fp32", 300, 4000, 2, {"attention": True, "tanh": True}),
+    (128, "fp32", 700, 20000, 0, {"attention": True}),
+    (256, "fp32", 400, 9000, 0, {"attention": True, "normalize": True}),
+    (64, "bf16", 500, 12000, 0, {"attention": True, "coords_agg": "sum"}),
+    (128, "bf16", 2000, 60000, 0, {"attention": True}),
+    (256, "bf16", 400, 9000, 0, {"attention": True}),
     # tensor-core path (bf16, H = 128, no edge attributes)
     (128, "bf16", 100, 90, 0, {}),
     (128, "bf16", 2000, 60000, 0, {"normalize": True, "tanh": True, "coords_agg": "sum"}),
@@ -151,7 +159,8 @@ LAYER_CASES = [
 @pytest.mark.parametrize("H,precision,N,E,d,flags", LAYER_CASES)
 def test_layer_matches_oracle(H, precision, N, E, d, flags, cuda_device):
     dev = cuda_device
-    row, col, p, h, x, ea, gh, gx = _seeded_layer_case(H * 7 + E, N, E, H, d, hub=True)
+    row, col, p, h, x, ea, gh, gx = _seeded_layer_case(H * 7 + E, N, E, H, d, hub=True,
+                                                       attention=flags.get("attention", False))
     ref = O.layer_grads(p, "", h, row, col, x, gh, gx, ea, **flags)
     layer = _layer_from_state(p, H, precision, dev, d, **flags)
     csr = CSR.from_edges(row, col, n_nodes=N, device=dev)

@@ -26,7 +26,7 @@ def test_oracle_matches_golden(name):
         h = c["h"].clone().requires_grad_(True)
         x = c["x"].clone().requires_grad_(True)
         leaf = {k: v.clone().requires_grad_(True) for k, v in p.items()}
-        ho, xo = O.egnn(leaf, h, x, c["row"], c["col"], c.get("edge_attr"))
+        ho, xo = O.egnn(leaf, h, x, c["row"], c["col"], c.get("edge_attr"), **_flags(c))
         if c["kind"] == "model":
             gi = torch.repeat_interleave(torch.arange(len(c["graph_ptr"]) - 1),
                                          c["graph_ptr"][1:] - c["graph_ptr"][:-1])
@@ -110,3 +110,21 @@ def test_fp32_oracle_within_layer_tolerance():
         assert rel_err(a, b) < 1e-5
     for k in r64[4]:
         assert rel_err(r32[4][k], r64[4][k]) < 1e-5, k
+
+
+@pytest.mark.parametrize("name", ["layer_default_h64", "layer_flags_h32", "layer_noresidual_h32",
+                                  "layer_attention_h64", "layer_attention_flags_h32"])
+def test_emulation_backward_matches_autograd(name):
+    """The rounding-exact model's hand-derived backward (the same algebra as the
+    kernels, attention gate included) equals the reference's autograd when
+    nothing is rounded."""
+    from oracle import egnn_emulation as EM
+    c = load_golden(name)
+    p = {k: v.double() for k, v in c["state_dict"].items()}
+    got = EM.layer_fwd_bwd(p, c["h"], c["row"], c["col"], c["x"], c["gh"], c["gx"], c.get("edge_attr"),
+                           precision="fp32", **_flags(c))
+    for a, b in zip(got[:4], (c["h_out"], c["x_out"], c["grad_h"], c["grad_x"])):
+        assert rel_err(a, b) < 1e-12
+    assert set(got[4]) == set(c["grads"])
+    for k, v in got[4].items():
+        assert rel_err(v, c["grads"][k]) < 1e-12, k

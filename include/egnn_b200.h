@@ -8,6 +8,9 @@
  *   unsorted_segment_sum/mean egnn_clean.py:149-164  -> fused into both
  *   edge list -> dst CSR      egnn_clean.py:167-191, forward_kernel.py:19-21
  *                                                    -> egnn_csr_build
+ *   get_edges_batch           egnn_clean.py:167-191  -> egnn_fc_graph
+ *   radius / kNN graphs and Morton order of the workloads
+ *                                                    -> egnn_spatial_*, egnn_morton_order
  * and the reference's fused-kernel entry points, which take the same CSR
  * triple (row_ptr, col_indices, edge_id):
  *   egnn_forward_kernel_node_parallel   forward_kernel.py:13-43
@@ -134,6 +137,73 @@ EGNN_API int egnn_csr_transpose(int64_t n_nodes, int64_t n_edges, const int32_t*
  * Synchronises `stream`.  EGNN_ERR_INDEX when it is malformed. */
 EGNN_API int egnn_graph_check(int64_t n_nodes, int64_t n_edges, const egnn_graph* g,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- graph builders (device) -------------------------------------------- */
+
+/* Scratch bytes of egnn_fc_graph for a batch of n_graphs graphs. */
+EGNN_API size_t egnn_fc_graph_workspace_size(int64_t n_graphs);
+
+/* Fully connected intra-graph edges of a batch, written directly as a dst CSR
+ * (get_edges / get_edges_batch, egnn_clean.py:167-191, generalised to graphs
+ * of different sizes): graph g owns nodes [graph_ptr[g], graph_ptr[g+1])
+ * (graph_ptr: device int64, n_graphs + 1 entries, from 0 to n_nodes); row i
+ * holds every other node j of its graph in increasing order.  n_edges must
+ * be sum n_g (n_g - 1).  Writes row_ptr (N+1), col_idx and row_idx (E); the
+ * edge ids are the CSR positions.  Synchronises `stream` (validation). */
+EGNN_API int egnn_fc_graph(int64_t n_nodes, int64_t n_graphs, const int64_t* graph_ptr, int64_t n_edges,
+                           int32_t* row_ptr, int32_t* col_idx, int32_t* row_idx, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+enum { EGNN_GRAPH_RADIUS = 0, EGNN_GRAPH_KNN = 1 };
+
+/* Spatial graph request.  Points x (N,3) float32 (device), optionally split
+ * into graphs by graph_ptr (device int64, n_graphs + 1 entries, nodes of a
+ * graph contiguous; NULL = one graph); edges never cross graphs.  Distances
+ * are d2 = (dx*dx + dy*dy) + dz*dz in float32 with every operation rounded,
+ * dx = x_i - x_j; ties in d2 go to the smaller j.
+ *   EGNN_GRAPH_RADIUS: row i holds every j != i of its graph with
+ *     d2 < cutoff*cutoff (float32), in increasing j; with max_nbrs > 0 only
+ *     the max_nbrs nearest, nearest first (the survey's radius graphs of
+ *     configs 3 and 4).
+ *   EGNN_GRAPH_KNN: row i holds the k = max_nbrs (<= 256) nearest j != i of
+ *     its graph (all of them in smaller graphs), nearest first (config 5);
+ *     `cutoff` > 0 is a cell-size hint, 0 = chosen from the point density. */
+typedef struct {
+  int64_t n_nodes;
+  int64_t n_graphs;
+  const float* x;
+  const int64_t* graph_ptr;
+  int32_t mode;
+  int32_t max_nbrs;
+  float cutoff;
+} egnn_spatial_desc;
+
+/* Scratch bytes of egnn_spatial_count / egnn_spatial_fill for n_nodes points. */
+EGNN_API size_t egnn_spatial_workspace_size(int64_t n_nodes);
+
+/* Phase 1: builds the cell grid in `workspace` and writes row_ptr (N+1), the
+ * exclusive scan of the row lengths (row_ptr[N] = E < 2^31).  The caller reads
+ * row_ptr[N] to size col_idx.  Synchronises `stream` when graph_ptr is given
+ * (validation) and to check that E fits int32. */
+EGNN_API int egnn_spatial_count(const egnn_spatial_desc* d, int32_t* row_ptr, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/* Phase 2: writes col_idx and row_idx (E) for the same request, row_ptr and
+ * workspace as phase 1 (unchanged in between).  Synchronises `stream`. */
+EGNN_API int egnn_spatial_fill(const egnn_spatial_desc* d, const int32_t* row_ptr, int32_t* col_idx,
+                               int32_t* row_idx, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes of egnn_morton_order. */
+EGNN_API size_t egnn_morton_workspace_size(int64_t n_nodes);
+
+/* Morton order of points x (N,3) float32 (the survey's config-5 node order):
+ * per axis q = floor((double(x) - lo) / (hi - lo) * 2^bits) clipped to
+ * [0, 2^bits), code = bits interleaved with bit b of axis a at 3b + a
+ * (bits <= 21; lo, hi: HOST arrays of 3 doubles).  Writes codes (N, uint64,
+ * node order) and perm (N): the nodes sorted stably by code. */
+EGNN_API int egnn_morton_order(int64_t n_nodes, const float* x, const double* lo, const double* hi, int bits,
+                               uint64_t* codes, int32_t* perm, void* workspace, size_t workspace_bytes,
+                               void* stream);
 
 /* ---- layer ------------------------------------------------------------- */
 

@@ -65,6 +65,15 @@ _PARAM_FIELDS = ["edge_w1", "edge_b1", "edge_w2", "edge_b2", "node_w1", "node_b1
                  "node_b2", "coord_w1", "coord_b1", "coord_w2", "att_w", "att_b"]
 
 
+GRAPH_RADIUS = 0
+GRAPH_KNN = 1
+
+
+class SpatialDesc(C.Structure):
+    _fields_ = [("n_nodes", C.c_int64), ("n_graphs", C.c_int64), ("x", VP), ("graph_ptr", VP),
+                ("mode", C.c_int32), ("max_nbrs", C.c_int32), ("cutoff", C.c_float)]
+
+
 class LayerParams(C.Structure):
     _fields_ = [(f, VP) for f in _PARAM_FIELDS]
 
@@ -79,6 +88,14 @@ _SIGNATURES = {
     "egnn_csr_build": (C.c_int, [C.c_int64, C.c_int64, VP, VP, VP, VP, VP, VP, VP, C.c_size_t, VP]),
     "egnn_csr_transpose": (C.c_int, [C.c_int64, C.c_int64, VP, VP, VP, VP, VP, C.c_size_t, VP]),
     "egnn_graph_check": (C.c_int, [C.c_int64, C.c_int64, C.POINTER(Graph), VP, C.c_size_t, VP]),
+    "egnn_fc_graph_workspace_size": (C.c_size_t, [C.c_int64]),
+    "egnn_fc_graph": (C.c_int, [C.c_int64, C.c_int64, VP, C.c_int64, VP, VP, VP, VP, C.c_size_t, VP]),
+    "egnn_spatial_workspace_size": (C.c_size_t, [C.c_int64]),
+    "egnn_spatial_count": (C.c_int, [C.POINTER(SpatialDesc), VP, VP, C.c_size_t, VP]),
+    "egnn_spatial_fill": (C.c_int, [C.POINTER(SpatialDesc), VP, VP, VP, VP, C.c_size_t, VP]),
+    "egnn_morton_workspace_size": (C.c_size_t, [C.c_int64]),
+    "egnn_morton_order": (C.c_int, [C.c_int64, VP, C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_int,
+                                    VP, VP, VP, C.c_size_t, VP]),
     "egnn_saved_size": (C.c_size_t, [C.POINTER(LayerDesc)]),
     "egnn_workspace_size": (C.c_size_t, [C.POINTER(LayerDesc), C.c_int, C.c_int]),
     "egnn_layer_fwd": (C.c_int, [C.POINTER(LayerDesc), C.POINTER(Graph), C.POINTER(LayerParams),

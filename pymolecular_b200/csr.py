@@ -115,6 +115,25 @@ class CSR:
                                              ws_bytes, s), "egnn_csr_transpose")
         return cls(N, row_ptr, col_idx, row_idx, edge_id.contiguous(), src_ptr, src_edge)
 
+    @classmethod
+    def from_sorted(cls, n_nodes: int, row_ptr, col_idx, row_idx) -> "CSR":
+        """Wrap a CSR the device builders produced (rows already in order, edge
+        ids = CSR positions) and build its transpose."""
+        device = row_ptr.device
+        N, E = int(n_nodes), int(col_idx.numel())
+        i32 = dict(dtype=torch.int32, device=device)
+        edge_id = torch.arange(E, **i32)
+        src_ptr = torch.empty(N + 1, **i32)
+        src_edge = torch.empty(E, **i32)
+        lib = nat.lib()
+        ws_bytes = max(lib.egnn_csr_workspace_size(N, E), 256)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        with torch.cuda.device(device):
+            nat.check(lib.egnn_csr_transpose(N, E, nat.ptr(row_ptr), nat.ptr(col_idx), nat.ptr(src_ptr),
+                                             nat.ptr(src_edge), nat.ptr(ws), ws_bytes, nat.stream_ptr()),
+                      "egnn_csr_transpose")
+        return cls(N, row_ptr, col_idx, row_idx, edge_id, src_ptr, src_edge)
+
     # ---- views -----------------------------------------------------------------
     def struct(self) -> nat.Graph:
         if self._struct is None:

@@ -125,13 +125,31 @@ CASES = {
 }
 
 
+def case_get_edges_batch(ref):
+    """The reference's fully connected batch edges (egnn_clean.py:167-191)."""
+    out = {}
+    for n, b in [(4, 8), (5, 3), (9, 1), (1, 3), (2, 5), (29, 4)]:
+        edges, attr = ref.get_edges_batch(n, b)
+        out[(n, b)] = (edges[0].clone(), edges[1].clone(), attr.clone())
+    return dict(kind="graphs", cases=out)
+
+
+# graph-construction fixtures live in golden/graphs/ (not layer or model cases)
+GRAPH_CASES = {"get_edges_batch": case_get_edges_batch}
+
+
 def main():
     root = Path(sys.argv[1]) if len(sys.argv) > 1 else None
     if root is None or not (root / "models" / "EGNN" / "egnn_clean.py").exists():
         raise SystemExit("usage: make_golden.py <reference checkout>")
     ref = load_reference(root)
-    names = sys.argv[2:] or list(CASES)   # optionally only the named cases
+    names = sys.argv[2:] or list(CASES) + list(GRAPH_CASES)   # optionally only the named cases
     for name in names:
+        if name in GRAPH_CASES:
+            (HERE / "graphs").mkdir(exist_ok=True)
+            torch.save(GRAPH_CASES[name](ref), HERE / "graphs" / f"{name}.pt")
+            print(name)
+            continue
         fn = CASES[name]
         data = fn(ref)
         data["name"] = name

@@ -308,11 +308,14 @@ class Problem:
             bufs["gp"] = self.graph_ptr.pin_memory()
         return bufs
 
-    def e2e_step(self, host, loss_host):
+    def e2e_step(self, host, loss_host, check=True):
         """Public-API step from pinned host tensors: H2D copies, CSR built on the
-        device from the edge list, forward, loss, backward, update, loss D2H."""
+        device from the edge list, forward, loss, backward, update, loss D2H.
+        check=False defers the edge-index validation to the device (the step
+        can then be captured as a CUDA graph); the CSR is returned so that the
+        caller can read its flag."""
         d = {k: v.to(self.dev, non_blocking=True) for k, v in host.items()}
-        csr = self.CSR.from_edges(d["row"], d["col"], n_nodes=self.n_nodes_csr, device=self.dev)
+        csr = self.CSR.from_edges(d["row"], d["col"], n_nodes=self.n_nodes_csr, device=self.dev, check=check)
         self.zero_grad()
         ho, _ = self.forward(d["h"], d["x"], csr)
         loss = self.loss(ho, d.get("gp"), d["tgt"])
@@ -320,6 +323,7 @@ class Problem:
         self.sync_grads()
         self.opt.step()
         loss_host.copy_(loss.detach().reshape(1), non_blocking=True)
+        return csr
 
 
 def run_b200(args):
@@ -412,27 +416,56 @@ def run_b200(args):
         host = prob.host_buffers()
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+
+        def time_e2e(run):
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                run()
+            e1.record()
+            torch.cuda.synchronize()
+            te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            return float(te.item()) / args.steps
+
+        def e2e_line(ms, path):
+            return {"value": mc.n_layers * prob.edges_job / (ms * 1e-3), "unit": "layer-edges/s",
+                    "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                    "molecules_per_s": prob.graphs_job / (ms * 1e-3), "path": path}
+
+        # eager: every call from Python, edge indices validated with a host read-back
         for _ in range(2):
             prob.e2e_step(host, loss_host)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            prob.e2e_step(host, loss_host)
-        e1.record()
-        torch.cuda.synchronize()
-        te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e_ms = float(te.item()) / args.steps
-        e2e = {"value": mc.n_layers * prob.edges_job / (e2e_ms * 1e-3), "unit": "layer-edges/s",
-               "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-               "molecules_per_s": prob.graphs_job / (e2e_ms * 1e-3),
-               "path": "EGNN.forward(h, x, [row, col]) from pinned host tensors, CSR built on the device "
-                       "each step, loss copied back"}
+        eager_ms = time_e2e(lambda: prob.e2e_step(host, loss_host))
+        eager = e2e_line(eager_ms, "eager EGNN.forward(h, x, csr) per step: pinned H2D of h, x, edge list, "
+                                   "targets; CSR.from_edges on the device; backward; SGD; loss D2H")
+        e2e = eager
+        if graphed is not None:
+            # the same public-API step captured once with GraphedStep: each replay
+            # copies the pinned host buffers in, builds the CSR (validation flag
+            # kept on the device, read after the timed steps), runs the step and
+            # copies the loss out
+            holder = {}
+
+            def captured():
+                holder["csr"] = prob.e2e_step(host, loss_host, check=False)
+                return None
+
+            g_e2e = GraphedStep(captured, warmup=1)
+            g_e2e.replay()
+            torch.cuda.synchronize()
+            graph_ms = time_e2e(g_e2e.replay)
+            holder["csr"].raise_if_invalid()
+            e2e = e2e_line(graph_ms, "GraphedStep over the same public-API step (pinned H2D of h, x, edge list, "
+                                     "targets; CSR.from_edges(check=False) on the device; forward; backward; "
+                                     "SGD; loss D2H), replayed once per step")
+            e2e["eager"] = {k: eager[k] for k in ("value", "ms_per_step", "path")}
+            g_e2e.release()
 
     peak_vram = torch.cuda.max_memory_allocated(dev) / 2**30
 

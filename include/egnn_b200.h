@@ -126,6 +126,15 @@ EGNN_API int egnn_csr_build(int64_t n_nodes, int64_t n_edges, const int64_t* row
                    int32_t* row_ptr, int32_t* col_idx, int32_t* row_idx, int32_t* edge_id,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* egnn_csr_build without the host read-back: the validation result goes to
+ * `status` (device int32; 0 = every index in range, nonzero = an edge index
+ * outside [0,N), in which case the CSR content is unspecified) and the call
+ * stays asynchronous, so it can be captured in a CUDA graph.  The caller
+ * reads `status` before trusting the CSR. */
+EGNN_API int egnn_csr_build_async(int64_t n_nodes, int64_t n_edges, const int64_t* row, const int64_t* col,
+                                  int32_t* row_ptr, int32_t* col_idx, int32_t* row_idx, int32_t* edge_id,
+                                  int32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Transpose of a dst CSR: for each source node, the CSR positions of its
  * out-edges in increasing position order.  Asynchronous. */
 EGNN_API int egnn_csr_transpose(int64_t n_nodes, int64_t n_edges, const int32_t* row_ptr,

@@ -86,6 +86,7 @@ class LayerGrads(C.Structure):
 _SIGNATURES = {
     "egnn_csr_workspace_size": (C.c_size_t, [C.c_int64, C.c_int64]),
     "egnn_csr_build": (C.c_int, [C.c_int64, C.c_int64, VP, VP, VP, VP, VP, VP, VP, C.c_size_t, VP]),
+    "egnn_csr_build_async": (C.c_int, [C.c_int64, C.c_int64, VP, VP, VP, VP, VP, VP, VP, VP, C.c_size_t, VP]),
     "egnn_csr_transpose": (C.c_int, [C.c_int64, C.c_int64, VP, VP, VP, VP, VP, C.c_size_t, VP]),
     "egnn_graph_check": (C.c_int, [C.c_int64, C.c_int64, C.POINTER(Graph), VP, C.c_size_t, VP]),
     "egnn_fc_graph_workspace_size": (C.c_size_t, [C.c_int64]),

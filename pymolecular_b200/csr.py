@@ -40,12 +40,20 @@ class CSR:
         self.row_ptr, self.col_idx, self.row_idx = row_ptr, col_idx, row_idx
         self.edge_id, self.src_ptr, self.src_edge = edge_id, src_ptr, src_edge
         self.device = row_ptr.device
+        self.status = None   # deferred validation flag (from_edges(check=False))
         self._struct = None
 
     # ---- construction --------------------------------------------------------
     @classmethod
-    def from_edges(cls, row, col, n_nodes: Optional[int] = None, device=None) -> "CSR":
-        """Build from an edge list (row = destination, col = source)."""
+    def from_edges(cls, row, col, n_nodes: Optional[int] = None, device=None, check: bool = True) -> "CSR":
+        """Build from an edge list (row = destination, col = source).
+
+        ``check=True`` validates the indices and raises on one outside
+        [0, n_nodes) (a host synchronisation).  ``check=False`` keeps the call
+        asynchronous (capturable in a CUDA graph): the result of the same
+        validation stays on the device in ``csr.status`` and
+        :meth:`raise_if_invalid` reads it; until then out-of-range sources are
+        mapped to node 0, so the layer never indexes out of bounds."""
         if device is None:
             device = row.device if row.is_cuda else torch.device("cuda", torch.cuda.current_device())
         device = _require_cuda(device)
@@ -66,15 +74,32 @@ class CSR:
         lib = nat.lib()
         ws_bytes = lib.egnn_csr_workspace_size(N, E)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
+        status = None if check else torch.zeros(1, **i32)
         with torch.cuda.device(device):
             s = nat.stream_ptr()
-            nat.check(lib.egnn_csr_build(N, E, nat.ptr(row), nat.ptr(col), nat.ptr(row_ptr),
-                                         nat.ptr(col_idx), nat.ptr(row_idx), nat.ptr(edge_id),
-                                         nat.ptr(ws), ws_bytes, s), "egnn_csr_build")
+            if check:
+                nat.check(lib.egnn_csr_build(N, E, nat.ptr(row), nat.ptr(col), nat.ptr(row_ptr),
+                                             nat.ptr(col_idx), nat.ptr(row_idx), nat.ptr(edge_id),
+                                             nat.ptr(ws), ws_bytes, s), "egnn_csr_build")
+            else:
+                nat.check(lib.egnn_csr_build_async(N, E, nat.ptr(row), nat.ptr(col), nat.ptr(row_ptr),
+                                                   nat.ptr(col_idx), nat.ptr(row_idx), nat.ptr(edge_id),
+                                                   nat.ptr(status), nat.ptr(ws), ws_bytes, s),
+                          "egnn_csr_build_async")
             nat.check(lib.egnn_csr_transpose(N, E, nat.ptr(row_ptr), nat.ptr(col_idx),
                                              nat.ptr(src_ptr), nat.ptr(src_edge), nat.ptr(ws),
                                              ws_bytes, s), "egnn_csr_transpose")
-        return cls(N, row_ptr, col_idx, row_idx, edge_id, src_ptr, src_edge)
+        out = cls(N, row_ptr, col_idx, row_idx, edge_id, src_ptr, src_edge)
+        out.status = status
+        return out
+
+    def raise_if_invalid(self) -> None:
+        """Reads the deferred validation of ``from_edges(check=False)`` (a host
+        synchronisation) and raises EgnnError(EGNN_ERR_INDEX) if an edge index
+        was outside [0, n_nodes)."""
+        if self.status is not None and int(self.status.item()) != 0:
+            raise nat.EgnnError(nat.EGNN_ERR_INDEX,
+                                f"edge index outside [0, {self.n_nodes}) in the edge list of this CSR")
 
     @classmethod
     def from_csr(cls, row_ptr, col_idx, edge_id=None, n_nodes: Optional[int] = None,

@@ -39,11 +39,15 @@ __global__ void segment_ptr_kernel(int64_t N, int64_t E, const int32_t* sorted_k
   }
 }
 
-__global__ void gather_cols_kernel(int64_t E, const int64_t* col, const int32_t* perm,
+// Out-of-range sources (already flagged) become node 0, so that a CSR whose
+// flag has not been read yet never sends a later kernel out of bounds.
+__global__ void gather_cols_kernel(int64_t E, int64_t N, const int64_t* col, const int32_t* perm,
                                    int32_t* col_idx) {
   for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < E;
-       k += (int64_t)gridDim.x * blockDim.x)
-    col_idx[k] = (int32_t)col[perm[k]];
+       k += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = col[perm[k]];
+    col_idx[k] = (c >= 0 && c < N) ? (int32_t)c : 0;
+  }
 }
 
 __global__ void iota_kernel(int64_t E, int32_t* v) {
@@ -116,10 +120,14 @@ extern "C" size_t egnn_csr_workspace_size(int64_t n_nodes, int64_t n_edges) {
   return c.size();
 }
 
-extern "C" int egnn_csr_build(int64_t N, int64_t E, const int64_t* row, const int64_t* col,
-                              int32_t* row_ptr, int32_t* col_idx, int32_t* row_idx,
-                              int32_t* edge_id, void* ws, size_t ws_bytes, void* stream) {
-  cudaStream_t s = (cudaStream_t)stream;
+namespace egnn {
+namespace {
+
+// Shared body of egnn_csr_build (flag in the workspace, read back) and
+// egnn_csr_build_async (flag in caller memory, left on the device).
+int csr_build(int64_t N, int64_t E, const int64_t* row, const int64_t* col, int32_t* row_ptr,
+              int32_t* col_idx, int32_t* row_idx, int32_t* edge_id, void* ws, size_t ws_bytes,
+              int32_t* status, cudaStream_t s) {
   if (N < 0 || E < 0 || N >= INT32_MAX || E >= INT32_MAX)
     return fail(EGNN_ERR_INVALID_ARG, "egnn_csr_build: sizes out of range (N=%lld, E=%lld)",
                 (long long)N, (long long)E);
@@ -128,7 +136,8 @@ extern "C" int egnn_csr_build(int64_t N, int64_t E, const int64_t* row, const in
   if (ws_bytes < egnn_csr_workspace_size(N, E) || !ws)
     return fail(EGNN_ERR_WORKSPACE, "egnn_csr_build: workspace too small");
   Carver c(ws);
-  int* err = c.take<int>(4);
+  int* ws_err = c.take<int>(4);
+  int* err = status ? reinterpret_cast<int*>(status) : ws_err;
   int32_t* kin = c.take<int32_t>(E);
   int32_t* vin = c.take<int32_t>(E);
   int32_t* kout = c.take<int32_t>(E);
@@ -142,18 +151,38 @@ extern "C" int egnn_csr_build(int64_t N, int64_t E, const int64_t* row, const in
     EGNN_CHECK_CUDA(cub::DeviceRadixSort::SortPairs(ctmp, cb, kin, kout, vin, vout, (int)E, 0,
                                                     end_bit_for(N), s));
     count_launch();
-    gather_cols_kernel<<<grid_for(E), 256, 0, s>>>(E, col, vout, col_idx);
+    gather_cols_kernel<<<grid_for(E), 256, 0, s>>>(E, N, col, vout, col_idx);
     EGNN_CHECK_LAUNCH();
     EGNN_CHECK_CUDA(cudaMemcpyAsync(row_idx, kout, E * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     EGNN_CHECK_CUDA(cudaMemcpyAsync(edge_id, vout, E * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
   }
   segment_ptr_kernel<<<grid_for(N + 1), 256, 0, s>>>(N, E, kout, row_ptr);
   EGNN_CHECK_LAUNCH();
+  if (status) return EGNN_OK;
   int herr = 0;
   EGNN_CHECK_CUDA(cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s));
   EGNN_CHECK_CUDA(cudaStreamSynchronize(s));
   if (herr) return fail(EGNN_ERR_INDEX, "egnn_csr_build: edge index outside [0, %lld)", (long long)N);
   return EGNN_OK;
+}
+
+}  // namespace
+}  // namespace egnn
+
+extern "C" int egnn_csr_build(int64_t N, int64_t E, const int64_t* row, const int64_t* col,
+                              int32_t* row_ptr, int32_t* col_idx, int32_t* row_idx,
+                              int32_t* edge_id, void* ws, size_t ws_bytes, void* stream) {
+  return csr_build(N, E, row, col, row_ptr, col_idx, row_idx, edge_id, ws, ws_bytes, nullptr,
+                   (cudaStream_t)stream);
+}
+
+extern "C" int egnn_csr_build_async(int64_t N, int64_t E, const int64_t* row, const int64_t* col,
+                                    int32_t* row_ptr, int32_t* col_idx, int32_t* row_idx,
+                                    int32_t* edge_id, int32_t* status, void* ws, size_t ws_bytes,
+                                    void* stream) {
+  if (!status) return fail(EGNN_ERR_INVALID_ARG, "egnn_csr_build_async: null status");
+  return csr_build(N, E, row, col, row_ptr, col_idx, row_idx, edge_id, ws, ws_bytes, status,
+                   (cudaStream_t)stream);
 }
 
 extern "C" int egnn_csr_transpose(int64_t N, int64_t E, const int32_t* row_ptr, const int32_t* col_idx,

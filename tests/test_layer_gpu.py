@@ -244,6 +244,28 @@ def test_csr_build_bit_exact(N, E, cuda_device):
     assert torch.equal(csr.edge_id.cpu().long(), perm)
 
 
+def test_csr_deferred_validation(cuda_device):
+    """from_edges(check=False) builds the same CSR without a host read-back and
+    leaves the validation result on the device; a bad index is flagged (and the
+    CSR stays in range) instead of raising at build time."""
+    g = torch.Generator().manual_seed(4)
+    N, E = 300, 5000
+    row = torch.randint(0, N, (E,), generator=g)
+    col = torch.randint(0, N, (E,), generator=g)
+    a = CSR.from_edges(row, col, n_nodes=N, device=cuda_device)
+    b = CSR.from_edges(row, col, n_nodes=N, device=cuda_device, check=False)
+    for f in ("row_ptr", "col_idx", "row_idx", "edge_id", "src_ptr", "src_edge"):
+        assert torch.equal(getattr(a, f), getattr(b, f)), f
+    b.raise_if_invalid()
+    bad_col = col.clone()
+    bad_col[17] = N + 4
+    c = CSR.from_edges(row, bad_col, n_nodes=N, device=cuda_device, check=False)
+    assert int(c.col_idx.min()) >= 0 and int(c.col_idx.max()) < N
+    with pytest.raises(nat.EgnnError) as ei:
+        c.raise_if_invalid()
+    assert ei.value.status == nat.EGNN_ERR_INDEX
+
+
 def test_csr_from_reference_triple(cuda_device):
     g = torch.Generator().manual_seed(3)
     N, E = 200, 3000

@@ -241,15 +241,17 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   return w;
 }
 
-// ---- side stream ------------------------------------------------------------------
-// The backward forks work that no later kernel of the layer needs (the node-MLP
-// and W1 weight gradients) onto a per-device side stream, so that it fills SMs
-// the edge kernels leave free and overlaps the main chain's latency.  Fork and
-// join are event waits, which stream capture records as graph edges; the
-// stream and events are created on the first call, outside any capture.
+// ---- side streams -----------------------------------------------------------------
+// The backward forks work that no later kernel of the layer needs (the
+// parameter gradients: node MLP, edge partial reduction, W1) onto two
+// per-device side streams, so that it fills SMs the edge kernels leave free
+// and stays off the main chain.  Fork and join are event waits, which stream
+// capture records as graph edges; streams and events are created on the
+// first call, outside any capture.
 struct SideStream {
-  cudaStream_t stream = nullptr;
-  cudaEvent_t ev[4] = {};
+  cudaStream_t stream = nullptr;    // node-MLP weight gradients, edge partials, dW_a
+  cudaStream_t stream2 = nullptr;   // dW_b
+  cudaEvent_t ev[8] = {};
 };
 
 int side_stream(SideStream** out) {
@@ -260,6 +262,7 @@ int side_stream(SideStream** out) {
   std::lock_guard<std::mutex> lk(mu);
   SideStream& ss = per_dev[dev & 63];
   if (!ss.stream) {
+    EGNN_CHECK_CUDA(cudaStreamCreateWithFlags(&ss.stream2, cudaStreamNonBlocking));
     EGNN_CHECK_CUDA(cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking));
     for (auto& e : ss.ev) EGNN_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
@@ -274,13 +277,14 @@ int stream_fork(cudaStream_t from, cudaStream_t to, cudaEvent_t ev) {
   return EGNN_OK;
 }
 
-// Joins the side stream back into the main one when it goes out of scope
+// Joins the side streams back into the main one when it goes out of scope
 // (also on an early error return, so no capture is left forked).
 struct SideJoin {
   cudaStream_t main_s;
   SideStream* side;
   ~SideJoin() {
-    if (cudaEventRecord(side->ev[3], side->stream) == cudaSuccess) cudaStreamWaitEvent(main_s, side->ev[3], 0);
+    if (cudaEventRecord(side->ev[6], side->stream) == cudaSuccess) cudaStreamWaitEvent(main_s, side->ev[6], 0);
+    if (cudaEventRecord(side->ev[7], side->stream2) == cudaSuccess) cudaStreamWaitEvent(main_s, side->ev[7], 0);
   }
 };
 
@@ -468,12 +472,17 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   a.att_scr = w.att_scr;
   if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
   else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
-  EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, s));
+  // per-CTA weight-gradient partials -> parameter gradients, on the side stream
+  EGNN_TRY(stream_fork(s, s2, side->ev[2]));
+  EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, s2));
   EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, tc, w.gdstore, gx_out, w.gxd, w.S_src,
                          grad_x, s));
 
-  // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb ;  dWa, db1 on the side stream, dWb here
-  EGNN_TRY(stream_fork(s, s2, side->ev[2]));
+  // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb here; dWa, db1 and dWb on the two side streams
+  EGNN_TRY(stream_fork(s, s2, side->ev[3]));
+  EGNN_TRY(stream_fork(s, side->stream2, side->ev[4]));
+  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, bf, w.wpart,
+                      side->stream2));
   EGNN_TRY(node_wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart_aux, s2));
   {
     GemmArgs gh;
@@ -484,7 +493,6 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.C = grad_h; gh.ldc = H;
     EGNN_TRY(node_gemm(gh, bf, s));
   }
-  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, bf, w.wpart, s));
   return EGNN_OK;
 }
 

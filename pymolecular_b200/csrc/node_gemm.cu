@@ -238,15 +238,16 @@ struct Slice {
     }
   }
   __device__ __forceinline__ void store(float* s) const {
-    if (KMAJ) return;
+    if constexpr (!KMAJ) {   // k-major slices went to shared memory by cp.async
 #pragma unroll
-    for (int q = 0; q < Q; ++q) {
-      const int c = threadIdx.x + 256 * q;
-      const int rl = c % ROWS, kl = (c / ROWS) * 4;
-      s[(kl + 0) * LD + rl] = r[q].x;
-      s[(kl + 1) * LD + rl] = r[q].y;
-      s[(kl + 2) * LD + rl] = r[q].z;
-      s[(kl + 3) * LD + rl] = r[q].w;
+      for (int q = 0; q < Q; ++q) {
+        const int c = threadIdx.x + 256 * q;
+        const int rl = c % ROWS, kl = (c / ROWS) * 4;
+        s[(kl + 0) * LD + rl] = r[q].x;
+        s[(kl + 1) * LD + rl] = r[q].y;
+        s[(kl + 2) * LD + rl] = r[q].z;
+        s[(kl + 3) * LD + rl] = r[q].w;
+      }
     }
   }
 };

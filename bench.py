@@ -404,7 +404,7 @@ def run_b200(args):
         flush.fill_(float(k))
         prob.step()
     torch.cuda.synchronize()
-    ktimes = {n: _native.kernel_time(n) for n in ("edge_bwd", "edge_fwd", "src_pass", "row_pass", "edge_fixup",
+    ktimes = {n: _native.kernel_time(n) for n in ("edge_bwd", "edge_fwd", "node_pass", "src_pass", "edge_fixup",
                                                   "part_reduce", "node_gemm", "gemm_reduce", "prep")}
     breakdown = {n: round(v[0] / kt_steps, 4) for n, v in ktimes.items() if v[1]}
     _native.lib().egnn_kernel_timing(0)
@@ -514,8 +514,8 @@ def run_b200(args):
                          "per_launch_ms": per_launch_ms, "launches": bwd_n,
                          "flops_per_launch": flops_launch,
                          "edge_fwd_per_launch_ms": fwd_ms / max(fwd_n, 1),
-                         "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1),
-                         "row_pass_per_launch_ms": ktimes["row_pass"][0] / max(ktimes["row_pass"][1], 1)},
+                         "node_pass_per_launch_ms": ktimes["node_pass"][0] / max(ktimes["node_pass"][1], 1),
+                         "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1)},
             "kernel_ms_per_step": breakdown,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -21,8 +21,8 @@
 //            g_a1 = (G W2) silu'(a1)              -> global, one bf16 H-vector per edge
 // The weight tiles live in shared memory for the whole kernel; one copy of
 // each serves the forward product (K-major B) and the data-gradient product
-// (MN-major B).  The row sums of g_a1 and of the coordinate gradients are
-// taken by row_pass_kernel (dst side) and the source pass (src side).
+// (MN-major B).  The row sums of g_a1 and of the coordinate gradients, over
+// each node's in-edges and out-edges, are taken by node_pass_kernel.
 #include <algorithm>
 #include <climits>
 
@@ -953,52 +953,92 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   if (g.warp == 0) tmem_dealloc(tmem, NCOL);
 }
 
-// ---- dst row pass: S_dst[i] = sum of g_a1 over row i, gxd[i] = sum of d-gradients ----
+// ---- node pass: the row sums of g_a1 and of the coordinate gradients -------------
+// For node v, over its in-edges (its CSR row: S_dst, gd_dst) and over its
+// out-edges (transpose CSR: S_src, gd_src), then
+// dL/dx_v = dL/dx'_v + gd_dst - gd_src.  One warp per node, lane owning H / 32
+// consecutive features; four rows of each list in flight, each list added in
+// CSR-position order.
 template <int H>
-__global__ void row_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
-                                const __nv_bfloat16* __restrict__ gstore,
-                                const float4* __restrict__ gdstore, float* __restrict__ S_dst,
-                                float* __restrict__ gxd) {
-  // One warp per destination row, lane owning H / 32 consecutive features;
-  // four edge rows in flight, added in CSR order.
+__global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
+                                 const int32_t* __restrict__ src_ptr, const int32_t* __restrict__ src_edge,
+                                 const __nv_bfloat16* __restrict__ gstore, const float4* __restrict__ gdstore,
+                                 const float* __restrict__ gx_out, float* __restrict__ S_dst,
+                                 float* __restrict__ S_src, float* __restrict__ gx) {
   constexpr int VW = H / 32;
   const int lane = threadIdx.x % 32;
-  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  if (r >= N) return;
-  float s[VW];
+  const int64_t v = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (v >= N) return;
+  float sd[VW], ss[VW];
 #pragma unroll
-  for (int c = 0; c < VW; ++c) s[c] = 0.f;
-  float gs = 0.f;
-  const int kb = row_ptr[r], ke = row_ptr[r + 1];
-  int k = kb;
-  for (; k + 4 <= ke; k += 4) {
-    float v[4][VW];
+  for (int c = 0; c < VW; ++c) { sd[c] = 0.f; ss[c] = 0.f; }
+  float gdd = 0.f, gds = 0.f;
+  // lanes 0..2 read component `lane` of a coordinate gradient
+  const float* gdf = reinterpret_cast<const float*>(gdstore);
+  auto comp = [&](int64_t k) { return (lane < 3) ? __ldg(gdf + k * 4 + lane) : 0.f; };
+  int kd = row_ptr[v];
+  const int ked = row_ptr[v + 1];
+  int ks = src_ptr[v];
+  const int kes = src_ptr[v + 1];
+  while (kd + 4 <= ked || ks + 4 <= kes) {   // warp-uniform
+    const bool bd = kd + 4 <= ked, bs = ks + 4 <= kes;
+    int64_t p[4];
+    float vd[4][VW], vs[4][VW], gd1[4], gs1[4];
+    if (bs) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) load_row_slice<H>(gstore + (int64_t)(k + u) * H, lane, v[u]);
-    float4 g[4];
-    if (lane < 3) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) g[u] = gdstore[k + u];
+      for (int u = 0; u < 4; ++u) p[u] = src_edge[ks + u];
     }
+    if (bd) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 4; ++u) {
+        load_row_slice<H>(gstore + (int64_t)(kd + u) * H, lane, vd[u]);
+        gd1[u] = comp(kd + u);
+      }
+    }
+    if (bs) {
 #pragma unroll
-      for (int c = 0; c < VW; ++c) s[c] += v[u][c];
-      if (lane < 3) gs += (lane == 0) ? g[u].x : (lane == 1 ? g[u].y : g[u].z);
+      for (int u = 0; u < 4; ++u) {
+        load_row_slice<H>(gstore + p[u] * H, lane, vs[u]);
+        gs1[u] = comp(p[u]);
+      }
+    }
+    if (bd) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int c = 0; c < VW; ++c) sd[c] += vd[u][c];
+        gdd += gd1[u];
+      }
+      kd += 4;
+    }
+    if (bs) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int c = 0; c < VW; ++c) ss[c] += vs[u][c];
+        gds += gs1[u];
+      }
+      ks += 4;
     }
   }
-  for (; k < ke; ++k) {
-    float v[VW];
-    load_row_slice<H>(gstore + (int64_t)k * H, lane, v);
+  for (; kd < ked; ++kd) {
+    float t[VW];
+    load_row_slice<H>(gstore + (int64_t)kd * H, lane, t);
 #pragma unroll
-    for (int c = 0; c < VW; ++c) s[c] += v[c];
-    if (lane < 3) {
-      const float4 g = gdstore[k];
-      gs += (lane == 0) ? g.x : (lane == 1 ? g.y : g.z);
-    }
+    for (int c = 0; c < VW; ++c) sd[c] += t[c];
+    gdd += comp(kd);
   }
-  store_row_slice<H>(S_dst + r * H, lane, s);
-  if (lane < 3) gxd[r * 3 + lane] = gs;
+  for (; ks < kes; ++ks) {
+    const int64_t q = src_edge[ks];
+    float t[VW];
+    load_row_slice<H>(gstore + q * H, lane, t);
+#pragma unroll
+    for (int c = 0; c < VW; ++c) ss[c] += t[c];
+    gds += comp(q);
+  }
+  store_row_slice<H>(S_dst + v * H, lane, sd);
+  store_row_slice<H>(S_src + v * H, lane, ss);
+  if (lane < 3) gx[v * 3 + lane] = gx_out[v * 3 + lane] + gdd - gds;
 }
 
 template <int H>
@@ -1061,13 +1101,21 @@ int edge_fwd_tc(int H, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s) 
 
 int edge_bwd_tc(int H, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
   if (H != 128) return fail(EGNN_ERR_UNSUPPORTED, "tensor-core edge path built for H = 128");
-  EGNN_TRY(launch_bwd_tc<128>(a, g.G, s));
-  if (a.N > 0) {
-    const int warps = 8;
-    const unsigned blocks = (unsigned)((a.N + warps - 1) / warps);
-    TimerScope ts("row_pass", s);
-    row_pass_kernel<128><<<blocks, warps * 32, 0, s>>>(a.N, a.row_ptr, reinterpret_cast<const __nv_bfloat16*>(a.gstore),
-                                                       a.gdstore, a.S_dst, a.gxd);
+  return launch_bwd_tc<128>(a, g.G, s);
+}
+
+int edge_node_pass_tc(int H, int64_t N, const int32_t* row_ptr, const int32_t* src_ptr, const int32_t* src_edge,
+                      const void* gstore, const float4* gdstore, const float* gx_out, float* S_dst, float* S_src,
+                      float* gx, cudaStream_t s) {
+  if (H != 128) return fail(EGNN_ERR_UNSUPPORTED, "tensor-core edge path built for H = 128");
+  if (N <= 0) return EGNN_OK;
+  const int warps = 8;
+  const unsigned blocks = (unsigned)((N + warps - 1) / warps);
+  {
+    TimerScope ts("node_pass", s);
+    node_pass_kernel<128><<<blocks, warps * 32, 0, s>>>(N, row_ptr, src_ptr, src_edge,
+                                                        static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out,
+                                                        S_dst, S_src, gx);
   }
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;

@@ -14,8 +14,15 @@ EdgeGrid edge_tc_grid(int64_t E, int num_sms);
 // Forward: agg, x_out (with the boundary fix-up).
 int edge_fwd_tc(int H, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s);
 
-// Backward dst pass: gstore, gdstore, per-CTA partials, then the row pass
-// that fills S_dst and gxd.
+// Backward edge kernel: per-edge dL/da1 rows (bf16) in gstore, coordinate
+// gradients in gdstore, per-CTA weight-gradient partials.
 int edge_bwd_tc(int H, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s);
+
+// Node pass after edge_bwd_tc: S_dst / S_src (sums of the bf16 gstore rows over
+// each node's in- / out-edges) and gx = gx_out + (in-edge) - (out-edge)
+// coordinate-gradient sums.
+int edge_node_pass_tc(int H, int64_t N, const int32_t* row_ptr, const int32_t* src_ptr, const int32_t* src_edge,
+                      const void* gstore, const float4* gdstore, const float* gx_out, float* S_dst, float* S_src,
+                      float* gx, cudaStream_t s);
 
 }  // namespace egnn

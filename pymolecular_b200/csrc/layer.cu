@@ -475,8 +475,12 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   // per-CTA weight-gradient partials -> parameter gradients, on the side stream
   EGNN_TRY(stream_fork(s, s2, side->ev[2]));
   EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, s2));
-  EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, tc, w.gdstore, gx_out, w.gxd, w.S_src,
-                         grad_x, s));
+  if (tc)
+    EGNN_TRY(edge_node_pass_tc(H, N, g->row_ptr, g->src_ptr, g->src_edge, w.gstore, w.gdstore, gx_out, w.S_dst,
+                               w.S_src, grad_x, s));
+  else
+    EGNN_TRY(edge_src_pass(H, N, g->src_ptr, g->src_edge, w.gstore, false, w.gdstore, gx_out, w.gxd, w.S_src,
+                           grad_x, s));
 
   // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb here; dWa, db1 and dWb on the two side streams
   EGNN_TRY(stream_fork(s, s2, side->ev[3]));

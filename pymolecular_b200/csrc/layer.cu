@@ -505,6 +505,7 @@ extern "C" int egnn_linear_fwd(int64_t m, int32_t k, int32_t o, const float* x, 
   if (m < 0 || k <= 0 || o <= 0) return fail(EGNN_ERR_INVALID_ARG, "egnn_linear_fwd: bad shape");
   if (m == 0) return EGNN_OK;
   if (!x || !w || !y) return fail(EGNN_ERR_INVALID_ARG, "egnn_linear_fwd: null pointer");
+  if (linear_small_ok(o, k)) return linear_small(m, o, k, x, k, w, 1, b, y, o, (cudaStream_t)stream);
   GemmArgs g;
   g.M = m; g.N = o; g.K = k;
   g.A = mat(x, k);
@@ -531,12 +532,16 @@ extern "C" int egnn_linear_bwd(int64_t m, int32_t k, int32_t o, const float* x, 
     return fail(EGNN_ERR_WORKSPACE, "egnn_linear_bwd: workspace too small");
   float* part = static_cast<float*>(ws);
   if (dx && m > 0) {
-    GemmArgs g;
-    g.M = m; g.N = k; g.K = o;
-    g.A = mat(dy, o);
-    g.B = mat(w, k); g.b_t = 0;
-    g.C = dx; g.ldc = k;
-    EGNN_TRY(gemm(g, s));
+    if (linear_small_ok(k, o)) {
+      EGNN_TRY(linear_small(m, k, o, dy, o, w, 0, nullptr, dx, k, s));
+    } else {
+      GemmArgs g;
+      g.M = m; g.N = k; g.K = o;
+      g.A = mat(dy, o);
+      g.B = mat(w, k); g.b_t = 0;
+      g.C = dx; g.ldc = k;
+      EGNN_TRY(gemm(g, s));
+    }
   }
   return wgrad(m, o, k, mat(dy, o), mat(x, k), dw, k, db, 0, part, s);
 }

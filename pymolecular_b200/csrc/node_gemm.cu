@@ -144,12 +144,22 @@ __global__ void gemm_reduce_kernel(GemmArgs a) {
   }
 }
 
+// Column sums in row order; rows are loaded eight at a time (independent
+// loads) and added one by one, so the result equals the plain row loop's.
 __global__ void colsum_partial_kernel(int64_t R, int64_t C, Mat G, int64_t rows_per, float* part) {
   int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   int64_t r0 = (int64_t)blockIdx.y * rows_per, r1 = min(R, r0 + rows_per);
   float s = 0.f;
-  for (int64_t r = r0; r < r1; ++r) s += G.at(r, c);
+  int64_t r = r0;
+  for (; r + 8 <= r1; r += 8) {
+    float t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t[u] = G.at(r + u, c);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s += t[u];
+  }
+  for (; r < r1; ++r) s += G.at(r, c);
   part[(int64_t)blockIdx.y * C + c] = s;
 }
 
@@ -157,10 +167,59 @@ __global__ void colsum_reduce_kernel(int64_t C, int S, const float* part, float*
   int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   float s = 0.f;
-  for (int z = 0; z < S; ++z) s += part[(int64_t)z * C + c];
+  int z = 0;
+  for (; z + 8 <= S; z += 8) {
+    float t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t[u] = part[(int64_t)(z + u) * C + c];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s += t[u];
+  }
+  for (; z < S; ++z) s += part[(int64_t)z * C + c];
   out[c] = s;
 }
 
+
+// ---- degenerate shapes of the embeddings ------------------------------------------
+// y = x W^T (+ b) with K <= 8 (embedding_in; the input gradient of
+// embedding_out, K = 1).  Thread (n, row slot): W's column n in registers,
+// one output per row, k in order then the bias (as the tiled kernels do).
+constexpr int kSmallK = 8;
+__global__ void linear_smallk_kernel(int64_t M, int N, int K, const float* __restrict__ x, int64_t ldx,
+                                     const float* __restrict__ w, int w_nk, const float* __restrict__ b,
+                                     float* __restrict__ y, int64_t ldy) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float wk[kSmallK];
+#pragma unroll
+  for (int k = 0; k < kSmallK; ++k) wk[k] = k < K ? (w_nk ? w[(int64_t)n * K + k] : w[(int64_t)k * N + n]) : 0.f;
+  const float bias = b ? b[n] : 0.f;
+  for (int64_t m = (int64_t)blockIdx.y * blockDim.y + threadIdx.y; m < M; m += (int64_t)gridDim.y * blockDim.y) {
+    const float* xr = x + m * ldx;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kSmallK; ++k)
+      if (k < K) acc = fmaf(__ldg(xr + k), wk[k], acc);
+    y[m * ldy + n] = b ? acc + bias : acc;
+  }
+}
+
+// y = x w (+ b) with one output column (embedding_out): one warp per row,
+// lanes over k, a fixed-order shuffle tree.
+__global__ void linear_n1_kernel(int64_t M, int K, const float* __restrict__ x, int64_t ldx,
+                                 const float* __restrict__ w, const float* __restrict__ b, float* __restrict__ y,
+                                 int64_t ldy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t m = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; m < M; m += warps) {
+    const float* xr = x + m * ldx;
+    float acc = 0.f;
+    for (int k = lane; k < K; k += 32) acc = fmaf(__ldg(xr + k), __ldg(w + k), acc);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) y[m * ldy] = b ? acc + b[0] : acc;
+  }
+}
 
 // ---- tiled path ------------------------------------------------------------------
 // C (M x N) = A B for every operand layout the layer uses.  Tile 64 x 128
@@ -460,7 +519,7 @@ int gemm(const GemmArgs& a_in, cudaStream_t s) {
   GemmArgs a = a_in;
   a.vec = vec_epilogue(a);
   {
-    TimerScope ts("node_gemm", s);
+    TimerScope ts(tiled_ok(a) ? "node_gemm" : "gemm_small", s);
     if (tiled_ok(a)) {
       EGNN_TRY(launch_tiled(a, s));
     } else {
@@ -473,6 +532,29 @@ int gemm(const GemmArgs& a_in, cudaStream_t s) {
   if (a.ksplit > 1) EGNN_TRY(gemm_reduce(a, s));
   return EGNN_OK;
 }
+
+int linear_small(int64_t M, int N, int K, const float* x, int64_t ldx, const float* w, int w_nk, const float* b,
+                 float* y, int64_t ldy, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return EGNN_OK;
+  TimerScope ts("linear_small", s);
+  if (K <= kSmallK) {
+    const int tx = N >= 32 ? 32 : N;
+    const int ty = 256 / tx;
+    dim3 block(tx, ty);
+    const int64_t rows = std::min<int64_t>((M + ty - 1) / ty, 65535);
+    dim3 grid((unsigned)((N + tx - 1) / tx), (unsigned)std::max<int64_t>(1, std::min<int64_t>(rows, 4096 / ((N + tx - 1) / tx) + 1)));
+    linear_smallk_kernel<<<grid, block, 0, s>>>(M, N, K, x, ldx, w, w_nk, b, y, ldy);
+  } else if (N == 1) {
+    const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((M + 7) / 8, 4096));
+    linear_n1_kernel<<<blocks, 256, 0, s>>>(M, K, x, ldx, w, b, y, ldy);
+  } else {
+    return fail(EGNN_ERR_UNSUPPORTED, "linear_small: shape not covered");
+  }
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+bool linear_small_ok(int N, int K) { return K <= kSmallK || N == 1; }
 
 int gemm_reduce(const GemmArgs& a_in, cudaStream_t s) {
   GemmArgs a = a_in;
@@ -514,7 +596,7 @@ int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw
 }
 
 int64_t colsum_splits(int64_t R) {
-  return std::max<int64_t>(1, std::min<int64_t>(64, R / 256));
+  return std::max<int64_t>(1, std::min<int64_t>(128, R / 64));
 }
 
 int colsum(int64_t R, int64_t C, Mat G, float* db, float* part, cudaStream_t s) {
@@ -523,7 +605,7 @@ int colsum(int64_t R, int64_t C, Mat G, float* db, float* part, cudaStream_t s) 
   int64_t rows_per = (R + S - 1) / S;
   if (R == 0) rows_per = 1;
   dim3 grid((unsigned)((C + 127) / 128), (unsigned)S);
-  TimerScope ts("node_gemm", s);
+  TimerScope ts("colsum", s);
   colsum_partial_kernel<<<grid, 128, 0, s>>>(R, C, G, rows_per, part);
   EGNN_CHECK_LAUNCH();
   colsum_reduce_kernel<<<(unsigned)((C + 127) / 128), 128, 0, s>>>(C, (int)S, part, db);

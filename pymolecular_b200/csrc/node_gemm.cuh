@@ -64,6 +64,13 @@ struct GemmArgs {
 
 int gemm(const GemmArgs& a, cudaStream_t s);
 
+// y (M x N, row stride ldy) = x (M x K, row stride ldx) W^T (+ b) for the
+// degenerate shapes of the embeddings: K <= 8, or N == 1.  W is (N x K)
+// row-major when w_nk, else (K x N).
+bool linear_small_ok(int N, int K);
+int linear_small(int64_t M, int N, int K, const float* x, int64_t ldx, const float* w, int w_nk, const float* b,
+                 float* y, int64_t ldy, cudaStream_t s);
+
 // The ordered split-K reduction (and epilogue) of a GEMM whose ksplit > 1
 // partial slices sit in a.part (and db slices in a.db_part).
 int gemm_reduce(const GemmArgs& a, cudaStream_t s);

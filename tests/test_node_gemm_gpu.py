@@ -12,7 +12,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("m,k,o", [(1000, 64, 128), (777, 96, 256), (10000, 128, 32), (9939, 5, 128),
-                                   (4097, 128, 1), (130, 256, 128), (33, 40, 64)])
+                                   (4097, 128, 1), (130, 256, 128), (33, 40, 64), (300, 1, 7), (5000, 8, 1),
+                                   (65, 3, 300)])
 def test_linear_fwd_bwd_fp32_accuracy(m, k, o, cuda_device):
     g = torch.Generator(device=cuda_device).manual_seed(m + k + o)
     x = torch.randn(m, k, device=cuda_device, generator=g)

@@ -405,7 +405,7 @@ def run_b200(args):
         prob.step()
     torch.cuda.synchronize()
     ktimes = {n: _native.kernel_time(n) for n in ("edge_bwd", "edge_fwd", "node_pass", "src_pass", "edge_fixup",
-                                                  "part_reduce", "node_gemm", "gemm_small", "linear_small", "colsum", "gemm_reduce",
+                                                  "part_reduce", "node_gemm", "gemm_small", "linear_small", "wgrad_small", "colsum", "gemm_reduce",
                                                   "prep")}
     breakdown = {n: round(v[0] / kt_steps, 4) for n, v in ktimes.items() if v[1]}
     _native.lib().egnn_kernel_timing(0)

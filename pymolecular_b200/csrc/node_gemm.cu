@@ -221,6 +221,89 @@ __global__ void linear_n1_kernel(int64_t M, int K, const float* __restrict__ x, 
   }
 }
 
+// ---- weight gradients with one narrow side (the embeddings) -----------------------
+// dW (M x N) = sum_r G[r][i] X[r][j] and db (M) = sum_r G[r][i], computed as
+// one product with X extended by a column of ones (db = its last column).
+// Block z sums rows [z rows_per, ...): warp w takes every 8th row from w, a
+// lane owns the wide indices lane + 32 t and every narrow one; warp
+// partials are added in warp order, then the block slices in block order.
+constexpr int kNarrow = 9;            // narrow side incl. the ones column
+constexpr int kWideSlots = 9;         // wide side up to 288 (with the ones column)
+constexpr int kSmallOut = 1040;       // M (N + 1) outputs at most
+
+__device__ __forceinline__ float ext_at(const Mat& X, int N, int64_t r, int j) {
+  return j < N ? X.at(r, j) : 1.f;
+}
+
+__global__ void __launch_bounds__(256) wgrad_small_partial_kernel(int64_t R, int M, int N, Mat G, Mat X,
+                                                                  int64_t rows_per, float* part) {
+  __shared__ float red[8][kSmallOut];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int N1 = N + 1;
+  const bool lanes_n = N1 >= M;            // lanes over the extended columns, else over the rows i
+  const int wide = lanes_n ? N1 : M, narrow = lanes_n ? M : N1;
+  float acc[kWideSlots][kNarrow];
+#pragma unroll
+  for (int t = 0; t < kWideSlots; ++t)
+#pragma unroll
+    for (int q = 0; q < kNarrow; ++q) acc[t][q] = 0.f;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per, r1 = min(R, r0 + rows_per);
+  for (int64_t r = r0 + warp; r < r1; r += 8) {
+    float wv[kWideSlots], nv[kNarrow];
+#pragma unroll
+    for (int t = 0; t < kWideSlots; ++t) {
+      const int w = lane + 32 * t;
+      wv[t] = (w < wide) ? (lanes_n ? ext_at(X, N, r, w) : G.at(r, w)) : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < kNarrow; ++q) nv[q] = (q < narrow) ? (lanes_n ? G.at(r, q) : ext_at(X, N, r, q)) : 0.f;
+#pragma unroll
+    for (int t = 0; t < kWideSlots; ++t)
+#pragma unroll
+      for (int q = 0; q < kNarrow; ++q)
+        acc[t][q] = lanes_n ? fmaf(nv[q], wv[t], acc[t][q]) : fmaf(wv[t], nv[q], acc[t][q]);
+  }
+#pragma unroll
+  for (int t = 0; t < kWideSlots; ++t) {
+    const int w = lane + 32 * t;
+    if (w >= wide) continue;
+#pragma unroll
+    for (int q = 0; q < kNarrow; ++q) {
+      if (q >= narrow) continue;
+      const int i = lanes_n ? q : w, j = lanes_n ? w : q;
+      red[warp][i * N1 + j] = acc[t][q];
+    }
+  }
+  __syncthreads();
+  const int O = M * N1;
+  for (int o = threadIdx.x; o < O; o += blockDim.x) {
+    float v = red[0][o];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) v += red[w][o];
+    part[(int64_t)blockIdx.x * O + o] = v;
+  }
+}
+
+__global__ void wgrad_small_reduce_kernel(int M, int N, int S, const float* part, float* dW, int64_t lddw,
+                                          float* db) {
+  const int N1 = N + 1, O = M * N1;
+  for (int o = blockIdx.x * blockDim.x + threadIdx.x; o < O; o += gridDim.x * blockDim.x) {
+    float v = 0.f;
+    int z = 0;
+    for (; z + 8 <= S; z += 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = part[(int64_t)(z + u) * O + o];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v += t[u];
+    }
+    for (; z < S; ++z) v += part[(int64_t)z * O + o];
+    const int i = o / N1, j = o % N1;
+    if (j < N) dW[(int64_t)i * lddw + j] = v;
+    else if (db) db[i] = v;
+  }
+}
+
 // ---- tiled path ------------------------------------------------------------------
 // C (M x N) = A B for every operand layout the layer uses.  Tile 64 x 128
 // per 256-thread CTA; thread (tx, ty) owns rows ty*4 + {0..3} and columns
@@ -574,8 +657,27 @@ int64_t wgrad_splits(int64_t K, int64_t M, int64_t N) {
   return std::max<int64_t>(1, std::min<int64_t>({want, by_len, 64}));
 }
 
+bool wgrad_small_ok(int64_t M, int64_t N) {
+  const int64_t n1 = N + 1;
+  return std::min(M, n1) <= kNarrow && std::max(M, n1) <= 32 * kWideSlots && M * n1 <= kSmallOut;
+}
+
 int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw,
           float* db, int round_bf16, float* part, cudaStream_t s) {
+  if (!round_bf16 && wgrad_small_ok(M, N) && R > 0) {
+    // S slices of the wgrad_splits count, so the caller's split-K workspace
+    // (S (M N + M) floats) holds the slices
+    const int64_t S = wgrad_splits(R, M, N);
+    const int64_t rows_per = (R + S - 1) / S;
+    TimerScope ts("wgrad_small", s);
+    wgrad_small_partial_kernel<<<(unsigned)S, 256, 0, s>>>(R, (int)M, (int)N, G, X, rows_per, part);
+    EGNN_CHECK_LAUNCH();
+    const int O = (int)(M * (N + 1));
+    wgrad_small_reduce_kernel<<<(unsigned)((O + 255) / 256), 256, 0, s>>>((int)M, (int)N, (int)S, part, dW, lddw,
+                                                                          db);
+    EGNN_CHECK_LAUNCH();
+    return EGNN_OK;
+  }
   GemmArgs a;
   a.M = M; a.N = N; a.K = R;
   a.A = G; a.a_t = 1;

@@ -54,6 +54,35 @@ int num_sms_current();
 // Bit of the current device (for per-device one-time setup flags).
 uint64_t device_bit();
 
+// ---- programmatic dependent launch ------------------------------------------
+// Kernels on the layer's hot path are launched with launch_pdl: such a kernel
+// may start while its predecessor in the stream is still finishing.  It calls
+// pdl_enter() before it reads or writes any memory its predecessor writes or
+// reads (griddepcontrol.wait returns once the predecessor grid has completed
+// and its writes are visible), and only then lets its own successor start, so
+// that anything written two or more kernels back is complete whenever a
+// kernel runs at all: a prologue may read such data (weights) before its wait.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // ---- workspace carving ----------------------------------------------------
 // Sub-buffers are 256-byte aligned so every float4 / TMA access is aligned.
 struct Carver {

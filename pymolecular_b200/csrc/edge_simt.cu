@@ -360,6 +360,7 @@ __device__ __forceinline__ void gather_phase(const EdgeCommon& a, int64_t c0, in
 // ---- forward kernel -----------------------------------------------------------
 template <int H, bool BF>
 __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeFwdArgs a) {
+  pdl_enter();
   using C = Cfg<H>;
   using S = FwdSmem<C>;
   extern __shared__ float4 smem_f4[];
@@ -487,6 +488,7 @@ __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeFwdArgs a) {
 // ---- backward kernel (dst pass) --------------------------------------------------
 template <int H, bool BF>
 __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeBwdArgs a) {
+  pdl_enter();
   using C = Cfg<H>;
   using S = BwdSmem<C>;
   extern __shared__ float4 smem_b4[];
@@ -842,6 +844,7 @@ template <bool BWD>
 __global__ void edge_fixup_kernel(int H, int64_t E, int G, int64_t epc, const int32_t* row_ptr,
                                   const int32_t* row_idx, const float* carry, int flags,
                                   const float* x, float* out_h, float* out_x) {
+  pdl_enter();
   const int c = blockIdx.x + 1;
   const int64_t b = (int64_t)c * epc;
   if (c >= G || b >= E || b == 0) return;
@@ -872,6 +875,7 @@ __global__ void src_pass_kernel(int64_t N, const int32_t* __restrict__ src_ptr,
                                 const float4* __restrict__ gdstore, const float* __restrict__ gx_out,
                                 const float* __restrict__ gxd, float* __restrict__ S_src,
                                 float* __restrict__ gx) {
+  pdl_enter();
   // One warp per source node; lane owns the H / 32 consecutive features
   // lane*VW .. +VW-1.  Edge rows are fetched four at a time (indices first),
   // and added in increasing CSR-position order as before.
@@ -921,6 +925,7 @@ __global__ void src_pass_kernel(int64_t N, const int32_t* __restrict__ src_ptr,
 
 __global__ void part_reduce_kernel(int H, int d, int att, int G, int64_t PF, const float* part,
                                    egnn_layer_grads gp, int64_t ld_w1) {
+  pdl_enter();
   const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -973,13 +978,13 @@ int launch_fwd(const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
   }
   {
     TimerScope ts("edge_fwd", s);
-    edge_fwd_kernel<H, BF><<<g.G, C::NT, bytes, s>>>(a);
+    EGNN_CHECK_CUDA(launch_pdl(edge_fwd_kernel<H, BF>, dim3(g.G), dim3(C::NT), bytes, s, a));
   }
   EGNN_CHECK_LAUNCH();
   if (g.G > 1) {
     TimerScope ts_fix("edge_fixup", s);
-    edge_fixup_kernel<false><<<g.G - 1, 128, 0, s>>>(H, a.E, g.G, g.epc, a.row_ptr, a.row_idx, a.carry,
-                                                     a.flags, a.x, a.agg, a.x_out);
+    EGNN_CHECK_CUDA(launch_pdl(edge_fixup_kernel<false>, dim3(g.G - 1), dim3(128), 0, s, H, a.E, g.G, g.epc,
+                               a.row_ptr, a.row_idx, (const float*)a.carry, a.flags, a.x, a.agg, a.x_out));
     EGNN_CHECK_LAUNCH();
   }
   return EGNN_OK;
@@ -999,13 +1004,14 @@ int launch_bwd(const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
   }
   {
     TimerScope ts("edge_bwd", s);
-    edge_bwd_kernel<H, BF><<<g.G, C::NT, bytes, s>>>(a);
+    EGNN_CHECK_CUDA(launch_pdl(edge_bwd_kernel<H, BF>, dim3(g.G), dim3(C::NT), bytes, s, a));
   }
   EGNN_CHECK_LAUNCH();
   if (g.G > 1) {
     TimerScope ts_fix("edge_fixup", s);
-    edge_fixup_kernel<true><<<g.G - 1, 128, 0, s>>>(H, a.E, g.G, g.epc, a.row_ptr, a.row_idx, a.carry,
-                                                    a.flags, nullptr, a.S_dst, a.gxd);
+    EGNN_CHECK_CUDA(launch_pdl(edge_fixup_kernel<true>, dim3(g.G - 1), dim3(128), 0, s, H, a.E, g.G, g.epc,
+                               a.row_ptr, a.row_idx, (const float*)a.carry, a.flags, (const float*)nullptr,
+                               a.S_dst, a.gxd));
     EGNN_CHECK_LAUNCH();
   }
   return EGNN_OK;
@@ -1083,8 +1089,8 @@ int edge_fwd(int H, bool bf16, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStre
 
 int edge_fixup_fwd(int H, const EdgeFwdArgs& a, const EdgeGrid& g, cudaStream_t s) {
   TimerScope ts_fix("edge_fixup", s);
-  edge_fixup_kernel<false><<<g.G - 1, 128, 0, s>>>(H, a.E, g.G, g.epc, a.row_ptr, a.row_idx, a.carry, a.flags,
-                                                   a.x, a.agg, a.x_out);
+  EGNN_CHECK_CUDA(launch_pdl(edge_fixup_kernel<false>, dim3(g.G - 1), dim3(128), 0, s, H, a.E, g.G, g.epc,
+                             a.row_ptr, a.row_idx, (const float*)a.carry, a.flags, a.x, a.agg, a.x_out));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
@@ -1107,11 +1113,11 @@ int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_e
   if (H == HH) {                                                                                   \
     TimerScope ts("src_pass", s);                                                                  \
     if (bf16_rows)                                                                                 \
-      src_pass_kernel<HH, __nv_bfloat16><<<blocks, warps * 32, 0, s>>>(                            \
-          N, src_ptr, src_edge, static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, gxd, S_src, gx); \
+      EGNN_CHECK_CUDA(launch_pdl(src_pass_kernel<HH, __nv_bfloat16>, dim3(blocks), dim3(warps * 32), 0, s, \
+          N, src_ptr, src_edge, static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, gxd, S_src, gx)); \
     else                                                                                           \
-      src_pass_kernel<HH, float><<<blocks, warps * 32, 0, s>>>(                                    \
-          N, src_ptr, src_edge, static_cast<const float*>(gstore), gdstore, gx_out, gxd, S_src, gx);         \
+      EGNN_CHECK_CUDA(launch_pdl(src_pass_kernel<HH, float>, dim3(blocks), dim3(warps * 32), 0, s,  \
+          N, src_ptr, src_edge, static_cast<const float*>(gstore), gdstore, gx_out, gxd, S_src, gx));       \
     EGNN_CHECK_LAUNCH();                                                                           \
     return EGNN_OK;                                                                                \
   }
@@ -1125,7 +1131,8 @@ int edge_part_reduce(int H, int d, bool att, int G, const float* part, const egn
   const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
   TimerScope ts("part_reduce", s);
-  part_reduce_kernel<<<blocks, 256, 0, s>>>(H, d, att ? 1 : 0, G, edge_part_floats(H, d), part, *gp, ld_w1);
+  EGNN_CHECK_CUDA(launch_pdl(part_reduce_kernel, dim3(blocks), dim3(256), 0, s, H, d, att ? 1 : 0, G,
+                             edge_part_floats(H, d), part, *gp, ld_w1));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

@@ -319,6 +319,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   for (int c = g.tid; c < H; c += kNT) {
     s_wr[c] = a.wr[c]; s_b2[c] = a.b2[c]; s_bc1[c] = a.bc1[c]; s_wc2[c] = a.wc2[c];
   }
+  pdl_enter();   // everything below reads the predecessor's output (P, Q) or writes
   const int cta = blockIdx.x, G = gridDim.x;
   const int64_t eb = std::min<int64_t>(a.E, (int64_t)cta * a.epc);
   const int64_t ee = std::min<int64_t>(a.E, eb + a.epc);
@@ -655,6 +656,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   for (int c = g.tid; c < H; c += kNT) {
     s_wr[c] = a.wr[c]; s_b2[c] = a.b2[c]; s_bc1[c] = a.bc1[c]; s_wc2[c] = a.wc2[c];
   }
+  pdl_enter();   // everything below reads the predecessor's output (dL/dagg) or writes
   fence_proxy_async();
   fence_before_sync();
   __syncthreads();
@@ -966,6 +968,7 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
                                  const float* __restrict__ gx_out, float* __restrict__ S_dst,
                                  float* __restrict__ S_src, float* __restrict__ gx) {
   constexpr int VW = H / 32;
+  pdl_enter();
   const int lane = threadIdx.x % 32;
   const int64_t v = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (v >= N) return;
@@ -1053,7 +1056,7 @@ int launch_fwd_tc(const EdgeFwdArgs& a, int G, cudaStream_t s) {
   }
   {
     TimerScope ts("edge_fwd", s);
-    edge_fwd_tc_kernel<H><<<G, kNT, bytes, s>>>(a);
+    EGNN_CHECK_CUDA(launch_pdl(edge_fwd_tc_kernel<H>, dim3(G), dim3(kNT), bytes, s, a));
   }
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
@@ -1071,7 +1074,7 @@ int launch_bwd_tc(const EdgeBwdArgs& a, int G, cudaStream_t s) {
   }
   {
     TimerScope ts("edge_bwd", s);
-    edge_bwd_tc_kernel<H><<<G, kNT, bytes, s>>>(a);
+    EGNN_CHECK_CUDA(launch_pdl(edge_bwd_tc_kernel<H>, dim3(G), dim3(kNT), bytes, s, a));
   }
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
@@ -1113,9 +1116,9 @@ int edge_node_pass_tc(int H, int64_t N, const int32_t* row_ptr, const int32_t* s
   const unsigned blocks = (unsigned)((N + warps - 1) / warps);
   {
     TimerScope ts("node_pass", s);
-    node_pass_kernel<128><<<blocks, warps * 32, 0, s>>>(N, row_ptr, src_ptr, src_edge,
-                                                        static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out,
-                                                        S_dst, S_src, gx);
+    EGNN_CHECK_CUDA(launch_pdl(node_pass_kernel<128>, dim3(blocks), dim3(warps * 32), 0, s, N, row_ptr, src_ptr,
+                               src_edge, static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, S_dst, S_src,
+                               gx));
   }
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;

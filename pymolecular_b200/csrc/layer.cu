@@ -87,6 +87,7 @@ __host__ __device__ inline int64_t prep_transposes(const Prep& o, int H) { retur
 
 __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_layer_params p,
                             const float* x, Prep o) {
+  pdl_enter();
   const int64_t HH = (int64_t)H * H;
   const int64_t total = N + 2 * H + 4 * HH + H + (int64_t)H * d + 2 * HH + prep_transposes(o, H);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -144,7 +145,7 @@ int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_
   const int64_t total = N + 2 * H + 6LL * H * H + H + (int64_t)H * d + prep_transposes(o, H);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
   TimerScope ts("prep", s);
-  prep_kernel<<<blocks, 256, 0, s>>>(N, H, d, ld1, bf ? 1 : 0, *p, x, o);
+  EGNN_CHECK_CUDA(launch_pdl(prep_kernel, dim3(blocks), dim3(256), 0, s, N, H, d, ld1, bf ? 1 : 0, *p, x, o));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

@@ -34,6 +34,7 @@ struct Epi {
 };
 
 __global__ void __launch_bounds__(NT) gemm_kernel(GemmArgs a) {
+  pdl_enter();
   __shared__ __align__(16) float As[BK][BM + 4];
   __shared__ __align__(16) float Bs[BK][BN + 4];
   const int tid = threadIdx.x;
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(NT) gemm_kernel(GemmArgs a) {
 }
 
 __global__ void gemm_reduce_kernel(GemmArgs a) {
+  pdl_enter();
   Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.resid_cols, a.C, a.ldc};
   const int64_t total = a.M * a.N;
   if (a.db && a.db_part) {
@@ -147,6 +149,7 @@ __global__ void gemm_reduce_kernel(GemmArgs a) {
 // Column sums in row order; rows are loaded eight at a time (independent
 // loads) and added one by one, so the result equals the plain row loop's.
 __global__ void colsum_partial_kernel(int64_t R, int64_t C, Mat G, int64_t rows_per, float* part) {
+  pdl_enter();
   int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   int64_t r0 = (int64_t)blockIdx.y * rows_per, r1 = min(R, r0 + rows_per);
@@ -164,6 +167,7 @@ __global__ void colsum_partial_kernel(int64_t R, int64_t C, Mat G, int64_t rows_
 }
 
 __global__ void colsum_reduce_kernel(int64_t C, int S, const float* part, float* out) {
+  pdl_enter();
   int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   float s = 0.f;
@@ -188,6 +192,7 @@ constexpr int kSmallK = 8;
 __global__ void linear_smallk_kernel(int64_t M, int N, int K, const float* __restrict__ x, int64_t ldx,
                                      const float* __restrict__ w, int w_nk, const float* __restrict__ b,
                                      float* __restrict__ y, int64_t ldy) {
+  pdl_enter();
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   float wk[kSmallK];
@@ -209,6 +214,7 @@ __global__ void linear_smallk_kernel(int64_t M, int N, int K, const float* __res
 __global__ void linear_n1_kernel(int64_t M, int K, const float* __restrict__ x, int64_t ldx,
                                  const float* __restrict__ w, const float* __restrict__ b, float* __restrict__ y,
                                  int64_t ldy) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   for (int64_t m = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; m < M; m += warps) {
@@ -237,6 +243,7 @@ __device__ __forceinline__ float ext_at(const Mat& X, int N, int64_t r, int j) {
 
 __global__ void __launch_bounds__(256) wgrad_small_partial_kernel(int64_t R, int M, int N, Mat G, Mat X,
                                                                   int64_t rows_per, float* part) {
+  pdl_enter();
   __shared__ float red[8][kSmallOut];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int N1 = N + 1;
@@ -286,6 +293,7 @@ __global__ void __launch_bounds__(256) wgrad_small_partial_kernel(int64_t R, int
 
 __global__ void wgrad_small_reduce_kernel(int M, int N, int S, const float* part, float* dW, int64_t lddw,
                                           float* db) {
+  pdl_enter();
   const int N1 = N + 1, O = M * N1;
   for (int o = blockIdx.x * blockDim.x + threadIdx.x; o < O; o += gridDim.x * blockDim.x) {
     float v = 0.f;
@@ -411,6 +419,7 @@ __device__ __forceinline__ float4 epi_act(float4 v, int act, const float* aux) {
 template <int TM, int A_T, int B_T>
 __global__ void __launch_bounds__(256, 2) gemm_tiled_kernel(GemmArgs a) {
   static_assert(TM == 4, "fragment loads below cover 4 rows per thread");
+  pdl_enter();
   constexpr int BM = 16 * TM, LDA = BM + 4, LDB = TBN + 4;
   constexpr int SA = TBK * LDA, SB = TBK * LDB;
   extern __shared__ __align__(16) float tsm[];
@@ -584,7 +593,7 @@ int launch_tiled_t(const GemmArgs& a, cudaStream_t s) {
   }
   const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
   const dim3 grid((unsigned)((a.N + TBN - 1) / TBN), (unsigned)((a.M + 16 * TM - 1) / (16 * TM)), z);
-  gemm_tiled_kernel<TM, A_T, B_T><<<grid, 256, bytes, s>>>(a);
+  EGNN_CHECK_CUDA(launch_pdl(gemm_tiled_kernel<TM, A_T, B_T>, grid, dim3(256), bytes, s, a));
   return EGNN_OK;
 }
 
@@ -608,7 +617,7 @@ int gemm(const GemmArgs& a_in, cudaStream_t s) {
     } else {
       const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
       dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), z);
-      gemm_kernel<<<grid, NT, 0, s>>>(a);
+      EGNN_CHECK_CUDA(launch_pdl(gemm_kernel, grid, dim3(NT), 0, s, a));
     }
   }
   EGNN_CHECK_LAUNCH();
@@ -626,10 +635,10 @@ int linear_small(int64_t M, int N, int K, const float* x, int64_t ldx, const flo
     dim3 block(tx, ty);
     const int64_t rows = std::min<int64_t>((M + ty - 1) / ty, 65535);
     dim3 grid((unsigned)((N + tx - 1) / tx), (unsigned)std::max<int64_t>(1, std::min<int64_t>(rows, 4096 / ((N + tx - 1) / tx) + 1)));
-    linear_smallk_kernel<<<grid, block, 0, s>>>(M, N, K, x, ldx, w, w_nk, b, y, ldy);
+    EGNN_CHECK_CUDA(launch_pdl(linear_smallk_kernel, grid, block, 0, s, M, N, K, x, ldx, w, w_nk, b, y, ldy));
   } else if (N == 1) {
     const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((M + 7) / 8, 4096));
-    linear_n1_kernel<<<blocks, 256, 0, s>>>(M, K, x, ldx, w, b, y, ldy);
+    EGNN_CHECK_CUDA(launch_pdl(linear_n1_kernel, dim3(blocks), dim3(256), 0, s, M, K, x, ldx, w, b, y, ldy));
   } else {
     return fail(EGNN_ERR_UNSUPPORTED, "linear_small: shape not covered");
   }
@@ -645,7 +654,7 @@ int gemm_reduce(const GemmArgs& a_in, cudaStream_t s) {
   const int64_t total = a.M * a.N;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
   TimerScope ts("gemm_reduce", s);
-  gemm_reduce_kernel<<<blocks, 256, 0, s>>>(a);
+  EGNN_CHECK_CUDA(launch_pdl(gemm_reduce_kernel, dim3(blocks), dim3(256), 0, s, a));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
@@ -670,11 +679,12 @@ int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw
     const int64_t S = wgrad_splits(R, M, N);
     const int64_t rows_per = (R + S - 1) / S;
     TimerScope ts("wgrad_small", s);
-    wgrad_small_partial_kernel<<<(unsigned)S, 256, 0, s>>>(R, (int)M, (int)N, G, X, rows_per, part);
+    EGNN_CHECK_CUDA(launch_pdl(wgrad_small_partial_kernel, dim3((unsigned)S), dim3(256), 0, s, R, (int)M, (int)N, G,
+                               X, rows_per, part));
     EGNN_CHECK_LAUNCH();
     const int O = (int)(M * (N + 1));
-    wgrad_small_reduce_kernel<<<(unsigned)((O + 255) / 256), 256, 0, s>>>((int)M, (int)N, (int)S, part, dW, lddw,
-                                                                          db);
+    EGNN_CHECK_CUDA(launch_pdl(wgrad_small_reduce_kernel, dim3((unsigned)((O + 255) / 256)), dim3(256), 0, s, (int)M,
+                               (int)N, (int)S, (const float*)part, dW, lddw, db));
     EGNN_CHECK_LAUNCH();
     return EGNN_OK;
   }
@@ -708,9 +718,10 @@ int colsum(int64_t R, int64_t C, Mat G, float* db, float* part, cudaStream_t s) 
   if (R == 0) rows_per = 1;
   dim3 grid((unsigned)((C + 127) / 128), (unsigned)S);
   TimerScope ts("colsum", s);
-  colsum_partial_kernel<<<grid, 128, 0, s>>>(R, C, G, rows_per, part);
+  EGNN_CHECK_CUDA(launch_pdl(colsum_partial_kernel, grid, dim3(128), 0, s, R, C, G, rows_per, part));
   EGNN_CHECK_LAUNCH();
-  colsum_reduce_kernel<<<(unsigned)((C + 127) / 128), 128, 0, s>>>(C, (int)S, part, db);
+  EGNN_CHECK_CUDA(launch_pdl(colsum_reduce_kernel, dim3((unsigned)((C + 127) / 128)), dim3(128), 0, s, C, (int)S,
+                             (const float*)part, db));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

@@ -168,6 +168,7 @@ __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t ph) {
 
 template <int A_T, int B_T, int BNT>
 __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
+  pdl_enter();
   using S = TcShape<BNT>;
   extern __shared__ __align__(1024) char tsm_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
@@ -402,7 +403,7 @@ int launch_t(const GemmArgs& a, cudaStream_t s) {
   const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
   const dim3 grid((unsigned)((a.N + BNT - 1) / BNT), (unsigned)((a.M + BMT - 1) / BMT), z);
   TimerScope ts("node_gemm", s);
-  gemm_tc_kernel<A_T, B_T, BNT><<<grid, NTH, bytes, s>>>(a);
+  EGNN_CHECK_CUDA(launch_pdl(gemm_tc_kernel<A_T, B_T, BNT>, grid, dim3(NTH), bytes, s, a));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

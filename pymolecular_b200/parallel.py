@@ -53,11 +53,12 @@ def partition_graphs(n_nodes: Sequence[int], n_edges: Sequence[int], world: int)
 class GradAllReduce:
     """Sum (or average) the gradients of `params` over the process group.
 
-    All gradients live in one flat fp32 buffer: ``zero_grad()`` clears it and
-    makes every ``p.grad`` a view of it, so the backward accumulates straight
-    into the buffer and the reduction is one all_reduce with no packing.
-    Gradients that arrive as separate tensors are copied in first.  Every rank
-    issues the same collective in the same order.
+    The backward leaves each gradient in its own tensor (``zero_grad()`` sets
+    them to None, so autograd assigns rather than accumulates: no extra add
+    kernel per parameter).  The call packs them into one flat fp32 buffer with
+    a single concatenation, reduces it with one all_reduce and makes every
+    ``p.grad`` a view of the reduced buffer.  Every rank issues the same
+    collective in the same order.
     """
 
     def __init__(self, params, average: bool = True, group=None):
@@ -73,22 +74,19 @@ class GradAllReduce:
             off += p.numel()
 
     def zero_grad(self):
-        self.flat.zero_()
-        for p, v in zip(self.params, self.views):
-            p.grad = v
+        for p in self.params:
+            p.grad = None
 
     def __call__(self):
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return
-        for p, v in zip(self.params, self.views):
-            if p.grad is None:
-                v.zero_()
-            elif p.grad.data_ptr() != v.data_ptr():
-                v.copy_(p.grad)
-            p.grad = v
+        parts = [(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1) for p in self.params]
+        torch.cat(parts, out=self.flat)
         dist.all_reduce(self.flat, group=self.group)
         if self.average:
             self.flat.div_(dist.get_world_size(self.group))
+        for p, v in zip(self.params, self.views):
+            p.grad = v
 
 
 # ---------------------------------------------------------------------------

@@ -157,3 +157,51 @@ def test_builder_guards(cuda_device):
     # empty inputs
     e = builders.radius_graph(torch.zeros(0, 3, device=cuda_device), 1.0)
     assert e.n_nodes == 0 and e.n_edges == 0
+
+
+
+def _same_up_to_float32_boundary(csr, b, cutoff, capped):
+    """Per-row neighbour sets of a device CSR against a generator batch: any
+    difference must sit on the cutoff (uncapped) or on the cap's k-th distance
+    (capped) to float32 precision.  Returns the number of rows that differ."""
+    rp, col = _rows(csr)
+    hrp = np.concatenate([[0], np.cumsum(np.bincount(b.row.numpy(), minlength=b.n_nodes))])
+    hcol = b.col.numpy()
+    x = b.x.numpy()
+    c2 = np.float32(cutoff) * np.float32(cutoff)
+    differ = 0
+    for i in range(b.n_nodes):
+        a, h = col[rp[i]:rp[i + 1]], hcol[hrp[i]:hrp[i + 1]]
+        if np.array_equal(a, h):
+            continue
+        sa, sh = set(a.tolist()), set(h.tolist())
+        d = GO.sqdist_f32(x[i], x[sorted(sa ^ sh)]) if sa != sh else np.zeros(0, np.float32)
+        if capped:
+            ref = np.sort(GO.sqdist_f32(x[i], x[a]))[-1] if len(a) else c2
+            assert np.allclose(d, ref, rtol=1e-5), i
+            # nearest first in both: position by position the distances agree, so
+            # only neighbours at equal float32 distances can trade places
+            if len(a) == len(h):
+                assert np.allclose(GO.sqdist_f32(x[i], x[a]), GO.sqdist_f32(x[i], x[h]), rtol=1e-5), i
+        else:
+            assert sa != sh and np.allclose(d, c2, rtol=1e-5), i
+        differ += 1
+    return differ
+
+
+def test_builders_reproduce_the_workload_graphs(cuda_device):
+    """The device builders give the graphs of the workload generators (scipy
+    cKDTree in float64) up to float32 ties at the cutoff or the cap: protein
+    walks with a 10 A radius graph (workload 3), slabs with a 6 A radius graph
+    capped at 50 nearest (workload 4), and the fully connected molecule batch
+    (workloads 1-2) edge for edge."""
+    from pymolecular_b200 import datasets
+    b3 = datasets.proteins(2, seed=3)
+    csr3 = builders.radius_graph(b3.x.to(cuda_device), 10.0, graph_ptr=b3.graph_ptr)
+    assert _same_up_to_float32_boundary(csr3, b3, 10.0, False) <= b3.n_nodes // 1000
+    b4 = datasets.slabs(16, seed=4)
+    csr4 = builders.radius_graph(b4.x.to(cuda_device), 6.0, graph_ptr=b4.graph_ptr, max_num_neighbors=50)
+    assert _same_up_to_float32_boundary(csr4, b4, 6.0, True) <= b4.n_nodes // 100
+    b2 = datasets.molecules(64, seed=2)
+    csr2 = builders.fc_graph(b2.graph_ptr, device=cuda_device)
+    assert torch.equal(csr2.row_idx.cpu().long(), b2.row) and torch.equal(csr2.col_idx.cpu().long(), b2.col)

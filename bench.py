@@ -479,6 +479,16 @@ def run_b200(args):
         flops_launch = 8.0 * H * H * prob.edges_rank   # dgrad + wgrad of the two H x H edge GEMMs
         achieved = flops_launch / (per_launch_ms * 1e-3) / 1e12
         peak = peaks["bf16_tflops_sustained"]
+        fp32_pipe = {}
+        if not (prob.precision == "bf16" and H == 128):
+            # the SIMT edge kernels (fp32 mode, and bf16 mode at H != 128) run the
+            # edge GEMMs on the FP32 pipe (FFMA), whose peak MEASURED_PEAKS.json
+            # does not hold: the nominal figure, SMs x 128 FMA lanes x 2 flop x
+            # the maximum SM clock seen during the run
+            props = torch.cuda.get_device_properties(dev)
+            mhz = (clk or {}).get("sm_max_mhz") or 1965.0
+            fp32_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+            fp32_pipe = {"fp32_pipe_peak_nominal": fp32_peak, "frac_of_fp32_pipe_nominal": achieved / fp32_peak}
         step_flops = model_flops(mc, prob.nodes_rank, prob.edges_rank) * world
         cpu = None
         if not args.no_cpu_baseline and world == 1:
@@ -514,6 +524,7 @@ def run_b200(args):
                          "traffic_unit": "bytes per launch (ncu capture)",
                          "per_launch_ms": per_launch_ms, "launches": bwd_n,
                          "flops_per_launch": flops_launch,
+                         **fp32_pipe,
                          "edge_fwd_per_launch_ms": fwd_ms / max(fwd_n, 1),
                          "node_pass_per_launch_ms": ktimes["node_pass"][0] / max(ktimes["node_pass"][1], 1),
                          "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1)},

@@ -66,14 +66,16 @@ struct Prep {
   float* WPQT;  // (H, 2H): WPQ^T
 };
 
-Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd) {
+// `tc`: the tensor-core edge kernels read W2 and W_c1 as given, so the SIMT
+// kernels' transposed / rounded copies are not made.
+Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd, bool tc) {
   Prep p{};
   p.xp = c.take<float4>(std::max<int64_t>(N, 1));
   p.bias2 = c.take<float>(2 * H);
-  p.W2T = c.take<float>((size_t)H * H);
-  p.Wc1T = c.take<float>((size_t)H * H);
-  p.W2r = bwd ? c.take<float>((size_t)H * H) : nullptr;
-  p.Wc1r = bwd ? c.take<float>((size_t)H * H) : nullptr;
+  p.W2T = tc ? nullptr : c.take<float>((size_t)H * H);
+  p.Wc1T = tc ? nullptr : c.take<float>((size_t)H * H);
+  p.W2r = (bwd && !tc) ? c.take<float>((size_t)H * H) : nullptr;
+  p.Wc1r = (bwd && !tc) ? c.take<float>((size_t)H * H) : nullptr;
   p.wr = c.take<float>(H);
   p.We = c.take<float>((size_t)H * std::max(d, 1));
   p.WPQ = c.take<float>((size_t)2 * H * H);
@@ -84,12 +86,29 @@ Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd) {
 }
 
 __host__ __device__ inline int64_t prep_transposes(const Prep& o, int H) { return o.Wn2T ? 5LL * H * H : 0; }
+// The H x H copies of W2 / W_c1 the layout asks for: W2T, Wc1T, W2r, Wc1r in
+// this order, the absent ones left out; sel[] lists the present ones.
+__host__ __device__ inline int prep_copies(const Prep& o, int* sel) {
+  int n = 0;
+  if (o.W2T) sel[n++] = 0;
+  if (o.Wc1T) sel[n++] = 1;
+  if (o.W2r) sel[n++] = 2;
+  if (o.Wc1r) sel[n++] = 3;
+  return n;
+}
+__host__ __device__ inline int64_t prep_total(int64_t N, int H, int d, const Prep& o) {
+  int sel[4];
+  const int64_t HH = (int64_t)H * H;
+  return N + 2 * H + prep_copies(o, sel) * HH + H + (int64_t)H * d + 2 * HH + prep_transposes(o, H);
+}
 
 __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_layer_params p,
                             const float* x, Prep o) {
   pdl_enter();
   const int64_t HH = (int64_t)H * H;
-  const int64_t total = N + 2 * H + 4 * HH + H + (int64_t)H * d + 2 * HH + prep_transposes(o, H);
+  int sel[4];
+  const int ncopy = prep_copies(o, sel);
+  const int64_t total = prep_total(N, H, d, o);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     int64_t t = idx;
@@ -121,19 +140,19 @@ __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_l
     t -= N;
     if (t < 2 * H) { o.bias2[t] = t < H ? p.edge_b1[t] : 0.f; continue; }
     t -= 2 * H;
-    if (t < 4 * HH) {
-      const int which = (int)(t / HH);
+    if (t < ncopy * HH) {
+      const int which = sel[t / HH];
       const int64_t r = t % HH, k = r / H, n = r % H;   // (k, n) of a [k][n] matrix
       float v;
       switch (which) {
-        case 0: v = p.edge_w2[n * H + k]; if (o.W2T) o.W2T[r] = bf ? bf16r(v) : v; break;
-        case 1: v = p.coord_w1[n * H + k]; if (o.Wc1T) o.Wc1T[r] = bf ? bf16r(v) : v; break;
-        case 2: v = p.edge_w2[r]; if (o.W2r) o.W2r[r] = bf ? bf16r(v) : v; break;
-        default: v = p.coord_w1[r]; if (o.Wc1r) o.Wc1r[r] = bf ? bf16r(v) : v; break;
+        case 0: v = p.edge_w2[n * H + k]; o.W2T[r] = bf ? bf16r(v) : v; break;
+        case 1: v = p.coord_w1[n * H + k]; o.Wc1T[r] = bf ? bf16r(v) : v; break;
+        case 2: v = p.edge_w2[r]; o.W2r[r] = bf ? bf16r(v) : v; break;
+        default: v = p.coord_w1[r]; o.Wc1r[r] = bf ? bf16r(v) : v; break;
       }
       continue;
     }
-    t -= 4 * HH;
+    t -= ncopy * HH;
     if (t < H) { o.wr[t] = p.edge_w1[t * ld1 + 2 * H]; continue; }
     t -= H;
     { const int64_t f = t / d, a = t % d; o.We[f * d + a] = p.edge_w1[f * ld1 + 2 * H + 1 + a]; }
@@ -142,7 +161,7 @@ __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_l
 
 int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_params* p,
                 const float* x, const Prep& o, cudaStream_t s) {
-  const int64_t total = N + 2 * H + 6LL * H * H + H + (int64_t)H * d + prep_transposes(o, H);
+  const int64_t total = prep_total(N, H, d, o);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
   TimerScope ts("prep", s);
   EGNN_CHECK_CUDA(launch_pdl(prep_kernel, dim3(blocks), dim3(256), 0, s, N, H, d, ld1, bf ? 1 : 0, *p, x, o));
@@ -195,7 +214,8 @@ FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int64_t N = d->n_nodes, E = d->n_edges;
   const int H = d->hidden;
   FwdWs w;
-  w.prep = carve_prep(c, N, H, d->edge_attr_dim, false);
+  w.prep = carve_prep(c, N, H, d->edge_attr_dim, false,
+                      edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
   const int64_t G = max_ctas(E, H, num_sms);
   w.carry = c.take<float>((size_t)G * 2 * (H + 4));
   w.carry_row = c.take<int32_t>((size_t)G * 2);
@@ -224,7 +244,8 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int64_t N = std::max<int64_t>(d->n_nodes, 1), E = d->n_edges;
   const int H = d->hidden;
   BwdWs w;
-  w.prep = carve_prep(c, N, H, d->edge_attr_dim, true);
+  w.prep = carve_prep(c, N, H, d->edge_attr_dim, true,
+                      edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
   w.g_n1pre = c.take<float>((size_t)N * H);
   w.ghg = c.take<float>((size_t)N * 2 * H);
   w.S_dst = c.take<float>((size_t)N * H);

@@ -408,7 +408,8 @@ def run_b200(args):
     torch.cuda.synchronize()
     ktimes = {n: _native.kernel_time(n) for n in ("edge_bwd", "edge_fwd", "node_pass", "src_pass", "edge_fixup",
                                                   "part_reduce", "node_gemm", "gemm_small", "linear_small", "wgrad_small", "colsum", "gemm_reduce",
-                                                  "prep")}
+                                                  "prep", "edge_rows_gemm", "edge_rows_wgrad", "edge_rows_u",
+                                                  "edge_rows_agg")}
     breakdown = {n: round(v[0] / kt_steps, 4) for n, v in ktimes.items() if v[1]}
     _native.lib().egnn_kernel_timing(0)
     status = _native.lib().egnn_device_status(_native.stream_ptr())
@@ -475,14 +476,26 @@ def run_b200(args):
     if rank == 0:
         H = mc.hidden_nf
         peaks = measured_peaks()
-        bwd_ms, bwd_n = ktimes["edge_bwd"]
         fwd_ms, fwd_n = ktimes["edge_fwd"]
-        per_launch_ms = bwd_ms / max(bwd_n, 1)
-        flops_launch = 8.0 * H * H * prob.edges_rank   # dgrad + wgrad of the two H x H edge GEMMs
-        achieved = flops_launch / (per_launch_ms * 1e-3) / 1e12
+        rows_path = prob.precision == "bf16" and H == 256
+        if rows_path:
+            # edge-row GEMMs (H = 256): six launches per layer (fwd: a2, c1;
+            # bwd: recomputed a2, c1 and the two data gradients).  Credited are
+            # the algorithmic flops only, 4 x 2 H^2 per edge and layer (the
+            # recompute is not credited), over the time of all six launches.
+            kname = "edge_rows_gemm"
+            bwd_ms, bwd_n = ktimes[kname]
+            per_launch_ms = bwd_ms / max(bwd_n, 1)
+            flops_launch = (4.0 / 6.0) * 2.0 * H * H * prob.edges_rank
+        else:
+            kname = "edge_bwd"
+            bwd_ms, bwd_n = ktimes[kname]
+            per_launch_ms = bwd_ms / max(bwd_n, 1)
+            flops_launch = 8.0 * H * H * prob.edges_rank   # dgrad + wgrad of the two H x H edge GEMMs
+        achieved = flops_launch / (max(per_launch_ms, 1e-9) * 1e-3) / 1e12
         peak = peaks["bf16_tflops_sustained"]
         fp32_pipe = {}
-        if not (prob.precision == "bf16" and H == 128):
+        if not (prob.precision == "bf16" and H in (128, 256)):
             # the SIMT edge kernels (fp32 mode, and bf16 mode at H != 128) run the
             # edge GEMMs on the FP32 pipe (FFMA), whose peak MEASURED_PEAKS.json
             # does not hold: the nominal figure, SMs x 128 FMA lanes x 2 flop x
@@ -518,7 +531,7 @@ def run_b200(args):
             "model_tflops": step_flops / (ms_per_step * 1e-3) / 1e12,
             "e2e": e2e,
             "gpu_launches": launches,
-            "roofline": {"kernel": "edge_bwd", "bound": "tensor", "achieved": achieved,
+            "roofline": {"kernel": kname, "bound": "tensor", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peaks['source']} bf16 sustained",
                          "traffic": (ncu_traffic(args.config, "edge_bwd", prob.edges_rank)

@@ -110,10 +110,10 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     gr = g_a1 @ wr
     self_loop = (row == col).to(d)
     gdl = g_trans * (phi * inv * (1 - self_loop))[:, None] + 2 * gr[:, None] * dlt
-    # the tensor-core path (bf16, H = 128, no edge attributes, no attention)
-    # stores g_a1 in bf16 for the dst / src row sums (edge_tc.cu backward);
-    # fp32 elsewhere
-    tc_path = on and H == 128 and (edge_attr is None or edge_attr.shape[1] == 0) and not attention
+    # the tensor-core paths (bf16, H = 128 fused edge kernels, H = 256 edge-row
+    # GEMMs; no edge attributes, no attention) store g_a1 in bf16 for the
+    # dst / src row sums (edge_tc.cu, edge_rows.cu); fp32 elsewhere
+    tc_path = on and H in (128, 256) and (edge_attr is None or edge_attr.shape[1] == 0) and not attention
     g_a1s = _bf(g_a1, tc_path)
     S_dst = segment_sum(g_a1s, row, N)
     S_src = segment_sum(g_a1s, col, N)

@@ -1,0 +1,919 @@
+// EGNN edge MLPs of a bf16-GEMM layer with H = 256 as edge-row GEMMs on the
+// 5th-generation tensor cores.
+//
+// At H = 256 the two bf16 weight tiles of the fused edge kernels (W2 and
+// W_c1, 128 KB each) do not fit one CTA's shared memory together, so each
+// per-edge product runs as its own persistent GEMM over 128-edge tiles with
+// ONE weight matrix resident in shared memory (128 KB) and a fused epilogue:
+//
+//   forward   u1 = silu(P_i + Q_j + w_r r)                gather kernel -> U
+//             a2 = U W2^T;  m = silu(a2 + b2)             GEMM -> Mb (bf16) and fp32 m
+//                                                         (backward: fp16 silu'(a2 + b2))
+//             c1 = Mb Wc1^T; phi = wc2 . silu(c1 + bc1)   GEMM -> phi
+//             agg_i = sum m, x'_i = x_i + s_i sum d phi   row kernel
+//   backward  (recompute U, a2, m, c1 as above)
+//             g_c1 = gphi wc2 silu'(c1)                   GEMM epilogue -> Gc1 (bf16)
+//             g_a2 = (Gc1 Wc1 + g_agg[i]) silu'(a2)       GEMM -> Ga2 (bf16)
+//             g_a1 = (Ga2 W2) silu'(a1)                   GEMM -> bf16 rows, g_d
+//             dWc1 = Gc1^T Mb, dW2 = Ga2^T U              split-K GEMMs over the edges
+//
+// The rounding points are those of the fused kernels (bf16 GEMM operands u1,
+// m, g_c1, g_a2 and weights; fp32 accumulation; fp32 m in the row sums; bf16
+// dL/da1 rows for the node pass; silu'(a2) kept in fp16 between kernels, as
+// the fused kernels stage it), so the same rounding-exact model covers both
+// paths.
+//
+// Operands move as "tiles": the bf16 (E, 256) matrices are stored tile-major,
+// 64 KB per 128 edges, as four 16 KB column blocks of 128 rows x 64 features
+// in the 128-byte swizzle (16-byte chunk c of row r at position c ^ (r % 8)),
+// exactly the shared-memory image the MMA reads.  One cp.async.bulk copy
+// (no tensor map, no multicast) moves a block; an mbarrier counts its bytes.
+//
+// GEMM kernel (one CTA per SM, 576 threads): warp 0 streams the A blocks of
+// the CTA's tiles through a 4-stage ring, warp 1 issues tcgen05.mma (M = 128
+// edges, N = 256, K = 16 per instruction) into one of two TMEM accumulators
+// (2 x 256 columns), warps 2..17 run the epilogue of tile j while the MMAs of
+// tile j + 1 run.  Every wait is bounded (2 s of global time); a thread that
+// gives up raises a CTA abort flag that every other wait honours, the count
+// is reported by egnn_device_status, and the CTA frees its TMEM and exits.
+// Column sums (bias and w_c2 / w_r gradients) are per-warp transposing
+// reductions kept per thread across tiles, then added per CTA in fixed order:
+// results are bit-deterministic for a given GPU.
+#include <algorithm>
+
+#include "edge_rows.cuh"
+#include "tc.cuh"
+
+namespace egnn {
+
+__device__ int g_rows_timeouts = 0;
+
+namespace {
+
+using namespace tc;
+
+constexpr int kH = 256;
+constexpr int kTile = 128 * kH * 2;   // bytes per 128-edge tile
+constexpr int kBlk = 128 * 128;       // bytes per 64-feature column block of a tile
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for phase `parity` of `bar`: false once 2 s have passed (the CTA's
+// abort flag is raised and the event counted) or, when `abort_flag` is
+// given, once another thread has raised it.
+__device__ __noinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* raise_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort_flag && *abort_flag) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      *reinterpret_cast<volatile int*>(raise_flag) = 1;
+      atomicAdd(&g_rows_timeouts, 1);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bulk copy global -> shared (16-byte aligned, size a multiple of 16), the
+// bytes counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Named barriers of the 16 epilogue warps (512 threads).
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+__device__ __forceinline__ bool epi_any(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred q, o;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred o, 2, 512, q;\n\t"
+      "selp.u32 %0, 1, 0, o;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)p)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+// 32 values = features 64 cs + 32 p .. + 31 of row `el` of the tile at `tb`.
+__device__ __forceinline__ void st_tile_piece(char* tb, int el, int cs, int p, const float (&v)[32]) {
+  char* rowp = tb + cs * kBlk + el * 128;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 u = make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                               pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+    *reinterpret_cast<uint4*>(rowp + ((((p << 2) + c) ^ (el & 7)) << 4)) = u;
+  }
+}
+
+__device__ __forceinline__ void st_f32_piece(float* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+}
+
+__device__ __forceinline__ void st_f16_piece(__half* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int t = 0; t < 32; t += 8) {
+    uint32_t w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const __half2 h = __floats2half2_rn(v[t + 2 * u], v[t + 2 * u + 1]);
+      w[u] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(dst + t) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// Sum over the warp's 32 lanes of x[c]; lane l returns the sum for c = l.
+__device__ __forceinline__ float colsum32(float (&x)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const bool up = lane & off;
+      const float send = up ? x[i] : x[i + off];
+      const float keep = up ? x[i + off] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return x[0];
+}
+
+// (256 x 256) fp32 nn.Linear weight -> bf16 tile with rows = out, columns = in
+// (K-major operand of x W^T, MN-major operand of g W).
+__device__ void load_w256(char* tile, const float* __restrict__ W) {
+  for (int idx = threadIdx.x; idx < kH * kH / 8; idx += blockDim.x) {
+    const int o = idx / (kH / 8), c8 = (idx % (kH / 8)) * 8;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(W + o * kH + c8));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(W + o * kH + c8 + 4));
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    st_row8_bf16(tile, kH, o, c8, v);
+  }
+}
+
+// ---- gather: geometry and u1 = bf16(silu(P_i + Q_j + w_r r)) -------------------------
+// One warp per edge of the padded tile range; lane owns features 8 lane .. + 7
+// (16 bytes of the tile row).  Padding rows (e >= E) are zero.
+__global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, const int32_t* __restrict__ row_idx,
+                                                     const int32_t* __restrict__ col_idx,
+                                                     const float4* __restrict__ xp, const float* __restrict__ PQ,
+                                                     const float* __restrict__ wr, char* __restrict__ U,
+                                                     float4* __restrict__ geo) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int64_t e = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (e >= Epad) return;
+  float u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (e < E) {
+    const int i = row_idx[e], j = col_idx[e];
+    const float4 xi = xp[i], xj = xp[j];
+    const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
+    const float r = dx * dx + dy * dy + dz * dz;
+    if (lane == 0) geo[e] = make_float4(dx, dy, dz, r);
+    const float* P = PQ + (int64_t)i * 2 * kH + 8 * lane;
+    const float* Q = PQ + (int64_t)j * 2 * kH + kH + 8 * lane;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float4 p = ldg4(P + 4 * h), q = ldg4(Q + 4 * h), w = ldg4(wr + 8 * lane + 4 * h);
+      u[4 * h + 0] = silu_edge(fmaf(w.x, r, p.x + q.x));
+      u[4 * h + 1] = silu_edge(fmaf(w.y, r, p.y + q.y));
+      u[4 * h + 2] = silu_edge(fmaf(w.z, r, p.z + q.z));
+      u[4 * h + 3] = silu_edge(fmaf(w.w, r, p.w + q.w));
+    }
+  }
+  const int64_t t = e >> 7;
+  const int rl = (int)(e & 127), blk = lane >> 3, ch = lane & 7;
+  const uint4 pk = make_uint4(pack_bf16x2(u[0], u[1]), pack_bf16x2(u[2], u[3]), pack_bf16x2(u[4], u[5]),
+                              pack_bf16x2(u[6], u[7]));
+  *reinterpret_cast<uint4*>(U + t * kTile + blk * kBlk + rl * 128 + ((ch ^ (rl & 7)) << 4)) = pk;
+}
+
+// ---- forward row sums: agg_i = sum m_e, x'_i = x_i + s_i sum d_e inv_e phi_e -----------
+// One warp per node, its CSR row in order (four rows in flight).
+__global__ void __launch_bounds__(256) rows_agg_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
+                                                       const float* __restrict__ M32, const float* __restrict__ phi,
+                                                       const float4* __restrict__ geo, const float* __restrict__ x,
+                                                       int flags, float* __restrict__ agg,
+                                                       float* __restrict__ x_out) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int64_t v = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (v >= N) return;
+  const bool normalize = flags & EGNN_FLAG_NORMALIZE;
+  const int k0 = row_ptr[v], k1 = row_ptr[v + 1];
+  float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float xs = 0.f;
+  auto xterm = [&](int64_t k) {
+    const float4 g = __ldg(geo + k);
+    const float inv = normalize ? 1.f / (sqrtf(g.w) + 1e-8f) : 1.f;
+    const float d = lane == 0 ? g.x : (lane == 1 ? g.y : g.z);
+    return (d * inv) * __ldg(phi + k);
+  };
+  int k = k0;
+  for (; k + 4 <= k1; k += 4) {
+    float4 a[4][2];
+    float xt[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float* r = M32 + (int64_t)(k + u) * kH + 8 * lane;
+      a[u][0] = ldg4(r);
+      a[u][1] = ldg4(r + 4);
+      xt[u] = lane < 3 ? xterm(k + u) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      s[0] += a[u][0].x; s[1] += a[u][0].y; s[2] += a[u][0].z; s[3] += a[u][0].w;
+      s[4] += a[u][1].x; s[5] += a[u][1].y; s[6] += a[u][1].z; s[7] += a[u][1].w;
+      xs += xt[u];
+    }
+  }
+  for (; k < k1; ++k) {
+    const float* r = M32 + (int64_t)k * kH + 8 * lane;
+    const float4 a0 = ldg4(r), a1 = ldg4(r + 4);
+    s[0] += a0.x; s[1] += a0.y; s[2] += a0.z; s[3] += a0.w;
+    s[4] += a1.x; s[5] += a1.y; s[6] += a1.z; s[7] += a1.w;
+    if (lane < 3) xs += xterm(k);
+  }
+  float* o = agg + v * kH + 8 * lane;
+  *reinterpret_cast<float4*>(o) = make_float4(s[0], s[1], s[2], s[3]);
+  *reinterpret_cast<float4*>(o + 4) = make_float4(s[4], s[5], s[6], s[7]);
+  if (lane < 3) {
+    const float sc = (flags & EGNN_FLAG_COORDS_SUM) ? 1.f : 1.f / (float)max(k1 - k0, 1);
+    x_out[v * 3 + lane] = x[v * 3 + lane] + xs * sc;
+  }
+}
+
+// ---- persistent edge-row GEMM with fused epilogues ------------------------------------
+enum { EPI_M_FWD = 0, EPI_M_BWD, EPI_PHI, EPI_GC1, EPI_GA2, EPI_GA1 };
+
+struct RowsGemmArgs {
+  const char* A = nullptr;        // tiles of the A operand (K-major, K = 256)
+  const float* W = nullptr;       // (256, 256) fp32 weight [out][in]
+  int64_t E = 0, ntiles = 0;
+  const float* bias = nullptr;    // b2 (EPI_M_*) or bc1 (EPI_PHI, EPI_GC1)
+  const float* wc2 = nullptr;
+  const float* wr = nullptr;
+  char* outb = nullptr;           // tiles written by the epilogue
+  float* outf = nullptr;          // (E, 256) fp32 m (EPI_M_FWD)
+  __half* outh = nullptr;         // (E, 256) fp16 silu'(a2 + b2) (EPI_M_BWD)
+  __nv_bfloat16* gstore = nullptr;
+  float* phi = nullptr;
+  const float4* geo = nullptr;
+  float4* gdstore = nullptr;
+  const __half* aux = nullptr;    // (E, 256) fp16 silu'(a2 + b2) (EPI_GA2)
+  const float* g_agg = nullptr;
+  int64_t ld_gagg = 0;
+  const float* PQ = nullptr;
+  const int32_t* row_ptr = nullptr;
+  const int32_t* row_idx = nullptr;
+  const int32_t* col_idx = nullptr;
+  const float* gx_out = nullptr;
+  float* part = nullptr;
+  int64_t PF = 0;
+  int flags = 0;
+};
+
+constexpr int GM_NTH = 576;   // warp 0: loads; warp 1: MMA + TMEM; warps 2..17: epilogue
+constexpr int GM_S = 4;       // A ring stages (one 16 KB block each)
+struct GmLayout {
+  static constexpr int W = 0;
+  static constexpr int A = kH * kH * 2;               // 131072
+  static constexpr int BAR = A + GM_S * kBlk;         // 196608
+  static constexpr int RED = BAR + 256;               // float[2][4][128]
+  static constexpr size_t BYTES = RED + 2 * 4 * 128 * 4 + 1024;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
+  constexpr bool BK = EPI <= EPI_GC1;   // B = W as [n][k] (x W^T), else W as [k][n] (g W)
+  constexpr uint32_t IDESC = make_idesc_bf16(128, kH, 0, BK ? 0 : 1);
+  constexpr int NV = EPI == EPI_GC1 ? 2 : (EPI == EPI_GA2 || EPI == EPI_GA1) ? 1 : 0;
+  extern __shared__ __align__(1024) char rg_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(rg_raw) + 1023) & ~uintptr_t(1023));
+  char* Wt = sm + GmLayout::W;
+  char* Ast = sm + GmLayout::A;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + GmLayout::BAR);
+  uint64_t* empty = full + GM_S;
+  uint64_t* accf = empty + GM_S;
+  uint64_t* acce = accf + 2;
+  uint64_t* fin = acce + 2;
+  uint32_t* tmem_s = reinterpret_cast<uint32_t*>(fin + 1);
+  int* abort_s = reinterpret_cast<int*>(tmem_s + 1);
+  float* red = reinterpret_cast<float*>(sm + GmLayout::RED);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t G = gridDim.x;
+  const int64_t ntl = (int64_t)blockIdx.x < a.ntiles ? (a.ntiles - 1 - blockIdx.x) / G + 1 : 0;
+
+  // prologue (parameters only, before the wait on the previous kernel)
+  load_w256(Wt, a.W);
+  if (warp == 1) tmem_alloc(tmem_s, 512);
+  if (tid == 0) {
+    for (int s = 0; s < GM_S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&accf[0], 1);
+    mbar_init(&accf[1], 1);
+    mbar_init(&acce[0], 16);
+    mbar_init(&acce[1], 16);
+    mbar_init(fin, 1);
+    *abort_s = 0;
+    fence_mbar_init();
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_s;
+  volatile int* abort_f = abort_s;
+  pdl_enter();
+
+  float acc0[2] = {0.f, 0.f}, acc1[2] = {0.f, 0.f};   // column sums (epilogue threads)
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- producer: A blocks of the CTA's tiles through the ring
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t j = 0; j < ntl && ok; ++j) {
+        const char* src = a.A + (size_t)(blockIdx.x + j * G) * kTile;
+        for (int b = 0; b < 4; ++b, ++it) {
+          const int s = it & (GM_S - 1);
+          if (it >= GM_S && !(ok = wait_bar(&empty[s], ((it / GM_S) - 1) & 1, abort_f, abort_s))) break;
+          mbar_expect_tx(&full[s], kBlk);
+          bulk_g2s(Ast + s * kBlk, src + b * kBlk, kBlk, &full[s]);
+        }
+      }
+      if (!ok)   // copies still in flight land before the CTA exits
+        for (uint32_t k = it > GM_S ? it - GM_S : 0; k < it; ++k)
+          wait_bar(&full[k & (GM_S - 1)], (k / GM_S) & 1, nullptr, abort_s);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      const uint32_t wb = smem_u32(Wt), ab = smem_u32(Ast);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t j = 0; j < ntl && ok; ++j) {
+        const int buf = (int)(j & 1);
+        if (j >= 2 && !(ok = wait_bar(&acce[buf], ((j >> 1) - 1) & 1, abort_f, abort_s))) break;
+        fence_after_sync();
+        const uint32_t d = tmem + buf * kH;
+        for (int b = 0; b < 4; ++b, ++it) {
+          const int s = it & (GM_S - 1);
+          if (!(ok = wait_bar(&full[s], (it / GM_S) & 1, abort_f, abort_s))) break;
+          fence_after_sync();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = make_desc(ab + s * kBlk + kk * 32, 16, 1024);
+            const uint64_t bd = BK ? make_desc(wb + b * (kH * 128) + kk * 32, 16, 1024)
+                                   : make_desc(wb + (4 * b + kk) * 2048, kH * 128, 1024);
+            mma_bf16(d, ad, bd, IDESC, (b | kk) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&accf[buf]);
+      }
+      mma_commit(fin);   // every MMA of this thread has completed once fin flips
+      wait_bar(fin, 0, nullptr, abort_s);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: thread = (edge row el, 64-feature slice cs)
+    const int q = warp & 3, cs = (warp - 2) >> 2, el = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const bool tanh_on = a.flags & EGNN_FLAG_TANH;
+    const bool normalize = a.flags & EGNN_FLAG_NORMALIZE;
+    const bool csum = a.flags & EGNN_FLAG_COORDS_SUM;
+    for (int64_t j = 0; j < ntl; ++j) {
+      const int buf = (int)(j & 1);
+      const bool ok = wait_bar(&accf[buf], (j >> 1) & 1, abort_f, abort_s);
+      if (epi_any(!ok)) break;
+      fence_after_sync();
+      const int64_t t = blockIdx.x + j * G;
+      const int64_t e = t * 128 + el;
+      const bool valid = e < a.E;
+      const uint32_t tacc = tmem + lane_base + buf * kH + cs * 64;
+      char* tb = a.outb ? a.outb + t * kTile : nullptr;
+      float* rbuf = red + (j & 1) * 512;
+      auto release = [&]() {
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive1(&acce[buf]);
+      };
+
+      if constexpr (EPI == EPI_M_FWD || EPI == EPI_M_BWD) {
+#pragma unroll 1
+        for (int p = 0; p < 2; ++p) {
+          float v[32];
+          tmem_ld32(tacc + 32 * p, v);
+          if (p == 1) release();
+          const int n0 = cs * 64 + 32 * p;
+#pragma unroll
+          for (int t4 = 0; t4 < 32; t4 += 4) {
+            const float4 b4 = ldg4(a.bias + n0 + t4);
+            v[t4] += b4.x; v[t4 + 1] += b4.y; v[t4 + 2] += b4.z; v[t4 + 3] += b4.w;
+          }
+          if constexpr (EPI == EPI_M_BWD) {
+            float d2[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              float yy, dy;
+              silu_grad_edge(v[k], yy, dy);
+              v[k] = valid ? yy : 0.f;
+              d2[k] = dy;
+            }
+            if (valid) st_f16_piece(a.outh + e * kH + n0, d2);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = valid ? silu_edge(v[k]) : 0.f;
+            if (valid) st_f32_piece(a.outf + e * kH + n0, v);
+          }
+          st_tile_piece(tb, el, cs, p, v);
+        }
+      } else if constexpr (EPI == EPI_PHI) {
+        float part = 0.f;
+#pragma unroll 1
+        for (int p = 0; p < 2; ++p) {
+          float v[32];
+          tmem_ld32(tacc + 32 * p, v);
+          if (p == 1) release();
+          const int n0 = cs * 64 + 32 * p;
+#pragma unroll
+          for (int t4 = 0; t4 < 32; t4 += 4) {
+            const float4 b4 = ldg4(a.bias + n0 + t4), w4 = ldg4(a.wc2 + n0 + t4);
+            part += w4.x * silu_edge(v[t4] + b4.x);
+            part += w4.y * silu_edge(v[t4 + 1] + b4.y);
+            part += w4.z * silu_edge(v[t4 + 2] + b4.z);
+            part += w4.w * silu_edge(v[t4 + 3] + b4.w);
+          }
+        }
+        rbuf[cs * 128 + el] = part;
+        epi_sync();
+        if (cs == 0 && valid) {
+          float f = rbuf[el] + rbuf[128 + el] + rbuf[256 + el] + rbuf[384 + el];
+          if (tanh_on) f = tanhf(f);
+          a.phi[e] = f;
+        }
+      } else if constexpr (EPI == EPI_GC1) {
+        // pass 1: phi_e (row sum over the four slices)
+        float part = 0.f;
+#pragma unroll 1
+        for (int p = 0; p < 2; ++p) {
+          float v[32];
+          tmem_ld32(tacc + 32 * p, v);
+          const int n0 = cs * 64 + 32 * p;
+#pragma unroll
+          for (int t4 = 0; t4 < 32; t4 += 4) {
+            const float4 b4 = ldg4(a.bias + n0 + t4), w4 = ldg4(a.wc2 + n0 + t4);
+            part += w4.x * silu_edge(v[t4] + b4.x);
+            part += w4.y * silu_edge(v[t4 + 1] + b4.y);
+            part += w4.z * silu_edge(v[t4 + 2] + b4.z);
+            part += w4.w * silu_edge(v[t4 + 3] + b4.w);
+          }
+        }
+        rbuf[cs * 128 + el] = part;
+        epi_sync();
+        float f = rbuf[el] + rbuf[128 + el] + rbuf[256 + el] + rbuf[384 + el];
+        if (tanh_on) f = tanhf(f);
+        float gphi = 0.f;
+        if (valid) {
+          const int i = a.row_idx[e];
+          const float4 gq = a.geo[e];
+          const float sc = csum ? 1.f : 1.f / (float)max(a.row_ptr[i + 1] - a.row_ptr[i], 1);
+          const float inv = normalize ? 1.f / (sqrtf(gq.w) + 1e-8f) : 1.f;
+          const float* gx = a.gx_out + (int64_t)i * 3;
+          gphi = (gx[0] * sc * gq.x + gx[1] * sc * gq.y + gx[2] * sc * gq.z) * inv;
+          if (tanh_on) gphi *= 1.f - f * f;
+          if (cs == 0) a.phi[e] = f;
+        }
+        // pass 2: g_c1 = gphi wc2 silu'(c1) -> Gc1; column sums of g_c1 and gphi silu(c1)
+#pragma unroll 1
+        for (int p = 0; p < 2; ++p) {
+          float v[32], y[32];
+          tmem_ld32(tacc + 32 * p, v);
+          if (p == 1) release();
+          const int n0 = cs * 64 + 32 * p;
+#pragma unroll
+          for (int t4 = 0; t4 < 32; t4 += 4) {
+            const float4 b4 = ldg4(a.bias + n0 + t4), w4 = ldg4(a.wc2 + n0 + t4);
+            const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float yy, dy;
+              silu_grad_edge(v[t4 + u] + bb[u], yy, dy);
+              v[t4 + u] = gphi * ww[u] * dy;
+              y[t4 + u] = gphi * yy;
+            }
+          }
+          st_tile_piece(tb, el, cs, p, v);
+          acc0[p] += colsum32(v);
+          acc1[p] += colsum32(y);
+        }
+      } else if constexpr (EPI == EPI_GA2) {
+        const int i = valid ? a.row_idx[e] : 0;
+#pragma unroll 1
+        for (int p = 0; p < 2; ++p) {
+          float v[32];
+          tmem_ld32(tacc + 32 * p, v);
+          if (p == 1) release();
+          const int n0 = cs * 64 + 32 * p;
+          const float* ga = a.g_agg + (int64_t)i * a.ld_gagg + n0;
+          const __half* d2p = a.aux + (valid ? e : 0) * kH + n0;
+#pragma unroll
+          for (int t8 = 0; t8 < 32; t8 += 8) {
+            const float4 g0 = ldg4(ga + t8), g1 = ldg4(ga + t8 + 4);
+            const uint4 hz = __ldg(reinterpret_cast<const uint4*>(d2p + t8));
+            const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            const uint32_t hw[4] = {hz.x, hz.y, hz.z, hz.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hw[u]));
+              v[t8 + 2 * u] = valid ? (v[t8 + 2 * u] + gg[2 * u]) * dd.x : 0.f;
+              v[t8 + 2 * u + 1] = valid ? (v[t8 + 2 * u + 1] + gg[2 * u + 1]) * dd.y : 0.f;
+            }
+          }
+          st_tile_piece(tb, el, cs, p, v);
+          acc0[p] += colsum32(v);
+        }
+      } else {   // EPI_GA1
+        int i = 0, jn = 0;
+        float4 gq = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) { i = a.row_idx[e]; jn = a.col_idx[e]; gq = a.geo[e]; }
+        float grp = 0.f;
+#pragma unroll 1
+        for (int p = 0; p < 2; ++p) {
+          float v[32], rr[32];
+          tmem_ld32(tacc + 32 * p, v);
+          if (p == 1) release();
+          const int n0 = cs * 64 + 32 * p;
+          const float* P = a.PQ + (int64_t)i * 2 * kH + n0;
+          const float* Q = a.PQ + (int64_t)jn * 2 * kH + kH + n0;
+#pragma unroll
+          for (int t4 = 0; t4 < 32; t4 += 4) {
+            const float4 p4 = ldg4(P + t4), q4 = ldg4(Q + t4), w4 = ldg4(a.wr + n0 + t4);
+            const float pp[4] = {p4.x, p4.y, p4.z, p4.w}, qq[4] = {q4.x, q4.y, q4.z, q4.w},
+                        ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float yy, dy;
+              silu_grad_edge(fmaf(ww[u], gq.w, pp[u] + qq[u]), yy, dy);
+              const float g = valid ? v[t4 + u] * dy : 0.f;
+              v[t4 + u] = g;
+              grp += g * ww[u];
+              rr[t4 + u] = g * gq.w;
+            }
+          }
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(a.gstore + e * kH + n0);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              dst[c] = make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                                  pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+          }
+          acc0[p] += colsum32(rr);
+        }
+        rbuf[cs * 128 + el] = grp;
+        epi_sync();
+        if (cs == 0 && valid) {
+          const float gr = rbuf[el] + rbuf[128 + el] + rbuf[256 + el] + rbuf[384 + el];
+          const float sc = csum ? 1.f : 1.f / (float)max(a.row_ptr[i + 1] - a.row_ptr[i], 1);
+          const float inv = normalize ? 1.f / (sqrtf(gq.w) + 1e-8f) : 1.f;
+          const float coef = (i == jn) ? 0.f : a.phi[e] * inv;   // self-loop: no coordinate gradient
+          const float* gx = a.gx_out + (int64_t)i * 3;
+          a.gdstore[e] = make_float4(gx[0] * sc * coef + 2.f * gr * gq.x, gx[1] * sc * coef + 2.f * gr * gq.y,
+                                     gx[2] * sc * coef + 2.f * gr * gq.z, 0.f);
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- per-CTA column sums -> partial slots (the A ring is idle now)
+  if constexpr (NV > 0) {
+    float* cs_s = reinterpret_cast<float*>(Ast);   // [4 q][NV][256]
+    if (warp >= 2) {
+      const int q = warp & 3, cs = (warp - 2) >> 2;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int n = cs * 64 + 32 * p + lane;
+        cs_s[(q * NV + 0) * kH + n] = acc0[p];
+        if (NV == 2) cs_s[(q * NV + 1) * kH + n] = acc1[p];
+      }
+    }
+    __syncthreads();
+    const int64_t HH = (int64_t)kH * kH;
+    for (int idx = tid; idx < NV * kH; idx += GM_NTH) {
+      const int vv = idx / kH, n = idx % kH;
+      const float s = cs_s[(0 * NV + vv) * kH + n] + cs_s[(1 * NV + vv) * kH + n] + cs_s[(2 * NV + vv) * kH + n] +
+                      cs_s[(3 * NV + vv) * kH + n];
+      int64_t slot;
+      if (EPI == EPI_GC1) slot = vv == 0 ? 2 * HH : 2 * HH + 2 * kH;   // gbc1, gwc2
+      else if (EPI == EPI_GA2) slot = 2 * HH + kH;                     // gb2
+      else slot = 2 * HH + 3 * kH;                                      // gwr
+      a.part[(int64_t)blockIdx.x * a.PF + slot + n] = s;
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ---- weight gradients: D = G^T X over the edges (split-K, one slice per CTA) ----------
+// Each CTA takes a contiguous range of tiles in 64-edge half tiles; one
+// thread streams them through a 3-stage ring (bulk copies of the 8 KB
+// half blocks) and issues the MMAs (A = G^T and B = X both MN-major, two
+// M = 128 halves of the 256 output rows in 2 x 256 TMEM columns).
+constexpr int WG_NTH = 256, WG_S = 3, WG_STAGE = 65536;
+constexpr size_t WG_BYTES = WG_S * WG_STAGE + 256 + 1024;
+
+__global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __restrict__ Gt, const char* __restrict__ Xt,
+                                                               int64_t ntiles, float* __restrict__ part, int64_t PF,
+                                                               int64_t off) {
+  constexpr uint32_t IDESC = make_idesc_bf16(128, kH, 1, 1);
+  extern __shared__ __align__(1024) char wg_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(wg_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + WG_S * WG_STAGE);
+  uint64_t* empty = full + WG_S;
+  uint64_t* done = empty + WG_S;
+  uint32_t* tmem_s = reinterpret_cast<uint32_t*>(done + 1);
+  int* abort_s = reinterpret_cast<int*>(tmem_s + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t tpc = (ntiles + gridDim.x - 1) / gridDim.x;
+  const int64_t t0 = std::min<int64_t>(ntiles, (int64_t)blockIdx.x * tpc);
+  const int64_t t1 = std::min<int64_t>(ntiles, t0 + tpc);
+  const int nslab = (int)(2 * (t1 - t0));
+
+  if (warp == 0) tmem_alloc(tmem_s, 512);
+  if (tid == 0) {
+    for (int s = 0; s < WG_S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_s = 0;
+    fence_mbar_init();
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_s;
+  volatile int* abort_f = abort_s;
+  pdl_enter();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int filled = 0, used = 0;
+      bool ok = true;
+      for (int it = 0; it < nslab + WG_S - 1 && ok; ++it) {
+        if (it < nslab) {
+          const int s = it % WG_S;
+          if (it >= WG_S && !(ok = wait_bar(&empty[s], ((it / WG_S) - 1) & 1, abort_f, abort_s))) break;
+          char* st = sm + s * WG_STAGE;
+          mbar_expect_tx(&full[s], WG_STAGE);
+          const size_t src = (size_t)(t0 + (it >> 1)) * kTile + (size_t)(it & 1) * (kBlk / 2);
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            bulk_g2s(st + b * (kBlk / 2), Gt + src + b * kBlk, kBlk / 2, &full[s]);
+            bulk_g2s(st + WG_STAGE / 2 + b * (kBlk / 2), Xt + src + b * kBlk, kBlk / 2, &full[s]);
+          }
+          filled = it + 1;
+        }
+        const int k = it - (WG_S - 1);
+        if (k >= 0) {
+          const int s = k % WG_S;
+          if (!(ok = wait_bar(&full[s], (k / WG_S) & 1, abort_f, abort_s))) break;
+          used = k + 1;
+          fence_after_sync();
+          const uint32_t gb = smem_u32(sm + s * WG_STAGE), xb = gb + WG_STAGE / 2;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+            for (int mh = 0; mh < 2; ++mh)
+              mma_bf16(tmem + mh * kH, make_desc(gb + mh * kBlk + kk * 2048, kBlk / 2, 1024),
+                       make_desc(xb + kk * 2048, kBlk / 2, 1024), IDESC, (k | kk) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+      }
+      if (!ok)
+        for (int k = used; k < filled; ++k) wait_bar(&full[k % WG_S], (k / WG_S) & 1, nullptr, abort_s);
+      mma_commit(done);
+    }
+    __syncwarp();
+  }
+  wait_bar(done, 0, nullptr, abort_s);
+  fence_after_sync();
+  {
+    const int q = warp & 3, mh = warp >> 2;
+    const int m = mh * 128 + q * 32 + lane;
+    float* dst = part + (int64_t)blockIdx.x * PF + off + (int64_t)m * kH;
+#pragma unroll 1
+    for (int c = 0; c < kH / 32; ++c) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + mh * kH + 32 * c, v);
+      if (nslab == 0) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = 0.f;
+      }
+      st_f32_piece(dst + 32 * c, v);
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+template <int EPI>
+int launch_gemm(const RowsGemmArgs& a, int G, cudaStream_t s, const char* name) {
+  constexpr size_t bytes = GmLayout::BYTES;
+  static uint64_t attr_set = 0;
+  const uint64_t bit = device_bit();
+  if (!(attr_set & bit)) {
+    EGNN_CHECK_CUDA(
+        cudaFuncSetAttribute(rows_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    attr_set |= bit;
+  }
+  {
+    TimerScope ts(name, s);
+    EGNN_CHECK_CUDA(launch_pdl(rows_gemm_kernel<EPI>, dim3(G), dim3(GM_NTH), bytes, s, a));
+  }
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+int launch_u(const EdgeCommon& a, const RowsBufs& b, cudaStream_t s) {
+  const int64_t Epad = rows_tiles(a.E) * 128;
+  if (Epad == 0) return EGNN_OK;
+  TimerScope ts("edge_rows_u", s);
+  EGNN_CHECK_CUDA(launch_pdl(rows_u_kernel, dim3((unsigned)(Epad / 8)), dim3(256), 0, s, a.E, Epad, a.row_idx,
+                             a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo));
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+RowsGemmArgs gemm_common(const EdgeCommon& a, const RowsBufs& b) {
+  RowsGemmArgs g;
+  g.E = a.E;
+  g.ntiles = rows_tiles(a.E);
+  g.wc2 = a.wc2;
+  g.wr = a.wr;
+  g.geo = b.geo;
+  g.phi = b.phi;
+  g.PQ = a.PQ;
+  g.row_ptr = a.row_ptr;
+  g.row_idx = a.row_idx;
+  g.col_idx = a.col_idx;
+  g.part = b.part;
+  g.PF = edge_part_floats(kH, 0);
+  g.flags = a.flags;
+  return g;
+}
+
+}  // namespace
+
+bool edge_rows_supported(int H, int d, int flags, int precision) {
+  return precision == EGNN_PREC_BF16 && H == kH && d == 0 && !(flags & EGNN_FLAG_ATTENTION);
+}
+
+int64_t rows_tiles(int64_t E) { return (E + 127) / 128; }
+
+int rows_grid(int64_t E, int num_sms) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>(num_sms, rows_tiles(E)));
+}
+
+RowsBufs carve_rows(Carver& c, int64_t E, int H, bool bwd, int num_sms) {
+  RowsBufs b;
+  const size_t tiles = (size_t)std::max<int64_t>(rows_tiles(E), 1) * kTile;
+  const size_t En = (size_t)std::max<int64_t>(E, 1);
+  b.U = c.take<char>(tiles);
+  b.Mb = c.take<char>(tiles);
+  if (bwd) {
+    b.Gc1 = c.take<char>(tiles);
+    b.Ga2 = c.take<char>(tiles);
+    b.D2 = c.take<__half>(En * H);
+  } else {
+    b.M32 = c.take<float>(En * H);
+  }
+  b.phi = c.take<float>(En);
+  b.geo = c.take<float4>(En);
+  b.G = rows_grid(E, num_sms);
+  if (bwd) b.part = c.take<float>((size_t)b.G * edge_part_floats(H, 0));
+  return b;
+}
+
+int edge_fwd_rows(const EdgeFwdArgs& a, const RowsBufs& b, cudaStream_t s) {
+  if (a.E > 0) {
+    EGNN_TRY(launch_u(a, b, s));
+    RowsGemmArgs g = gemm_common(a, b);
+    g.A = b.U;
+    g.W = a.W2_src;
+    g.bias = a.b2;
+    g.outb = b.Mb;
+    g.outf = b.M32;
+    EGNN_TRY(launch_gemm<EPI_M_FWD>(g, b.G, s, "edge_rows_gemm"));
+    g.A = b.Mb;
+    g.W = a.Wc1_src;
+    g.bias = a.bc1;
+    g.outb = nullptr;
+    g.outf = nullptr;
+    EGNN_TRY(launch_gemm<EPI_PHI>(g, b.G, s, "edge_rows_gemm"));
+  }
+  if (a.N > 0) {
+    TimerScope ts("edge_rows_agg", s);
+    EGNN_CHECK_CUDA(launch_pdl(rows_agg_kernel, dim3((unsigned)((a.N + 7) / 8)), dim3(256), 0, s, a.N, a.row_ptr,
+                               b.M32, b.phi, b.geo, a.x, a.flags, a.agg, a.x_out));
+    EGNN_CHECK_LAUNCH();
+  }
+  return EGNN_OK;
+}
+
+int edge_bwd_rows(const EdgeBwdArgs& a, const RowsBufs& b, cudaStream_t s) {
+  RowsGemmArgs g = gemm_common(a, b);
+  if (a.E > 0) {
+    EGNN_TRY(launch_u(a, b, s));
+    g.A = b.U;
+    g.W = a.W2_src;
+    g.bias = a.b2;
+    g.outb = b.Mb;
+    g.outh = b.D2;
+    EGNN_TRY(launch_gemm<EPI_M_BWD>(g, b.G, s, "edge_rows_gemm"));
+  }
+  // the three gradient GEMMs also run without edges: they write the zero
+  // column-sum slots of the partials
+  g.A = b.Mb;
+  g.W = a.Wc1_src;
+  g.bias = a.bc1;
+  g.outb = b.Gc1;
+  g.outf = nullptr;
+  g.gx_out = a.gx_out;
+  EGNN_TRY(launch_gemm<EPI_GC1>(g, b.G, s, "edge_rows_gemm"));
+  g.A = b.Gc1;
+  g.bias = nullptr;
+  g.outb = b.Ga2;
+  g.aux = b.D2;
+  g.g_agg = a.g_agg;
+  g.ld_gagg = a.ld_gagg ? a.ld_gagg : kH;
+  EGNN_TRY(launch_gemm<EPI_GA2>(g, b.G, s, "edge_rows_gemm"));
+  g.A = b.Ga2;
+  g.W = a.W2_src;
+  g.outb = nullptr;
+  g.gstore = reinterpret_cast<__nv_bfloat16*>(a.gstore);
+  g.gdstore = a.gdstore;
+  EGNN_TRY(launch_gemm<EPI_GA1>(g, b.G, s, "edge_rows_gemm"));
+  return EGNN_OK;
+}
+
+int edge_wgrad_rows(int64_t E, const RowsBufs& b, cudaStream_t s) {
+  static uint64_t attr_set = 0;
+  const uint64_t bit = device_bit();
+  if (!(attr_set & bit)) {
+    EGNN_CHECK_CUDA(
+        cudaFuncSetAttribute(rows_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WG_BYTES));
+    attr_set |= bit;
+  }
+  const int64_t T = rows_tiles(E), PF = edge_part_floats(kH, 0), HH = (int64_t)kH * kH;
+  TimerScope ts("edge_rows_wgrad", s);
+  EGNN_CHECK_CUDA(launch_pdl(rows_wgrad_kernel, dim3(b.G), dim3(WG_NTH), WG_BYTES, s, (const char*)b.Gc1,
+                             (const char*)b.Mb, T, b.part, PF, (int64_t)0));
+  EGNN_CHECK_LAUNCH();
+  EGNN_CHECK_CUDA(launch_pdl(rows_wgrad_kernel, dim3(b.G), dim3(WG_NTH), WG_BYTES, s, (const char*)b.Ga2,
+                             (const char*)b.U, T, b.part, PF, HH));
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
+int rows_take_timeouts() {
+  int n = 0;
+  if (cudaMemcpyFromSymbol(&n, g_rows_timeouts, sizeof(int)) != cudaSuccess) return 0;
+  if (n) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_rows_timeouts, &zero, sizeof(int));
+  }
+  return n;
+}
+
+}  // namespace egnn

@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <climits>
 
+#include "edge_rows.cuh"
 #include "edge_simt.cuh"
 #include "edge_tc.cuh"
 #include "node_tc.cuh"
@@ -1110,15 +1111,15 @@ int edge_bwd_tc(int H, const EdgeBwdArgs& a, const EdgeGrid& g, cudaStream_t s) 
 int edge_node_pass_tc(int H, int64_t N, const int32_t* row_ptr, const int32_t* src_ptr, const int32_t* src_edge,
                       const void* gstore, const float4* gdstore, const float* gx_out, float* S_dst, float* S_src,
                       float* gx, cudaStream_t s) {
-  if (H != 128) return fail(EGNN_ERR_UNSUPPORTED, "tensor-core edge path built for H = 128");
+  if (H != 128 && H != 256) return fail(EGNN_ERR_UNSUPPORTED, "node pass built for H = 128, 256");
   if (N <= 0) return EGNN_OK;
   const int warps = 8;
   const unsigned blocks = (unsigned)((N + warps - 1) / warps);
   {
     TimerScope ts("node_pass", s);
-    EGNN_CHECK_CUDA(launch_pdl(node_pass_kernel<128>, dim3(blocks), dim3(warps * 32), 0, s, N, row_ptr, src_ptr,
-                               src_edge, static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, S_dst, S_src,
-                               gx));
+    auto kern = H == 128 ? node_pass_kernel<128> : node_pass_kernel<256>;
+    EGNN_CHECK_CUDA(launch_pdl(kern, dim3(blocks), dim3(warps * 32), 0, s, N, row_ptr, src_ptr, src_edge,
+                               static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, S_dst, S_src, gx));
   }
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
@@ -1137,6 +1138,7 @@ extern "C" int egnn_device_status(void* stream) {
     EGNN_CHECK_CUDA(cudaMemcpyToSymbol(g_tc_wait_timeouts, &zero, sizeof(int)));
   }
   n += node_tc_take_timeouts();
+  n += rows_take_timeouts();
   if (n != 0) {
     return fail(EGNN_ERR_CUDA, "%d tensor-core wait(s) timed out; results are invalid", n);
   }

@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "edge_rows.cuh"
 #include "edge_simt.cuh"
 #include "edge_tc.cuh"
 #include "node_gemm.cuh"
@@ -208,20 +209,23 @@ Saved carve_saved(Carver& c, int64_t N, int H) {
 
 struct FwdWs {
   Prep prep; float* carry; int32_t* carry_row; char* saved_tmp;
+  RowsBufs rows;   // edge-row GEMM path only
 };
 
 FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int64_t N = d->n_nodes, E = d->n_edges;
   const int H = d->hidden;
   FwdWs w;
+  const bool rows = edge_rows_supported(H, d->edge_attr_dim, d->flags, d->precision);
   w.prep = carve_prep(c, N, H, d->edge_attr_dim, false,
-                      edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
+                      rows || edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
   const int64_t G = max_ctas(E, H, num_sms);
   w.carry = c.take<float>((size_t)G * 2 * (H + 4));
   w.carry_row = c.take<int32_t>((size_t)G * 2);
   Carver probe(nullptr);
   carve_saved(probe, N, H);
   w.saved_tmp = c.take<char>(probe.size());   // used when the caller keeps no state
+  if (rows) w.rows = carve_rows(c, E, H, false, num_sms);
   return w;
 }
 
@@ -231,6 +235,7 @@ struct BwdWs {
   int32_t* carry_row; float* part; float* wpart;
   float* wpart_aux;   // split-K scratch of the weight gradients run on the side stream
   float* att_scr;     // attention only: per-CTA scratch of the SIMT edge backward
+  RowsBufs rows;      // edge-row GEMM path only
 };
 
 int64_t wpart_floats(int64_t N, int H) {
@@ -244,8 +249,9 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int64_t N = std::max<int64_t>(d->n_nodes, 1), E = d->n_edges;
   const int H = d->hidden;
   BwdWs w;
+  const bool rows = edge_rows_supported(H, d->edge_attr_dim, d->flags, d->precision);
   w.prep = carve_prep(c, N, H, d->edge_attr_dim, true,
-                      edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
+                      rows || edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
   w.g_n1pre = c.take<float>((size_t)N * H);
   w.ghg = c.take<float>((size_t)N * 2 * H);
   w.S_dst = c.take<float>((size_t)N * H);
@@ -256,10 +262,12 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int64_t G = max_ctas(E, H, num_sms);
   w.carry = c.take<float>((size_t)G * 2 * (H + 4));
   w.carry_row = c.take<int32_t>((size_t)G * 2);
-  w.part = c.take<float>((size_t)G * edge_part_floats(H, d->edge_attr_dim));
+  // the edge-row path keeps its per-CTA partials in w.rows.part
+  w.part = rows ? nullptr : c.take<float>((size_t)G * edge_part_floats(H, d->edge_attr_dim));
   w.wpart = c.take<float>((size_t)wpart_floats(N, H));
   w.wpart_aux = c.take<float>((size_t)wpart_floats(N, H));
   w.att_scr = (d->flags & EGNN_FLAG_ATTENTION) ? c.take<float>((size_t)(G * edge_att_scratch_floats(H))) : nullptr;
+  if (rows) w.rows = carve_rows(c, E, H, true, num_sms);
   return w;
 }
 
@@ -384,15 +392,17 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
   EGNN_TRY(gemm_pq(N, H, h, w.prep.WPQT, w.prep.bias2, sv.PQ, bf, s));
 
+  const bool rows = edge_rows_supported(H, dd, d->flags, d->precision);
   const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
-  EdgeGrid eg;
+  EdgeGrid eg{1, 0};
   if (tc) eg = edge_tc_grid(E, sms);
-  else EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));
+  else if (!rows) EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));
   EdgeFwdArgs a;
   fill_common(a, d, g, w.prep, sv.PQ, edge_attr, p, eg);
   a.carry = w.carry; a.carry_row = w.carry_row;
   a.x = x; a.agg = agg; a.x_out = x_out;
-  if (tc) EGNN_TRY(edge_fwd_tc(H, a, eg, s));
+  if (rows) EGNN_TRY(edge_fwd_rows(a, w.rows, s));
+  else if (tc) EGNN_TRY(edge_fwd_tc(H, a, eg, s));
   else EGNN_TRY(edge_fwd(H, bf, a, eg, s));
 
   GemmArgs n1;
@@ -480,10 +490,11 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   }
 
   // ---- edge backward: dst pass, fix-up, partial reduction, src pass
+  const bool rows = edge_rows_supported(H, dd, d->flags, d->precision);
   const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
-  EdgeGrid eg;
+  EdgeGrid eg{1, 0};
   if (tc) eg = edge_tc_grid(E, sms);
-  else EGNN_TRY(edge_grid(H, true, bf, E, sms, &eg));
+  else if (!rows) EGNN_TRY(edge_grid(H, true, bf, E, sms, &eg));
   EdgeBwdArgs a;
   fill_common(a, d, g, w.prep, sv.PQ, edge_attr, p, eg);
   a.carry = w.carry; a.carry_row = w.carry_row;
@@ -492,12 +503,20 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   a.gx_out = gx_out; a.g_agg = w.ghg + H; a.ld_gagg = 2 * H;
   a.S_dst = w.S_dst; a.gxd = w.gxd; a.gstore = w.gstore; a.gdstore = w.gdstore; a.part = w.part;
   a.att_scr = w.att_scr;
-  if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
-  else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
-  // per-CTA weight-gradient partials -> parameter gradients, on the side stream
-  EGNN_TRY(stream_fork(s, s2, side->ev[2]));
-  EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, s2));
-  if (tc)
+  if (rows) {
+    EGNN_TRY(edge_bwd_rows(a, w.rows, s));
+    // dW_c1, dW_2 and the partial reduction on the side stream
+    EGNN_TRY(stream_fork(s, s2, side->ev[2]));
+    EGNN_TRY(edge_wgrad_rows(E, w.rows, s2));
+    EGNN_TRY(edge_part_reduce(H, dd, false, w.rows.G, w.rows.part, gp, ld1, s2));
+  } else {
+    if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
+    else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
+    // per-CTA weight-gradient partials -> parameter gradients, on the side stream
+    EGNN_TRY(stream_fork(s, s2, side->ev[2]));
+    EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, s2));
+  }
+  if (tc || rows)
     EGNN_TRY(edge_node_pass_tc(H, N, g->row_ptr, g->src_ptr, g->src_edge, w.gstore, w.gdstore, gx_out, w.S_dst,
                                w.S_src, grad_x, s));
   else

@@ -149,7 +149,11 @@ LAYER_CASES = [
     (64, "bf16", 500, 12000, 0, {"attention": True, "coords_agg": "sum"}),
     (128, "bf16", 2000, 60000, 0, {"attention": True}),
     (256, "bf16", 400, 9000, 0, {"attention": True}),
-    # tensor-core path (bf16, H = 128, no edge attributes)
+    # tensor-core paths (bf16, no edge attributes): fused edge kernels at H = 128,
+    # edge-row GEMMs at H = 256 (fewer edges than one tile; several tiles per CTA)
+    (256, "bf16", 100, 90, 0, {}),
+    (256, "bf16", 2000, 60000, 0, {"normalize": True, "tanh": True, "coords_agg": "sum"}),
+    (256, "bf16", 3000, 100000, 0, {"residual": False}),
     (128, "bf16", 100, 90, 0, {}),
     (128, "bf16", 2000, 60000, 0, {"normalize": True, "tanh": True, "coords_agg": "sum"}),
     (128, "bf16", 3000, 100000, 0, {"residual": False}),
@@ -178,18 +182,25 @@ def test_layer_matches_oracle(H, precision, N, E, d, flags, cuda_device):
     check_tensors(got, emu, tight, what + " vs rounding-exact bf16 model")
 
 
-def test_layer_without_edges(cuda_device):
-    """E = 0: agg = 0, x' = x, only the node MLP acts."""
+@pytest.mark.parametrize("H,precision", [(64, "fp32"), (256, "bf16")])
+def test_layer_without_edges(H, precision, cuda_device):
+    """E = 0: agg = 0, x' = x, only the node MLP acts (the edge-row path at
+    H = 256 still writes zero edge-weight gradients)."""
     dev = cuda_device
-    N, H = 20, 64
+    N = 20
     row = torch.zeros(0, dtype=torch.int64)
     col = torch.zeros(0, dtype=torch.int64)
     _, _, p, h, x, _, gh, gx = _seeded_layer_case(1, N, 10, H)
     ref = O.layer_grads(p, "", h, row, col, x, gh, gx)
-    layer = _layer_from_state(p, H, "fp32", dev)
+    layer = _layer_from_state(p, H, precision, dev)
     csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
     res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev), gx.float().to(dev))
-    check_tensors(as_dict(res), as_dict(ref), _fp32_tol(p, h, row, col, x, gh, gx, None, ref, {}), "no edges")
+    if precision == "fp32":
+        tol = _fp32_tol(p, h, row, col, x, gh, gx, None, ref, {})
+    else:
+        emu = as_dict(EM.layer_fwd_bwd(p, h, row, col, x, gh, gx, None, precision="bf16"))
+        tol = tolerances(as_dict(ref), emu, TOL["bf16"], 3.0)
+    check_tensors(as_dict(res), as_dict(ref), tol, f"no edges H={H} {precision}")
 
 
 def test_single_edge_and_isolated_nodes(cuda_device):
@@ -205,10 +216,10 @@ def test_single_edge_and_isolated_nodes(cuda_device):
     check_tensors(as_dict(res), as_dict(ref), _fp32_tol(p, h, row, col, x, gh, gx, None, ref, {}), "single edge")
 
 
-@pytest.mark.parametrize("precision", ["fp32", "bf16"])
-def test_backward_is_deterministic(precision, cuda_device):
+@pytest.mark.parametrize("precision,H", [("fp32", 128), ("bf16", 128), ("bf16", 256)])
+def test_backward_is_deterministic(precision, H, cuda_device):
     dev = cuda_device
-    N, E, H = 2000, 60000, 128
+    N, E = 2000, 60000
     row, col, p, h, x, _, gh, gx = _seeded_layer_case(9, N, E, H)
     layer = _layer_from_state(p, H, precision, dev)
     csr = CSR.from_edges(row, col, n_nodes=N, device=dev)

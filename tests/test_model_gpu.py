@@ -48,7 +48,7 @@ def _as_flat(loss, ho, xo, grads):
 
 
 @pytest.mark.parametrize("cfg_id,precision,n_graphs", [(1, "fp32", None), (2, "bf16", None),
-                                                       (2, "fp32", 128)])
+                                                       (2, "fp32", 128), (4, "bf16", 8)])
 def test_molecule_workload_matches_oracle(cfg_id, precision, n_graphs, cuda_device):
     dev = cuda_device
     b = make_workload(cfg_id, n_graphs=n_graphs)

@@ -15,6 +15,7 @@
 //             g_c1 = gphi wc2 silu'(c1)                   GEMM epilogue -> Gc1 (bf16)
 //             g_a2 = (Gc1 Wc1 + g_agg[i]) silu'(a2)       GEMM -> Ga2 (bf16)
 //             g_a1 = (Ga2 W2) silu'(a1)                   GEMM -> bf16 rows, g_d
+//                    (silu'(a1) stored in fp16 by the backward's gather)
 //             dWc1 = Gc1^T Mb, dW2 = Ga2^T U              split-K GEMMs over the edges
 //
 // The rounding points are those of the fused kernels (bf16 GEMM operands u1,
@@ -116,33 +117,66 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&p);
 }
 
-// 32 values = features 64 cs + 32 p .. + 31 of row `el` of the tile at `tb`.
-__device__ __forceinline__ void st_tile_piece(char* tb, int el, int cs, int p, const float (&v)[32]) {
-  char* rowp = tb + cs * kBlk + el * 128;
+// Warp-collective store of one 64-byte piece per row through the warp's 2 KB
+// staging buffer: lane l owns row l's 16 words w[]; `dst` is that row's
+// 64-byte destination (nullptr: not stored) and its logical 16-byte chunk c
+// goes to position c ^ perm there.  Rows are written to the staging in an
+// XOR-swizzled slot order (no bank conflicts) and read back four lanes per
+// row, so every global store instruction covers eight whole 64-byte pieces
+// (whole 32-byte sectors) instead of 16 bytes of 32 different rows.
+__device__ __forceinline__ void store_rows64(char* stg, const uint32_t (&w)[16], char* dst, int perm) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint4 u = make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
-                               pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
-    *reinterpret_cast<uint4*>(rowp + ((((p << 2) + c) ^ (el & 7)) << 4)) = u;
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+  __syncwarp();
+  const unsigned long long dv = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int hr = 8 * k + (lane >> 2), cc = lane & 3;
+    const uint4 val = *reinterpret_cast<const uint4*>(stg + hr * 64 + ((cc ^ ((hr >> 1) & 3)) << 4));
+    const unsigned long long d = __shfl_sync(0xffffffffu, dv, hr);
+    const int pm = __shfl_sync(0xffffffffu, perm, hr);
+    if (d) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(d) + ((cc ^ pm) << 4)) = val;
   }
+  __syncwarp();
 }
 
-__device__ __forceinline__ void st_f32_piece(float* dst, const float (&v)[32]) {
+// 32 values = features 64 cs + 32 p .. + 31 of row `el` of the tile at `tb`
+// (in the 128-byte swizzle the piece is one aligned 64-byte half row whose
+// chunks are permuted by el % 4).
+__device__ __forceinline__ void st_tile_piece(char* stg, char* tb, int el, int cs, int p, const float (&v)[32]) {
+  uint32_t w[16];
 #pragma unroll
-  for (int t = 0; t < 32; t += 4) *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+  for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  store_rows64(stg, w, tb + cs * kBlk + el * 128 + ((((p << 2) ^ (el & 4))) << 4), el & 3);
 }
 
-__device__ __forceinline__ void st_f16_piece(__half* dst, const float (&v)[32]) {
+// 32 values of a row-major row at `dst` (nullptr: row not stored).
+__device__ __forceinline__ void st_f32_piece(char* stg, float* dst, const float (&v)[32]) {
+  uint32_t w[16];
 #pragma unroll
-  for (int t = 0; t < 32; t += 8) {
-    uint32_t w[4];
+  for (int h = 0; h < 2; ++h) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const __half2 h = __floats2half2_rn(v[t + 2 * u], v[t + 2 * u + 1]);
-      w[u] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    *reinterpret_cast<uint4*>(dst + t) = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[16 * h + i]);
+    store_rows64(stg, w, dst ? reinterpret_cast<char*>(dst + 16 * h) : nullptr, 0);
   }
+}
+__device__ __forceinline__ void st_f16_piece(char* stg, __half* dst, const float (&v)[32]) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  store_rows64(stg, w, reinterpret_cast<char*>(dst), 0);
+}
+__device__ __forceinline__ void st_bf16_piece(char* stg, __nv_bfloat16* dst, const float (&v)[32]) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  store_rows64(stg, w, reinterpret_cast<char*>(dst), 0);
 }
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
@@ -176,40 +210,71 @@ __device__ void load_w256(char* tile, const float* __restrict__ W) {
 }
 
 // ---- gather: geometry and u1 = bf16(silu(P_i + Q_j + w_r r)) -------------------------
-// One warp per edge of the padded tile range; lane owns features 8 lane .. + 7
-// (16 bytes of the tile row).  Padding rows (e >= E) are zero.
+// One warp per EPW consecutive edges of the padded tile range, their index,
+// coordinate and P / Q row loads all in flight together; lane owns features
+// 8 lane .. + 7 (16 bytes of each tile row).  Padding rows (e >= E) are zero.
+// With S1 (backward) the warp also stores silu'(a1) as fp16 rows (E, 256).
+constexpr int EPW = 4;
 __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, const int32_t* __restrict__ row_idx,
                                                      const int32_t* __restrict__ col_idx,
                                                      const float4* __restrict__ xp, const float* __restrict__ PQ,
                                                      const float* __restrict__ wr, char* __restrict__ U,
-                                                     float4* __restrict__ geo) {
+                                                     float4* __restrict__ geo, __half* __restrict__ S1) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
-  const int64_t e = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (e >= Epad) return;
-  float u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (e < E) {
-    const int i = row_idx[e], j = col_idx[e];
-    const float4 xi = xp[i], xj = xp[j];
-    const float dx = xi.x - xj.x, dy = xi.y - xj.y, dz = xi.z - xj.z;
-    const float r = dx * dx + dy * dy + dz * dz;
-    if (lane == 0) geo[e] = make_float4(dx, dy, dz, r);
-    const float* P = PQ + (int64_t)i * 2 * kH + 8 * lane;
-    const float* Q = PQ + (int64_t)j * 2 * kH + kH + 8 * lane;
+  const int64_t e0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * EPW;
+  if (e0 >= Epad) return;
+  int iv[EPW], jv[EPW];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float4 p = ldg4(P + 4 * h), q = ldg4(Q + 4 * h), w = ldg4(wr + 8 * lane + 4 * h);
-      u[4 * h + 0] = silu_edge(fmaf(w.x, r, p.x + q.x));
-      u[4 * h + 1] = silu_edge(fmaf(w.y, r, p.y + q.y));
-      u[4 * h + 2] = silu_edge(fmaf(w.z, r, p.z + q.z));
-      u[4 * h + 3] = silu_edge(fmaf(w.w, r, p.w + q.w));
+  for (int k = 0; k < EPW; ++k) {
+    const bool ok = e0 + k < E;
+    iv[k] = ok ? row_idx[e0 + k] : 0;
+    jv[k] = ok ? col_idx[e0 + k] : 0;
+  }
+  float4 xi[EPW], xj[EPW], pv[EPW][2], qv[EPW][2];
+#pragma unroll
+  for (int k = 0; k < EPW; ++k) {
+    xi[k] = xp[iv[k]];
+    xj[k] = xp[jv[k]];
+    const float* P = PQ + (int64_t)iv[k] * 2 * kH + 8 * lane;
+    const float* Q = PQ + (int64_t)jv[k] * 2 * kH + kH + 8 * lane;
+    pv[k][0] = ldg4(P);
+    pv[k][1] = ldg4(P + 4);
+    qv[k][0] = ldg4(Q);
+    qv[k][1] = ldg4(Q + 4);
+  }
+  const float4 w0 = ldg4(wr + 8 * lane), w1 = ldg4(wr + 8 * lane + 4);
+  const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+  for (int k = 0; k < EPW; ++k) {
+    const int64_t e = e0 + k;
+    const bool ok = e < E;
+    const float dx = xi[k].x - xj[k].x, dy = xi[k].y - xj[k].y, dz = xi[k].z - xj[k].z;
+    const float r = dx * dx + dy * dy + dz * dz;
+    if (ok && lane == 0) geo[e] = make_float4(dx, dy, dz, r);
+    const float pp[8] = {pv[k][0].x, pv[k][0].y, pv[k][0].z, pv[k][0].w, pv[k][1].x, pv[k][1].y, pv[k][1].z, pv[k][1].w};
+    const float qq[8] = {qv[k][0].x, qv[k][0].y, qv[k][0].z, qv[k][0].w, qv[k][1].x, qv[k][1].y, qv[k][1].z, qv[k][1].w};
+    float u[8], d[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      silu_grad_edge(fmaf(w[c], r, pp[c] + qq[c]), u[c], d[c]);
+      if (!ok) u[c] = 0.f;
+    }
+    const int64_t t = e >> 7;
+    const int rl = (int)(e & 127), blk = lane >> 3, ch = lane & 7;
+    const uint4 pk = make_uint4(pack_bf16x2(u[0], u[1]), pack_bf16x2(u[2], u[3]), pack_bf16x2(u[4], u[5]),
+                                pack_bf16x2(u[6], u[7]));
+    *reinterpret_cast<uint4*>(U + t * kTile + blk * kBlk + rl * 128 + ((ch ^ (rl & 7)) << 4)) = pk;
+    if (S1 && ok) {
+      uint32_t hw[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const __half2 h2 = __floats2half2_rn(d[2 * c], d[2 * c + 1]);
+        hw[c] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint4*>(S1 + e * kH + 8 * lane) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
   }
-  const int64_t t = e >> 7;
-  const int rl = (int)(e & 127), blk = lane >> 3, ch = lane & 7;
-  const uint4 pk = make_uint4(pack_bf16x2(u[0], u[1]), pack_bf16x2(u[2], u[3]), pack_bf16x2(u[4], u[5]),
-                              pack_bf16x2(u[6], u[7]));
-  *reinterpret_cast<uint4*>(U + t * kTile + blk * kBlk + rl * 128 + ((ch ^ (rl & 7)) << 4)) = pk;
 }
 
 // ---- forward row sums: agg_i = sum m_e, x'_i = x_i + s_i sum d_e inv_e phi_e -----------
@@ -285,9 +350,9 @@ struct RowsGemmArgs {
   const float4* geo = nullptr;
   float4* gdstore = nullptr;
   const __half* aux = nullptr;    // (E, 256) fp16 silu'(a2 + b2) (EPI_GA2)
+  const __half* s1 = nullptr;     // (E, 256) fp16 silu'(a1) (EPI_GA1)
   const float* g_agg = nullptr;
   int64_t ld_gagg = 0;
-  const float* PQ = nullptr;
   const int32_t* row_ptr = nullptr;
   const int32_t* row_idx = nullptr;
   const int32_t* col_idx = nullptr;
@@ -298,13 +363,15 @@ struct RowsGemmArgs {
 };
 
 constexpr int GM_NTH = 576;   // warp 0: loads; warp 1: MMA + TMEM; warps 2..17: epilogue
-constexpr int GM_S = 4;       // A ring stages (one 16 KB block each)
+constexpr int GM_S = 3;       // A ring stages (one 16 KB block each)
 struct GmLayout {
   static constexpr int W = 0;
   static constexpr int A = kH * kH * 2;               // 131072
-  static constexpr int BAR = A + GM_S * kBlk;         // 196608
+  static constexpr int BAR = A + GM_S * kBlk;         // 180224
   static constexpr int RED = BAR + 256;               // float[2][4][128]
-  static constexpr size_t BYTES = RED + 2 * 4 * 128 * 4 + 1024;
+  static constexpr int VEC = RED + 2 * 4 * 128 * 4;   // float[3][256]: bias, w_c2, w_r
+  static constexpr int STG = VEC + 3 * kH * 4;        // 16 epilogue warps x 2 KB store staging
+  static constexpr size_t BYTES = STG + 16 * 2048 + 1024;
 };
 
 template <int EPI>
@@ -324,6 +391,9 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
   uint32_t* tmem_s = reinterpret_cast<uint32_t*>(fin + 1);
   int* abort_s = reinterpret_cast<int*>(tmem_s + 1);
   float* red = reinterpret_cast<float*>(sm + GmLayout::RED);
+  float* vbias = reinterpret_cast<float*>(sm + GmLayout::VEC);
+  float* vwc2 = vbias + kH;
+  float* vwr = vwc2 + kH;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t G = gridDim.x;
   const int64_t ntl = (int64_t)blockIdx.x < a.ntiles ? (a.ntiles - 1 - blockIdx.x) / G + 1 : 0;
@@ -361,7 +431,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
       for (int64_t j = 0; j < ntl && ok; ++j) {
         const char* src = a.A + (size_t)(blockIdx.x + j * G) * kTile;
         for (int b = 0; b < 4; ++b, ++it) {
-          const int s = it & (GM_S - 1);
+          const int s = it % GM_S;
           if (it >= GM_S && !(ok = wait_bar(&empty[s], ((it / GM_S) - 1) & 1, abort_f, abort_s))) break;
           mbar_expect_tx(&full[s], kBlk);
           bulk_g2s(Ast + s * kBlk, src + b * kBlk, kBlk, &full[s]);
@@ -369,7 +439,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
       }
       if (!ok)   // copies still in flight land before the CTA exits
         for (uint32_t k = it > GM_S ? it - GM_S : 0; k < it; ++k)
-          wait_bar(&full[k & (GM_S - 1)], (k / GM_S) & 1, nullptr, abort_s);
+          wait_bar(&full[k % GM_S], (k / GM_S) & 1, nullptr, abort_s);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -384,7 +454,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
         fence_after_sync();
         const uint32_t d = tmem + buf * kH;
         for (int b = 0; b < 4; ++b, ++it) {
-          const int s = it & (GM_S - 1);
+          const int s = it % GM_S;
           if (!(ok = wait_bar(&full[s], (it / GM_S) & 1, abort_f, abort_s))) break;
           fence_after_sync();
 #pragma unroll
@@ -406,13 +476,24 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
     // ---- epilogue: thread = (edge row el, 64-feature slice cs)
     const int q = warp & 3, cs = (warp - 2) >> 2, el = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    char* stg = sm + GmLayout::STG + (warp - 2) * 2048;
     const bool tanh_on = a.flags & EGNN_FLAG_TANH;
     const bool normalize = a.flags & EGNN_FLAG_NORMALIZE;
     const bool csum = a.flags & EGNN_FLAG_COORDS_SUM;
+    // per-feature vectors (w_r comes from the prep kernel: read after the wait)
+    for (int n = tid - 64; n < kH; n += 512) {
+      vbias[n] = a.bias ? a.bias[n] : 0.f;
+      vwc2[n] = a.wc2 ? a.wc2[n] : 0.f;
+      vwr[n] = a.wr ? a.wr[n] : 0.f;
+    }
+    epi_sync();
+    // variants with a named barrier inside the tile decide a timeout together;
+    // the others per warp
+    constexpr bool kJoint = EPI == EPI_PHI || EPI == EPI_GC1 || EPI == EPI_GA1;
     for (int64_t j = 0; j < ntl; ++j) {
       const int buf = (int)(j & 1);
       const bool ok = wait_bar(&accf[buf], (j >> 1) & 1, abort_f, abort_s);
-      if (epi_any(!ok)) break;
+      if (kJoint ? epi_any(!ok) : !__all_sync(0xffffffffu, ok)) break;
       fence_after_sync();
       const int64_t t = blockIdx.x + j * G;
       const int64_t e = t * 128 + el;
@@ -435,7 +516,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           const int n0 = cs * 64 + 32 * p;
 #pragma unroll
           for (int t4 = 0; t4 < 32; t4 += 4) {
-            const float4 b4 = ldg4(a.bias + n0 + t4);
+            const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4);
             v[t4] += b4.x; v[t4 + 1] += b4.y; v[t4 + 2] += b4.z; v[t4 + 3] += b4.w;
           }
           if constexpr (EPI == EPI_M_BWD) {
@@ -447,13 +528,13 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
               v[k] = valid ? yy : 0.f;
               d2[k] = dy;
             }
-            if (valid) st_f16_piece(a.outh + e * kH + n0, d2);
+            st_f16_piece(stg, valid ? a.outh + e * kH + n0 : nullptr, d2);
           } else {
 #pragma unroll
             for (int k = 0; k < 32; ++k) v[k] = valid ? silu_edge(v[k]) : 0.f;
-            if (valid) st_f32_piece(a.outf + e * kH + n0, v);
+            st_f32_piece(stg, valid ? a.outf + e * kH + n0 : nullptr, v);
           }
-          st_tile_piece(tb, el, cs, p, v);
+          st_tile_piece(stg, tb, el, cs, p, v);
         }
       } else if constexpr (EPI == EPI_PHI) {
         float part = 0.f;
@@ -465,7 +546,8 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           const int n0 = cs * 64 + 32 * p;
 #pragma unroll
           for (int t4 = 0; t4 < 32; t4 += 4) {
-            const float4 b4 = ldg4(a.bias + n0 + t4), w4 = ldg4(a.wc2 + n0 + t4);
+            const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4),
+                         w4 = *reinterpret_cast<const float4*>(vwc2 + n0 + t4);
             part += w4.x * silu_edge(v[t4] + b4.x);
             part += w4.y * silu_edge(v[t4 + 1] + b4.y);
             part += w4.z * silu_edge(v[t4 + 2] + b4.z);
@@ -489,7 +571,8 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           const int n0 = cs * 64 + 32 * p;
 #pragma unroll
           for (int t4 = 0; t4 < 32; t4 += 4) {
-            const float4 b4 = ldg4(a.bias + n0 + t4), w4 = ldg4(a.wc2 + n0 + t4);
+            const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4),
+                         w4 = *reinterpret_cast<const float4*>(vwc2 + n0 + t4);
             part += w4.x * silu_edge(v[t4] + b4.x);
             part += w4.y * silu_edge(v[t4 + 1] + b4.y);
             part += w4.z * silu_edge(v[t4 + 2] + b4.z);
@@ -520,7 +603,8 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           const int n0 = cs * 64 + 32 * p;
 #pragma unroll
           for (int t4 = 0; t4 < 32; t4 += 4) {
-            const float4 b4 = ldg4(a.bias + n0 + t4), w4 = ldg4(a.wc2 + n0 + t4);
+            const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4),
+                         w4 = *reinterpret_cast<const float4*>(vwc2 + n0 + t4);
             const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
@@ -530,7 +614,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
               y[t4 + u] = gphi * yy;
             }
           }
-          st_tile_piece(tb, el, cs, p, v);
+          st_tile_piece(stg, tb, el, cs, p, v);
           acc0[p] += colsum32(v);
           acc1[p] += colsum32(y);
         }
@@ -557,7 +641,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
               v[t8 + 2 * u + 1] = valid ? (v[t8 + 2 * u + 1] + gg[2 * u + 1]) * dd.y : 0.f;
             }
           }
-          st_tile_piece(tb, el, cs, p, v);
+          st_tile_piece(stg, tb, el, cs, p, v);
           acc0[p] += colsum32(v);
         }
       } else {   // EPI_GA1
@@ -571,30 +655,24 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           tmem_ld32(tacc + 32 * p, v);
           if (p == 1) release();
           const int n0 = cs * 64 + 32 * p;
-          const float* P = a.PQ + (int64_t)i * 2 * kH + n0;
-          const float* Q = a.PQ + (int64_t)jn * 2 * kH + kH + n0;
+          const __half* s1p = a.s1 + (valid ? e : 0) * kH + n0;
 #pragma unroll
-          for (int t4 = 0; t4 < 32; t4 += 4) {
-            const float4 p4 = ldg4(P + t4), q4 = ldg4(Q + t4), w4 = ldg4(a.wr + n0 + t4);
-            const float pp[4] = {p4.x, p4.y, p4.z, p4.w}, qq[4] = {q4.x, q4.y, q4.z, q4.w},
-                        ww[4] = {w4.x, w4.y, w4.z, w4.w};
+          for (int t8 = 0; t8 < 32; t8 += 8) {
+            const uint4 hz = __ldg(reinterpret_cast<const uint4*>(s1p + t8));
+            const uint32_t hw[4] = {hz.x, hz.y, hz.z, hz.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              float yy, dy;
-              silu_grad_edge(fmaf(ww[u], gq.w, pp[u] + qq[u]), yy, dy);
-              const float g = valid ? v[t4 + u] * dy : 0.f;
-              v[t4 + u] = g;
-              grp += g * ww[u];
-              rr[t4 + u] = g * gq.w;
+              const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hw[u]));
+              const float g0 = valid ? v[t8 + 2 * u] * dd.x : 0.f;
+              const float g1 = valid ? v[t8 + 2 * u + 1] * dd.y : 0.f;
+              v[t8 + 2 * u] = g0;
+              v[t8 + 2 * u + 1] = g1;
+              grp += g0 * vwr[n0 + t8 + 2 * u] + g1 * vwr[n0 + t8 + 2 * u + 1];
+              rr[t8 + 2 * u] = g0 * gq.w;
+              rr[t8 + 2 * u + 1] = g1 * gq.w;
             }
           }
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(a.gstore + e * kH + n0);
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              dst[c] = make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
-                                  pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
-          }
+          st_bf16_piece(stg, valid ? a.gstore + e * kH + n0 : nullptr, v);
           acc0[p] += colsum32(rr);
         }
         rbuf[cs * 128 + el] = grp;
@@ -731,6 +809,7 @@ __global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __res
     const int q = warp & 3, mh = warp >> 2;
     const int m = mh * 128 + q * 32 + lane;
     float* dst = part + (int64_t)blockIdx.x * PF + off + (int64_t)m * kH;
+    char* stg = sm + warp * 2048;   // the operand ring is idle once `done` has flipped
 #pragma unroll 1
     for (int c = 0; c < kH / 32; ++c) {
       float v[32];
@@ -739,7 +818,7 @@ __global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __res
 #pragma unroll
         for (int k = 0; k < 32; ++k) v[k] = 0.f;
       }
-      st_f32_piece(dst + 32 * c, v);
+      st_f32_piece(stg, dst + 32 * c, v);
     }
   }
   fence_before_sync();
@@ -769,8 +848,8 @@ int launch_u(const EdgeCommon& a, const RowsBufs& b, cudaStream_t s) {
   const int64_t Epad = rows_tiles(a.E) * 128;
   if (Epad == 0) return EGNN_OK;
   TimerScope ts("edge_rows_u", s);
-  EGNN_CHECK_CUDA(launch_pdl(rows_u_kernel, dim3((unsigned)(Epad / 8)), dim3(256), 0, s, a.E, Epad, a.row_idx,
-                             a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo));
+  EGNN_CHECK_CUDA(launch_pdl(rows_u_kernel, dim3((unsigned)(Epad / (8 * EPW))), dim3(256), 0, s, a.E, Epad,
+                             a.row_idx, a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo, b.S1));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
@@ -783,7 +862,6 @@ RowsGemmArgs gemm_common(const EdgeCommon& a, const RowsBufs& b) {
   g.wr = a.wr;
   g.geo = b.geo;
   g.phi = b.phi;
-  g.PQ = a.PQ;
   g.row_ptr = a.row_ptr;
   g.row_idx = a.row_idx;
   g.col_idx = a.col_idx;
@@ -815,6 +893,7 @@ RowsBufs carve_rows(Carver& c, int64_t E, int H, bool bwd, int num_sms) {
     b.Gc1 = c.take<char>(tiles);
     b.Ga2 = c.take<char>(tiles);
     b.D2 = c.take<__half>(En * H);
+    b.S1 = c.take<__half>(En * H);
   } else {
     b.M32 = c.take<float>(En * H);
   }
@@ -881,6 +960,7 @@ int edge_bwd_rows(const EdgeBwdArgs& a, const RowsBufs& b, cudaStream_t s) {
   g.A = b.Ga2;
   g.W = a.W2_src;
   g.outb = nullptr;
+  g.s1 = b.S1;
   g.gstore = reinterpret_cast<__nv_bfloat16*>(a.gstore);
   g.gdstore = a.gdstore;
   EGNN_TRY(launch_gemm<EPI_GA1>(g, b.G, s, "edge_rows_gemm"));

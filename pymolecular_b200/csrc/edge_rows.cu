@@ -278,7 +278,9 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
 }
 
 // ---- forward row sums: agg_i = sum m_e, x'_i = x_i + s_i sum d_e inv_e phi_e -----------
-// One warp per node, its CSR row in order (four rows in flight).
+// Two warps per node, each owning 128 features (lane: 4 consecutive ones), its
+// CSR row in order with four rows in flight; the first warp also sums the
+// coordinate terms.
 __global__ void __launch_bounds__(256) rows_agg_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
                                                        const float* __restrict__ M32, const float* __restrict__ phi,
                                                        const float4* __restrict__ geo, const float* __restrict__ x,
@@ -286,11 +288,15 @@ __global__ void __launch_bounds__(256) rows_agg_kernel(int64_t N, const int32_t*
                                                        float* __restrict__ x_out) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
-  const int64_t v = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t gw = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t v = gw >> 1;
+  const int part = (int)(gw & 1);
   if (v >= N) return;
   const bool normalize = flags & EGNN_FLAG_NORMALIZE;
+  const bool xl = part == 0 && lane < 3;   // lanes that sum a coordinate component
   const int k0 = row_ptr[v], k1 = row_ptr[v + 1];
-  float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const int f0 = part * (kH / 2) + 4 * lane;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
   float xs = 0.f;
   auto xterm = [&](int64_t k) {
     const float4 g = __ldg(geo + k);
@@ -300,33 +306,26 @@ __global__ void __launch_bounds__(256) rows_agg_kernel(int64_t N, const int32_t*
   };
   int k = k0;
   for (; k + 4 <= k1; k += 4) {
-    float4 a[4][2];
+    float4 a[4];
     float xt[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const float* r = M32 + (int64_t)(k + u) * kH + 8 * lane;
-      a[u][0] = ldg4(r);
-      a[u][1] = ldg4(r + 4);
-      xt[u] = lane < 3 ? xterm(k + u) : 0.f;
+      a[u] = ldg4(M32 + (int64_t)(k + u) * kH + f0);
+      xt[u] = xl ? xterm(k + u) : 0.f;
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      s[0] += a[u][0].x; s[1] += a[u][0].y; s[2] += a[u][0].z; s[3] += a[u][0].w;
-      s[4] += a[u][1].x; s[5] += a[u][1].y; s[6] += a[u][1].z; s[7] += a[u][1].w;
+      s[0] += a[u].x; s[1] += a[u].y; s[2] += a[u].z; s[3] += a[u].w;
       xs += xt[u];
     }
   }
   for (; k < k1; ++k) {
-    const float* r = M32 + (int64_t)k * kH + 8 * lane;
-    const float4 a0 = ldg4(r), a1 = ldg4(r + 4);
+    const float4 a0 = ldg4(M32 + (int64_t)k * kH + f0);
     s[0] += a0.x; s[1] += a0.y; s[2] += a0.z; s[3] += a0.w;
-    s[4] += a1.x; s[5] += a1.y; s[6] += a1.z; s[7] += a1.w;
-    if (lane < 3) xs += xterm(k);
+    if (xl) xs += xterm(k);
   }
-  float* o = agg + v * kH + 8 * lane;
-  *reinterpret_cast<float4*>(o) = make_float4(s[0], s[1], s[2], s[3]);
-  *reinterpret_cast<float4*>(o + 4) = make_float4(s[4], s[5], s[6], s[7]);
-  if (lane < 3) {
+  *reinterpret_cast<float4*>(agg + v * kH + f0) = make_float4(s[0], s[1], s[2], s[3]);
+  if (xl) {
     const float sc = (flags & EGNN_FLAG_COORDS_SUM) ? 1.f : 1.f / (float)max(k1 - k0, 1);
     x_out[v * 3 + lane] = x[v * 3 + lane] + xs * sc;
   }
@@ -722,11 +721,13 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
 }
 
 // ---- weight gradients: D = G^T X over the edges (split-K, one slice per CTA) ----------
-// Each CTA takes a contiguous range of tiles in 64-edge half tiles; one
-// thread streams them through a 3-stage ring (bulk copies of the 8 KB
-// half blocks) and issues the MMAs (A = G^T and B = X both MN-major, two
-// M = 128 halves of the 256 output rows in 2 x 256 TMEM columns).
-constexpr int WG_NTH = 256, WG_S = 3, WG_STAGE = 65536;
+// Each CTA takes a contiguous range of tiles in 32-edge slabs (a quarter
+// tile: the 4 KB row range of each of the four column blocks of both
+// operands, 32 KB per stage); one thread streams them through a 6-stage ring
+// with five slabs in flight ahead of the MMAs, and issues the MMAs (A = G^T
+// and B = X both MN-major, two M = 128 halves of the 256 output rows in
+// 2 x 256 TMEM columns).
+constexpr int WG_NTH = 256, WG_S = 6, WG_STAGE = 32768, WG_SLAB = 32 * 128;
 constexpr size_t WG_BYTES = WG_S * WG_STAGE + 256 + 1024;
 
 __global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __restrict__ Gt, const char* __restrict__ Xt,
@@ -744,7 +745,7 @@ __global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __res
   const int64_t tpc = (ntiles + gridDim.x - 1) / gridDim.x;
   const int64_t t0 = std::min<int64_t>(ntiles, (int64_t)blockIdx.x * tpc);
   const int64_t t1 = std::min<int64_t>(ntiles, t0 + tpc);
-  const int nslab = (int)(2 * (t1 - t0));
+  const int nslab = (int)(4 * (t1 - t0));
 
   if (warp == 0) tmem_alloc(tmem_s, 512);
   if (tid == 0) {
@@ -773,11 +774,11 @@ __global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __res
           if (it >= WG_S && !(ok = wait_bar(&empty[s], ((it / WG_S) - 1) & 1, abort_f, abort_s))) break;
           char* st = sm + s * WG_STAGE;
           mbar_expect_tx(&full[s], WG_STAGE);
-          const size_t src = (size_t)(t0 + (it >> 1)) * kTile + (size_t)(it & 1) * (kBlk / 2);
+          const size_t src = (size_t)(t0 + (it >> 2)) * kTile + (size_t)(it & 3) * WG_SLAB;
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
-            bulk_g2s(st + b * (kBlk / 2), Gt + src + b * kBlk, kBlk / 2, &full[s]);
-            bulk_g2s(st + WG_STAGE / 2 + b * (kBlk / 2), Xt + src + b * kBlk, kBlk / 2, &full[s]);
+            bulk_g2s(st + b * WG_SLAB, Gt + src + b * kBlk, WG_SLAB, &full[s]);
+            bulk_g2s(st + WG_STAGE / 2 + b * WG_SLAB, Xt + src + b * kBlk, WG_SLAB, &full[s]);
           }
           filled = it + 1;
         }
@@ -789,11 +790,11 @@ __global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __res
           fence_after_sync();
           const uint32_t gb = smem_u32(sm + s * WG_STAGE), xb = gb + WG_STAGE / 2;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
+          for (int kk = 0; kk < 2; ++kk)
 #pragma unroll
             for (int mh = 0; mh < 2; ++mh)
-              mma_bf16(tmem + mh * kH, make_desc(gb + mh * kBlk + kk * 2048, kBlk / 2, 1024),
-                       make_desc(xb + kk * 2048, kBlk / 2, 1024), IDESC, (k | kk) ? 1u : 0u);
+              mma_bf16(tmem + mh * kH, make_desc(gb + mh * 2 * WG_SLAB + kk * 2048, WG_SLAB, 1024),
+                       make_desc(xb + kk * 2048, WG_SLAB, 1024), IDESC, (k | kk) ? 1u : 0u);
           mma_commit(&empty[s]);
         }
       }
@@ -923,7 +924,7 @@ int edge_fwd_rows(const EdgeFwdArgs& a, const RowsBufs& b, cudaStream_t s) {
   }
   if (a.N > 0) {
     TimerScope ts("edge_rows_agg", s);
-    EGNN_CHECK_CUDA(launch_pdl(rows_agg_kernel, dim3((unsigned)((a.N + 7) / 8)), dim3(256), 0, s, a.N, a.row_ptr,
+    EGNN_CHECK_CUDA(launch_pdl(rows_agg_kernel, dim3((unsigned)((2 * a.N + 7) / 8)), dim3(256), 0, s, a.N, a.row_ptr,
                                b.M32, b.phi, b.geo, a.x, a.flags, a.agg, a.x_out));
     EGNN_CHECK_LAUNCH();
   }

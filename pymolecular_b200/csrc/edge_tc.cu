@@ -959,20 +959,23 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
 // ---- node pass: the row sums of g_a1 and of the coordinate gradients -------------
 // For node v, over its in-edges (its CSR row: S_dst, gd_dst) and over its
 // out-edges (transpose CSR: S_src, gd_src), then
-// dL/dx_v = dL/dx'_v + gd_dst - gd_src.  One warp per node, lane owning H / 32
-// consecutive features; four rows of each list in flight, each list added in
-// CSR-position order.
-template <int H>
+// dL/dx_v = dL/dx'_v + gd_dst - gd_src.  SPLIT warps per node, each owning
+// H / SPLIT features (lane: H / (32 SPLIT) consecutive ones); four rows of
+// each list in flight per warp, each list added in CSR-position order.
+template <int H, int SPLIT>
 __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
                                  const int32_t* __restrict__ src_ptr, const int32_t* __restrict__ src_edge,
                                  const __nv_bfloat16* __restrict__ gstore, const float4* __restrict__ gdstore,
                                  const float* __restrict__ gx_out, float* __restrict__ S_dst,
                                  float* __restrict__ S_src, float* __restrict__ gx) {
-  constexpr int VW = H / 32;
+  constexpr int HS = H / SPLIT, VW = HS / 32;
   pdl_enter();
   const int lane = threadIdx.x % 32;
-  const int64_t v = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int64_t v = gw / SPLIT;
+  const int part = (int)(gw % SPLIT);
   if (v >= N) return;
+  gstore += part * HS;
   float sd[VW], ss[VW];
 #pragma unroll
   for (int c = 0; c < VW; ++c) { sd[c] = 0.f; ss[c] = 0.f; }
@@ -995,14 +998,14 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
     if (bd) {
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        load_row_slice<H>(gstore + (int64_t)(kd + u) * H, lane, vd[u]);
+        load_row_slice<HS>(gstore + (int64_t)(kd + u) * H, lane, vd[u]);
         gd1[u] = comp(kd + u);
       }
     }
     if (bs) {
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        load_row_slice<H>(gstore + p[u] * H, lane, vs[u]);
+        load_row_slice<HS>(gstore + p[u] * H, lane, vs[u]);
         gs1[u] = comp(p[u]);
       }
     }
@@ -1027,7 +1030,7 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
   }
   for (; kd < ked; ++kd) {
     float t[VW];
-    load_row_slice<H>(gstore + (int64_t)kd * H, lane, t);
+    load_row_slice<HS>(gstore + (int64_t)kd * H, lane, t);
 #pragma unroll
     for (int c = 0; c < VW; ++c) sd[c] += t[c];
     gdd += comp(kd);
@@ -1035,14 +1038,14 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
   for (; ks < kes; ++ks) {
     const int64_t q = src_edge[ks];
     float t[VW];
-    load_row_slice<H>(gstore + q * H, lane, t);
+    load_row_slice<HS>(gstore + q * H, lane, t);
 #pragma unroll
     for (int c = 0; c < VW; ++c) ss[c] += t[c];
     gds += comp(q);
   }
-  store_row_slice<H>(S_dst + v * H, lane, sd);
-  store_row_slice<H>(S_src + v * H, lane, ss);
-  if (lane < 3) gx[v * 3 + lane] = gx_out[v * 3 + lane] + gdd - gds;
+  store_row_slice<HS>(S_dst + v * H + part * HS, lane, sd);
+  store_row_slice<HS>(S_src + v * H + part * HS, lane, ss);
+  if (lane < 3 && part == 0) gx[v * 3 + lane] = gx_out[v * 3 + lane] + gdd - gds;
 }
 
 template <int H>
@@ -1113,11 +1116,12 @@ int edge_node_pass_tc(int H, int64_t N, const int32_t* row_ptr, const int32_t* s
                       float* gx, cudaStream_t s) {
   if (H != 128 && H != 256) return fail(EGNN_ERR_UNSUPPORTED, "node pass built for H = 128, 256");
   if (N <= 0) return EGNN_OK;
-  const int warps = 8;
-  const unsigned blocks = (unsigned)((N + warps - 1) / warps);
+  // H = 256: two warps per node (more rows in flight per node)
+  const int warps = 8, split = H == 128 ? 1 : 2;
+  const unsigned blocks = (unsigned)((N * split + warps - 1) / warps);
   {
     TimerScope ts("node_pass", s);
-    auto kern = H == 128 ? node_pass_kernel<128> : node_pass_kernel<256>;
+    auto kern = H == 128 ? node_pass_kernel<128, 1> : node_pass_kernel<256, 2>;
     EGNN_CHECK_CUDA(launch_pdl(kern, dim3(blocks), dim3(warps * 32), 0, s, N, row_ptr, src_ptr, src_edge,
                                static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, S_dst, S_src, gx));
   }

@@ -29,10 +29,12 @@ def rel_err(a, b) -> float:
 
 
 def graph_sum(values, graph_ptr):
-    """Deterministic per-graph sum of node values (nodes grouped by graph)."""
-    cs = torch.cat([values.new_zeros(1), values.cumsum(0)])
+    """Deterministic per-graph sum of node values (nodes grouped by graph).
+
+    segment_reduce adds each graph's nodes in order; a float cumsum on the GPU
+    is a look-back scan whose association order can change from run to run."""
     gp = graph_ptr.to(values.device)
-    return cs[gp[1:]] - cs[gp[:-1]]
+    return torch.segment_reduce(values, "sum", lengths=gp[1:] - gp[:-1], unsafe=True)
 
 
 def tolerances(ref, approx, floor, factor):

@@ -487,7 +487,23 @@ def run_b200(args):
             bwd_ms, bwd_n = ktimes[kname]
             per_launch_ms = bwd_ms / max(bwd_n, 1)
             flops_launch = (4.0 / 6.0) * 2.0 * H * H * prob.edges_rank
+            # the same launches are HBM-bound by design (per-edge operands in
+            # HBM): bytes per edge and layer moved by the six GEMMs, with
+            # 2H-byte bf16 / fp16 rows and 4H-byte fp32 rows --
+            #   a2 fwd: U in, Mb + fp32 m out        2H + 2H + 4H
+            #   c1 fwd: Mb in, phi out               2H + 4
+            #   a2 bwd: U in, Mb + silu'(a2) out     2H + 2H + 2H
+            #   g_c1:   Mb in, G_c1 + phi out        2H + 2H + 4 (+ geometry 16)
+            #   g_a2:   G_c1 + silu'(a2) in, G_a2    2H + 2H + 2H
+            #   g_a1:   G_a2 + silu'(a1) in, rows    2H + 2H + 2H (+ geometry, g_d 32)
+            rows_bytes_layer = (8 * H + (2 * H + 4) + 6 * H + (4 * H + 20) + 6 * H + (6 * H + 32)) * prob.edges_rank
+            rows_hbm = {"bytes_per_layer": rows_bytes_layer,
+                        "achieved_gbs": rows_bytes_layer * (bwd_n / 6.0) / (max(bwd_ms, 1e-9) * 1e-3) / 1e9,
+                        "peak_gbs": peaks.get("hbm_gbs")}
+            if rows_hbm["peak_gbs"]:
+                rows_hbm["frac"] = rows_hbm["achieved_gbs"] / rows_hbm["peak_gbs"]
         else:
+            rows_hbm = None
             kname = "edge_bwd"
             bwd_ms, bwd_n = ktimes[kname]
             per_launch_ms = bwd_ms / max(bwd_n, 1)
@@ -540,6 +556,7 @@ def run_b200(args):
                          "per_launch_ms": per_launch_ms, "launches": bwd_n,
                          "flops_per_launch": flops_launch,
                          **fp32_pipe,
+                         **({"hbm_view": rows_hbm} if rows_hbm else {}),
                          "edge_fwd_per_launch_ms": fwd_ms / max(fwd_n, 1),
                          "node_pass_per_launch_ms": ktimes["node_pass"][0] / max(ktimes["node_pass"][1], 1),
                          "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1)},

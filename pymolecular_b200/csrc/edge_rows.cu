@@ -561,61 +561,72 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           a.phi[e] = f;
         }
       } else if constexpr (EPI == EPI_GC1) {
-        // pass 1: phi_e (row sum over the four slices)
-        float part = 0.f;
-#pragma unroll 1
-        for (int p = 0; p < 2; ++p) {
-          float v[32];
-          tmem_ld32(tacc + 32 * p, v);
-          const int n0 = cs * 64 + 32 * p;
-#pragma unroll
-          for (int t4 = 0; t4 < 32; t4 += 4) {
-            const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4),
-                         w4 = *reinterpret_cast<const float4*>(vwc2 + n0 + t4);
-            part += w4.x * silu_edge(v[t4] + b4.x);
-            part += w4.y * silu_edge(v[t4 + 1] + b4.y);
-            part += w4.z * silu_edge(v[t4 + 2] + b4.z);
-            part += w4.w * silu_edge(v[t4 + 3] + b4.w);
-          }
-        }
-        rbuf[cs * 128 + el] = part;
-        epi_sync();
-        float f = rbuf[el] + rbuf[128 + el] + rbuf[256 + el] + rbuf[384 + el];
-        if (tanh_on) f = tanhf(f);
-        float gphi = 0.f;
+        // gphi_e = (g_t . d) inv, times (1 - phi^2) with tanh: only then does
+        // it wait for phi (the row sum over the four slices)
+        float gbase = 0.f;
         if (valid) {
           const int i = a.row_idx[e];
           const float4 gq = a.geo[e];
           const float sc = csum ? 1.f : 1.f / (float)max(a.row_ptr[i + 1] - a.row_ptr[i], 1);
           const float inv = normalize ? 1.f / (sqrtf(gq.w) + 1e-8f) : 1.f;
           const float* gx = a.gx_out + (int64_t)i * 3;
-          gphi = (gx[0] * sc * gq.x + gx[1] * sc * gq.y + gx[2] * sc * gq.z) * inv;
-          if (tanh_on) gphi *= 1.f - f * f;
-          if (cs == 0) a.phi[e] = f;
+          gbase = (gx[0] * sc * gq.x + gx[1] * sc * gq.y + gx[2] * sc * gq.z) * inv;
         }
-        // pass 2: g_c1 = gphi wc2 silu'(c1) -> Gc1; column sums of g_c1 and gphi silu(c1)
+        // g_c1 = gphi wc2 silu'(c1) -> Gc1; column sums of g_c1 and gphi silu(c1)
+        auto grad_pass = [&](float gphi, float& part) {
 #pragma unroll 1
-        for (int p = 0; p < 2; ++p) {
-          float v[32], y[32];
-          tmem_ld32(tacc + 32 * p, v);
-          if (p == 1) release();
-          const int n0 = cs * 64 + 32 * p;
+          for (int p = 0; p < 2; ++p) {
+            float v[32], y[32];
+            tmem_ld32(tacc + 32 * p, v);
+            if (p == 1) release();
+            const int n0 = cs * 64 + 32 * p;
 #pragma unroll
-          for (int t4 = 0; t4 < 32; t4 += 4) {
-            const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4),
-                         w4 = *reinterpret_cast<const float4*>(vwc2 + n0 + t4);
-            const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
+            for (int t4 = 0; t4 < 32; t4 += 4) {
+              const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4),
+                           w4 = *reinterpret_cast<const float4*>(vwc2 + n0 + t4);
+              const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float yy, dy;
-              silu_grad_edge(v[t4 + u] + bb[u], yy, dy);
-              v[t4 + u] = gphi * ww[u] * dy;
-              y[t4 + u] = gphi * yy;
+              for (int u = 0; u < 4; ++u) {
+                float yy, dy;
+                silu_grad_edge(v[t4 + u] + bb[u], yy, dy);
+                part += ww[u] * yy;
+                v[t4 + u] = gphi * ww[u] * dy;
+                y[t4 + u] = gphi * yy;
+              }
+            }
+            st_tile_piece(stg, tb, el, cs, p, v);
+            acc0[p] += colsum32(v);
+            acc1[p] += colsum32(y);
+          }
+        };
+        float part = 0.f;
+        if (!tanh_on) {
+          grad_pass(gbase, part);   // one pass: phi's partial sum rides along
+          rbuf[cs * 128 + el] = part;
+          epi_sync();
+          if (cs == 0 && valid) a.phi[e] = rbuf[el] + rbuf[128 + el] + rbuf[256 + el] + rbuf[384 + el];
+        } else {
+#pragma unroll 1
+          for (int p = 0; p < 2; ++p) {
+            float v[32];
+            tmem_ld32(tacc + 32 * p, v);
+            const int n0 = cs * 64 + 32 * p;
+#pragma unroll
+            for (int t4 = 0; t4 < 32; t4 += 4) {
+              const float4 b4 = *reinterpret_cast<const float4*>(vbias + n0 + t4),
+                           w4 = *reinterpret_cast<const float4*>(vwc2 + n0 + t4);
+              part += w4.x * silu_edge(v[t4] + b4.x);
+              part += w4.y * silu_edge(v[t4 + 1] + b4.y);
+              part += w4.z * silu_edge(v[t4 + 2] + b4.z);
+              part += w4.w * silu_edge(v[t4 + 3] + b4.w);
             }
           }
-          st_tile_piece(stg, tb, el, cs, p, v);
-          acc0[p] += colsum32(v);
-          acc1[p] += colsum32(y);
+          rbuf[cs * 128 + el] = part;
+          epi_sync();
+          const float f = tanhf(rbuf[el] + rbuf[128 + el] + rbuf[256 + el] + rbuf[384 + el]);
+          if (cs == 0 && valid) a.phi[e] = f;
+          float unused = 0.f;
+          grad_pass(gbase * (1.f - f * f), unused);
         }
       } else if constexpr (EPI == EPI_GA2) {
         const int i = valid ? a.row_idx[e] : 0;

@@ -239,8 +239,9 @@ struct BwdWs {
 };
 
 int64_t wpart_floats(int64_t N, int H) {
-  int64_t a = wgrad_splits(N, H, 2 * H) * ((int64_t)H * 2 * H + H);
-  int64_t b = wgrad_splits(N, H, H) * ((int64_t)H * H + H);
+  // slices of the FFMA split (wgrad) or of the tensor-core split (wgrad_tc)
+  int64_t a = std::max(wgrad_splits(N, H, 2 * H), wgrad_tc_splits(N, H, 2 * H)) * ((int64_t)H * 2 * H + H);
+  int64_t b = std::max(wgrad_splits(N, H, H), wgrad_tc_splits(N, H, H)) * ((int64_t)H * H + H);
   int64_t c = colsum_splits(N) * (int64_t)2 * H;
   return std::max<int64_t>({a, b, c, 1});
 }

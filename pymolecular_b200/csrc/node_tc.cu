@@ -447,6 +447,12 @@ int gemm_tc(const GemmArgs& a_in, cudaStream_t s) {
   return EGNN_OK;
 }
 
+int64_t wgrad_tc_splits(int64_t R, int64_t M, int64_t N) {
+  const int64_t tiles = std::max<int64_t>(1, ((M + 127) / 128) * ((N + 127) / 128));
+  const int64_t chunks = (R + 63) / 64;
+  return std::max<int64_t>(1, std::min<int64_t>({148 / tiles, chunks / 2, 64}));
+}
+
 int wgrad_tc(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw, float* db, float* part,
              cudaStream_t s) {
   GemmArgs a;
@@ -454,10 +460,10 @@ int wgrad_tc(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t l
   a.A = G; a.a_t = 1;
   a.B = X; a.b_t = 0;
   a.C = dW; a.ldc = lddw;
-  // at least 2 chunks of 64 rows per split, never more splits than wgrad()
-  // sizes its workspace for, and no empty splits
+  // about one wave of 128 x 128 tiles, at least 2 chunks of 64 rows per
+  // split, and no empty splits
   const int64_t chunks = (R + 63) / 64;
-  const int64_t cap = std::max<int64_t>(1, std::min<int64_t>(wgrad_splits(R, M, N), chunks / 2));
+  const int64_t cap = wgrad_tc_splits(R, M, N);
   const int64_t per = (chunks + cap - 1) / cap;
   a.ksplit = (int)std::max<int64_t>(1, (chunks + per - 1) / per);
   a.part = a.ksplit > 1 ? part : nullptr;

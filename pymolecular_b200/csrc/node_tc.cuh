@@ -15,7 +15,13 @@ bool gemm_tc_ok(const GemmArgs& a);
 // are added by the same ordered reduction as gemm().
 int gemm_tc(const GemmArgs& a, cudaStream_t s);
 
-// Weight gradient as wgrad() (same workspace bound), on the tensor cores.
+// Split-K count of wgrad_tc() for R rows: about one wave of 128 x 128 output
+// tiles, at least two 64-row chunks per slice, at most 64 slices.  The
+// split-K workspace holds that many slices of M x N (+ M for the bias).
+int64_t wgrad_tc_splits(int64_t R, int64_t M, int64_t N);
+
+// Weight gradient as wgrad(), on the tensor cores; `part` holds
+// max(wgrad_splits, wgrad_tc_splits) slices.
 int wgrad_tc(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw, float* db, float* part,
              cudaStream_t s);
 

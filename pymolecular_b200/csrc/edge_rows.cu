@@ -491,6 +491,15 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
     constexpr bool kJoint = EPI == EPI_PHI || EPI == EPI_GC1 || EPI == EPI_GA1;
     for (int64_t j = 0; j < ntl; ++j) {
       const int buf = (int)(j & 1);
+      // g_a2 / g_a1: this thread's fp16 side row (silu'(a2) / silu'(a1), features
+      // 64 cs .. + 63) is requested before the wait for the accumulator
+      uint4 side[8];
+      if constexpr (EPI == EPI_GA2 || EPI == EPI_GA1) {
+        const int64_t ep = (blockIdx.x + j * G) * 128 + el;
+        const __half* sp = (EPI == EPI_GA2 ? a.aux : a.s1) + (ep < a.E ? ep : 0) * kH + cs * 64;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) side[c] = __ldg(reinterpret_cast<const uint4*>(sp) + c);
+      }
       const bool ok = wait_bar(&accf[buf], (j >> 1) & 1, abort_f, abort_s);
       if (kJoint ? epi_any(!ok) : !__all_sync(0xffffffffu, ok)) break;
       fence_after_sync();
@@ -637,11 +646,10 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           if (p == 1) release();
           const int n0 = cs * 64 + 32 * p;
           const float* ga = a.g_agg + (int64_t)i * a.ld_gagg + n0;
-          const __half* d2p = a.aux + (valid ? e : 0) * kH + n0;
 #pragma unroll
           for (int t8 = 0; t8 < 32; t8 += 8) {
             const float4 g0 = ldg4(ga + t8), g1 = ldg4(ga + t8 + 4);
-            const uint4 hz = __ldg(reinterpret_cast<const uint4*>(d2p + t8));
+            const uint4 hz = p ? side[4 + t8 / 8] : side[t8 / 8];
             const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
             const uint32_t hw[4] = {hz.x, hz.y, hz.z, hz.w};
 #pragma unroll
@@ -665,10 +673,9 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           tmem_ld32(tacc + 32 * p, v);
           if (p == 1) release();
           const int n0 = cs * 64 + 32 * p;
-          const __half* s1p = a.s1 + (valid ? e : 0) * kH + n0;
 #pragma unroll
           for (int t8 = 0; t8 < 32; t8 += 8) {
-            const uint4 hz = __ldg(reinterpret_cast<const uint4*>(s1p + t8));
+            const uint4 hz = p ? side[4 + t8 / 8] : side[t8 / 8];
             const uint32_t hw[4] = {hz.x, hz.y, hz.z, hz.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {

@@ -215,6 +215,7 @@ __device__ void load_w256(char* tile, const float* __restrict__ W) {
 // 8 lane .. + 7 (16 bytes of each tile row).  Padding rows (e >= E) are zero.
 // With S1 (backward) the warp also stores silu'(a1) as fp16 rows (E, 256).
 constexpr int EPW = 4;
+template <bool WITH_S1>
 __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, const int32_t* __restrict__ row_idx,
                                                      const int32_t* __restrict__ col_idx,
                                                      const float4* __restrict__ xp, const float* __restrict__ PQ,
@@ -257,7 +258,9 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
     float u[8], d[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      silu_grad_edge(fmaf(w[c], r, pp[c] + qq[c]), u[c], d[c]);
+      const float a1 = fmaf(w[c], r, pp[c] + qq[c]);
+      if constexpr (WITH_S1) silu_grad_edge(a1, u[c], d[c]);
+      else u[c] = silu_edge(a1);
       if (!ok) u[c] = 0.f;
     }
     const int64_t t = e >> 7;
@@ -265,7 +268,7 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
     const uint4 pk = make_uint4(pack_bf16x2(u[0], u[1]), pack_bf16x2(u[2], u[3]), pack_bf16x2(u[4], u[5]),
                                 pack_bf16x2(u[6], u[7]));
     *reinterpret_cast<uint4*>(U + t * kTile + blk * kBlk + rl * 128 + ((ch ^ (rl & 7)) << 4)) = pk;
-    if (S1 && ok) {
+    if (WITH_S1 && ok) {
       uint32_t hw[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -677,6 +680,9 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           for (int t8 = 0; t8 < 32; t8 += 8) {
             const uint4 hz = p ? side[4 + t8 / 8] : side[t8 / 8];
             const uint32_t hw[4] = {hz.x, hz.y, hz.z, hz.w};
+            const float4 wa = *reinterpret_cast<const float4*>(vwr + n0 + t8),
+                         wb = *reinterpret_cast<const float4*>(vwr + n0 + t8 + 4);
+            const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hw[u]));
@@ -684,7 +690,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
               const float g1 = valid ? v[t8 + 2 * u + 1] * dd.y : 0.f;
               v[t8 + 2 * u] = g0;
               v[t8 + 2 * u + 1] = g1;
-              grp += g0 * vwr[n0 + t8 + 2 * u] + g1 * vwr[n0 + t8 + 2 * u + 1];
+              grp += g0 * wv[2 * u] + g1 * wv[2 * u + 1];
               rr[t8 + 2 * u] = g0 * gq.w;
               rr[t8 + 2 * u + 1] = g1 * gq.w;
             }
@@ -867,8 +873,8 @@ int launch_u(const EdgeCommon& a, const RowsBufs& b, cudaStream_t s) {
   const int64_t Epad = rows_tiles(a.E) * 128;
   if (Epad == 0) return EGNN_OK;
   TimerScope ts("edge_rows_u", s);
-  EGNN_CHECK_CUDA(launch_pdl(rows_u_kernel, dim3((unsigned)(Epad / (8 * EPW))), dim3(256), 0, s, a.E, Epad,
-                             a.row_idx, a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo, b.S1));
+  EGNN_CHECK_CUDA(launch_pdl(b.S1 ? rows_u_kernel<true> : rows_u_kernel<false>, dim3((unsigned)(Epad / (8 * EPW))),
+                             dim3(256), 0, s, a.E, Epad, a.row_idx, a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo, b.S1));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

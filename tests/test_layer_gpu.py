@@ -152,6 +152,8 @@ LAYER_CASES = [
     # tensor-core paths (bf16, no edge attributes): fused edge kernels at H = 128,
     # edge-row GEMMs at H = 256 (fewer edges than one tile; several tiles per CTA)
     (256, "bf16", 100, 90, 0, {}),
+    (256, "bf16", 300, 128, 0, {}),                      # exactly one tile
+    (256, "bf16", 1000, 128 * 148 + 1, 0, {"tanh": True}),   # 149 tiles: a second, one-row tile
     (256, "bf16", 2000, 60000, 0, {"normalize": True, "tanh": True, "coords_agg": "sum"}),
     (256, "bf16", 3000, 100000, 0, {"residual": False}),
     (128, "bf16", 100, 90, 0, {}),

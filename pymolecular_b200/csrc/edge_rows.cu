@@ -220,7 +220,10 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
                                                      const int32_t* __restrict__ col_idx,
                                                      const float4* __restrict__ xp, const float* __restrict__ PQ,
                                                      const float* __restrict__ wr, char* __restrict__ U,
-                                                     float4* __restrict__ geo, __half* __restrict__ S1) {
+                                                     float4* __restrict__ geo, __half* __restrict__ S1,
+                                                     const int32_t* __restrict__ row_ptr,
+                                                     const float* __restrict__ gx_out, int flags,
+                                                     float4* __restrict__ gtr) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t e0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * EPW;
@@ -231,6 +234,20 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
     const bool ok = e0 + k < E;
     iv[k] = ok ? row_idx[e0 + k] : 0;
     jv[k] = ok ? col_idx[e0 + k] : 0;
+  }
+  // backward: lane k < EPW also forms edge e0 + k's coordinate-gradient
+  // factors (its loads issued here, beside the row loads below)
+  const bool gl = WITH_S1 && lane < EPW && e0 + lane < E;
+  int mi = 0, mj = 0, rp0 = 0, rp1 = 0;
+  float gxv[3] = {0.f, 0.f, 0.f}, myr = 0.f;
+#pragma unroll
+  for (int k = 0; k < EPW; ++k)
+    if (lane == k) { mi = iv[k]; mj = jv[k]; }
+  if (gl) {
+    rp0 = row_ptr[mi];
+    rp1 = row_ptr[mi + 1];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) gxv[c] = gx_out[(int64_t)mi * 3 + c];
   }
   float4 xi[EPW], xj[EPW], pv[EPW][2], qv[EPW][2];
 #pragma unroll
@@ -253,6 +270,7 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
     const float dx = xi[k].x - xj[k].x, dy = xi[k].y - xj[k].y, dz = xi[k].z - xj[k].z;
     const float r = dx * dx + dy * dy + dz * dz;
     if (ok && lane == 0) geo[e] = make_float4(dx, dy, dz, r);
+    if (lane == k) myr = r;
     const float pp[8] = {pv[k][0].x, pv[k][0].y, pv[k][0].z, pv[k][0].w, pv[k][1].x, pv[k][1].y, pv[k][1].z, pv[k][1].w};
     const float qq[8] = {qv[k][0].x, qv[k][0].y, qv[k][0].z, qv[k][0].w, qv[k][1].x, qv[k][1].y, qv[k][1].z, qv[k][1].w};
     float u[8], d[8];
@@ -277,6 +295,11 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
       }
       *reinterpret_cast<uint4*>(S1 + e * kH + 8 * lane) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
+  }
+  if (gl) {   // (g_t s_i, 1 / (|d| + eps)) with the second term 0 on self-loops
+    const float sc = (flags & EGNN_FLAG_COORDS_SUM) ? 1.f : 1.f / (float)max(rp1 - rp0, 1);
+    const float inv = (flags & EGNN_FLAG_NORMALIZE) ? 1.f / (sqrtf(myr) + 1e-8f) : 1.f;
+    gtr[e0 + lane] = make_float4(gxv[0] * sc, gxv[1] * sc, gxv[2] * sc, mi == mj ? 0.f : inv);
   }
 }
 
@@ -353,12 +376,10 @@ struct RowsGemmArgs {
   float4* gdstore = nullptr;
   const __half* aux = nullptr;    // (E, 256) fp16 silu'(a2 + b2) (EPI_GA2)
   const __half* s1 = nullptr;     // (E, 256) fp16 silu'(a1) (EPI_GA1)
+  const float4* gtr = nullptr;    // (E) dL/dx'_i s_i, 1 / (|d| + eps) or 0 (EPI_GC1, EPI_GA1)
   const float* g_agg = nullptr;
   int64_t ld_gagg = 0;
-  const int32_t* row_ptr = nullptr;
   const int32_t* row_idx = nullptr;
-  const int32_t* col_idx = nullptr;
-  const float* gx_out = nullptr;
   float* part = nullptr;
   int64_t PF = 0;
   int flags = 0;
@@ -480,8 +501,6 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     char* stg = sm + GmLayout::STG + (warp - 2) * 2048;
     const bool tanh_on = a.flags & EGNN_FLAG_TANH;
-    const bool normalize = a.flags & EGNN_FLAG_NORMALIZE;
-    const bool csum = a.flags & EGNN_FLAG_COORDS_SUM;
     // per-feature vectors (w_r comes from the prep kernel: read after the wait)
     for (int n = tid - 64; n < kH; n += 512) {
       vbias[n] = a.bias ? a.bias[n] : 0.f;
@@ -497,6 +516,18 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
       // g_a2 / g_a1: this thread's fp16 side row (silu'(a2) / silu'(a1), features
       // 64 cs .. + 63) is requested before the wait for the accumulator
       uint4 side[8];
+      // g_c1 / g_a1: the edge's geometry and coordinate-gradient factors (and
+      // phi for g_a1), likewise requested before the wait
+      float4 pg = make_float4(0.f, 0.f, 0.f, 0.f), pt = pg;
+      float pphi = 0.f;
+      if constexpr (EPI == EPI_GC1 || EPI == EPI_GA1) {
+        const int64_t ep = (blockIdx.x + j * G) * 128 + el;
+        if (ep < a.E) {
+          pg = a.geo[ep];
+          pt = a.gtr[ep];
+          if (EPI == EPI_GA1) pphi = a.phi[ep];
+        }
+      }
       if constexpr (EPI == EPI_GA2 || EPI == EPI_GA1) {
         const int64_t ep = (blockIdx.x + j * G) * 128 + el;
         const __half* sp = (EPI == EPI_GA2 ? a.aux : a.s1) + (ep < a.E ? ep : 0) * kH + cs * 64;
@@ -575,15 +606,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
       } else if constexpr (EPI == EPI_GC1) {
         // gphi_e = (g_t . d) inv, times (1 - phi^2) with tanh: only then does
         // it wait for phi (the row sum over the four slices)
-        float gbase = 0.f;
-        if (valid) {
-          const int i = a.row_idx[e];
-          const float4 gq = a.geo[e];
-          const float sc = csum ? 1.f : 1.f / (float)max(a.row_ptr[i + 1] - a.row_ptr[i], 1);
-          const float inv = normalize ? 1.f / (sqrtf(gq.w) + 1e-8f) : 1.f;
-          const float* gx = a.gx_out + (int64_t)i * 3;
-          gbase = (gx[0] * sc * gq.x + gx[1] * sc * gq.y + gx[2] * sc * gq.z) * inv;
-        }
+        const float gbase = valid ? (pt.x * pg.x + pt.y * pg.y + pt.z * pg.z) * pt.w : 0.f;
         // g_c1 = gphi wc2 silu'(c1) -> Gc1; column sums of g_c1 and gphi silu(c1)
         auto grad_pass = [&](float gphi, float& part) {
 #pragma unroll 1
@@ -666,9 +689,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           acc0[p] += colsum32(v);
         }
       } else {   // EPI_GA1
-        int i = 0, jn = 0;
-        float4 gq = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) { i = a.row_idx[e]; jn = a.col_idx[e]; gq = a.geo[e]; }
+        const float4 gq = pg;
         float grp = 0.f;
 #pragma unroll 1
         for (int p = 0; p < 2; ++p) {
@@ -702,12 +723,9 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
         epi_sync();
         if (cs == 0 && valid) {
           const float gr = rbuf[el] + rbuf[128 + el] + rbuf[256 + el] + rbuf[384 + el];
-          const float sc = csum ? 1.f : 1.f / (float)max(a.row_ptr[i + 1] - a.row_ptr[i], 1);
-          const float inv = normalize ? 1.f / (sqrtf(gq.w) + 1e-8f) : 1.f;
-          const float coef = (i == jn) ? 0.f : a.phi[e] * inv;   // self-loop: no coordinate gradient
-          const float* gx = a.gx_out + (int64_t)i * 3;
-          a.gdstore[e] = make_float4(gx[0] * sc * coef + 2.f * gr * gq.x, gx[1] * sc * coef + 2.f * gr * gq.y,
-                                     gx[2] * sc * coef + 2.f * gr * gq.z, 0.f);
+          const float coef = pphi * pt.w;   // pt.w is 0 on a self-loop: no coordinate gradient
+          a.gdstore[e] = make_float4(pt.x * coef + 2.f * gr * gq.x, pt.y * coef + 2.f * gr * gq.y,
+                                     pt.z * coef + 2.f * gr * gq.z, 0.f);
         }
       }
     }
@@ -869,12 +887,14 @@ int launch_gemm(const RowsGemmArgs& a, int G, cudaStream_t s, const char* name) 
   return EGNN_OK;
 }
 
-int launch_u(const EdgeCommon& a, const RowsBufs& b, cudaStream_t s) {
+// gx_out: the backward's dL/dx' (the gather then also writes S1 and gtr).
+int launch_u(const EdgeCommon& a, const RowsBufs& b, const float* gx_out, cudaStream_t s) {
   const int64_t Epad = rows_tiles(a.E) * 128;
   if (Epad == 0) return EGNN_OK;
   TimerScope ts("edge_rows_u", s);
-  EGNN_CHECK_CUDA(launch_pdl(b.S1 ? rows_u_kernel<true> : rows_u_kernel<false>, dim3((unsigned)(Epad / (8 * EPW))),
-                             dim3(256), 0, s, a.E, Epad, a.row_idx, a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo, b.S1));
+  EGNN_CHECK_CUDA(launch_pdl(gx_out ? rows_u_kernel<true> : rows_u_kernel<false>, dim3((unsigned)(Epad / (8 * EPW))),
+                             dim3(256), 0, s, a.E, Epad, a.row_idx, a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo, b.S1,
+                             a.row_ptr, gx_out, a.flags, b.gtr));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
@@ -886,10 +906,9 @@ RowsGemmArgs gemm_common(const EdgeCommon& a, const RowsBufs& b) {
   g.wc2 = a.wc2;
   g.wr = a.wr;
   g.geo = b.geo;
+  g.gtr = b.gtr;
   g.phi = b.phi;
-  g.row_ptr = a.row_ptr;
   g.row_idx = a.row_idx;
-  g.col_idx = a.col_idx;
   g.part = b.part;
   g.PF = edge_part_floats(kH, 0);
   g.flags = a.flags;
@@ -919,6 +938,7 @@ RowsBufs carve_rows(Carver& c, int64_t E, int H, bool bwd, int num_sms) {
     b.Ga2 = c.take<char>(tiles);
     b.D2 = c.take<__half>(En * H);
     b.S1 = c.take<__half>(En * H);
+    b.gtr = c.take<float4>(En);
   } else {
     b.M32 = c.take<float>(En * H);
   }
@@ -931,7 +951,7 @@ RowsBufs carve_rows(Carver& c, int64_t E, int H, bool bwd, int num_sms) {
 
 int edge_fwd_rows(const EdgeFwdArgs& a, const RowsBufs& b, cudaStream_t s) {
   if (a.E > 0) {
-    EGNN_TRY(launch_u(a, b, s));
+    EGNN_TRY(launch_u(a, b, nullptr, s));
     RowsGemmArgs g = gemm_common(a, b);
     g.A = b.U;
     g.W = a.W2_src;
@@ -958,7 +978,7 @@ int edge_fwd_rows(const EdgeFwdArgs& a, const RowsBufs& b, cudaStream_t s) {
 int edge_bwd_rows(const EdgeBwdArgs& a, const RowsBufs& b, cudaStream_t s) {
   RowsGemmArgs g = gemm_common(a, b);
   if (a.E > 0) {
-    EGNN_TRY(launch_u(a, b, s));
+    EGNN_TRY(launch_u(a, b, a.gx_out, s));
     g.A = b.U;
     g.W = a.W2_src;
     g.bias = a.b2;
@@ -973,7 +993,6 @@ int edge_bwd_rows(const EdgeBwdArgs& a, const RowsBufs& b, cudaStream_t s) {
   g.bias = a.bc1;
   g.outb = b.Gc1;
   g.outf = nullptr;
-  g.gx_out = a.gx_out;
   EGNN_TRY(launch_gemm<EPI_GC1>(g, b.G, s, "edge_rows_gemm"));
   g.A = b.Gc1;
   g.bias = nullptr;

@@ -30,6 +30,7 @@ struct RowsBufs {
   float* M32 = nullptr;  // (E, H) fp32 m (forward, for the row sums)
   __half* D2 = nullptr;  // (E, H) fp16 silu'(a2 + b2) (backward)
   __half* S1 = nullptr;  // (E, H) fp16 silu'(a1) (backward)
+  float4* gtr = nullptr; // (E) backward: dL/dx'_i s_i (xyz), 1 / (|d| + eps) or 0 on a self-loop (w)
   float* phi = nullptr;  // (E) coordinate weight phi_e
   float4* geo = nullptr; // (E) x_i - x_j, |x_i - x_j|^2
   float* part = nullptr; // (G, edge_part_floats(H, 0)) per-CTA weight-gradient partials
@@ -37,7 +38,7 @@ struct RowsBufs {
 };
 
 // Carves the buffers from a workspace (fwd: U, Mb, M32, phi, geo; bwd: U,
-// Mb, Gc1, Ga2, D2, S1, phi, geo, part).
+// Mb, Gc1, Ga2, D2, S1, gtr, phi, geo, part).
 RowsBufs carve_rows(Carver& c, int64_t E, int H, bool bwd, int num_sms);
 
 // Forward: agg, x_out.

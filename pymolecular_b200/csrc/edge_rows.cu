@@ -520,6 +520,11 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
       // phi for g_a1), likewise requested before the wait
       float4 pg = make_float4(0.f, 0.f, 0.f, 0.f), pt = pg;
       float pphi = 0.f;
+      int prow = 0;   // g_a2: the edge's destination row of dL/dagg
+      if constexpr (EPI == EPI_GA2) {
+        const int64_t ep = (blockIdx.x + j * G) * 128 + el;
+        if (ep < a.E) prow = a.row_idx[ep];
+      }
       if constexpr (EPI == EPI_GC1 || EPI == EPI_GA1) {
         const int64_t ep = (blockIdx.x + j * G) * 128 + el;
         if (ep < a.E) {
@@ -664,7 +669,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           grad_pass(gbase * (1.f - f * f), unused);
         }
       } else if constexpr (EPI == EPI_GA2) {
-        const int i = valid ? a.row_idx[e] : 0;
+        const int i = prow;
 #pragma unroll 1
         for (int p = 0; p < 2; ++p) {
           float v[32];

@@ -960,9 +960,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
 // For node v, over its in-edges (its CSR row: S_dst, gd_dst) and over its
 // out-edges (transpose CSR: S_src, gd_src), then
 // dL/dx_v = dL/dx'_v + gd_dst - gd_src.  SPLIT warps per node, each owning
-// H / SPLIT features (lane: H / (32 SPLIT) consecutive ones); four rows of
-// each list in flight per warp, each list added in CSR-position order.
-template <int H, int SPLIT>
+// H / SPLIT features (lane: H / (32 SPLIT) consecutive ones); UR rows of each
+// list in flight per warp, each list added in CSR-position order.
+template <int H, int SPLIT, int UR>
 __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
                                  const int32_t* __restrict__ src_ptr, const int32_t* __restrict__ src_edge,
                                  const __nv_bfloat16* __restrict__ gstore, const float4* __restrict__ gdstore,
@@ -987,45 +987,45 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
   const int ked = row_ptr[v + 1];
   int ks = src_ptr[v];
   const int kes = src_ptr[v + 1];
-  while (kd + 4 <= ked || ks + 4 <= kes) {   // warp-uniform
-    const bool bd = kd + 4 <= ked, bs = ks + 4 <= kes;
-    int64_t p[4];
-    float vd[4][VW], vs[4][VW], gd1[4], gs1[4];
+  while (kd + UR <= ked || ks + UR <= kes) {   // warp-uniform
+    const bool bd = kd + UR <= ked, bs = ks + UR <= kes;
+    int64_t p[UR];
+    float vd[UR][VW], vs[UR][VW], gd1[UR], gs1[UR];
     if (bs) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) p[u] = src_edge[ks + u];
+      for (int u = 0; u < UR; ++u) p[u] = src_edge[ks + u];
     }
     if (bd) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < UR; ++u) {
         load_row_slice<HS>(gstore + (int64_t)(kd + u) * H, lane, vd[u]);
         gd1[u] = comp(kd + u);
       }
     }
     if (bs) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < UR; ++u) {
         load_row_slice<HS>(gstore + p[u] * H, lane, vs[u]);
         gs1[u] = comp(p[u]);
       }
     }
     if (bd) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < UR; ++u) {
 #pragma unroll
         for (int c = 0; c < VW; ++c) sd[c] += vd[u][c];
         gdd += gd1[u];
       }
-      kd += 4;
+      kd += UR;
     }
     if (bs) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < UR; ++u) {
 #pragma unroll
         for (int c = 0; c < VW; ++c) ss[c] += vs[u][c];
         gds += gs1[u];
       }
-      ks += 4;
+      ks += UR;
     }
   }
   for (; kd < ked; ++kd) {
@@ -1121,7 +1121,7 @@ int edge_node_pass_tc(int H, int64_t N, const int32_t* row_ptr, const int32_t* s
   const unsigned blocks = (unsigned)((N * split + warps - 1) / warps);
   {
     TimerScope ts("node_pass", s);
-    auto kern = H == 128 ? node_pass_kernel<128, 1> : node_pass_kernel<256, 2>;
+    auto kern = H == 128 ? node_pass_kernel<128, 1, 4> : node_pass_kernel<256, 2, 4>;
     EGNN_CHECK_CUDA(launch_pdl(kern, dim3(blocks), dim3(warps * 32), 0, s, N, row_ptr, src_ptr, src_edge,
                                static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, S_dst, S_src, gx));
   }

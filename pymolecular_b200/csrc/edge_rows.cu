@@ -210,7 +210,7 @@ __device__ void load_w256(char* tile, const float* __restrict__ W) {
 }
 
 // ---- gather: geometry and u1 = bf16(silu(P_i + Q_j + w_r r)) -------------------------
-// One warp per EPW consecutive edges of the padded tile range, their index,
+// A warp takes groups of EPW consecutive edges of the padded tile range, their
 // coordinate and P / Q row loads all in flight together; lane owns features
 // 8 lane .. + 7 (16 bytes of each tile row).  Padding rows (e >= E) are zero.
 // With S1 (backward) the warp also stores silu'(a1) as fp16 rows (E, 256).
@@ -226,80 +226,96 @@ __global__ void __launch_bounds__(256) rows_u_kernel(int64_t E, int64_t Epad, co
                                                      float4* __restrict__ gtr) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
-  const int64_t e0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * EPW;
-  if (e0 >= Epad) return;
+  const int64_t ngroups = Epad / EPW, gstride = (int64_t)gridDim.x * 8;
+  int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (g >= ngroups) return;
+  const float4 w0 = ldg4(wr + 8 * lane), w1 = ldg4(wr + 8 * lane + 4);
+  const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  // grid-stride over groups of EPW edges; each iteration requests the next
+  // group's indices while this group's rows are in flight
   int iv[EPW], jv[EPW];
 #pragma unroll
   for (int k = 0; k < EPW; ++k) {
-    const bool ok = e0 + k < E;
-    iv[k] = ok ? row_idx[e0 + k] : 0;
-    jv[k] = ok ? col_idx[e0 + k] : 0;
+    const int64_t e = g * EPW + k;
+    iv[k] = e < E ? row_idx[e] : 0;
+    jv[k] = e < E ? col_idx[e] : 0;
   }
-  // backward: lane k < EPW also forms edge e0 + k's coordinate-gradient
-  // factors (its loads issued here, beside the row loads below)
-  const bool gl = WITH_S1 && lane < EPW && e0 + lane < E;
-  int mi = 0, mj = 0, rp0 = 0, rp1 = 0;
-  float gxv[3] = {0.f, 0.f, 0.f}, myr = 0.f;
+#pragma unroll 1
+  for (; g < ngroups; g += gstride) {
+    const int64_t e0 = g * EPW;
+    // backward: lane k < EPW also forms edge e0 + k's coordinate-gradient
+    // factors (its loads issued here, beside the row loads below)
+    const bool gl = WITH_S1 && lane < EPW && e0 + lane < E;
+    int mi = 0, mj = 0, rp0 = 0, rp1 = 0;
+    float gxv[3] = {0.f, 0.f, 0.f}, myr = 0.f;
 #pragma unroll
-  for (int k = 0; k < EPW; ++k)
-    if (lane == k) { mi = iv[k]; mj = jv[k]; }
-  if (gl) {
-    rp0 = row_ptr[mi];
-    rp1 = row_ptr[mi + 1];
+    for (int k = 0; k < EPW; ++k)
+      if (lane == k) { mi = iv[k]; mj = jv[k]; }
+    if (gl) {
+      rp0 = row_ptr[mi];
+      rp1 = row_ptr[mi + 1];
 #pragma unroll
-    for (int c = 0; c < 3; ++c) gxv[c] = gx_out[(int64_t)mi * 3 + c];
-  }
-  float4 xi[EPW], xj[EPW], pv[EPW][2], qv[EPW][2];
-#pragma unroll
-  for (int k = 0; k < EPW; ++k) {
-    xi[k] = xp[iv[k]];
-    xj[k] = xp[jv[k]];
-    const float* P = PQ + (int64_t)iv[k] * 2 * kH + 8 * lane;
-    const float* Q = PQ + (int64_t)jv[k] * 2 * kH + kH + 8 * lane;
-    pv[k][0] = ldg4(P);
-    pv[k][1] = ldg4(P + 4);
-    qv[k][0] = ldg4(Q);
-    qv[k][1] = ldg4(Q + 4);
-  }
-  const float4 w0 = ldg4(wr + 8 * lane), w1 = ldg4(wr + 8 * lane + 4);
-  const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-  for (int k = 0; k < EPW; ++k) {
-    const int64_t e = e0 + k;
-    const bool ok = e < E;
-    const float dx = xi[k].x - xj[k].x, dy = xi[k].y - xj[k].y, dz = xi[k].z - xj[k].z;
-    const float r = dx * dx + dy * dy + dz * dz;
-    if (ok && lane == 0) geo[e] = make_float4(dx, dy, dz, r);
-    if (lane == k) myr = r;
-    const float pp[8] = {pv[k][0].x, pv[k][0].y, pv[k][0].z, pv[k][0].w, pv[k][1].x, pv[k][1].y, pv[k][1].z, pv[k][1].w};
-    const float qq[8] = {qv[k][0].x, qv[k][0].y, qv[k][0].z, qv[k][0].w, qv[k][1].x, qv[k][1].y, qv[k][1].z, qv[k][1].w};
-    float u[8], d[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float a1 = fmaf(w[c], r, pp[c] + qq[c]);
-      if constexpr (WITH_S1) silu_grad_edge(a1, u[c], d[c]);
-      else u[c] = silu_edge(a1);
-      if (!ok) u[c] = 0.f;
+      for (int c = 0; c < 3; ++c) gxv[c] = gx_out[(int64_t)mi * 3 + c];
     }
-    const int64_t t = e >> 7;
-    const int rl = (int)(e & 127), blk = lane >> 3, ch = lane & 7;
-    const uint4 pk = make_uint4(pack_bf16x2(u[0], u[1]), pack_bf16x2(u[2], u[3]), pack_bf16x2(u[4], u[5]),
-                                pack_bf16x2(u[6], u[7]));
-    *reinterpret_cast<uint4*>(U + t * kTile + blk * kBlk + rl * 128 + ((ch ^ (rl & 7)) << 4)) = pk;
-    if (WITH_S1 && ok) {
-      uint32_t hw[4];
+    float4 xi[EPW], xj[EPW], pv[EPW][2], qv[EPW][2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const __half2 h2 = __floats2half2_rn(d[2 * c], d[2 * c + 1]);
-        hw[c] = *reinterpret_cast<const uint32_t*>(&h2);
+    for (int k = 0; k < EPW; ++k) {
+      xi[k] = xp[iv[k]];
+      xj[k] = xp[jv[k]];
+      const float* P = PQ + (int64_t)iv[k] * 2 * kH + 8 * lane;
+      const float* Q = PQ + (int64_t)jv[k] * 2 * kH + kH + 8 * lane;
+      pv[k][0] = ldg4(P);
+      pv[k][1] = ldg4(P + 4);
+      qv[k][0] = ldg4(Q);
+      qv[k][1] = ldg4(Q + 4);
+    }
+    const int64_t gn = g + gstride;
+#pragma unroll
+    for (int k = 0; k < EPW; ++k) {
+      const int64_t e = gn * EPW + k;
+      iv[k] = (gn < ngroups && e < E) ? row_idx[e] : 0;
+      jv[k] = (gn < ngroups && e < E) ? col_idx[e] : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < EPW; ++k) {
+      const int64_t e = e0 + k;
+      const bool ok = e < E;
+      const float dx = xi[k].x - xj[k].x, dy = xi[k].y - xj[k].y, dz = xi[k].z - xj[k].z;
+      const float r = dx * dx + dy * dy + dz * dz;
+      if (ok && lane == 0) geo[e] = make_float4(dx, dy, dz, r);
+      if (lane == k) myr = r;
+      const float pp[8] = {pv[k][0].x, pv[k][0].y, pv[k][0].z, pv[k][0].w,
+                           pv[k][1].x, pv[k][1].y, pv[k][1].z, pv[k][1].w};
+      const float qq[8] = {qv[k][0].x, qv[k][0].y, qv[k][0].z, qv[k][0].w,
+                           qv[k][1].x, qv[k][1].y, qv[k][1].z, qv[k][1].w};
+      float u[8], d[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float a1 = fmaf(w[c], r, pp[c] + qq[c]);
+        if constexpr (WITH_S1) silu_grad_edge(a1, u[c], d[c]);
+        else u[c] = silu_edge(a1);
+        if (!ok) u[c] = 0.f;
       }
-      *reinterpret_cast<uint4*>(S1 + e * kH + 8 * lane) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      const int64_t t = e >> 7;
+      const int rl = (int)(e & 127), blk = lane >> 3, ch = lane & 7;
+      const uint4 pk = make_uint4(pack_bf16x2(u[0], u[1]), pack_bf16x2(u[2], u[3]), pack_bf16x2(u[4], u[5]),
+                                  pack_bf16x2(u[6], u[7]));
+      *reinterpret_cast<uint4*>(U + t * kTile + blk * kBlk + rl * 128 + ((ch ^ (rl & 7)) << 4)) = pk;
+      if (WITH_S1 && ok) {
+        uint32_t hw[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const __half2 h2 = __floats2half2_rn(d[2 * c], d[2 * c + 1]);
+          hw[c] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(S1 + e * kH + 8 * lane) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      }
     }
-  }
-  if (gl) {   // (g_t s_i, 1 / (|d| + eps)) with the second term 0 on self-loops
-    const float sc = (flags & EGNN_FLAG_COORDS_SUM) ? 1.f : 1.f / (float)max(rp1 - rp0, 1);
-    const float inv = (flags & EGNN_FLAG_NORMALIZE) ? 1.f / (sqrtf(myr) + 1e-8f) : 1.f;
-    gtr[e0 + lane] = make_float4(gxv[0] * sc, gxv[1] * sc, gxv[2] * sc, mi == mj ? 0.f : inv);
+    if (gl) {   // (g_t s_i, 1 / (|d| + eps)) with the second term 0 on self-loops
+      const float sc = (flags & EGNN_FLAG_COORDS_SUM) ? 1.f : 1.f / (float)max(rp1 - rp0, 1);
+      const float inv = (flags & EGNN_FLAG_NORMALIZE) ? 1.f / (sqrtf(myr) + 1e-8f) : 1.f;
+      gtr[e0 + lane] = make_float4(gxv[0] * sc, gxv[1] * sc, gxv[2] * sc, mi == mj ? 0.f : inv);
+    }
   }
 }
 
@@ -897,7 +913,10 @@ int launch_u(const EdgeCommon& a, const RowsBufs& b, const float* gx_out, cudaSt
   const int64_t Epad = rows_tiles(a.E) * 128;
   if (Epad == 0) return EGNN_OK;
   TimerScope ts("edge_rows_u", s);
-  EGNN_CHECK_CUDA(launch_pdl(gx_out ? rows_u_kernel<true> : rows_u_kernel<false>, dim3((unsigned)(Epad / (8 * EPW))),
+  // grid-stride: the 256-thread blocks that fit an SM by registers (about 60 per
+  // thread in the forward variant, 128 in the backward one)
+  const int64_t blocks = std::min<int64_t>(Epad / (8 * EPW), (gx_out ? 2 : 4) * (int64_t)num_sms_current());
+  EGNN_CHECK_CUDA(launch_pdl(gx_out ? rows_u_kernel<true> : rows_u_kernel<false>, dim3((unsigned)blocks),
                              dim3(256), 0, s, a.E, Epad, a.row_idx, a.col_idx, a.xp, a.PQ, a.wr, b.U, b.geo, b.S1,
                              a.row_ptr, gx_out, a.flags, b.gtr));
   EGNN_CHECK_LAUNCH();

@@ -67,7 +67,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Wait for phase `parity` of `bar`: false once 2 s have passed (the CTA's
 // abort flag is raised and the event counted) or, when `abort_flag` is
 // given, once another thread has raised it.
-__device__ __noinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* raise_flag) {
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* raise_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (;;) {
@@ -141,6 +141,33 @@ __device__ __forceinline__ void store_rows64(char* stg, const uint32_t (&w)[16],
     if (d) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(d) + ((cc ^ pm) << 4)) = val;
   }
   __syncwarp();
+}
+
+// Warp-collective load of the 128-byte slices (fp16 features 64 cs .. + 63) of
+// rows row0 .. row0 + 31 of a row-major (E, 256) fp16 matrix: lane l receives
+// row row0 + l in side[].  Eight lanes read each slice (four whole 128-byte
+// lines per load instruction), in two rounds of 16 rows through the warp's
+// 2 KB staging (XOR-swizzled slots); rows >= E read row 0 (the caller masks them).
+__device__ __forceinline__ void load_rows128(char* stg, const __half* base, int64_t row0, int64_t E, int cs,
+                                             uint4 (&side)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int rr = 4 * k + (lane >> 3), c = lane & 7;
+      const int64_t row = row0 + 16 * h + rr;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + (row < E ? row : 0) * kH + cs * 64) + c);
+      *reinterpret_cast<uint4*>(stg + rr * 128 + ((c ^ (rr & 7)) << 4)) = v;
+    }
+    __syncwarp();
+    if ((lane >> 4) == h) {
+      const int rr = lane & 15;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) side[c] = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((c ^ (rr & 7)) << 4));
+    }
+    __syncwarp();
+  }
 }
 
 // 32 values = features 64 cs + 32 p .. + 31 of row `el` of the tile at `tb`
@@ -549,12 +576,8 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           if (EPI == EPI_GA1) pphi = a.phi[ep];
         }
       }
-      if constexpr (EPI == EPI_GA2 || EPI == EPI_GA1) {
-        const int64_t ep = (blockIdx.x + j * G) * 128 + el;
-        const __half* sp = (EPI == EPI_GA2 ? a.aux : a.s1) + (ep < a.E ? ep : 0) * kH + cs * 64;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) side[c] = __ldg(reinterpret_cast<const uint4*>(sp) + c);
-      }
+      if constexpr (EPI == EPI_GA2 || EPI == EPI_GA1)
+        load_rows128(stg, EPI == EPI_GA2 ? a.aux : a.s1, (blockIdx.x + j * G) * 128 + q * 32, a.E, cs, side);
       const bool ok = wait_bar(&accf[buf], (j >> 1) & 1, abort_f, abort_s);
       if (kJoint ? epi_any(!ok) : !__all_sync(0xffffffffu, ok)) break;
       fence_after_sync();

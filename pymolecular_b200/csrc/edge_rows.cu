@@ -31,10 +31,14 @@
 // (no tensor map, no multicast) moves a block; an mbarrier counts its bytes.
 //
 // GEMM kernel (one CTA per SM, 576 threads): warp 0 streams the A blocks of
-// the CTA's tiles through a 4-stage ring, warp 1 issues tcgen05.mma (M = 128
+// the CTA's tiles through a 3-stage ring, warp 1 issues tcgen05.mma (M = 128
 // edges, N = 256, K = 16 per instruction) into one of two TMEM accumulators
 // (2 x 256 columns), warps 2..17 run the epilogue of tile j while the MMAs of
-// tile j + 1 run.  Every wait is bounded (2 s of global time); a thread that
+// tile j + 1 run.  An epilogue thread owns one edge row and 64 features, so its
+// row-major global traffic would touch 32 rows per warp instruction: stores and
+// the fp16 side-row loads go through a 2 KB per-warp shared staging instead, so
+// that each instruction moves whole 64- or 128-byte row pieces.  Every wait is
+// bounded (2 s of global time); a thread that
 // gives up raises a CTA abort flag that every other wait honours, the count
 // is reported by egnn_device_status, and the CTA frees its TMEM and exits.
 // Column sums (bias and w_c2 / w_r gradients) are per-warp transposing

@@ -1116,12 +1116,13 @@ int edge_node_pass_tc(int H, int64_t N, const int32_t* row_ptr, const int32_t* s
                       float* gx, cudaStream_t s) {
   if (H != 128 && H != 256) return fail(EGNN_ERR_UNSUPPORTED, "node pass built for H = 128, 256");
   if (N <= 0) return EGNN_OK;
-  // H = 256: two warps per node (more rows in flight per node)
-  const int warps = 8, split = H == 128 ? 1 : 2;
+  // H = 256: four warps per node (more rows in flight per node; at H = 128 a
+  // second warp per node measured slower)
+  const int warps = 8, split = H == 128 ? 1 : 4;
   const unsigned blocks = (unsigned)((N * split + warps - 1) / warps);
   {
     TimerScope ts("node_pass", s);
-    auto kern = H == 128 ? node_pass_kernel<128, 1, 4> : node_pass_kernel<256, 2, 4>;
+    auto kern = H == 128 ? node_pass_kernel<128, 1, 4> : node_pass_kernel<256, 4, 4>;
     EGNN_CHECK_CUDA(launch_pdl(kern, dim3(blocks), dim3(warps * 32), 0, s, N, row_ptr, src_ptr, src_edge,
                                static_cast<const __nv_bfloat16*>(gstore), gdstore, gx_out, S_dst, S_src, gx));
   }

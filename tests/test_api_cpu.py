@@ -76,6 +76,31 @@ def test_attention_workspace_holds_gate_scratch():
     assert 0 < extra <= 148 * 8 * (64 * 128 + 16 * 129) * 4 + 256
 
 
+def test_edge_row_path_workspace_holds_the_per_edge_operands():
+    """bf16 mode at H = 256 runs the edge-row tensor-core GEMMs, whose workspace
+    carries the per-edge operands between kernels; the fused paths keep only
+    per-edge gradients (backward) and nothing per edge in the forward."""
+    lib = nat.lib()
+
+    def per_edge(which, prec, H):
+        E0, E1 = 100_000, 1_100_000
+        d0 = nat.LayerDesc(30000, E0, H, 0, nat.FLAG_RESIDUAL, prec)
+        d1 = nat.LayerDesc(30000, E1, H, 0, nat.FLAG_RESIDUAL, prec)
+        return (lib.egnn_workspace_size(C.byref(d1), which, 148) -
+                lib.egnn_workspace_size(C.byref(d0), which, 148)) / (E1 - E0)
+
+    # forward: u1 and m tiles (2 x 512 B), fp32 m (1 KB), phi, geometry (16 B)
+    assert 2048 + 16 <= per_edge(nat.WS_FWD, nat.PREC_BF16, 256) < 2048 + 64
+    # backward: four bf16 tiles and two fp16 row sets (6 x 512 B), dL/da1 rows
+    # (1 KB slot), coordinate gradients, factors, geometry, phi
+    assert 3072 + 1024 + 48 <= per_edge(nat.WS_BWD, nat.PREC_BF16, 256) < 3072 + 1024 + 128
+    # fp32 mode (SIMT kernels) and the fused H = 128 tensor-core path
+    assert per_edge(nat.WS_FWD, nat.PREC_FP32, 256) == 0
+    assert per_edge(nat.WS_BWD, nat.PREC_FP32, 256) == 256 * 4 + 16
+    assert per_edge(nat.WS_FWD, nat.PREC_BF16, 128) == 0
+    assert per_edge(nat.WS_BWD, nat.PREC_BF16, 128) == 128 * 4 + 16
+
+
 def test_attention_state_dict_matches_reference():
     c = load_golden("model_attention_molecules")
     torch.manual_seed(7)

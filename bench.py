@@ -551,7 +551,8 @@ def run_b200(args):
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peaks['source']} bf16 sustained",
                          "traffic": (ncu_traffic(args.config, "edge_bwd", prob.edges_rank)
-                                     if prob.precision == "bf16" and H == 128 else None),
+                                     if prob.precision == "bf16" and H == 128 else
+                                     ncu_traffic(args.config, kname, prob.edges_rank) if rows_path else None),
                          "traffic_unit": "bytes per launch (ncu capture)",
                          "per_launch_ms": per_launch_ms, "launches": bwd_n,
                          "flops_per_launch": flops_launch,

@@ -5,7 +5,8 @@ says how the CUDA kernels round while computing it, so that a bf16-GEMM
 result can be checked much tighter than against fp64 alone.  It follows the
 same factored algorithm as the kernels (egnn_clean.py:49-103 restated with
 W1 [h_i, h_j, r] = P_i + Q_j + w_r r) and rounds to bf16 exactly the GEMM
-operands the kernels round in bf16 mode; accumulation is float64.  With
+operands the kernels round in bf16 mode (edge_mlp.2.weight as a hi + lo
+pair of bf16 values); accumulation is float64.  With
 precision='fp32' nothing is rounded and it is a second fp64 restatement of
 the layer's forward and hand-derived backward.
 """
@@ -21,14 +22,24 @@ def _bf(t, on):
     return t.to(torch.bfloat16).to(t.dtype) if on else t
 
 
+def _split(t, on):
+    """hi + lo with hi = bf16(t), lo = bf16(t - hi): the value a pair of bf16
+    MMAs (x W_hi + x W_lo) multiplies by, about 16 significant bits."""
+    if not on:
+        return t
+    hi = _bf(t, True)
+    return hi + _bf(t - hi, True)
+
+
 def _silu(a):
     s = torch.sigmoid(a)
     return a * s, s * (1 + a * (1 - s))
 
 
 def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", residual=True,
-                  attention=False, normalize=False, tanh=False, coords_agg="mean"):
-    """(h', x', dL/dh, dL/dx, {param: grad}) with the kernels' rounding points."""
+                  attention=False, normalize=False, tanh=False, coords_agg="mean", backward=True):
+    """(h', x', dL/dh, dL/dx, {param: grad}) with the kernels' rounding points
+    (with backward=False: (h', x', None, None, {}))."""
     on = precision == "bf16"
     d = torch.float64
     h, x, gh, gx = h.to(d), x.to(d), gh.to(d), gx.to(d)
@@ -41,7 +52,7 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     Wn1, bn1, Wn2, bn2 = p["node_mlp.0.weight"], p["node_mlp.0.bias"], p["node_mlp.2.weight"], p["node_mlp.2.bias"]
     Wc1, bc1, wc2 = p["coord_mlp.0.weight"], p["coord_mlp.0.bias"], p["coord_mlp.2.weight"][0]
     deg = torch.bincount(row, minlength=N).to(d)
-    scale = torch.ones(N, dtype=d) if coords_agg == "sum" else 1.0 / deg.clamp(min=1)
+    scale = torch.ones(N, dtype=d, device=h.device) if coords_agg == "sum" else 1.0 / deg.clamp(min=1)
 
     # ---- forward
     P = h @ Wa.t() + b1
@@ -54,7 +65,11 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
         a1 = a1 + edge_attr.to(d) @ We.t()
     u1, s1 = _silu(a1)
     u1 = _bf(u1, on)
-    a2 = u1 @ _bf(W2, on).t() + b2
+    # W2 enters every product as hi + lo (two bf16 MMAs): a plain bf16 W2 is
+    # the same rounding on every edge, and that systematic error is what the
+    # coordinate-MLP weight gradients (sums with heavy cancellation) amplify
+    W2s = _split(W2, on)
+    a2 = u1 @ W2s.t() + b2
     m, d2 = _silu(a2)
     if attention:
         # gate in full precision on the ungated message (egnn_clean.py:55-57)
@@ -76,6 +91,8 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     h_out = n1 @ Wn2.t() + bn2
     if residual:
         h_out = h_out + h
+    if not backward:
+        return h_out, x_out, None, None, {}
 
     # ---- backward
     g = {}
@@ -106,7 +123,7 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     g["edge_mlp.2.bias"] = g_a2.sum(0)
     ga2b = _bf(g_a2, on)
     g["edge_mlp.2.weight"] = ga2b.t() @ u1
-    g_a1 = (ga2b @ _bf(W2, on)) * s1
+    g_a1 = (ga2b @ W2s) * s1
     gr = g_a1 @ wr
     self_loop = (row == col).to(d)
     gdl = g_trans * (phi * inv * (1 - self_loop))[:, None] + 2 * gr[:, None] * dlt
@@ -145,8 +162,7 @@ def model_fwd_bwd(p, h0, x0, row, col, graph_index, target, n_layers, precision=
         pre = f"gcl_{i}."
         lp = {k[len(pre):]: v for k, v in p.items() if k.startswith(pre)}
         ins.append((h, x, lp))
-        zero_h, zero_x = torch.zeros_like(h), torch.zeros_like(x)
-        h, x, _, _, _ = layer_fwd_bwd(lp, h, row, col, x, zero_h, zero_x, precision=precision, **flags)
+        h, x, _, _, _ = layer_fwd_bwd(lp, h, row, col, x, h, x, precision=precision, backward=False, **flags)
     h_last = h
     out = h_last @ p["embedding_out.weight"].t() + p["embedding_out.bias"]
     G = target.shape[0]

@@ -148,6 +148,13 @@ __device__ __forceinline__ float bf16r(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// hi + lo with hi = bf16(v), lo = bf16(v - hi): the value a weight stored as
+// a pair of bf16 tiles contributes to a pair of MMAs (exact in fp32).
+__device__ __forceinline__ float bf16_split(float v) {
+  const float hi = bf16r(v);
+  return hi + bf16r(v - hi);
+}
+
 template <bool BF>
 __device__ __forceinline__ float maybe_bf(float v) {
   if constexpr (BF) return bf16r(v); else return v;

@@ -34,7 +34,15 @@
 // the CTA's tiles through a 3-stage ring, warp 1 issues tcgen05.mma (M = 128
 // edges, N = 256, K = 16 per instruction) into one of two TMEM accumulators
 // (2 x 256 columns), warps 2..17 run the epilogue of tile j while the MMAs of
-// tile j + 1 run.  An epilogue thread owns one edge row and 64 features, so its
+// tile j + 1 run.  The three products with W2 (a2 in the forward and in the
+// backward's recompute, g_u = G_a2 W2) multiply by W2 as a pair of bf16
+// matrices, hi = bf16(W2) and lo = bf16(W2 - hi): a single bf16 W2 is one
+// rounding shared by every edge, a systematic error that the coordinate-MLP
+// weight gradients amplify far past the bf16 tolerance.  Both halves (256 KB)
+// do not fit beside the ring, so these variants keep no weight resident: each
+// ring stage carries an A block and the matching 64-deep K slice of W2 hi and
+// lo (80 KB, two stages), copied from a bf16 image of W2 in global memory
+// that stays in L2 (written per layer call by rows_wimg_kernel).  An epilogue thread owns one edge row and 64 features, so its
 // row-major global traffic would touch 32 rows per warp instruction: stores and
 // the fp16 side-row loads go through a 2 KB per-warp shared staging instead, so
 // that each instruction moves whole 64- or 128-byte row pieces.  Every wait is
@@ -228,6 +236,23 @@ __device__ __forceinline__ float colsum32(float (&x)[32]) {
   return x[0];
 }
 
+// (256 x 256) fp32 W -> two bf16 tile images in global memory, the exact
+// shared-memory image load_w256 writes: img = bf16(W), img + 128 KB =
+// bf16(W - bf16(W)).
+__global__ void __launch_bounds__(256) rows_wimg_kernel(const float* __restrict__ W, char* __restrict__ img) {
+  pdl_enter();
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < kH * kH / 8; idx += gridDim.x * blockDim.x) {
+    const int o = idx / (kH / 8), c8 = (idx % (kH / 8)) * 8;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(W + o * kH + c8));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(W + o * kH + c8 + 4));
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    st_row8_bf16(img, kH, o, c8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] -= bf16r(v[k]);
+    st_row8_bf16(img + kH * kH * 2, kH, o, c8, v);
+  }
+}
+
 // (256 x 256) fp32 nn.Linear weight -> bf16 tile with rows = out, columns = in
 // (K-major operand of x W^T, MN-major operand of g W).
 __device__ void load_w256(char* tile, const float* __restrict__ W) {
@@ -410,6 +435,7 @@ enum { EPI_M_FWD = 0, EPI_M_BWD, EPI_PHI, EPI_GC1, EPI_GA2, EPI_GA1 };
 struct RowsGemmArgs {
   const char* A = nullptr;        // tiles of the A operand (K-major, K = 256)
   const float* W = nullptr;       // (256, 256) fp32 weight [out][in]
+  const char* Wimg = nullptr;     // W2 products: bf16 hi | lo images of W (rows_wimg_kernel)
   int64_t E = 0, ntiles = 0;
   const float* bias = nullptr;    // b2 (EPI_M_*) or bc1 (EPI_PHI, EPI_GC1)
   const float* wc2 = nullptr;
@@ -433,35 +459,44 @@ struct RowsGemmArgs {
 };
 
 constexpr int GM_NTH = 576;   // warp 0: loads; warp 1: MMA + TMEM; warps 2..17: epilogue
-constexpr int GM_S = 3;       // A ring stages (one 16 KB block each)
+constexpr int kWBlk = kH * 128;   // 32 KB: one 64-deep K slice of a 256 x 256 bf16 weight
+constexpr bool split_w(int epi) { return epi == EPI_M_FWD || epi == EPI_M_BWD || epi == EPI_GA1; }
+// Resident weight: W (128 KB) | ring of 3 A blocks.  Split W2 products: no
+// resident weight, a ring of 2 stages of [A block | W hi slice | W lo slice].
+template <bool SPLIT>
 struct GmLayout {
+  static constexpr int S = SPLIT ? 2 : 3;                          // ring stages
+  static constexpr int STAGE = SPLIT ? kBlk + 2 * kWBlk : kBlk;    // bytes per stage
   static constexpr int W = 0;
-  static constexpr int A = kH * kH * 2;               // 131072
-  static constexpr int BAR = A + GM_S * kBlk;         // 180224
-  static constexpr int RED = BAR + 256;               // float[2][4][128]
-  static constexpr int VEC = RED + 2 * 4 * 128 * 4;   // float[3][256]: bias, w_c2, w_r
-  static constexpr int STG = VEC + 3 * kH * 4;        // 16 epilogue warps x 2 KB store staging
+  static constexpr int A = SPLIT ? 0 : kH * kH * 2;
+  static constexpr int BAR = A + S * STAGE;             // 180224 / 163840
+  static constexpr int RED = BAR + 256;                 // float[2][4][128]
+  static constexpr int VEC = RED + 2 * 4 * 128 * 4;     // float[3][256]: bias, w_c2, w_r
+  static constexpr int STG = VEC + 3 * kH * 4;          // 16 epilogue warps x 2 KB store staging
   static constexpr size_t BYTES = STG + 16 * 2048 + 1024;
 };
 
 template <int EPI>
 __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
   constexpr bool BK = EPI <= EPI_GC1;   // B = W as [n][k] (x W^T), else W as [k][n] (g W)
+  constexpr bool SPLIT = split_w(EPI);
+  using L = GmLayout<SPLIT>;
+  constexpr int GM_S = L::S;
   constexpr uint32_t IDESC = make_idesc_bf16(128, kH, 0, BK ? 0 : 1);
   constexpr int NV = EPI == EPI_GC1 ? 2 : (EPI == EPI_GA2 || EPI == EPI_GA1) ? 1 : 0;
   extern __shared__ __align__(1024) char rg_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(rg_raw) + 1023) & ~uintptr_t(1023));
-  char* Wt = sm + GmLayout::W;
-  char* Ast = sm + GmLayout::A;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + GmLayout::BAR);
+  char* Wt = sm + L::W;
+  char* Ast = sm + L::A;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint64_t* empty = full + GM_S;
   uint64_t* accf = empty + GM_S;
   uint64_t* acce = accf + 2;
   uint64_t* fin = acce + 2;
   uint32_t* tmem_s = reinterpret_cast<uint32_t*>(fin + 1);
   int* abort_s = reinterpret_cast<int*>(tmem_s + 1);
-  float* red = reinterpret_cast<float*>(sm + GmLayout::RED);
-  float* vbias = reinterpret_cast<float*>(sm + GmLayout::VEC);
+  float* red = reinterpret_cast<float*>(sm + L::RED);
+  float* vbias = reinterpret_cast<float*>(sm + L::VEC);
   float* vwc2 = vbias + kH;
   float* vwr = vwc2 + kH;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -469,7 +504,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
   const int64_t ntl = (int64_t)blockIdx.x < a.ntiles ? (a.ntiles - 1 - blockIdx.x) / G + 1 : 0;
 
   // prologue (parameters only, before the wait on the previous kernel)
-  load_w256(Wt, a.W);
+  if constexpr (!SPLIT) load_w256(Wt, a.W);
   if (warp == 1) tmem_alloc(tmem_s, 512);
   if (tid == 0) {
     for (int s = 0; s < GM_S; ++s) {
@@ -503,8 +538,26 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
         for (int b = 0; b < 4; ++b, ++it) {
           const int s = it % GM_S;
           if (it >= GM_S && !(ok = wait_bar(&empty[s], ((it / GM_S) - 1) & 1, abort_f, abort_s))) break;
-          mbar_expect_tx(&full[s], kBlk);
-          bulk_g2s(Ast + s * kBlk, src + b * kBlk, kBlk, &full[s]);
+          char* st = Ast + s * L::STAGE;
+          mbar_expect_tx(&full[s], L::STAGE);
+          bulk_g2s(st, src + b * kBlk, kBlk, &full[s]);
+          if constexpr (SPLIT) {
+            // K slice b of W hi and lo: rows 64 b .. + 63 of the [k][n] image
+            // (4 column blocks of 8 KB) for g W, column block b of the [n][k]
+            // image (32 KB) for x W^T
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const char* wsrc = a.Wimg + h * kH * kH * 2;
+              char* wdst = st + kBlk + h * kWBlk;
+              if constexpr (BK) {
+                bulk_g2s(wdst, wsrc + b * kWBlk, kWBlk, &full[s]);
+              } else {
+#pragma unroll
+                for (int cb = 0; cb < 4; ++cb)
+                  bulk_g2s(wdst + cb * (kWBlk / 4), wsrc + cb * kWBlk + b * (kWBlk / 4), kWBlk / 4, &full[s]);
+              }
+            }
+          }
         }
       }
       if (!ok)   // copies still in flight land before the CTA exits
@@ -527,12 +580,27 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
           const int s = it % GM_S;
           if (!(ok = wait_bar(&full[s], (it / GM_S) & 1, abort_f, abort_s))) break;
           fence_after_sync();
+          const uint32_t sa = ab + s * L::STAGE;
+          if constexpr (SPLIT) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = make_desc(ab + s * kBlk + kk * 32, 16, 1024);
-            const uint64_t bd = BK ? make_desc(wb + b * (kH * 128) + kk * 32, 16, 1024)
-                                   : make_desc(wb + (4 * b + kk) * 2048, kH * 128, 1024);
-            mma_bf16(d, ad, bd, IDESC, (b | kk) ? 1u : 0u);
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t sw = sa + kBlk + h * kWBlk;
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = make_desc(sa + kk * 32, 16, 1024);
+                const uint64_t bd = BK ? make_desc(sw + kk * 32, 16, 1024)
+                                       : make_desc(sw + kk * 2048, kWBlk / 4, 1024);
+                mma_bf16(d, ad, bd, IDESC, (h | b | kk) ? 1u : 0u);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = make_desc(sa + kk * 32, 16, 1024);
+              const uint64_t bd = BK ? make_desc(wb + b * (kH * 128) + kk * 32, 16, 1024)
+                                     : make_desc(wb + (4 * b + kk) * 2048, kH * 128, 1024);
+              mma_bf16(d, ad, bd, IDESC, (b | kk) ? 1u : 0u);
+            }
           }
           mma_commit(&empty[s]);
         }
@@ -546,7 +614,7 @@ __global__ void __launch_bounds__(GM_NTH, 1) rows_gemm_kernel(RowsGemmArgs a) {
     // ---- epilogue: thread = (edge row el, 64-feature slice cs)
     const int q = warp & 3, cs = (warp - 2) >> 2, el = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    char* stg = sm + GmLayout::STG + (warp - 2) * 2048;
+    char* stg = sm + L::STG + (warp - 2) * 2048;
     const bool tanh_on = a.flags & EGNN_FLAG_TANH;
     // per-feature vectors (w_r comes from the prep kernel: read after the wait)
     for (int n = tid - 64; n < kH; n += 512) {
@@ -919,7 +987,8 @@ __global__ void __launch_bounds__(WG_NTH, 1) rows_wgrad_kernel(const char* __res
 
 template <int EPI>
 int launch_gemm(const RowsGemmArgs& a, int G, cudaStream_t s, const char* name) {
-  constexpr size_t bytes = GmLayout::BYTES;
+  constexpr size_t bytes = GmLayout<split_w(EPI)>::BYTES;
+  if (split_w(EPI) && !a.Wimg) return fail(EGNN_ERR_INVALID_ARG, "edge-row W2 product without its weight image");
   static uint64_t attr_set = 0;
   const uint64_t bit = device_bit();
   if (!(attr_set & bit)) {
@@ -980,6 +1049,7 @@ int rows_grid(int64_t E, int num_sms) {
 
 RowsBufs carve_rows(Carver& c, int64_t E, int H, bool bwd, int num_sms) {
   RowsBufs b;
+  b.W2img = c.take<char>((size_t)2 * kH * kH * 2);
   const size_t tiles = (size_t)std::max<int64_t>(rows_tiles(E), 1) * kTile;
   const size_t En = (size_t)std::max<int64_t>(E, 1);
   b.U = c.take<char>(tiles);
@@ -1000,12 +1070,22 @@ RowsBufs carve_rows(Carver& c, int64_t E, int H, bool bwd, int num_sms) {
   return b;
 }
 
+// bf16 hi / lo images of W2 for the split products.
+int launch_wimg(const float* W2, char* img, cudaStream_t s) {
+  TimerScope ts("edge_rows_wimg", s);
+  EGNN_CHECK_CUDA(launch_pdl(rows_wimg_kernel, dim3(32), dim3(256), 0, s, W2, img));
+  EGNN_CHECK_LAUNCH();
+  return EGNN_OK;
+}
+
 int edge_fwd_rows(const EdgeFwdArgs& a, const RowsBufs& b, cudaStream_t s) {
   if (a.E > 0) {
+    EGNN_TRY(launch_wimg(a.W2_src, b.W2img, s));
     EGNN_TRY(launch_u(a, b, nullptr, s));
     RowsGemmArgs g = gemm_common(a, b);
     g.A = b.U;
     g.W = a.W2_src;
+    g.Wimg = b.W2img;
     g.bias = a.b2;
     g.outb = b.Mb;
     g.outf = b.M32;
@@ -1028,6 +1108,8 @@ int edge_fwd_rows(const EdgeFwdArgs& a, const RowsBufs& b, cudaStream_t s) {
 
 int edge_bwd_rows(const EdgeBwdArgs& a, const RowsBufs& b, cudaStream_t s) {
   RowsGemmArgs g = gemm_common(a, b);
+  g.Wimg = b.W2img;
+  EGNN_TRY(launch_wimg(a.W2_src, b.W2img, s));
   if (a.E > 0) {
     EGNN_TRY(launch_u(a, b, a.gx_out, s));
     g.A = b.U;

@@ -23,6 +23,7 @@ int rows_grid(int64_t E, int num_sms);
 // 16 KB column blocks of 128 rows x 64 features in the 128-byte swizzle) or
 // row-major fp32.
 struct RowsBufs {
+  char* W2img = nullptr; // bf16 images of W2 hi | lo (256 KB) for the split W2 products
   char* U = nullptr;     // tiles: u1 = silu(a1)
   char* Mb = nullptr;    // tiles: m = silu(a2 + b2)
   char* Gc1 = nullptr;   // tiles: dL/dc1 (backward)

@@ -7,7 +7,7 @@
 // MMA tile and lane t of TMEM:
 //
 //   forward  u1 = silu(P_i + Q_j + w_r r)        CUDA cores -> bf16 tile U
-//            a2 = U W2^T                          tcgen05 -> TMEM
+//            a2 = U W2hi^T + U W2lo^T             tcgen05 -> TMEM
 //            m  = silu(a2 + b2)                   -> bf16 tile M, fp32 staging
 //            c1 = M Wc1^T                         tcgen05 -> TMEM
 //            phi = wc2 . silu(c1 + bc1)           per thread
@@ -18,10 +18,13 @@
 //            g_m  = G Wc1 + g_agg[i]              tcgen05 + CUDA cores
 //            g_a2 = g_m silu'(a2)                 -> tile G
 //            dW2  += G^T U   (TMEM, persistent)
-//            g_a1 = (G W2) silu'(a1)              -> global, one bf16 H-vector per edge
+//            g_a1 = (G W2hi + G W2lo) silu'(a1)   -> global, one bf16 H-vector per edge
 // The weight tiles live in shared memory for the whole kernel; one copy of
 // each serves the forward product (K-major B) and the data-gradient product
-// (MN-major B).  The row sums of g_a1 and of the coordinate gradients, over
+// (MN-major B).  W2 is held as two bf16 tiles, hi = bf16(W2) and
+// lo = bf16(W2 - hi), and every product with it is the pair of MMAs: a single
+// bf16 W2 would be one rounding shared by every edge, a systematic error that
+// the coordinate-MLP weight gradients amplify far past the bf16 tolerance.  The row sums of g_a1 and of the coordinate gradients, over
 // each node's in-edges and out-edges, are taken by node_pass_kernel.
 #include <algorithm>
 #include <climits>
@@ -51,21 +54,26 @@ struct TC {
   static_assert(H == 128, "tensor-core path built for H = 128");
   static constexpr int TILE = kM * H * 2;   // [128 x H] bf16 tile
   static constexpr int WT = H * H * 2;      // [H x H] bf16 weight tile
-  static constexpr int LDD = H + 8;         // fp16 staging row stride (halves)
   static constexpr uint32_t IDESC_FWD = make_idesc_bf16(kM, H, 0, 0);    // A K-major, B K-major
   static constexpr uint32_t IDESC_DGRAD = make_idesc_bf16(kM, H, 0, 1);  // B = W, MN-major
   static constexpr uint32_t IDESC_WGRAD = make_idesc_bf16(H, H, 1, 1);   // A = G^T, B = X, both MN-major
 };
 
 // Load an (H x H) fp32 nn.Linear weight into an SW128 bf16 tile (rows = out).
+// With `lo`, also the residual tile lo = bf16(W - bf16(W)).
 template <int H>
-__device__ void load_weight_tile(char* tile, const float* __restrict__ W) {
+__device__ void load_weight_tile(char* tile, const float* __restrict__ W, char* lo = nullptr) {
   for (int idx = threadIdx.x; idx < H * H / 8; idx += blockDim.x) {
     const int o = idx / (H / 8), c8 = (idx % (H / 8)) * 8;
     const float4 a = __ldg(reinterpret_cast<const float4*>(W + o * H + c8));
     const float4 b = __ldg(reinterpret_cast<const float4*>(W + o * H + c8 + 4));
-    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     st_row8_bf16(tile, H, o, c8, v);
+    if (lo) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] -= bf16r(v[k]);
+      st_row8_bf16(lo, H, o, c8, v);
+    }
   }
 }
 
@@ -243,14 +251,16 @@ __device__ __forceinline__ void st_row32_bf16(char* tile, int row, int col0, con
 }
 
 // ---- forward ----------------------------------------------------------------------
+// The U tile is free once the a2 product has completed, so the residual tile
+// of m (bf16(m - bf16(m)), the second operand of the agg product) reuses it.
 template <int H>
 struct FwdLayout {
   static constexpr size_t W2 = 0;
-  static constexpr size_t WC1 = W2 + TC<H>::WT;
-  static constexpr size_t U = WC1 + TC<H>::WT;
+  static constexpr size_t W2LO = W2 + TC<H>::WT;
+  static constexpr size_t WC1 = W2LO + TC<H>::WT;
+  static constexpr size_t U = WC1 + TC<H>::WT;         // u1, then bf16(m - bf16(m))
   static constexpr size_t M = U + TC<H>::TILE;
-  static constexpr size_t MLO = M + TC<H>::TILE;       // bf16(m - bf16(m))
-  static constexpr size_t S = MLO + TC<H>::TILE;       // 0/1 segment matrix [slot][edge]
+  static constexpr size_t S = M + TC<H>::TILE;         // 0/1 segment matrix [slot][edge]
   static constexpr size_t VEC = S + TC<H>::TILE;       // wr, b2, bc1, wc2
   static constexpr size_t PART = VEC + 4 * H * 4;      // float[4][128]
   static constexpr size_t DL = PART + 4 * kM * 4;      // float4[128]: dn.xyz, r
@@ -280,10 +290,11 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   extern __shared__ __align__(1024) char smem_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   char* W2t = sm + L::W2;
+  char* W2lo = sm + L::W2LO;
   char* Wc1t = sm + L::WC1;
   char* Ut = sm + L::U;
   char* Mt = sm + L::M;
-  char* Mlo = sm + L::MLO;
+  char* Mlo = Ut;   // U is dead once the a2 product has completed
   char* St = sm + L::S;
   float* s_wr = reinterpret_cast<float*>(sm + L::VEC);
   float* s_b2 = s_wr + H;
@@ -315,7 +326,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  load_weight_tile<H>(W2t, a.W2_src);
+  load_weight_tile<H>(W2t, a.W2_src, W2lo);
   load_weight_tile<H>(Wc1t, a.Wc1_src);
   for (int c = g.tid; c < H; c += kNT) {
     s_wr[c] = a.wr[c]; s_b2[c] = a.b2[c]; s_bc1[c] = a.bc1[c]; s_wc2[c] = a.wc2[c];
@@ -450,6 +461,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
 #pragma unroll
       for (int kk = 0; kk < H / 16; ++kk)
         mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2t, H, kk), C::IDESC_FWD, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2lo, H, kk), C::IDESC_FWD, 1u);
       mma_commit(bar);
     }
     if (prefetcher) {
@@ -586,15 +600,17 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
 }
 
 // ---- backward (dst pass) ---------------------------------------------------------------
+// silu'(a1) and silu'(a2) of the chunk live in TMEM as fp16 pairs (the
+// columns after the accumulator), so shared memory holds both W2 tiles.
 template <int H>
 struct BwdLayout {
   static constexpr size_t W2 = 0;
-  static constexpr size_t WC1 = W2 + TC<H>::WT;
+  static constexpr size_t W2LO = W2 + TC<H>::WT;
+  static constexpr size_t WC1 = W2LO + TC<H>::WT;
   static constexpr size_t U = WC1 + TC<H>::WT;
   static constexpr size_t M = U + TC<H>::TILE;
   static constexpr size_t G = M + TC<H>::TILE;
-  static constexpr size_t D2 = G + TC<H>::TILE;                       // fp16 [128][LDD]
-  static constexpr size_t VEC = D2 + (size_t)kM * TC<H>::LDD * 2;    // wr, b2, bc1, wc2
+  static constexpr size_t VEC = G + TC<H>::TILE;                      // wr, b2, bc1, wc2
   static constexpr size_t PART = VEC + 4 * H * 4;                     // float[4][128]
   static constexpr size_t DL = PART + 4 * kM * 4;                     // float4[128]: d.xyz, r
   static constexpr size_t GT = DL + kM * 16;                          // float4[128]: g_trans.xyz, inv
@@ -620,11 +636,11 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   extern __shared__ __align__(1024) char smem_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   char* W2t = sm + L::W2;
+  char* W2lo = sm + L::W2LO;
   char* Wc1t = sm + L::WC1;
   char* Ut = sm + L::U;
   char* Mt = sm + L::M;
   char* Gt = sm + L::G;
-  __half* d2s = reinterpret_cast<__half*>(sm + L::D2);
   float* s_wr = reinterpret_cast<float*>(sm + L::VEC);
   float* s_b2 = s_wr + H;
   float* s_bc1 = s_b2 + H;
@@ -646,13 +662,13 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
 
   const Geo g;
-  constexpr uint32_t NCOL = 4 * H;   // D0 | s1 | dWc1 | dW2
+  constexpr uint32_t NCOL = 4 * H;   // D0 | fp16 pairs of silu'(a1), silu'(a2) | dWc1 | dW2
   if (g.warp == 0) tmem_alloc(tmem_base_s, NCOL);
   if (g.tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  load_weight_tile<H>(W2t, a.W2_src);
+  load_weight_tile<H>(W2t, a.W2_src, W2lo);
   load_weight_tile<H>(Wc1t, a.Wc1_src);
   for (int c = g.tid; c < H; c += kNT) {
     s_wr[c] = a.wr[c]; s_b2[c] = a.b2[c]; s_bc1[c] = a.bc1[c]; s_wc2[c] = a.wc2[c];
@@ -663,7 +679,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tmem_base_s;
-  const uint32_t tD0 = tmem, tS1 = tmem + H, tWC1 = tmem + 2 * H, tW2 = tmem + 3 * H;
+  // tS1: silu'(a1) of feature f as the fp16 half (f & 1) of column f / 2;
+  // tD2 = tS1 + H / 2: silu'(a2) likewise
+  const uint32_t tD0 = tmem, tS1 = tmem + H, tD2 = tmem + H + H / 2, tWC1 = tmem + 2 * H, tW2 = tmem + 3 * H;
   uint32_t phase = 0;
 
   const int cta = blockIdx.x;
@@ -718,7 +736,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       }
     }
     __syncthreads();
-    // ---- a1 rows (coalesced); u1 slice -> tile U, s1 = silu'(a1) slice -> TMEM
+    // ---- a1 rows (coalesced); u1 slice -> tile U, s1 = silu'(a1) slice -> TMEM (fp16)
     gather_a1<4>(stage, a.PQ, rowi, coli, dl, s_wr, n, g.warp, g.lane);
     __syncthreads();
     {
@@ -730,13 +748,18 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
         if (!valid) { u[q] = 0.f; s1v[q] = 0.f; }
       }
       st_row32_bf16(Ut, g.e, g.col0, u);
-      tmem_st32(tS1 + g.lane_base + g.col0, s1v);
+      uint32_t w[16];
+      pack_half32(s1v, w);
+      tmem_st16u(tS1 + g.lane_base + g.col0 / 2, w);
     }
     handoff_to_mma();
     if (g.tid == 0) {
 #pragma unroll
       for (int kk = 0; kk < H / 16; ++kk)
         mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2t, H, kk), C::IDESC_FWD, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2lo, H, kk), C::IDESC_FWD, 1u);
       mma_commit(bar);
     }
     if (prefetcher) {
@@ -758,20 +781,16 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       cp_async_commit_group();
     }
 
-    // ---- m = silu(a2 + b2) -> tile M ; silu'(a2) -> fp16 staging
+    // ---- m = silu(a2 + b2) -> tile M ; silu'(a2) -> TMEM (fp16)
     {
-      float v[32];
+      float v[32], d2v[32];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
-      __half2* drow = reinterpret_cast<__half2*>(d2s + g.e * C::LDD + g.col0);
 #pragma unroll
-      for (int q = 0; q < 32; q += 2) {
-        float y0, d0, y1, d1;
-        silu_grad_edge(v[q] + s_b2[g.col0 + q], y0, d0);
-        silu_grad_edge(v[q + 1] + s_b2[g.col0 + q + 1], y1, d1);
-        v[q] = y0; v[q + 1] = y1;
-        drow[q / 2] = __floats2half2_rn(d0, d1);
-      }
+      for (int q = 0; q < 32; ++q) silu_grad_edge(v[q] + s_b2[g.col0 + q], v[q], d2v[q]);
       st_row32_bf16(Mt, g.e, g.col0, v);
+      uint32_t w[16];
+      pack_half32(d2v, w);
+      tmem_st16u(tD2 + g.lane_base + g.col0 / 2, w);
     }
     handoff_to_mma();
     if (g.tid == 0) {
@@ -841,13 +860,14 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
     // ---- g_a2 = (g_m + g_agg[i]) silu'(a2) -> tile G ; column sums
     {
       float v[32];
+      uint32_t w[16];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
-      const __half2* drow = reinterpret_cast<const __half2*>(d2s + g.e * C::LDD + g.col0);
+      tmem_ld16u(tD2 + g.lane_base + g.col0 / 2, w);
 #pragma unroll
       for (int q = 0; q < 32; q += 4) {
         const float4 g4 = gagg[q / 4];
-        const float2 d01 = __half22float2(drow[q / 2]);
-        const float2 d23 = __half22float2(drow[q / 2 + 1]);
+        const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&w[q / 2]));
+        const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&w[q / 2 + 1]));
         v[q] = valid ? (v[q] + g4.x) * d01.x : 0.f;
         v[q + 1] = valid ? (v[q + 1] + g4.y) * d01.y : 0.f;
         v[q + 2] = valid ? (v[q + 2] + g4.z) * d23.x : 0.f;
@@ -864,6 +884,9 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
 #pragma unroll
       for (int kk = 0; kk < H / 16; ++kk)
         mma_bf16(tD0, desc_k(Gt, kM, kk), desc_mn(W2t, H, kk), C::IDESC_DGRAD, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < H / 16; ++kk)
+        mma_bf16(tD0, desc_k(Gt, kM, kk), desc_mn(W2lo, H, kk), C::IDESC_DGRAD, 1u);
       mma_commit(bar);
     }
     first = false;
@@ -872,14 +895,18 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
     // ---- g_a1 = g_u1 silu'(a1) -> global ; d-gradient
     {
       const float4 d = dl[g.e];
-      float v[32], sv[32];
+      float v[32];
+      uint32_t w[16];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
-      tmem_ld32(tS1 + g.lane_base + g.col0, sv);
+      tmem_ld16u(tS1 + g.lane_base + g.col0 / 2, w);
       float pr = 0.f;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        v[q] = valid ? v[q] * sv[q] : 0.f;
+      for (int q = 0; q < 32; q += 2) {
+        const float2 sv = __half22float2(*reinterpret_cast<const __half2*>(&w[q / 2]));
+        v[q] = valid ? v[q] * sv.x : 0.f;
+        v[q + 1] = valid ? v[q + 1] * sv.y : 0.f;
         pr = fmaf(v[q], s_wr[g.col0 + q], pr);
+        pr = fmaf(v[q + 1], s_wr[g.col0 + q + 1], pr);
       }
       stage_write32(stage, g.e, g.col0, v);   // the M and G tiles are free again here
       part[g.cg * kM + g.e] = pr;

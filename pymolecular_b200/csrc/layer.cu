@@ -11,7 +11,11 @@
 //           dL/dh by node GEMMs.
 // Precision: fp32 mode runs every GEMM in fp32 FFMA.  bf16 mode rounds the
 // operands of the per-edge GEMMs (phi_e layer 2, phi_x layer 1 and their
-// gradients, E rows) to bf16, and runs the node-side GEMMs (N rows) on the
+// gradients, E rows) to bf16, except edge_mlp.2.weight (W2), which enters
+// as hi + lo = bf16(W2) + bf16(W2 - bf16(W2)) (two MMAs on the tensor cores):
+// a plain bf16 W2 is one fixed rounding shared by every edge, and the
+// coordinate-MLP weight gradients (sums with heavy cancellation) amplify that
+// systematic error tenfold past 2e-2.  The node-side GEMMs (N rows) run on the
 // tensor cores with each fp32 operand split into two bf16 parts (about 16
 // bits of precision).  Plain bf16 node-side operands would cost far more
 // accuracy than time: on graphs with high in-degree rows the node MLP input
@@ -146,9 +150,9 @@ __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_l
       const int64_t r = t % HH, k = r / H, n = r % H;   // (k, n) of a [k][n] matrix
       float v;
       switch (which) {
-        case 0: v = p.edge_w2[n * H + k]; o.W2T[r] = bf ? bf16r(v) : v; break;
+        case 0: v = p.edge_w2[n * H + k]; o.W2T[r] = bf ? bf16_split(v) : v; break;
         case 1: v = p.coord_w1[n * H + k]; o.Wc1T[r] = bf ? bf16r(v) : v; break;
-        case 2: v = p.edge_w2[r]; o.W2r[r] = bf ? bf16r(v) : v; break;
+        case 2: v = p.edge_w2[r]; o.W2r[r] = bf ? bf16_split(v) : v; break;
         default: v = p.coord_w1[r]; o.Wc1r[r] = bf ? bf16r(v) : v; break;
       }
       continue;

@@ -47,6 +47,21 @@ def tolerances(ref, approx, floor, factor):
     return {k: max(floor, factor * rel_err(approx[k], ref[k])) for k in ref}
 
 
+BF16_TOL = 2e-2    # north star: bf16-GEMM mode against the fp64 reference
+BF16_MODEL_TOL = 5e-3
+
+
+def check_bf16(got, ref, emu, what=""):
+    """bf16-GEMM bar: every tensor within 2e-2 of fp64, and within 5e-3 of the
+    rounding-exact bf16 model (oracle/egnn_emulation.py) on every tensor that
+    model itself computes to better than 5e-3."""
+    errs = check_tensors(got, ref, {k: BF16_TOL for k in ref}, what + " vs fp64")
+    emu_err = {k: rel_err(emu[k], ref[k]) for k in ref}
+    tight = {k: (BF16_MODEL_TOL if emu_err[k] < BF16_MODEL_TOL else float("inf")) for k in ref}
+    check_tensors(got, emu, tight, what + " vs rounding-exact bf16 model")
+    return errs
+
+
 def as_dict(res):
     """(h, x, dh, dx, {grads}) -> flat dict."""
     out = {"h": res[0], "x": res[1], "dh": res[2], "dx": res[3]}

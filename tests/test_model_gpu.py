@@ -1,24 +1,27 @@
 """Whole-model parity on the benchmark workloads, and size-independent
 properties at sizes the CPU oracle cannot run in seconds.
 
-Tolerance policy as in test_layer_gpu.py: each tensor within
-max(1e-5, 3 x the fp32 reference's error) in fp32 mode, and within
-max(2e-2, 3 x the error of the rounding-exact bf16 model) in bf16 mode, of
-the fp64 oracle.  The loss uses a deterministic per-graph sum."""
+Tolerance policy as in test_layer_gpu.py: in fp32 mode each tensor within
+max(1e-5, 3 x the fp32 reference's own error) of the fp64 oracle; in bf16
+mode every tensor within a flat 2e-2 of the fp64 oracle and within 5e-3 of
+the rounding-exact bf16 model wherever that model is within 5e-3 of fp64.
+The loss uses a deterministic per-graph sum.
+
+The fp64 oracle (and the rounding model) run on the test's CUDA device for
+these sizes: the config-5 block has 2.1M edges, whose E x H float64
+intermediates the CPU would take minutes over."""
 import math
 
 import pytest
 import torch
 
-from conftest import check_tensors, graph_sum, rel_err, tolerances
+from conftest import check_bf16, check_tensors, graph_sum, rel_err, tolerances
 from oracle import egnn_emulation as EM
 from oracle import egnn_oracle as O
 from pymolecular_b200 import CSR, EGNN
-from pymolecular_b200.datasets import CONFIGS, make_workload, molecules, point_cloud, proteins, slabs
+from pymolecular_b200.datasets import CONFIGS, make_workload, point_cloud, proteins, slabs
 
 pytestmark = pytest.mark.gpu
-
-TOL = {"fp32": 1e-5, "bf16": 2e-2}
 
 
 def _model(cfg_id, precision, dev, seed=0):
@@ -47,31 +50,56 @@ def _as_flat(loss, ho, xo, grads):
     return d
 
 
-@pytest.mark.parametrize("cfg_id,precision,n_graphs", [(1, "fp32", None), (2, "bf16", None),
-                                                       (2, "fp32", 128), (4, "bf16", 8)])
-def test_molecule_workload_matches_oracle(cfg_id, precision, n_graphs, cuda_device):
+def _batch(cfg_id, size):
+    """The workload of a parity case: a graph count for configs 1-4, and for
+    config 5 a point cloud of `size` nodes at config 5's point density (2^20
+    points in a 200 A box), with its 32 nearest neighbours per node."""
+    if cfg_id == 5:
+        return point_cloud(n_nodes=size, box=200.0 * (size / float(1 << 20)) ** (1.0 / 3.0), seed=0)
+    return make_workload(cfg_id, n_graphs=size)
+
+
+def _oracle(p, b, dev, fn, *extra, **kw):
+    """fp64 oracle / rounding model on `dev`; results back on the CPU."""
+    args = (b.h.double().to(dev), b.x.double().to(dev), b.row.to(dev), b.col.to(dev),
+            b.graph_index().to(dev), b.target.double().to(dev))
+    pd = {k: v.to(dev) for k, v in p.items()}
+    loss, h, x, g = fn(pd, *args, *extra, **kw)
+    g = {k: (v.cpu() if v is not None else torch.zeros_like(p[k])) for k, v in g.items()}
+    return _as_flat(loss.cpu(), h.cpu(), x.cpu(), g)
+
+
+# (config, precision, graphs or config-5 nodes; None = the whole config)
+MODEL_CASES = [
+    (1, "fp32", None),
+    (2, "bf16", None),
+    (2, "fp32", 128),
+    (3, "fp32", 1),
+    (3, "bf16", 1),
+    (4, "bf16", 16),
+    (5, "bf16", 1 << 16),
+]
+
+
+@pytest.mark.parametrize("cfg_id,precision,size", MODEL_CASES)
+def test_workload_matches_oracle(cfg_id, precision, size, cuda_device):
     dev = cuda_device
-    b = make_workload(cfg_id, n_graphs=n_graphs)
+    b = _batch(cfg_id, size)
     model = _model(cfg_id, precision, dev)
     csr = CSR.from_edges(b.row, b.col, n_nodes=b.n_nodes, device=dev)
     loss, ho, xo, _, grads = _step(model, b, csr, dev)
     got = _as_flat(loss, ho, xo, grads)
     p = {k: v.detach().double().cpu() for k, v in model.state_dict().items()}
-    rl, rh, rx, rg = O.model_grads(p, b.h.double(), b.x.double(), b.row, b.col, b.graph_index(),
-                                   b.target.double())
-    rg = {k: (g if g is not None else torch.zeros_like(p[k])) for k, g in rg.items()}
-    ref = _as_flat(rl, rh, rx, rg)
+    ref = _oracle(p, b, dev, O.model_grads)
+    what = f"config{cfg_id} {precision} ({b.n_nodes} nodes, {b.n_edges} edges)"
     if precision == "fp32":
         p32 = {k: v.float() for k, v in p.items()}
         l32, h32, x32, g32 = O.model_grads(p32, b.h, b.x, b.row, b.col, b.graph_index(), b.target)
         g32 = {k: (g if g is not None else torch.zeros_like(p32[k])) for k, g in g32.items()}
-        tol = tolerances(ref, _as_flat(l32, h32, x32, g32), 1e-5, 3.0)
+        check_tensors(got, ref, tolerances(ref, _as_flat(l32, h32, x32, g32), 1e-5, 3.0), what)
     else:
-        mc = CONFIGS[cfg_id]
-        el, eh, ex, eg = EM.model_fwd_bwd(p, b.h, b.x, b.row, b.col, b.graph_index(), b.target,
-                                          mc.n_layers, precision="bf16")
-        tol = tolerances(ref, _as_flat(el, eh, ex, eg), 2e-2, 3.0)
-    check_tensors(got, ref, tol, f"config{cfg_id} {precision}")
+        emu = _oracle(p, b, dev, EM.model_fwd_bwd, CONFIGS[cfg_id].n_layers, precision="bf16")
+        check_bf16(got, ref, emu, what)
 
 
 def _rotation(seed):

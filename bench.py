@@ -37,8 +37,13 @@ def parse():
     ap.add_argument("--n-graphs", type=int, default=None, help="shrink the batch (profiling runs)")
     ap.add_argument("--n-nodes", type=int, default=None, help="config 5: node count (default 2^20)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--allreduce", default="layers", choices=["layers", "flat"],
+                    help="data parallel: per-layer buckets all-reduced as the backward produces them "
+                         "(layers) or one flat all-reduce after the backward (flat)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the fp32-mode and other-workload measurements of the default 1-GPU run")
     ap.add_argument("--no-graphs", action="store_true",
                     help="time eager steps instead of replays of the captured training step")
     ap.add_argument("--profile", action="store_true",
@@ -158,7 +163,10 @@ def cpu_step_timer(cfg_id, n_graphs_sample, steps, warmup, threads):
     torch.set_num_threads(threads)
     mc = CONFIGS[cfg_id]
     if cfg_id == 5:
-        b = make_workload(5, n_nodes=n_graphs_sample)
+        # a block of config 5's point cloud: the same density (2^20 points in
+        # a 200 A box) and 32 nearest neighbours per node
+        from pymolecular_b200.datasets import point_cloud
+        b = point_cloud(n_graphs_sample, box=200.0 * (n_graphs_sample / float(1 << 20)) ** (1.0 / 3.0), seed=0)
     else:
         b = make_workload(cfg_id, n_graphs=n_graphs_sample)
     p = O.init_params(mc.in_node_nf, mc.hidden_nf, mc.out_node_nf, mc.n_layers, seed=0)
@@ -175,7 +183,14 @@ def cpu_step_timer(cfg_id, n_graphs_sample, steps, warmup, threads):
 
 
 def cpu_sample_size(cfg_id):
-    return {1: 96, 2: 96, 3: 1, 4: 16, 5: 65536}[cfg_id]
+    """Graphs (config-5: nodes) the CPU arm times: configs 1-2 whole; the
+    seeded subsets of configs 3-5 whose fp32 intermediates fit the host."""
+    return {1: 96, 2: 512, 3: 1, 4: 16, 5: 16384}[cfg_id]
+
+
+def full_size(cfg_id):
+    from pymolecular_b200.datasets import GRAPHS_PER_BATCH
+    return GRAPHS_PER_BATCH[cfg_id] if cfg_id != 5 else 1 << 20
 
 
 def run_reference(args):
@@ -186,19 +201,25 @@ def run_reference(args):
     mc = CONFIGS[args.config]
     threads = os.cpu_count() or 1
     sample = cpu_sample_size(args.config)
-    r = cpu_step_timer(args.config, sample, args.steps, args.warmup, threads)
+    # a CPU step of the whole config 2 takes seconds: at most 10 timed steps
+    # and one warm-up keep the arm within a few minutes
+    steps, warmup = max(1, min(args.steps, 10)), max(1, min(args.warmup, 1))
+    r = cpu_step_timer(args.config, sample, steps, warmup, threads)
     unit = "layer-edges/s"
     line = {
         "impl": "reference", "metric": "egnn_train_layer_edges_per_s", "value": r["layer_edges_per_s"],
-        "unit": unit, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "unit": unit, "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
+        "steps_requested": args.steps, "warmup_requested": args.warmup,
         "ms_per_step": r["step_s"] * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": f"config{args.config}", "hidden": mc.hidden_nf, "layers": mc.n_layers},
+        "config": {"workload": f"config{args.config}", "graphs": r["graphs"], "nodes": r["nodes"],
+                   "edges": r["edges"], "layers": mc.n_layers, "hidden": mc.hidden_nf, "precision": "fp32",
+                   "same_workload_as_b200_arm": sample == full_size(args.config)},
         "molecules_per_s": r["molecules_per_s"],
         "cpu_baseline": {"value": r["layer_edges_per_s"], "unit": unit, "cores": threads, "kind": "port",
                          "sample": f"{r['graphs']} graphs / {r['nodes']} nodes / {r['edges']} edges of "
                                    f"config{args.config}, fp32 oracle (egnn_clean restatement), median of "
-                                   f"{args.steps} steps"},
+                                   f"{steps} steps"},
         "e2e": {"value": r["layer_edges_per_s"], "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -226,6 +247,7 @@ class Problem:
         from pymolecular_b200.datasets import CONFIGS, make_workload
         self.torch, self.parallel, self.CSR = torch, parallel, CSR
         self.dev, self.world, self.rank = dev, world, rank
+        self.cfg_id = args.config
         self.mc = mc = CONFIGS[args.config]
         self.precision = args.precision or mc.precision
         self.halo = args.config == 5 and world > 1
@@ -258,7 +280,12 @@ class Problem:
                           precision=self.precision)
         self.params = list(self.model.parameters())
         self.opt = torch.optim.SGD(self.params, lr=1e-4)
-        self.sync_grads = parallel.GradAllReduce(self.params, average=not self.halo)
+        self.allreduce = "flat" if self.halo else args.allreduce
+        names = [n for n, _ in self.model.named_parameters()]
+        self.sync_grads = parallel.GradAllReduce(
+            self.params, average=not self.halo,
+            buckets=parallel.layer_buckets(names) if self.allreduce == "layers" else None,
+            overlap=self.allreduce == "layers")
         self.csr = CSR.from_edges(self.row_host, self.col_host, n_nodes=self.n_nodes_csr, device=dev)
         self.h = self.h_host.to(dev)
         self.x = self.x_host.to(dev)
@@ -328,35 +355,20 @@ class Problem:
         return csr
 
 
-def run_b200(args):
+KERNELS = ("edge_bwd", "edge_fwd", "node_pass", "src_pass", "edge_fixup", "part_reduce", "node_gemm", "gemm_small",
+           "linear_small", "wgrad_small", "colsum", "gemm_reduce", "prep", "edge_rows_gemm", "edge_rows_wgrad",
+           "edge_rows_u", "edge_rows_agg", "edge_rows_wimg")
+
+
+def measure(prob, args, world, dev, steps, warmup, graphs=True, e2e=True):
+    """Times `steps` training steps of `prob` (CUDA events, L2 flushed between
+    steps, max over ranks), then a separate pass with the library's kernel
+    timer, then (optionally) the end-to-end public-API step.  Returns a dict."""
     import torch
     import torch.distributed as dist
     from pymolecular_b200 import _native
 
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
-    prob = Problem(args, world, rank, dev)
-    mc = prob.mc
-
-    if args.profile:
-        prob.step()
-        torch.cuda.synchronize()
-        for _ in range(args.steps):
-            prob.step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
-        return 0
-
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
-    clocks = ClockSampler(local)
-    clocks.start()
-    warmup = max(args.warmup, 3)
     for _ in range(warmup - 1):
         prob.step()
     torch.cuda.synchronize()
@@ -370,206 +382,336 @@ def run_b200(args):
     # node-partitioned config (host-sized halo exchanges) runs eagerly.
     graphed = None
     run_step = prob.step
-    if not args.no_graphs and not prob.halo:
+    if graphs and not prob.halo:
         from pymolecular_b200.graphs import GraphedStep
         graphed = GraphedStep(prob.step, warmup=1)
         run_step = graphed.replay
         run_step()                   # one untimed replay
         torch.cuda.synchronize()
 
-    # ---- device-resident timed region (L2 flushed between steps, untimed)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    for k in range(args.steps):
+    for k in range(steps):
         flush.fill_(float(k))
         starts[k].record()
         run_step()
         ends[k].record()
     torch.cuda.synchronize()
-    launches = launches_per_step * args.steps
     if world > 1:
         dist.barrier()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    clk = clocks.stop()
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_per_step = float(t.item()) / args.steps
+    ms_per_step = float(t.item()) / steps
 
-    # ---- live kernel timing of the fused edge kernels (separate pass)
+    # live kernel timing (events around each launch on its own stream; a
+    # separate eager pass, since it perturbs the step)
     _native.lib().egnn_kernel_timing(1)
-    kt_steps = min(args.steps, 5)
+    kt_steps = min(steps, 5)
     for k in range(kt_steps):
         flush.fill_(float(k))
         prob.step()
     torch.cuda.synchronize()
-    ktimes = {n: _native.kernel_time(n) for n in ("edge_bwd", "edge_fwd", "node_pass", "src_pass", "edge_fixup",
-                                                  "part_reduce", "node_gemm", "gemm_small", "linear_small", "wgrad_small", "colsum", "gemm_reduce",
-                                                  "prep", "edge_rows_gemm", "edge_rows_wgrad", "edge_rows_u",
-                                                  "edge_rows_agg")}
-    breakdown = {n: round(v[0] / kt_steps, 4) for n, v in ktimes.items() if v[1]}
+    ktimes = {n: _native.kernel_time(n) for n in KERNELS}
     _native.lib().egnn_kernel_timing(0)
     status = _native.lib().egnn_device_status(_native.stream_ptr())
 
-    # ---- end to end through the public API from pinned host buffers
-    e2e = None
-    if not args.no_e2e:
-        host = prob.host_buffers()
-        h2d = sum(v.numel() * v.element_size() for v in host.values())
-        loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
-
-        def time_e2e(run):
-            if world > 1:
-                dist.barrier()
-            torch.cuda.synchronize()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(args.steps):
-                run()
-            e1.record()
-            torch.cuda.synchronize()
-            te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-            if world > 1:
-                dist.all_reduce(te, op=dist.ReduceOp.MAX)
-            return float(te.item()) / args.steps
-
-        def e2e_line(ms, path):
-            return {"value": mc.n_layers * prob.edges_job / (ms * 1e-3), "unit": "layer-edges/s",
-                    "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-                    "molecules_per_s": prob.graphs_job / (ms * 1e-3), "path": path}
-
-        # eager: every call from Python, edge indices validated with a host read-back
-        for _ in range(2):
-            prob.e2e_step(host, loss_host)
-        eager_ms = time_e2e(lambda: prob.e2e_step(host, loss_host))
-        eager = e2e_line(eager_ms, "eager EGNN.forward(h, x, csr) per step: pinned H2D of h, x, edge list, "
-                                   "targets; CSR.from_edges on the device; backward; SGD; loss D2H")
-        e2e = eager
-        if graphed is not None:
-            # the same public-API step captured once with GraphedStep: each replay
-            # copies the pinned host buffers in, builds the CSR (validation flag
-            # kept on the device, read after the timed steps), runs the step and
-            # copies the loss out
-            holder = {}
-
-            def captured():
-                holder["csr"] = prob.e2e_step(host, loss_host, check=False)
-                return None
-
-            g_e2e = GraphedStep(captured, warmup=1)
-            g_e2e.replay()
-            torch.cuda.synchronize()
-            graph_ms = time_e2e(g_e2e.replay)
-            holder["csr"].raise_if_invalid()
-            e2e = e2e_line(graph_ms, "GraphedStep over the same public-API step (pinned H2D of h, x, edge list, "
-                                     "targets; CSR.from_edges(check=False) on the device; forward; backward; "
-                                     "SGD; loss D2H), replayed once per step")
-            e2e["eager"] = {k: eager[k] for k in ("value", "ms_per_step", "path")}
-            g_e2e.release()
-
-    peak_vram = torch.cuda.max_memory_allocated(dev) / 2**30
-
-    if rank == 0:
-        H = mc.hidden_nf
-        peaks = measured_peaks()
-        fwd_ms, fwd_n = ktimes["edge_fwd"]
-        rows_path = prob.precision == "bf16" and H == 256
-        if rows_path:
-            # edge-row GEMMs (H = 256): six launches per layer (fwd: a2, c1;
-            # bwd: recomputed a2, c1 and the two data gradients).  Credited are
-            # the algorithmic flops only, 4 x 2 H^2 per edge and layer (the
-            # recompute is not credited), over the time of all six launches.
-            kname = "edge_rows_gemm"
-            bwd_ms, bwd_n = ktimes[kname]
-            per_launch_ms = bwd_ms / max(bwd_n, 1)
-            flops_launch = (4.0 / 6.0) * 2.0 * H * H * prob.edges_rank
-            # the same launches are HBM-bound by design (per-edge operands in
-            # HBM): bytes per edge and layer moved by the six GEMMs, with
-            # 2H-byte bf16 / fp16 rows and 4H-byte fp32 rows --
-            #   a2 fwd: U in, Mb + fp32 m out        2H + 2H + 4H
-            #   c1 fwd: Mb in, phi out               2H + 4
-            #   a2 bwd: U in, Mb + silu'(a2) out     2H + 2H + 2H
-            #   g_c1:   Mb in, G_c1 + phi out        2H + 2H + 4 (+ geometry 16)
-            #   g_a2:   G_c1 + silu'(a2) in, G_a2    2H + 2H + 2H
-            #   g_a1:   G_a2 + silu'(a1) in, rows    2H + 2H + 2H (+ geometry, g_d 32)
-            rows_bytes_layer = (8 * H + (2 * H + 4) + 6 * H + (4 * H + 20) + 6 * H + (6 * H + 32)) * prob.edges_rank
-            rows_hbm = {"bytes_per_layer": rows_bytes_layer,
-                        "achieved_gbs": rows_bytes_layer * (bwd_n / 6.0) / (max(bwd_ms, 1e-9) * 1e-3) / 1e9,
-                        "peak_gbs": peaks.get("hbm_gbs")}
-            if rows_hbm["peak_gbs"]:
-                rows_hbm["frac"] = rows_hbm["achieved_gbs"] / rows_hbm["peak_gbs"]
-        else:
-            rows_hbm = None
-            kname = "edge_bwd"
-            bwd_ms, bwd_n = ktimes[kname]
-            per_launch_ms = bwd_ms / max(bwd_n, 1)
-            flops_launch = 8.0 * H * H * prob.edges_rank   # dgrad + wgrad of the two H x H edge GEMMs
-        achieved = flops_launch / (max(per_launch_ms, 1e-9) * 1e-3) / 1e12
-        peak = peaks["bf16_tflops_sustained"]
-        fp32_pipe = {}
-        if not (prob.precision == "bf16" and H in (128, 256)):
-            # the SIMT edge kernels (fp32 mode, and bf16 mode at H != 128) run the
-            # edge GEMMs on the FP32 pipe (FFMA), whose peak MEASURED_PEAKS.json
-            # does not hold: the nominal figure, SMs x 128 FMA lanes x 2 flop x
-            # the maximum SM clock seen during the run
-            props = torch.cuda.get_device_properties(dev)
-            mhz = (clk or {}).get("sm_max_mhz") or 1965.0
-            fp32_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
-            fp32_pipe = {"fp32_pipe_peak_nominal": fp32_peak, "frac_of_fp32_pipe_nominal": achieved / fp32_peak}
-        step_flops = model_flops(mc, prob.nodes_rank, prob.edges_rank) * world
-        cpu = None
-        if not args.no_cpu_baseline and world == 1:
-            threads = os.cpu_count() or 1
-            sample = cpu_sample_size(args.config)
-            r = cpu_step_timer(args.config, sample, 3, 1, threads)
-            cpu = {"value": r["layer_edges_per_s"], "unit": "layer-edges/s", "cores": threads, "kind": "port",
-                   "sample": f"{r['graphs']} graphs / {r['edges']} edges of config{args.config}, fp32 "
-                             f"oracle restatement of egnn_clean.EGNN, median of 3 steps"}
-        line = {
-            "metric": "egnn_train_layer_edges_per_s",
-            "value": mc.n_layers * prob.edges_job / (ms_per_step * 1e-3),
-            "unit": "layer-edges/s",
-            "n_gpus": world, "steps": args.steps, "warmup": warmup,
-            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": prob.scaling,
-            "vs_baseline": None, "dtype": prob.precision,
-            "data": "synthetic (seeded generators, random init)",
-            "config": {"workload": f"config{args.config}", "graphs_per_gpu": prob.graphs_job // world,
-                       "nodes_per_gpu": prob.nodes_rank, "edges_per_gpu": prob.edges_rank,
-                       "layers": mc.n_layers, "hidden": H, "precision": prob.precision,
-                       "l2": "flushed between timed steps (252 MB write)",
-                       "parallelism": ("nodepart" if prob.halo else "dp") + str(world), "optimizer": "SGD",
-                       "cuda_graph": graphed is not None},
-            "molecules_per_s": prob.graphs_job / (ms_per_step * 1e-3),
-            "model_tflops": step_flops / (ms_per_step * 1e-3) / 1e12,
-            "e2e": e2e,
-            "gpu_launches": launches,
-            "roofline": {"kernel": kname, "bound": "tensor", "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": f"{peaks['source']} bf16 sustained",
-                         "traffic": (ncu_traffic(args.config, "edge_bwd", prob.edges_rank)
-                                     if prob.precision == "bf16" and H == 128 else
-                                     ncu_traffic(args.config, kname, prob.edges_rank) if rows_path else None),
-                         "traffic_unit": "bytes per launch (ncu capture)",
-                         "per_launch_ms": per_launch_ms, "launches": bwd_n,
-                         "flops_per_launch": flops_launch,
-                         **fp32_pipe,
-                         **({"hbm_view": rows_hbm} if rows_hbm else {}),
-                         "edge_fwd_per_launch_ms": fwd_ms / max(fwd_n, 1),
-                         "node_pass_per_launch_ms": ktimes["node_pass"][0] / max(ktimes["node_pass"][1], 1),
-                         "src_pass_per_launch_ms": ktimes["src_pass"][0] / max(ktimes["src_pass"][1], 1)},
-            "kernel_ms_per_step": breakdown,
-            "cpu_baseline": cpu,
-            "clocks": clk,
-            "peak_vram_gb": peak_vram,
-            "device_status": "ok" if status == 0 else _native.last_error(),
-        }
-        print(json.dumps(line), flush=True)
+    e2e_rec = None
+    if e2e:
+        e2e_rec = measure_e2e(prob, args, world, dev, steps, graphs)
     if graphed is not None:
         graphed.release()
+    del flush
+    return {"ms_per_step": ms_per_step, "launches": launches_per_step * steps, "ktimes": ktimes,
+            "kt_steps": kt_steps, "status": status, "graphed": graphed is not None, "e2e": e2e_rec}
+
+
+def measure_e2e(prob, args, world, dev, steps, graphs):
+    """The same metric through the public API from pinned host buffers."""
+    import torch
+    import torch.distributed as dist
+    mc = prob.mc
+    host = prob.host_buffers()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+
+    def time_e2e(run):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        return float(te.item()) / steps
+
+    def e2e_line(ms, path):
+        return {"value": mc.n_layers * prob.edges_job / (ms * 1e-3), "unit": "layer-edges/s",
+                "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                "molecules_per_s": prob.graphs_job / (ms * 1e-3), "path": path}
+
+    # eager: every call from Python, edge indices validated with a host read-back
+    for _ in range(2):
+        prob.e2e_step(host, loss_host)
+    eager_ms = time_e2e(lambda: prob.e2e_step(host, loss_host))
+    eager = e2e_line(eager_ms, "eager EGNN.forward(h, x, csr) per step: pinned H2D of h, x, edge list, "
+                               "targets; CSR.from_edges on the device; backward; SGD; loss D2H")
+    if not graphs or prob.halo:
+        return eager
+    # the same public-API step captured once with GraphedStep: each replay
+    # copies the pinned host buffers in, builds the CSR (validation flag kept
+    # on the device, read after the timed steps), runs the step and copies
+    # the loss out
+    from pymolecular_b200.graphs import GraphedStep
+    holder = {}
+
+    def captured():
+        holder["csr"] = prob.e2e_step(host, loss_host, check=False)
+        return None
+
+    g_e2e = GraphedStep(captured, warmup=1)
+    g_e2e.replay()
+    torch.cuda.synchronize()
+    graph_ms = time_e2e(g_e2e.replay)
+    holder["csr"].raise_if_invalid()
+    rec = e2e_line(graph_ms, "GraphedStep over the same public-API step (pinned H2D of h, x, edge list, "
+                             "targets; CSR.from_edges(check=False) on the device; forward; backward; "
+                             "SGD; loss D2H), replayed once per step")
+    rec["eager"] = {k: eager[k] for k in ("value", "ms_per_step", "path")}
+    g_e2e.release()
+    return rec
+
+
+def _per_step(ktimes, names, kt_steps):
+    return sum(ktimes[n][0] for n in names) / kt_steps
+
+
+def roofline(prob, m, peaks, clk, dev):
+    """Roofline records of the kernel groups of one measured workload.
+
+    Tensor-pipe groups: credited (algorithmic) flops, the factored EGNN
+    count (recompute not credited), over the groups' CUDA-event time,
+    against the measured sustained bf16 peak (bf16 mode) or the nominal FP32
+    pipe (fp32 mode: FFMA kernels).  HBM groups: algorithmic bytes over time
+    against the measured HBM bandwidth.  Returns (dominant, groups)."""
+    import torch
+    mc, kt, n = prob.mc, m["ktimes"], m["kt_steps"]
+    H, L, E, N = mc.hidden_nf, mc.n_layers, prob.edges_rank, prob.nodes_rank
+    bf = prob.precision == "bf16"
+    props = torch.cuda.get_device_properties(dev)
+    mhz = (clk or {}).get("sm_max_mhz") or 1965.0
+    fp32_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+    tc_peak, hbm = peaks["bf16_tflops_sustained"], peaks["hbm_gbs"]
+    groups = {}
+
+    def tensor(name, flops_step, ms_step, launches, on_tc=True, extra=None):
+        if ms_step <= 0:
+            return
+        ach = flops_step / (ms_step * 1e-3) / 1e12
+        peak = tc_peak if on_tc else fp32_peak
+        rec = {"bound": "tensor" if on_tc else "fp32_pipe", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+               "frac": ach / peak, "peak_source": (f"{peaks['source']} bf16 sustained" if on_tc else
+                                                   "nominal FP32 pipe (SMs x 128 lanes x 2 x max SM clock)"),
+               "ms_per_step": ms_step, "launches_per_step": launches / n,
+               "flops_per_launch": flops_step / max(launches / n, 1e-9)}
+        rec.update(extra or {})
+        groups[name] = rec
+
+    def memory(name, bytes_step, ms_step, launches, note):
+        if ms_step <= 0:
+            return
+        ach = bytes_step / (ms_step * 1e-3) / 1e9
+        groups[name] = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                        "peak_source": f"{peaks['source']} HBM copy", "ms_per_step": ms_step,
+                        "launches_per_step": launches / n, "bytes_per_launch": bytes_step / max(launches / n, 1e-9),
+                        "bytes": note}
+
+    rows_path = bf and H == 256
+    tc_edge = bf and H == 128 and "edge_bwd" in kt and kt["edge_bwd"][1] > 0
+    # per-edge GEMMs: forward 4 H^2 per edge (phi_e layer 2, phi_x layer 1),
+    # backward 8 H^2 (their data and weight gradients)
+    if rows_path:
+        ms = _per_step(kt, ["edge_rows_gemm"], n)
+        tensor("edge_rows_gemm", 8.0 * H * H * E * L, ms, kt["edge_rows_gemm"][1],
+               extra={"credited": "4 of the 6 launches per layer (the backward's recompute is not credited)"})
+        ms = _per_step(kt, ["edge_rows_wgrad"], n)
+        tensor("edge_rows_wgrad", 4.0 * H * H * E * L, ms, kt["edge_rows_wgrad"][1])
+    else:
+        tensor("edge_fwd", 4.0 * H * H * E * L, _per_step(kt, ["edge_fwd"], n), kt["edge_fwd"][1], on_tc=tc_edge)
+        tensor("edge_bwd", 8.0 * H * H * E * L, _per_step(kt, ["edge_bwd"], n), kt["edge_bwd"][1], on_tc=tc_edge)
+    # node GEMMs (P|Q projection, node MLP; forward, data and weight
+    # gradients: 30 H^2 per node and layer) with their split-K reductions
+    node_names = ["node_gemm", "gemm_reduce", "gemm_small"]
+    tensor("node_gemm", 30.0 * H * H * N * L, _per_step(kt, node_names, n),
+           sum(kt[x][1] for x in node_names), on_tc=bf,
+           extra={"kernels": node_names, "operands": "split bf16 (hi*hi + hi*lo + lo*hi)" if bf else "fp32 FFMA"})
+    # node pass (tensor-core paths): per node, the bf16 dL/da1 rows of its
+    # in-edges and out-edges (2 x 2H bytes per edge), their g_d (2 x 16),
+    # the transpose-CSR positions (4), and per node the row pointers, dL/dx',
+    # S_dst, S_src (2 x 4H) and dL/dx
+    if kt["node_pass"][1]:
+        memory("node_pass", (E * (4 * H + 32 + 4) + N * (8 * H + 8 + 24)) * L,
+               _per_step(kt, ["node_pass"], n), kt["node_pass"][1],
+               "E (4H + 36) + N (8H + 32) per layer")
+    if kt["src_pass"][1]:
+        memory("src_pass", (E * (4 * H + 16 + 4) + N * (4 * H + 8 + 24)) * L,
+               _per_step(kt, ["src_pass"], n), kt["src_pass"][1], "E (4H + 20) + N (4H + 32) per layer")
+    if rows_path:
+        # gather: indices, P/Q rows (2 x 4H), u1 tile row (2H), geometry,
+        # backward also silu'(a1) fp16 (2H) and the gradient factors
+        memory("edge_rows_u", E * ((8 + 8 * H + 2 * H + 16) * 2 + 2 * H + 16) * L,
+               _per_step(kt, ["edge_rows_u"], n), kt["edge_rows_u"][1], "E (18H + 48) + E (2H + 16) per layer")
+        memory("edge_rows_agg", (E * (4 * H + 20) + N * (4 * H + 24)) * L,
+               _per_step(kt, ["edge_rows_agg"], n), kt["edge_rows_agg"][1], "E (4H + 20) + N (4H + 24) per layer")
+    if rows_path:
+        dom = "edge_rows_gemm"
+    else:
+        dom = "edge_bwd"
+    return dom, groups
+
+
+def make_line(args, prob, m, world, clk, cpu, dev):
+    mc = prob.mc
+    H = mc.hidden_nf
+    peaks = measured_peaks()
+    dom, groups = roofline(prob, m, peaks, clk, dev)
+    kt, n = m["ktimes"], m["kt_steps"]
+    d = dict(groups.get(dom, {}))
+    d["kernel"] = dom
+    launches = max(kt[dom][1], 1) if dom in kt else 1
+    d["per_launch_ms"] = kt[dom][0] / launches if dom in kt else None
+    d["launches"] = kt[dom][1] if dom in kt else 0
+    if prob.precision == "bf16" and H == 128:
+        d["traffic"] = ncu_traffic(args.config, "edge_bwd", prob.edges_rank)
+    elif prob.precision == "bf16" and H == 256:
+        d["traffic"] = ncu_traffic(args.config, dom, prob.edges_rank)
+    else:
+        d["traffic"] = None
+    d["traffic_unit"] = "bytes per launch (ncu capture)"
+    d["groups"] = groups
+    step_flops = model_flops(mc, prob.nodes_rank, prob.edges_rank) * world
+    ms = m["ms_per_step"]
+    return {
+        "metric": "egnn_train_layer_edges_per_s",
+        "value": mc.n_layers * prob.edges_job / (ms * 1e-3),
+        "unit": "layer-edges/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": prob.scaling,
+        "vs_baseline": None, "dtype": prob.precision,
+        "data": "synthetic (seeded generators, random init)",
+        "config": {"workload": f"config{prob.cfg_id}", "graphs_per_gpu": prob.graphs_job // world,
+                   "nodes_per_gpu": prob.nodes_rank, "edges_per_gpu": prob.edges_rank,
+                   "layers": mc.n_layers, "hidden": H, "precision": prob.precision,
+                   "l2": "flushed between timed steps (252 MB write)",
+                   "parallelism": ("nodepart" if prob.halo else "dp") + str(world), "optimizer": "SGD",
+                   "allreduce": ("per-layer buckets, issued as the backward produces them"
+                                 if prob.allreduce == "layers" else "one flat all-reduce after the backward")
+                   if world > 1 else None,
+                   "cuda_graph": m["graphed"]},
+        "molecules_per_s": prob.graphs_job / (ms * 1e-3),
+        "model_tflops": step_flops / (ms * 1e-3) / 1e12,
+        "e2e": m["e2e"],
+        "gpu_launches": m["launches"],
+        "roofline": d,
+        "kernel_ms_per_step": {k: round(v[0] / n, 4) for k, v in kt.items() if v[1]},
+        "cpu_baseline": cpu,
+        "clocks": clk,
+        "device_status": "ok" if m["status"] == 0 else "error",
+    }
+
+
+def cpu_baseline(cfg_id, steps):
+    threads = os.cpu_count() or 1
+    sample = cpu_sample_size(cfg_id)
+    r = cpu_step_timer(cfg_id, sample, steps, 1, threads)
+    full = sample == full_size(cfg_id)
+    return {"value": r["layer_edges_per_s"], "unit": "layer-edges/s", "cores": threads, "kind": "port",
+            "molecules_per_s": r["molecules_per_s"], "step_s": r["step_s"],
+            "sample": (f"{'the whole' if full else 'a seeded subset of'} config{cfg_id}: {r['graphs']} graphs / "
+                       f"{r['nodes']} nodes / {r['edges']} edges, fp32 oracle restatement of egnn_clean.EGNN, "
+                       f"median of {steps} steps" + ("" if full else "; per-edge throughput extrapolates"))}
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    prob = Problem(args, world, rank, dev)
+
+    if args.profile:
+        prob.step()
+        torch.cuda.synchronize()
+        for _ in range(args.steps):
+            prob.step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    warmup = max(args.warmup, 3)
+    m = measure(prob, args, world, dev, args.steps, warmup, graphs=not args.no_graphs, e2e=not args.no_e2e)
+    clk = clocks.stop()
+    peak_vram = torch.cuda.max_memory_allocated(dev) / 2**30
+    line = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            cpu = cpu_baseline(args.config, 5)
+        line = make_line(args, prob, m, world, clk, cpu, dev)
+        line["peak_vram_gb"] = peak_vram
+    del prob
+    torch.cuda.empty_cache()
+
+    # ---- one GPU, default run: the same step in fp32 mode (an equal-precision
+    # ratio against the fp32 CPU arm) and the other workloads, each with its
+    # roofline (shorter runs, no end-to-end pass)
+    if world == 1 and not args.no_extras:
+        extra_steps = min(args.steps, 10)
+        if rank == 0:
+            line["extras"] = {}
+        runs = [(args.config, "fp32")] + [(c, None) for c in (1, 2, 3, 4, 5) if c != args.config]
+        if args.config != 3:
+            runs.append((3, "bf16"))   # config 3 is quoted in both modes
+        for cfg_id, prec in runs:
+            sub = argparse.Namespace(**vars(args))
+            sub.config, sub.precision, sub.n_graphs, sub.n_nodes = cfg_id, prec, None, None
+            p2 = Problem(sub, world, rank, dev)
+            clocks = ClockSampler(local)
+            clocks.start()
+            m2 = measure(p2, sub, world, dev, extra_steps, 3, graphs=not args.no_graphs, e2e=False)
+            clk2 = clocks.stop()
+            cpu2 = None
+            if not args.no_cpu_baseline and prec is None:
+                cpu2 = cpu_baseline(cfg_id, 2)
+            if rank == 0:
+                rec = make_line(sub, p2, m2, world, clk2, cpu2, dev)
+                for k in ("metric", "unit", "higher_is_better", "vs_baseline", "data", "e2e", "n_gpus", "warmup"):
+                    rec.pop(k, None)
+                rec["steps"] = extra_steps
+                line["extras"][f"config{cfg_id}_{p2.precision}"] = rec
+            del p2
+            torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

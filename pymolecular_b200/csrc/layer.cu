@@ -22,7 +22,9 @@
 // [h, agg] and the projections P, Q lose several percent in their weight
 // gradients.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <thread>
 
 #include "edge_rows.cuh"
 #include "edge_simt.cuh"
@@ -278,30 +280,69 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
 
 // ---- side streams -----------------------------------------------------------------
 // The backward forks work that no later kernel of the layer needs (the
-// parameter gradients: node MLP, edge partial reduction, W1) onto two
-// per-device side streams, so that it fills SMs the edge kernels leave free
-// and stays off the main chain.  Fork and join are event waits, which stream
-// capture records as graph edges; streams and events are created on the
-// first call, outside any capture.
+// parameter gradients: node MLP, edge partial reduction, W1) onto two side
+// streams, so that it fills SMs the edge kernels leave free and stays off the
+// main chain.  Fork and join are event waits, which stream capture records as
+// graph edges.
+//
+// Each caller stream gets its own pair of side streams and its own events
+// (keyed by device and stream handle, and by thread for the per-thread
+// default stream, whose handle every thread shares).  Calls on different
+// streams therefore never record or wait on each other's events, and two host
+// threads may run backwards concurrently on distinct streams.  Calls on the
+// same stream are ordered by that stream; their host-side event records can
+// only make one call wait for more of the other's work, never for less.  The
+// streams and events of a new caller stream are created on its first call,
+// with the thread switched to relaxed capture mode so that a first call made
+// while that stream is being captured may create them.
 struct SideStream {
   cudaStream_t stream = nullptr;    // node-MLP weight gradients, edge partials, dW_a
   cudaStream_t stream2 = nullptr;   // dW_b
   cudaEvent_t ev[8] = {};
 };
 
-int side_stream(SideStream** out) {
+struct SideKey {
+  int dev;
+  uintptr_t stream;
+  std::thread::id thread;   // only for the per-thread default stream
+  bool operator<(const SideKey& o) const {
+    if (dev != o.dev) return dev < o.dev;
+    if (stream != o.stream) return stream < o.stream;
+    return thread < o.thread;
+  }
+};
+
+int create_side(SideStream& ss) {
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  EGNN_CHECK_CUDA(cudaThreadExchangeStreamCaptureMode(&mode));
+  cudaError_t e = cudaStreamCreateWithFlags(&ss.stream2, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking);
+  for (auto& ev : ss.ev)
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  EGNN_CHECK_CUDA(e);
+  return EGNN_OK;
+}
+
+int side_stream(cudaStream_t caller, SideStream** out) {
   static std::mutex mu;
-  static SideStream per_dev[64];
+  static std::map<SideKey, SideStream*> sides;   // one entry per (device, caller stream); kept until exit
   int dev = 0;
   EGNN_CHECK_CUDA(cudaGetDevice(&dev));
+  const uintptr_t h = reinterpret_cast<uintptr_t>(caller);
+  const SideKey key{dev, h, h == reinterpret_cast<uintptr_t>(cudaStreamPerThread) ? std::this_thread::get_id()
+                                                                                   : std::thread::id()};
   std::lock_guard<std::mutex> lk(mu);
-  SideStream& ss = per_dev[dev & 63];
-  if (!ss.stream) {
-    EGNN_CHECK_CUDA(cudaStreamCreateWithFlags(&ss.stream2, cudaStreamNonBlocking));
-    EGNN_CHECK_CUDA(cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking));
-    for (auto& e : ss.ev) EGNN_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  auto it = sides.find(key);
+  if (it == sides.end()) {
+    SideStream* ss = new SideStream();
+    if (create_side(*ss) != EGNN_OK) {
+      delete ss;
+      return EGNN_ERR_CUDA;
+    }
+    it = sides.emplace(key, ss).first;
   }
-  *out = &ss;
+  *out = it->second;
   return EGNN_OK;
 }
 
@@ -462,7 +503,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
 
   EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
   SideStream* side = nullptr;
-  EGNN_TRY(side_stream(&side));
+  EGNN_TRY(side_stream(s, &side));
   const cudaStream_t s2 = side->stream;
   SideJoin join{s, side};
 

@@ -50,43 +50,128 @@ def partition_graphs(n_nodes: Sequence[int], n_edges: Sequence[int], world: int)
     return [sorted(p) for p in parts]
 
 
+def layer_buckets(names: Sequence[str]) -> List[List[int]]:
+    """Group parameter indices into all-reduce buckets, one per module of
+    the layer stack (the prefix before the first '.': ``embedding_in``,
+    ``gcl_0`` ... ``gcl_{L-1}``, ``embedding_out``), ordered as the backward
+    produces them: the last module first (egnn_clean.py:142-145 run in
+    reverse)."""
+    groups: dict = {}
+    order: List[str] = []
+    for i, n in enumerate(names):
+        key = n.split(".")[0]
+        if key not in groups:
+            groups[key] = []
+            order.append(key)
+        groups[key].append(i)
+    return [groups[k] for k in reversed(order)]
+
+
 class GradAllReduce:
     """Sum (or average) the gradients of `params` over the process group.
 
-    The backward leaves each gradient in its own tensor (``zero_grad()`` sets
-    them to None, so autograd assigns rather than accumulates: no extra add
-    kernel per parameter).  The call packs them into one flat fp32 buffer with
-    a single concatenation, reduces it with one all_reduce and makes every
-    ``p.grad`` a view of the reduced buffer.  Every rank issues the same
-    collective in the same order.
+    Gradients are reduced in buckets (``buckets``: lists of parameter
+    indices; default one bucket for everything).  With ``overlap=True`` each
+    parameter gets a post-accumulate-grad hook, and a bucket's all_reduce is
+    issued (asynchronously) as soon as every one of its parameters has its
+    gradient -- during the backward, while the earlier layers' backward runs
+    on the compute stream.  Calling the object finishes the step: it issues
+    the buckets that are still pending, waits for every reduction, averages,
+    and makes every ``p.grad`` a view of its reduced bucket.
+
+    Each bucket has two buffers used in turn: a step packs the local
+    gradients into the buffer that the current ``p.grad`` views do not point
+    into, so a gradient kept from the previous step (``zero_grad(set_to_none=
+    False)``, or accumulation) is never reduced under autograd's feet.  The
+    backward leaves fresh gradients in their own tensors (``zero_grad()`` sets
+    them to None) and one concatenation packs a bucket.  A second backward
+    before the call (gradient accumulation) re-packs and re-reduces the
+    buckets it touched once their first reduction has finished, so the result
+    is the reduced sum of everything accumulated.
+
+    Every rank issues the same collectives in the same order: hooks fire in
+    the backward's (deterministic) order and the pending buckets follow in
+    bucket order.
     """
 
-    def __init__(self, params, average: bool = True, group=None):
+    def __init__(self, params, average: bool = True, group=None, buckets=None, overlap: bool = False):
         self.params = [p for p in params]
         self.average = average
         self.group = group
-        n = sum(p.numel() for p in self.params)
+        self.buckets = buckets if buckets is not None else [list(range(len(self.params)))]
         dev = self.params[0].device if self.params else torch.device("cpu")
-        self.flat = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.views, off = [], 0
-        for p in self.params:
-            self.views.append(self.flat[off:off + p.numel()].view_as(p))
-            off += p.numel()
+        self.bucket_of = [0] * len(self.params)
+        self.flat = [[], []]                        # [side][bucket]
+        self._views = [[None] * len(self.params), [None] * len(self.params)]
+        for side in range(2):
+            for b, idx in enumerate(self.buckets):
+                buf = torch.zeros(sum(self.params[i].numel() for i in idx), dtype=torch.float32, device=dev)
+                off = 0
+                for i in idx:
+                    n = self.params[i].numel()
+                    self._views[side][i] = buf[off:off + n].view_as(self.params[i])
+                    self.bucket_of[i] = b
+                    off += n
+                self.flat[side].append(buf)
+        self.side = 0   # buffers this step packs into and reduces
+        self._reset()
+        self.overlap = overlap and self._active()
+        if self.overlap:
+            for i, p in enumerate(self.params):
+                p.register_post_accumulate_grad_hook(self._hook(i))
+
+    @property
+    def views(self):
+        """The views the gradients point at after the last call."""
+        return self._views[1 - self.side]
+
+    def _active(self) -> bool:
+        return dist.is_initialized() and dist.get_world_size(self.group) > 1
+
+    def _reset(self):
+        self.ready = [set() for _ in self.buckets]
+        self.work = [None] * len(self.buckets)
+        self.dirty = [False] * len(self.buckets)
+
+    def _hook(self, i):
+        def hook(_p):
+            b = self.bucket_of[i]
+            if self.work[b] is not None:   # accumulated again after the bucket was issued
+                self.dirty[b] = True
+                return
+            self.ready[b].add(i)
+            if len(self.ready[b]) == len(self.buckets[b]):
+                self._issue(b)
+        return hook
+
+    def _issue(self, b):
+        idx = self.buckets[b]
+        torch.cat([(self.params[i].grad if self.params[i].grad is not None
+                    else torch.zeros_like(self.params[i])).reshape(-1) for i in idx], out=self.flat[self.side][b])
+        self.work[b] = dist.all_reduce(self.flat[self.side][b], group=self.group, async_op=True)
 
     def zero_grad(self):
         for p in self.params:
             p.grad = None
 
     def __call__(self):
-        if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+        if not self._active():
             return
-        parts = [(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1) for p in self.params]
-        torch.cat(parts, out=self.flat)
-        dist.all_reduce(self.flat, group=self.group)
-        if self.average:
-            self.flat.div_(dist.get_world_size(self.group))
-        for p, v in zip(self.params, self.views):
+        for b in range(len(self.buckets)):
+            if self.work[b] is None:
+                self._issue(b)
+            elif self.dirty[b]:
+                self.work[b].wait()
+                self._issue(b)
+        world = dist.get_world_size(self.group)
+        for b in range(len(self.buckets)):
+            self.work[b].wait()
+            if self.average:
+                self.flat[self.side][b].div_(world)
+        for p, v in zip(self.params, self._views[self.side]):
             p.grad = v
+        self.side ^= 1
+        self._reset()
 
 
 # ---------------------------------------------------------------------------
@@ -245,7 +330,7 @@ def halo_exchange(h_own: torch.Tensor, plan: HaloPlan, group=None) -> torch.Tens
     return _HaloExchange.apply(h_own, plan, group)
 
 
-__all__ = ["partition_graphs", "GradAllReduce", "node_ranges", "HaloPlan", "build_halo_plan",
+__all__ = ["partition_graphs", "layer_buckets", "GradAllReduce", "node_ranges", "HaloPlan", "build_halo_plan",
            "halo_exchange", "local_edges"]
 
 

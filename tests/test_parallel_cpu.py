@@ -91,6 +91,64 @@ def test_grad_allreduce_two_ranks():
     _run(2, _grad_allreduce_worker)
 
 
+class _Stack(torch.nn.Module):
+    """Three modules named like the EGNN stack (embedding_in, gcl_0, embedding_out)."""
+
+    def __init__(self):
+        super().__init__()
+        self.embedding_in = torch.nn.Linear(4, 6)
+        self.gcl_0 = torch.nn.Sequential(torch.nn.Linear(6, 6), torch.nn.SiLU(), torch.nn.Linear(6, 6))
+        self.embedding_out = torch.nn.Linear(6, 1)
+
+    def forward(self, x):
+        return self.embedding_out(self.gcl_0(self.embedding_in(x)))
+
+
+def _bucket_worker(rank, world, overlap):
+    """Per-module buckets (issued from the backward's hooks with overlap)
+    give the same averaged gradients as one flat all-reduce; gradients kept
+    in the buckets between steps (zero_grad(set_to_none=False)) and two
+    backwards accumulated before one call are reduced in full."""
+    torch.manual_seed(0)
+    m = _Stack()
+    names = [n for n, _ in m.named_parameters()]
+    buckets = P.layer_buckets(names)
+    assert [names[b[0]].split(".")[0] for b in buckets] == ["embedding_out", "gcl_0", "embedding_in"]
+    sync = P.GradAllReduce(m.parameters(), buckets=buckets, overlap=overlap)
+    x = [torch.randn(5, 4, generator=torch.Generator().manual_seed(10 * r + k)) for r in range(world)
+         for k in range(2)]
+
+    def expected(ks):
+        # mean over ranks of the sum over the accumulated backwards
+        ref = _Stack()
+        ref.load_state_dict(m.state_dict())
+        for r in range(world):
+            for k in ks:
+                ref(x[2 * r + k]).pow(2).sum().backward()
+        return [p.grad / world for p in ref.parameters()]
+
+    # step 1: fresh gradients
+    sync.zero_grad()
+    m(x[2 * rank]).pow(2).sum().backward()
+    sync()
+    for g, e in zip([p.grad for p in m.parameters()], expected([0])):
+        assert torch.allclose(g, e, atol=1e-6), (g, e)
+    # step 2: gradients stay in the buckets, zeroed in place; two backwards, one call
+    m.zero_grad(set_to_none=False)
+    m(x[2 * rank]).pow(2).sum().backward()
+    m(x[2 * rank + 1]).pow(2).sum().backward()
+    sync()
+    for g, e in zip([p.grad for p in m.parameters()], expected([0, 1])):
+        assert torch.allclose(g, e, atol=1e-6), (g, e)
+    for p, v in zip(m.parameters(), sync.views):
+        assert p.grad.data_ptr() == v.data_ptr()
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_bucketed_grad_allreduce_two_ranks(overlap):
+    _run(2, _bucket_worker, overlap)
+
+
 def _graph(seed, n=160, k=6):
     g = torch.Generator().manual_seed(seed)
     x = torch.rand(n, 3, generator=g, dtype=torch.float64) * 10

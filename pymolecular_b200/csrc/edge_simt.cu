@@ -923,43 +923,54 @@ __global__ void src_pass_kernel(int64_t N, const int32_t* __restrict__ src_ptr,
   if (lane < 3) gx[j * 3 + lane] = gx_out[j * 3 + lane] + gxd[j * 3 + lane] - gs;
 }
 
-__global__ void part_reduce_kernel(int H, int d, int att, int G, int64_t PF, const float* part,
-                                   egnn_layer_grads gp, int64_t ld_w1) {
+// Per-CTA weight-gradient partials -> parameter gradients.  A block takes 32
+// consecutive slots (one per lane); its 8 warps each add a contiguous eighth
+// of the CTA partials (eight loads in flight), and warp 0 adds the 8 sums in
+// warp order (a fixed association: bit-reproducible).
+__global__ void __launch_bounds__(256) part_reduce_kernel(int H, int d, int att, int G, int64_t PF,
+                                                          const float* part, egnn_layer_grads gp, int64_t ld_w1) {
   pdl_enter();
+  __shared__ float red[8][33];
   const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    // CTA partials loaded eight at a time (independent loads), added in CTA order
-    float s = 0.f;
-    int c = 0;
-    for (; c + 8 <= G; c += 8) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t idx = (int64_t)blockIdx.x * 32 + lane;
+  const int per = (G + 7) / 8;
+  const int c0 = min(G, warp * per), c1 = min(G, c0 + per);
+  float v = 0.f;
+  if (idx < total) {
+    for (int c = c0; c < c1; c += 8) {
       float t[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) t[u] = part[(int64_t)(c + u) * PF + idx];
+      for (int u = 0; u < 8; ++u) t[u] = (c + u < c1) ? part[(int64_t)(c + u) * PF + idx] : 0.f;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) s += t[u];
+      for (int u = 0; u < 8; ++u) v += t[u];
     }
-    for (; c < G; ++c) s += part[(int64_t)c * PF + idx];
-    const int64_t HH = (int64_t)H * H;
-    if (idx < HH) {
-      gp.coord_w1[idx] = s;
-    } else if (idx < 2 * HH) {
-      gp.edge_w2[idx - HH] = s;
+  }
+  red[warp][lane] = v;
+  __syncthreads();
+  if (warp != 0 || idx >= total) return;
+  float s = red[0][lane];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) s += red[w][lane];
+  const int64_t HH = (int64_t)H * H;
+  if (idx < HH) {
+    gp.coord_w1[idx] = s;
+  } else if (idx < 2 * HH) {
+    gp.edge_w2[idx - HH] = s;
+  } else {
+    const int64_t v2 = idx - 2 * HH;
+    if (v2 < H) gp.coord_b1[v2] = s;
+    else if (v2 < 2 * H) gp.edge_b2[v2 - H] = s;
+    else if (v2 < 3 * H) gp.coord_w2[v2 - 2 * H] = s;
+    else if (v2 < 4 * H) gp.edge_w1[(v2 - 3 * H) * ld_w1 + 2 * H] = s;
+    else if (v2 < 4 * H + (int64_t)H * d) {
+      const int64_t w = v2 - 4 * H;
+      const int64_t f = w / d, t = w % d;
+      gp.edge_w1[f * ld_w1 + 2 * H + 1 + t] = s;
     } else {
-      const int64_t v = idx - 2 * HH;
-      if (v < H) gp.coord_b1[v] = s;
-      else if (v < 2 * H) gp.edge_b2[v - H] = s;
-      else if (v < 3 * H) gp.coord_w2[v - 2 * H] = s;
-      else if (v < 4 * H) gp.edge_w1[(v - 3 * H) * ld_w1 + 2 * H] = s;
-      else if (v < 4 * H + (int64_t)H * d) {
-        const int64_t w = v - 4 * H;
-        const int64_t f = w / d, t = w % d;
-        gp.edge_w1[f * ld_w1 + 2 * H + 1 + t] = s;
-      } else {
-        const int64_t w = v - 4 * H - (int64_t)H * d;
-        if (w < H) gp.att_w[w] = s;
-        else gp.att_b[0] = s;
-      }
+      const int64_t w = v2 - 4 * H - (int64_t)H * d;
+      if (w < H) gp.att_w[w] = s;
+      else gp.att_b[0] = s;
     }
   }
 }
@@ -1129,7 +1140,7 @@ int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_e
 int edge_part_reduce(int H, int d, bool att, int G, const float* part, const egnn_layer_grads* gp,
                      int64_t ld_w1, cudaStream_t s) {
   const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+  const int blocks = (int)((total + 31) / 32);
   TimerScope ts("part_reduce", s);
   EGNN_CHECK_CUDA(launch_pdl(part_reduce_kernel, dim3(blocks), dim3(256), 0, s, H, d, att ? 1 : 0, G,
                              edge_part_floats(H, d), part, *gp, ld_w1));

@@ -117,32 +117,42 @@ __global__ void __launch_bounds__(NT) gemm_kernel(GemmArgs a) {
   }
 }
 
-__global__ void gemm_reduce_kernel(GemmArgs a) {
+// Split-K reduction: a block takes 32 consecutive outputs (one per lane);
+// its 8 warps each add a contiguous eighth of the slices (all loads of a
+// warp in flight at once), and warp 0 adds the 8 partial sums in warp order:
+// a fixed association, so the result is bit-reproducible.  Blocks past the
+// outputs do the same for the db slices.
+__global__ void __launch_bounds__(256) gemm_reduce_kernel(GemmArgs a) {
   pdl_enter();
+  __shared__ float red[8][33];
   Epi e{a.bias, a.pre, a.ldp, a.act, a.aux, a.ldaux, a.resid, a.ldr, a.resid_cols, a.C, a.ldc};
   const int64_t total = a.M * a.N;
-  if (a.db && a.db_part) {
-    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < a.M;
-         m += (int64_t)gridDim.x * blockDim.x) {
-      float v = 0.f;
-      for (int z = 0; z < a.ksplit; ++z) v += a.db_part[(int64_t)z * a.M + m];
-      a.db[m] = v;
-    }
-  }
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    // slices loaded eight at a time (independent loads), added in slice order
-    float v = 0.f;
-    int z = 0;
-    for (; z + 8 <= a.ksplit; z += 8) {
+  const int64_t nb_main = (total + 31) / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool main = blockIdx.x < nb_main;
+  const int64_t stride = main ? total : a.M;
+  const int64_t idx = (main ? (int64_t)blockIdx.x : (int64_t)blockIdx.x - nb_main) * 32 + lane;
+  const float* src = main ? a.part : a.db_part;
+  const int S = a.ksplit, per = (S + 7) / 8;
+  const int z0 = min(S, warp * per), z1 = min(S, z0 + per);
+  float v = 0.f;
+  if (idx < stride) {
+    for (int z = z0; z < z1; z += 8) {
       float t[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) t[u] = a.part[(int64_t)(z + u) * total + idx];
+      for (int u = 0; u < 8; ++u) t[u] = (z + u < z1) ? src[(int64_t)(z + u) * stride + idx] : 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u) v += t[u];
     }
-    for (; z < a.ksplit; ++z) v += a.part[(int64_t)z * total + idx];
-    e.apply(idx / a.N, idx % a.N, v);
+  }
+  red[warp][lane] = v;
+  __syncthreads();
+  if (warp == 0 && idx < stride) {
+    float s = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) s += red[w][lane];
+    if (main) e.apply(idx / a.N, idx % a.N, s);
+    else a.db[idx] = s;
   }
 }
 
@@ -652,9 +662,10 @@ int gemm_reduce(const GemmArgs& a_in, cudaStream_t s) {
   GemmArgs a = a_in;
   a.vec = 0;
   const int64_t total = a.M * a.N;
-  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
+  const int64_t blocks = (total + 31) / 32 + ((a.db && a.db_part) ? (a.M + 31) / 32 : 0);
+  if (blocks == 0) return EGNN_OK;
   TimerScope ts("gemm_reduce", s);
-  EGNN_CHECK_CUDA(launch_pdl(gemm_reduce_kernel, dim3(blocks), dim3(256), 0, s, a));
+  EGNN_CHECK_CUDA(launch_pdl(gemm_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, s, a));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

@@ -109,19 +109,21 @@ __device__ __forceinline__ float4 ld4(const Mat& X, int64_t r, int64_t c, int64_
 // Shared-memory layout of one kernel instance.
 //   data: W hi | W lo (resident, kWMax bytes reserved) | ring of 2 stages of
 //         the A chunk (128 m x 64 k, hi + lo) | staging | barriers
-//   WG:   ring of 2 stages of [A^T chunk (64 k x 128 m, hi + lo) | X chunk
-//         (64 k x BN, hi + lo)] | staging | db partials | barriers
+//   WG:   ring of 4 stages of [A^T chunk (32 k x 128 m, hi + lo) | X chunk
+//         (32 k x BN, hi + lo)] | staging | db partials | barriers
+constexpr int kBKW = 32;                  // node rows per weight-gradient stage
 template <int BN, bool WG>
 struct NL {
-  static constexpr int A_PART = kBM * kBK * 2;                      // 16 KB
-  static constexpr int B_PART = kBK * BN * 2;                       // WG only
+  static constexpr int KS = WG ? kBKW : kBK;                        // K per stage
+  static constexpr int A_PART = kBM * KS * 2;                       // 16 / 8 KB
+  static constexpr int B_PART = KS * BN * 2;                        // WG only
   static constexpr int STAGE = WG ? 2 * A_PART + 2 * B_PART : 2 * A_PART;
-  static constexpr int S = 2;
+  static constexpr int S = WG ? 4 : 2;
   static constexpr int RING = WG ? 0 : kWMax;
   static constexpr int STG = RING + S * STAGE;                       // float[128][33]
   static constexpr int RED = STG + kBM * kStgLd * 4;                 // WG: db partials float[4][128]
   static constexpr int BAR = RED + 4 * kBM * 4;
-  static constexpr size_t BYTES = BAR + 128 + 1024;
+  static constexpr size_t BYTES = BAR + 160 + 1024;
 };
 
 struct Bars {
@@ -134,8 +136,8 @@ struct Bars {
   int* abort_s;
   __device__ Bars(char* p) {
     full = reinterpret_cast<uint64_t*>(p);
-    empty = full + 2;
-    accf = empty + 2;
+    empty = full + 4;
+    accf = empty + 4;
     acce = accf + 2;
     fin = acce + 2;
     tmem_s = reinterpret_cast<uint32_t*>(fin + 1);
@@ -143,10 +145,12 @@ struct Bars {
   }
 };
 
-__device__ __forceinline__ void init_bars(const Bars& b) {
-  for (int s = 0; s < 2; ++s) {
+__device__ __forceinline__ void init_bars(const Bars& b, int stages) {
+  for (int s = 0; s < stages; ++s) {
     mbar_init(&b.full[s], 128);
     mbar_init(&b.empty[s], 1);
+  }
+  for (int s = 0; s < 2; ++s) {
     mbar_init(&b.accf[s], 1);
     mbar_init(&b.acce[s], 4);
   }
@@ -240,7 +244,7 @@ struct DataArgs {
 };
 
 template <int BN>
-__global__ void __launch_bounds__(kNT, 1) nmm_data_kernel(DataArgs a) {
+__global__ void __maxnreg__(224) nmm_data_kernel(DataArgs a) {
   using L = NL<BN, false>;
   constexpr uint32_t IDESC = make_idesc_bf16(kBM, BN, 0, 1);   // A K-major, B MN-major
   extern __shared__ __align__(1024) char nm_raw[];
@@ -262,14 +266,23 @@ __global__ void __launch_bounds__(kNT, 1) nmm_data_kernel(DataArgs a) {
   const int64_t n0 = (int64_t)nc * BN;
   const int nkc = Kp / kBK;
 
-  // resident weight chunk B[0:Kpad][n0:n0+BN] -> hi / lo MN-major tiles
-  for (int idx = tid; idx < Kp * BN / 4; idx += kNT) {
-    const int k = idx / (BN / 4), c = (idx % (BN / 4)) * 4;
-    const float4 v = ld4(a.B, k, n0 + c, a.K, a.N);
-    st4_split(w_hi, w_lo, sw128_offset(k, c, Kp), v);
+  // resident weight chunk B[0:Kpad][n0:n0+BN] -> hi / lo MN-major tiles,
+  // eight 16-byte loads of every thread in flight per round
+  for (int base = 0; base < Kp * BN / 4; base += 8 * kNT) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = base + u * kNT + tid, k = idx / (BN / 4), c = (idx % (BN / 4)) * 4;
+      v[u] = idx < Kp * BN / 4 ? ld4(a.B, k, n0 + c, a.K, a.N) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = base + u * kNT + tid, k = idx / (BN / 4), c = (idx % (BN / 4)) * 4;
+      if (idx < Kp * BN / 4) st4_split(w_hi, w_lo, sw128_offset(k, c, Kp), v[u]);
+    }
   }
   if (warp == 8) tmem_alloc(bars.tmem_s, 2 * BN);
-  if (tid == 0) init_bars(bars);
+  if (tid == 0) init_bars(bars, L::S);
   fence_proxy_async();
   fence_before_sync();
   __syncthreads();
@@ -278,30 +291,41 @@ __global__ void __launch_bounds__(kNT, 1) nmm_data_kernel(DataArgs a) {
   volatile int* abort_f = bars.abort_s;
 
   if (warp < 4) {
-    // ---- producers: A rows of each tile, 64 columns per stage
+    // ---- producers: A rows of each tile, 64 columns per stage.  Stage
+    // it + 1 is loaded into the second register buffer before stage it waits
+    // for its ring slot and is split, so 32-64 KB stay in flight per SM.
     const int ptid = tid;
-    uint32_t it = 0;
-    bool ok = true;
-    for (int64_t j = 0; j < ntl && ok; ++j) {
-      const int64_t m0 = (rt0 + j * stride) * kBM;
-      for (int kc = 0; kc < nkc; ++kc, ++it) {
-        const int s = it & 1;
-        if (it >= 2 && !(ok = wait_bar(&bars.empty[s], ((it >> 1) - 1) & 1, abort_f))) break;
-        char* st = sm + L::RING + s * L::STAGE;
-        float4 v[16];
+    const int64_t total = ntl * nkc;
+    auto load = [&](float4 (&v)[16], int64_t it) {
+      const int64_t m0 = (rt0 + (it / nkc) * stride) * kBM;
+      const int64_t k0 = (it % nkc) * kBK;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int idx = i * 128 + ptid, r = idx >> 4, c = (idx & 15) * 4;
-          v[i] = ld4(a.A, m0 + r, (int64_t)kc * kBK + c, a.M, a.K);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int idx = i * 128 + ptid, r = idx >> 4, c = (idx & 15) * 4;
-          st4_split(st, st + L::A_PART, sw128_offset(r, c, kBM), v[i]);
-        }
-        fence_proxy_async();
-        mbar_arrive1(&bars.full[s]);
+      for (int i = 0; i < 16; ++i) {
+        const int idx = i * 128 + ptid, r = idx >> 4, c = (idx & 15) * 4;
+        v[i] = ld4(a.A, m0 + r, k0 + c, a.M, a.K);
       }
+    };
+    auto put = [&](const float4 (&v)[16], int64_t it) -> bool {
+      const int s = (int)(it & 1);
+      if (it >= 2 && !wait_bar(&bars.empty[s], (uint32_t)((it >> 1) - 1) & 1, abort_f)) return false;
+      char* st = sm + L::RING + s * L::STAGE;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int idx = i * 128 + ptid, r = idx >> 4, c = (idx & 15) * 4;
+        st4_split(st, st + L::A_PART, sw128_offset(r, c, kBM), v[i]);
+      }
+      fence_proxy_async();
+      mbar_arrive1(&bars.full[s]);
+      return true;
+    };
+    float4 va[16], vb[16];
+    if (total > 0) load(va, 0);
+    for (int64_t it = 0; it < total; it += 2) {
+      if (it + 1 < total) load(vb, it + 1);
+      if (!put(va, it)) break;
+      if (it + 1 >= total) break;
+      if (it + 2 < total) load(va, it + 2);
+      if (!put(vb, it + 1)) break;
     }
   } else if (warp < 8) {
     // ---- epilogue: thread = TMEM lane (row 32 q + lane) for the loads
@@ -367,7 +391,7 @@ struct WgArgs {
   Mat G, X;                 // G[r][m] (M columns), X[r][n] (N columns), r < R
   int64_t M, N, R;
   int ksplit;
-  int64_t rows_per;         // node rows per split (a multiple of 64)
+  int64_t rows_per;         // node rows per split (a multiple of 32)
   float* C; int64_t ldc;    // ksplit == 1
   float* part;              // ksplit > 1: [ksplit][M][N]
   float* db;                // column sums of G (ksplit == 1)
@@ -375,7 +399,7 @@ struct WgArgs {
 };
 
 template <int BN>
-__global__ void __launch_bounds__(kNT, 1) nmm_wgrad_kernel(WgArgs a) {
+__global__ void __maxnreg__(224) nmm_wgrad_kernel(WgArgs a) {
   using L = NL<BN, true>;
   constexpr uint32_t IDESC = make_idesc_bf16(kBM, BN, 1, 1);   // both MN-major
   extern __shared__ __align__(1024) char nm_raw[];
@@ -389,11 +413,11 @@ __global__ void __launch_bounds__(kNT, 1) nmm_wgrad_kernel(WgArgs a) {
   const int64_t mb = blockIdx.x, nb = blockIdx.y, z = blockIdx.z;
   const int64_t m0 = mb * kBM, n0 = nb * BN;
   const int64_t r0 = std::min<int64_t>(a.R, z * a.rows_per), r1 = std::min<int64_t>(a.R, r0 + a.rows_per);
-  const int nkc = (int)((r1 - r0 + kBK - 1) / kBK);
+  const int nkc = (int)((r1 - r0 + kBKW - 1) / kBKW);
   const bool do_db = a.db != nullptr && nb == 0;
 
   if (warp == 8) tmem_alloc(bars.tmem_s, BN);
-  if (tid == 0) init_bars(bars);
+  if (tid == 0) init_bars(bars, L::S);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -401,49 +425,57 @@ __global__ void __launch_bounds__(kNT, 1) nmm_wgrad_kernel(WgArgs a) {
   volatile int* abort_f = bars.abort_s;
 
   if (warp < 4) {
-    // ---- producers: 64 node rows per stage of G (128 m columns) and X (BN n columns)
+    // ---- producers: 32 node rows per stage of G (128 m columns) and X (BN n
+    // columns), 8 + BN / 16 words per thread; the next stage is loaded into
+    // the second register buffer before this one waits for its ring slot
     const int ptid = tid;
+    constexpr int BW = BN / 4;                      // float4 words per X row
+    constexpr int XW = kBKW * BW / 128;             // X words per thread: 4 or 8
+    constexpr int NW = 8 + XW;
     float4 dbs = make_float4(0.f, 0.f, 0.f, 0.f);   // sums of columns m0 + 4 (ptid & 31) .. + 3
-    bool ok = true;
-    for (int kc = 0; kc < nkc; ++kc) {
-      const int s = kc & 1;
-      if (kc >= 2 && !(ok = wait_bar(&bars.empty[s], ((kc >> 1) - 1) & 1, abort_f))) break;
+    auto load = [&](float4 (&v)[16], int kc) {
+      const int64_t rb = r0 + (int64_t)kc * kBKW;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = i * 128 + ptid, k = idx >> 5, c = (idx & 31) * 4;
+        v[i] = ld4(a.G, rb + k, m0 + c, r1, a.M);
+      }
+#pragma unroll
+      for (int i = 0; i < XW; ++i) {
+        const int idx = i * 128 + ptid, k = idx / BW, c = (idx % BW) * 4;
+        v[8 + i] = ld4(a.X, rb + k, n0 + c, r1, a.N);
+      }
+    };
+    auto put = [&](const float4 (&v)[16], int kc) -> bool {
+      const int s = kc & (L::S - 1);
+      if (kc >= L::S && !wait_bar(&bars.empty[s], (uint32_t)((kc / L::S) - 1) & 1, abort_f)) return false;
       char* st = sm + s * L::STAGE;
-      const int64_t rb = r0 + (int64_t)kc * kBK;
-      {
-        float4 v[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int idx = i * 128 + ptid, k = idx >> 5, c = (idx & 31) * 4;
-          v[i] = ld4(a.G, rb + k, m0 + c, r1, a.M);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int idx = i * 128 + ptid, k = idx >> 5, c = (idx & 31) * 4;
-          st4_split(st, st + L::A_PART, sw128_offset(k, c, kBK), v[i]);
-          dbs.x += v[i].x; dbs.y += v[i].y; dbs.z += v[i].z; dbs.w += v[i].w;
-        }
+      for (int i = 0; i < 8; ++i) {
+        const int idx = i * 128 + ptid, k = idx >> 5, c = (idx & 31) * 4;
+        st4_split(st, st + L::A_PART, sw128_offset(k, c, kBKW), v[i]);
+        dbs.x += v[i].x; dbs.y += v[i].y; dbs.z += v[i].z; dbs.w += v[i].w;
       }
       char* bst = st + 2 * L::A_PART;
-      constexpr int BW = BN / 4;                      // float4 words per X row
-      constexpr int WPT = kBK * BW / 128;             // words per thread: 8, 16 or 32
-      static_assert(WPT % 8 == 0, "X chunk in rounds of 8 words per thread");
-#pragma unroll 1
-      for (int rd = 0; rd < WPT / 8; ++rd) {
-        float4 v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int idx = (rd * 8 + i) * 128 + ptid, k = idx / BW, c = (idx % BW) * 4;
-          v[i] = ld4(a.X, rb + k, n0 + c, r1, a.N);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int idx = (rd * 8 + i) * 128 + ptid, k = idx / BW, c = (idx % BW) * 4;
-          st4_split(bst, bst + L::B_PART, sw128_offset(k, c, kBK), v[i]);
-        }
+      for (int i = 0; i < XW; ++i) {
+        const int idx = i * 128 + ptid, k = idx / BW, c = (idx % BW) * 4;
+        st4_split(bst, bst + L::B_PART, sw128_offset(k, c, kBKW), v[8 + i]);
       }
       fence_proxy_async();
       mbar_arrive1(&bars.full[s]);
+      return true;
+    };
+    static_assert(NW <= 16, "one register buffer per stage");
+    float4 va[16], vb[16];
+    bool ok = true;
+    if (nkc > 0) load(va, 0);
+    for (int kc = 0; kc < nkc; kc += 2) {
+      if (kc + 1 < nkc) load(vb, kc + 1);
+      if (!(ok = put(va, kc))) break;
+      if (kc + 1 >= nkc) break;
+      if (kc + 2 < nkc) load(va, kc + 2);
+      if (!(ok = put(vb, kc + 1))) break;
     }
     if (do_db && ok) {
       // the four threads of a column word (row classes ptid >> 5), combined in fixed order below
@@ -454,15 +486,15 @@ __global__ void __launch_bounds__(kNT, 1) nmm_wgrad_kernel(WgArgs a) {
       const uint32_t ring = smem_u32(sm);
       bool ok = true;
       for (int kc = 0; kc < nkc; ++kc) {
-        const int s = kc & 1;
-        if (!(ok = wait_bar(&bars.full[s], (kc >> 1) & 1, abort_f))) break;
+        const int s = kc & (L::S - 1);
+        if (!(ok = wait_bar(&bars.full[s], (uint32_t)(kc / L::S) & 1, abort_f))) break;
         fence_after_sync();
         const uint32_t ah = ring + s * L::STAGE, al = ah + L::A_PART, bh = ah + 2 * L::A_PART, bl = bh + L::B_PART;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
+        for (int kk = 0; kk < kBKW / 16; ++kk) {
           const uint32_t off = kk * 2048;
-          const uint64_t dah = make_desc(ah + off, kBK * 128, 1024), dal = make_desc(al + off, kBK * 128, 1024);
-          const uint64_t dbh = make_desc(bh + off, kBK * 128, 1024), dbl = make_desc(bl + off, kBK * 128, 1024);
+          const uint64_t dah = make_desc(ah + off, kBKW * 128, 1024), dal = make_desc(al + off, kBKW * 128, 1024);
+          const uint64_t dbh = make_desc(bh + off, kBKW * 128, 1024), dbl = make_desc(bl + off, kBKW * 128, 1024);
           mma_bf16(tmem, dah, dbh, IDESC, (kc | kk) ? 1u : 0u);
           mma_bf16(tmem, dah, dbl, IDESC, 1u);
           mma_bf16(tmem, dal, dbh, IDESC, 1u);
@@ -541,13 +573,18 @@ int set_smem(K kernel, size_t bytes) {
   return EGNN_OK;
 }
 
-// Resident weight chunk width: the widest of 256 / 128 / 64 columns whose
-// hi + lo tiles for all of K fit the 128 KB budget (K padded to 64).
-int data_bn(int64_t N, int64_t Kpad) {
-  const int64_t npad = (N + 63) / 64 * 64;
-  for (int bn : {256, 128, 64})
-    if (bn <= npad && Kpad * bn * 4 <= kWMax) return bn;
-  return 64;
+// Resident weight chunk width: of 256 / 128 / 64 columns whose hi + lo tiles
+// for all of K fit the 128 KB budget (K padded to 64), the widest that still
+// gives at least one tile per SM (narrower chunks give small-M GEMMs more
+// CTAs and less weight to load each; A is then re-read from L2).
+int data_bn(int64_t M, int64_t N, int64_t Kpad, int sms) {
+  const int64_t npad = (N + 63) / 64 * 64, row_tiles = (M + kBM - 1) / kBM;
+  int best = 64;
+  for (int bn : {64, 128, 256}) {
+    if (bn > npad || Kpad * bn * 4 > kWMax) break;
+    if (bn == 64 || row_tiles * ((N + bn - 1) / bn) >= sms) best = bn;
+  }
+  return best;
 }
 
 template <int BN>
@@ -585,7 +622,7 @@ int launch_wgrad(const WgArgs& w, cudaStream_t s) {
   return EGNN_OK;
 }
 
-int wgrad_bn(int64_t N) { return N > 128 ? 256 : (N > 64 ? 128 : 64); }
+int wgrad_bn(int64_t N) { return N > 64 ? 128 : 64; }
 
 }  // namespace
 
@@ -606,7 +643,7 @@ int gemm_tc(const GemmArgs& a, cudaStream_t s) {
   d.B = a.B;
   d.M = a.M; d.N = a.N; d.K = a.K;
   d.Kpad = (a.K + kBK - 1) / kBK * kBK;
-  const int bn = data_bn(a.N, d.Kpad);
+  const int bn = data_bn(a.M, a.N, d.Kpad, num_sms_current());
   d.n_chunks = (int)((a.N + bn - 1) / bn);
   Epilogue& e = d.epi;
   e.bias = a.bias;
@@ -651,8 +688,7 @@ int wgrad_tc(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t l
   w.db = db;
   w.db_part = (db && w.ksplit > 1) ? part + (int64_t)w.ksplit * M * N : nullptr;
   const int bn = wgrad_bn(N);
-  if (bn == 256) EGNN_TRY(launch_wgrad<256>(w, s));
-  else if (bn == 128) EGNN_TRY(launch_wgrad<128>(w, s));
+  if (bn == 128) EGNN_TRY(launch_wgrad<128>(w, s));
   else EGNN_TRY(launch_wgrad<64>(w, s));
   if (w.ksplit > 1) {
     GemmArgs r;

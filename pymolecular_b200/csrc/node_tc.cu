@@ -244,7 +244,7 @@ struct DataArgs {
 };
 
 template <int BN>
-__global__ void __maxnreg__(224) nmm_data_kernel(DataArgs a) {
+__global__ void __launch_bounds__(kNT, 1) nmm_data_kernel(DataArgs a) {
   using L = NL<BN, false>;
   constexpr uint32_t IDESC = make_idesc_bf16(kBM, BN, 0, 1);   // A K-major, B MN-major
   extern __shared__ __align__(1024) char nm_raw[];
@@ -399,7 +399,7 @@ struct WgArgs {
 };
 
 template <int BN>
-__global__ void __maxnreg__(224) nmm_wgrad_kernel(WgArgs a) {
+__global__ void __launch_bounds__(kNT, 1) nmm_wgrad_kernel(WgArgs a) {
   using L = NL<BN, true>;
   constexpr uint32_t IDESC = make_idesc_bf16(kBM, BN, 1, 1);   // both MN-major
   extern __shared__ __align__(1024) char nm_raw[];

@@ -162,10 +162,15 @@ __device__ __forceinline__ void init_bars(const Bars& b, int stages) {
 // Epilogue of one 128 x 32 slab: the thread's TMEM row (v[], row 32 q + lane)
 // goes through the staging tile, then every thread moves 8 four-column words
 // (consecutive threads on consecutive words: whole 128-byte row pieces per
-// quarter warp).  `emit(row, word, float4)` applies the epilogue and stores.
-template <class Emit>
-__device__ __forceinline__ void slab_out(float* stg, int q, int lane, int etid, const float (&v)[32], Emit emit) {
+// quarter warp).  `fetch(row, word, i)` issues the global loads word i needs
+// (all 8 words' loads are in flight before the first result is formed) and
+// `emit(row, word, i, float4)` applies the epilogue and stores.
+template <class Fetch, class Emit>
+__device__ __forceinline__ void slab_out(float* stg, int q, int lane, int etid, const float (&v)[32], Fetch fetch,
+                                         Emit emit) {
   float* row = stg + (q * 32 + lane) * kStgLd;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) fetch(i * 16 + (etid >> 3), etid & 7, i);
 #pragma unroll
   for (int c = 0; c < 32; ++c) row[c] = v[c];
   epi_sync();
@@ -173,10 +178,15 @@ __device__ __forceinline__ void slab_out(float* stg, int q, int lane, int etid, 
   for (int i = 0; i < 8; ++i) {
     const int r = i * 16 + (etid >> 3), w = etid & 7;
     const float* src = stg + r * kStgLd + 4 * w;
-    emit(r, w, make_float4(src[0], src[1], src[2], src[3]));
+    emit(r, w, i, make_float4(src[0], src[1], src[2], src[3]));
   }
   epi_sync();
 }
+
+// Per-word operands of the fused epilogue, loaded ahead of the math.
+struct Side {
+  float4 bias, aux, resid;
+};
 
 struct Epilogue {
   const float* bias;
@@ -200,21 +210,25 @@ struct Epilogue {
     if (resid && n < resid_cols) y += resid[m * ldr + n];
     return y;
   }
-  __device__ __forceinline__ void apply4(int64_t m, int64_t n, float4 acc) const {
+  // vector path: the word's bias, SiLU' operand and residual
+  __device__ __forceinline__ void fetch(int64_t m, int64_t n, Side& sd) const {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    sd.bias = sd.aux = sd.resid = z;
+    if (!vec || m >= M || n >= N) return;
+    if (bias) sd.bias = __ldg(reinterpret_cast<const float4*>(bias + n));
+    if (act == ACT_DSILU) sd.aux = *reinterpret_cast<const float4*>(aux + m * ldaux + n);
+    if (resid && n < resid_cols) sd.resid = *reinterpret_cast<const float4*>(resid + m * ldr + n);
+  }
+  __device__ __forceinline__ void apply4(int64_t m, int64_t n, float4 acc, const Side& sd) const {
     if (m >= M || n >= N) return;
     if (vec) {
-      float y[4] = {acc.x, acc.y, acc.z, acc.w};
-      if (bias) {
-        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + n));
-        y[0] += b.x; y[1] += b.y; y[2] += b.z; y[3] += b.w;
-      }
+      float y[4] = {acc.x + sd.bias.x, acc.y + sd.bias.y, acc.z + sd.bias.z, acc.w + sd.bias.w};
       if (pre) *reinterpret_cast<float4*>(pre + m * ldp + n) = make_float4(y[0], y[1], y[2], y[3]);
       if (act == ACT_SILU) {
 #pragma unroll
         for (int t = 0; t < 4; ++t) y[t] = silu_fast(y[t]);
       } else if (act == ACT_DSILU) {
-        const float4 z = *reinterpret_cast<const float4*>(aux + m * ldaux + n);
-        const float zz[4] = {z.x, z.y, z.z, z.w};
+        const float zz[4] = {sd.aux.x, sd.aux.y, sd.aux.z, sd.aux.w};
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           float yy, d;
@@ -222,10 +236,7 @@ struct Epilogue {
           y[t] *= d;
         }
       }
-      if (resid && n < resid_cols) {
-        const float4 r = *reinterpret_cast<const float4*>(resid + m * ldr + n);
-        y[0] += r.x; y[1] += r.y; y[2] += r.z; y[3] += r.w;
-      }
+      y[0] += sd.resid.x; y[1] += sd.resid.y; y[2] += sd.resid.z; y[3] += sd.resid.w;
       *reinterpret_cast<float4*>(C + m * ldc + n) = make_float4(y[0], y[1], y[2], y[3]);
     } else {
       const float a[4] = {acc.x, acc.y, acc.z, acc.w};
@@ -345,9 +356,11 @@ __global__ void __launch_bounds__(kNT, 1) nmm_data_kernel(DataArgs a) {
           __syncwarp();
           if (lane == 0) mbar_arrive1(&bars.acce[buf]);
         }
-        slab_out(stg, q, lane, etid, v, [&](int r, int w, float4 val) {
-          a.epi.apply4(m0 + r, n0 + cs * 32 + 4 * w, val);
-        });
+        Side sd[8];
+        slab_out(
+            stg, q, lane, etid, v,
+            [&](int r, int w, int i) { a.epi.fetch(m0 + r, n0 + cs * 32 + 4 * w, sd[i]); },
+            [&](int r, int w, int i, float4 val) { a.epi.apply4(m0 + r, n0 + cs * 32 + 4 * w, val, sd[i]); });
       }
     }
   } else if (lane == 0) {
@@ -528,7 +541,7 @@ __global__ void __launch_bounds__(kNT, 1) nmm_wgrad_kernel(WgArgs a) {
 #pragma unroll
           for (int t = 0; t < 32; ++t) v[t] = 0.f;
         }
-        slab_out(stg, q, lane, etid, v, [&](int r, int w, float4 val) {
+        slab_out(stg, q, lane, etid, v, [](int, int, int) {}, [&](int r, int w, int, float4 val) {
           const int64_t m = m0 + r, n = n0 + cs * 32 + 4 * w;
           if (m >= a.M || n >= a.N) return;
           float* dst = out + m * ld + n;

@@ -263,17 +263,19 @@ EGNN_API int egnn_linear_bwd(int64_t m, int32_t k, int32_t o, const float* x, co
 
 /* egnn_linear_bwd for callers that cannot allocate device memory.
  * No counterpart in the reference: it exists for host code that must not
- * call cudaMalloc, e.g. code that runs while a stream is being captured
- * (allocation is forbidden there), or a plugin living inside a framework
- * that owns every device allocation and hands out no workspace.  Same
+ * call cudaMalloc, e.g. a plugin living inside a framework that owns every
+ * device allocation and hands out no workspace, or a latency-critical host
+ * path that must not add a synchronising allocation.  Same
  * inputs, outputs and results as egnn_linear_bwd; its scratch is a fixed
  * device array inside the library instead of a caller workspace, and it
  * calls no cudaMalloc, cudaFree or allocating library routine.
  * - Shapes whose egnn_linear_workspace_size(m, k, o) exceeds
  *   EGNN_LINEAR_BWD_STATIC_SCRATCH_BYTES are rejected with
  *   EGNN_ERR_WORKSPACE before anything is launched.
- * - The first call on each device looks up the array's device address with
- *   that device current; make that first call before any stream capture.
+ * - The first call on each device (and on each CUDA context, so again after
+ *   a cudaDeviceReset or under a caller's own context) looks up the array's
+ *   device address with that device current; make that first call before
+ *   any stream capture.
  * - All calls on a device share the one array and it keeps the previous
  *   call's contents (this entry point writes every scratch word before it
  *   reads it, so nothing needs clearing).  Calls whose GPU work overlaps,

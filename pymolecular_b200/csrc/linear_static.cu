@@ -2,11 +2,13 @@
 // cannot allocate device memory.
 //
 // Some callers cannot call cudaMalloc at the point where they need the
-// backward: host code running inside a stream capture (allocation is not a
-// capturable operation), or a plugin whose host framework owns all device
-// memory and offers it no workspace.  This entry point gives them the same
+// backward: a plugin whose host framework owns all device memory and offers
+// it no workspace, or host code that must not add a synchronising allocation
+// to a latency-critical path.  This entry point gives them the same
 // computation as egnn_linear_bwd with its split-K scratch taken from a fixed
 // array compiled into the library.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -21,24 +23,52 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) float g_linear_bwd_scratch[kScratchFloats];
 
 std::mutex g_addr_mu;
+// Device address of the array per CUDA context: a cudaDeviceReset, or a
+// caller that makes a different (non-primary) context current, gets a fresh
+// lookup instead of a stale address.
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 float* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of g_linear_bwd_scratch on the current device.  The host
-// symbol is only a stand-in for the array, so the address is looked up once
-// per device, with that device current.
+// symbol is only a stand-in for the array, so the address is looked up with
+// that device (and context) current, once per context.
+// The driver's cuCtxGetCurrent, found through the runtime (the library does
+// not link the driver library itself).
+CUresult current_context(CUcontext* ctx) {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !p)
+      return CUDA_ERROR_NOT_FOUND;
+    fn = reinterpret_cast<Fn>(p);
+  }
+  return fn(ctx);
+}
+
 int scratch_address(float** out) {
   int dev = 0;
   EGNN_CHECK_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices)
     return fail(EGNN_ERR_INVALID_ARG, "egnn_linear_bwd_static: device %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_addr_mu);
-  if (!g_scratch_addr[dev]) {
+  CUcontext ctx = nullptr;
+  if (current_context(&ctx) != CUDA_SUCCESS)
+    return fail(EGNN_ERR_CUDA, "egnn_linear_bwd_static: cuCtxGetCurrent unavailable");
+  if (!ctx || !g_scratch_addr[dev] || g_scratch_ctx[dev] != ctx) {
+    // the lookup itself makes the device's primary context current if no
+    // context was
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_linear_bwd_scratch);
     if (e != cudaSuccess || !p)
       return fail(EGNN_ERR_CUDA, "egnn_linear_bwd_static: cudaGetSymbolAddress failed: %s",
                   cudaGetErrorString(e));
+    if (!ctx && (current_context(&ctx) != CUDA_SUCCESS || !ctx))
+      return fail(EGNN_ERR_CUDA, "egnn_linear_bwd_static: no current CUDA context");
     g_scratch_addr[dev] = static_cast<float*>(p);
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_addr[dev];
   return EGNN_OK;

@@ -27,7 +27,6 @@ egnn_clean.py:29 vs :63-64), CPU tensors.
 from __future__ import annotations
 
 import ctypes as C
-from typing import Optional
 
 import torch
 from torch import nn
@@ -273,4 +272,3 @@ class EGNN(nn.Module):
 
 
 __all__ = ["E_GCL", "EGNN", "CSR", "linear"]
-_ = Optional

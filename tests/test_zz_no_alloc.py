@@ -1,7 +1,7 @@
 """egnn_linear_bwd_static: the allocation-free embedding backward.
 
-Callers that cannot call cudaMalloc (code running under stream capture, or a
-plugin whose host framework owns all device memory) use this entry point; its
+Callers that cannot call cudaMalloc (a plugin whose host framework owns all
+device memory and offers it no workspace) use this entry point; its
 scratch is a fixed array inside the library.  It must give the same result
 as egnn_linear_bwd with a caller workspace, call after call, and refuse
 shapes whose scratch would not fit.  This file is collected last on purpose.

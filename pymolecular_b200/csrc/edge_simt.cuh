@@ -94,6 +94,11 @@ struct EdgeCommon {
   int64_t epc = 0;               // edges per CTA (multiple of the chunk size)
   float* carry = nullptr;        // (G, 2, H+4) partial rows at CTA range edges
   int32_t* carry_row = nullptr;  // (G, 2)
+  // Tensor-core kernels: poll limit of the MMA-completion waits (-1: the
+  // built-in limit).  Only a debugging aid sets it (EGNN_DEBUG_WAIT_POLLS),
+  // to make the give-up path run; the drain wait that precedes freeing the
+  // tensor memory always keeps the built-in limit.
+  int wait_polls = -1;
 };
 
 struct EdgeFwdArgs : EdgeCommon {

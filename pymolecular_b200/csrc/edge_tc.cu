@@ -28,6 +28,7 @@
 // each node's in-edges and out-edges, are taken by node_pass_kernel.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 
 #include "edge_rows.cuh"
 #include "edge_simt.cuh"
@@ -87,9 +88,10 @@ __device__ __forceinline__ uint64_t desc_mn(const char* tile, int rows, int kk) 
 }
 
 // Thread-uniform bounded wait on the chunk barrier; false on timeout, after
-// one more bounded wait for the MMAs still in flight.
-__device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase) {
-  const bool ok = mbar_wait(bar, phase);
+// one more bounded wait (the built-in limit) for the MMAs still in flight.
+// polls < 0: the built-in limit for the first wait too.
+__device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase, int polls) {
+  const bool ok = mbar_wait(bar, phase, polls < 0 ? (1u << 22) : (uint32_t)polls);
   const int bad = __syncthreads_or(!ok);
   if (bad) {
     if (threadIdx.x == 0) {
@@ -471,7 +473,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       cp_async4(&ncol[g.e], a.col_idx + c1 + g.e);
       cp_async_commit_group();
     }
-    if (!(ok = wait_mma(bar, phase))) break;
+    if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
     if (prefetcher) {
       cp_async_wait_all_groups();
       cp_async16_ca(&nxi[g.e], a.xp + nrow[g.e]);
@@ -506,7 +508,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
         mma_bf16(tAGG, desc_k(St, kM, kk), desc_mn(Mlo, kM, kk), C::IDESC_DGRAD, 1u);
       mma_commit(bar);
     }
-    if (!(ok = wait_mma(bar, phase))) break;
+    if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
 
     // ---- phi = wc2 . silu(c1 + bc1), four column slices per edge
     {
@@ -767,7 +769,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       cp_async4(&ncol[g.e], a.col_idx + c1 + g.e);
       cp_async_commit_group();
     }
-    if (!(ok = wait_mma(bar, phase))) break;
+    if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
     if (prefetcher) {
       cp_async_wait_all_groups();
       const int i = nrow[g.e], j = ncol[g.e];
@@ -799,7 +801,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
         mma_bf16(tD0, desc_k(Mt, kM, kk), desc_k(Wc1t, H, kk), C::IDESC_FWD, kk > 0);
       mma_commit(bar);
     }
-    if (!(ok = wait_mma(bar, phase))) break;
+    if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
 
     // ---- phi and its gradient (row sums across the four column slices)
     {
@@ -855,7 +857,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       for (int q = 0; q < 8; ++q)
         gagg[q] = valid ? *reinterpret_cast<const float4*>(ga + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (!(ok = wait_mma(bar, phase))) break;
+    if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
 
     // ---- g_a2 = (g_m + g_agg[i]) silu'(a2) -> tile G ; column sums
     {
@@ -890,7 +892,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       mma_commit(bar);
     }
     first = false;
-    if (!(ok = wait_mma(bar, phase))) break;
+    if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
 
     // ---- g_a1 = g_u1 silu'(a1) -> global ; d-gradient
     {
@@ -1075,8 +1077,20 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
   if (lane < 3 && part == 0) gx[v * 3 + lane] = gx_out[v * 3 + lane] + gdd - gds;
 }
 
+// EGNN_DEBUG_WAIT_POLLS (debugging aid, read at every launch): the poll
+// limit of the tensor-core kernels' MMA-completion waits; 0 makes every such
+// wait give up at once, which exercises the give-up path.  Unset: -1.
+int debug_wait_polls() {
+  const char* v = getenv("EGNN_DEBUG_WAIT_POLLS");
+  if (!v || !*v) return -1;
+  const long n = strtol(v, nullptr, 10);
+  return n < 0 ? -1 : (int)std::min<long>(n, 1L << 22);
+}
+
 template <int H>
-int launch_fwd_tc(const EdgeFwdArgs& a, int G, cudaStream_t s) {
+int launch_fwd_tc(const EdgeFwdArgs& a_in, int G, cudaStream_t s) {
+  EdgeFwdArgs a = a_in;
+  a.wait_polls = debug_wait_polls();
   constexpr size_t bytes = FwdLayout<H>::BYTES;
   static uint64_t attr_set = 0;
   const uint64_t bit = device_bit();
@@ -1094,7 +1108,9 @@ int launch_fwd_tc(const EdgeFwdArgs& a, int G, cudaStream_t s) {
 }
 
 template <int H>
-int launch_bwd_tc(const EdgeBwdArgs& a, int G, cudaStream_t s) {
+int launch_bwd_tc(const EdgeBwdArgs& a_in, int G, cudaStream_t s) {
+  EdgeBwdArgs a = a_in;
+  a.wait_polls = debug_wait_polls();
   constexpr size_t bytes = BwdLayout<H>::BYTES;
   static uint64_t attr_set = 0;
   const uint64_t bit = device_bit();

@@ -220,3 +220,60 @@ def test_halo_plan_lists():
     assert torch.all((r >= b[0]) & (r < b[1]))
     assert torch.all((halo >= b[1]))
     assert torch.equal(halo, torch.unique(halo))
+
+
+# ---------------------------------------------------------------------------
+# failure detection on the host: a rank that dies, a collective that times out
+# ---------------------------------------------------------------------------
+
+def _failure_entry(rank, world, port, mode, q):
+    import time
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=4))
+    t = torch.ones(16)
+    dist.all_reduce(t)            # a healthy step first
+    if rank == 1:
+        if mode == "exit":
+            q.put(("left", 0.0))
+            q.close()
+            q.join_thread()       # the message is out before the process dies
+            os._exit(0)           # dies between steps, no collective in flight
+        time.sleep(10)            # alive but never joins the next collective
+        q.put(("slept", 0.0))
+        return
+    t0 = time.time()
+    try:
+        sync = P.GradAllReduce([torch.nn.Parameter(torch.zeros(4))])
+        sync.params[0].grad = torch.ones(4)
+        sync()
+        q.put(("no error", time.time() - t0))
+    except Exception as exc:      # the peer's absence surfaces as an error, not a hang
+        q.put((type(exc).__name__, time.time() - t0))
+    finally:
+        q.close()
+        q.join_thread()
+        os._exit(0)               # no teardown handshake with a missing peer
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_missing_rank_surfaces_as_an_error(mode):
+    """A gradient all-reduce whose peer has died (or never joins) ends with an
+    exception on the surviving rank within the process-group timeout."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_failure_entry, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    survivor = [g for g in got if g[0] not in ("left", "slept")]
+    assert len(survivor) == 1, got
+    name, elapsed = survivor[0]
+    assert name != "no error", got
+    assert elapsed < 60, got

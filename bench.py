@@ -37,9 +37,10 @@ def parse():
     ap.add_argument("--n-graphs", type=int, default=None, help="shrink the batch (profiling runs)")
     ap.add_argument("--n-nodes", type=int, default=None, help="config 5: node count (default 2^20)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--allreduce", default="layers", choices=["layers", "flat"],
-                    help="data parallel: per-layer buckets all-reduced as the backward produces them "
-                         "(layers) or one flat all-reduce after the backward (flat)")
+    ap.add_argument("--allreduce", default="flat", choices=["layers", "flat"],
+                    help="data parallel: one flat all-reduce after the backward (flat, measured equal or "
+                         "faster at 2 and 8 GPUs) or per-layer buckets all-reduced as the backward "
+                         "produces them (layers)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",

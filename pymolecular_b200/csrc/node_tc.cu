@@ -35,7 +35,7 @@ constexpr int BMT = 128, BKT = 64, NTH = 512, NDB = NTH / 16;
 
 template <int BN>
 struct TcShape {
-  static constexpr int NRAW = BN == 64 ? 3 : 2;       // raw fp32 ring depth
+  static constexpr int NRAW = BN == 64 ? 3 : (BN == 128 ? 2 : 1);   // raw fp32 ring depth
   static constexpr int RAW_A = BMT * BKT * 4;          // 32 KB
   static constexpr int RAW_B = BN * BKT * 4;
   static constexpr int RAW_STAGE = RAW_A + RAW_B;
@@ -289,21 +289,28 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
 
   // ---- epilogue.  1: warp w moves TMEM lanes 32 (w % 4) .. (rows), column
   // quarter w / 4, into an fp32 staging tile over the (idle) raw ring.
-  constexpr int NCW = BNT / 4;       // 32 or 16 columns per warp
-  constexpr int LDO = BNT + 4;       // staging row stride: 33 or 17 16-byte words (odd)
-  float* ostage = reinterpret_cast<float*>(sm + S::OFF_RAW);
+  constexpr int NCW = BNT / 4;       // 64, 32 or 16 columns per warp
+  constexpr int LDO = BNT + 4;       // staging row stride: 65, 33 or 17 16-byte words (odd)
+  // the staging tile (128 x LDO floats) lies over the idle raw ring, or for
+  // 256-column tiles over the operand tiles and the raw ring together
+  float* ostage = reinterpret_cast<float*>(sm + (BNT == 256 ? 0 : S::OFF_RAW));
+  static_assert((BNT == 256 ? 0 : S::OFF_RAW) + BMT * LDO * 4 <= S::OFF_BAR, "staging fits");
   {
     const int q = warp & 3, h = warp >> 2;
-    float v[NCW];
-    if constexpr (NCW == 32) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
-    else tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
-    if (nkc == 0) {   // empty K slice of a split: the accumulator was never written
+#pragma unroll 1
+    for (int part = 0; part < (NCW > 32 ? NCW / 32 : 1); ++part) {
+      constexpr int W = NCW > 32 ? 32 : NCW;
+      float v[W];
+      if constexpr (W == 32) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + h * NCW + part * 32, v);
+      else tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
+      if (nkc == 0) {   // empty K slice of a split: the accumulator was never written
 #pragma unroll
-      for (int t = 0; t < NCW; ++t) v[t] = 0.f;
+        for (int t = 0; t < W; ++t) v[t] = 0.f;
+      }
+      float* dst = ostage + (q * 32 + lane) * LDO + h * NCW + part * 32;
+#pragma unroll
+      for (int t = 0; t < W; t += 4) *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
     }
-    float* dst = ostage + (q * 32 + lane) * LDO + h * NCW;
-#pragma unroll
-    for (int t = 0; t < NCW; t += 4) *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
   }
   fence_before_sync();
   __syncthreads();
@@ -408,13 +415,19 @@ int launch_t(const GemmArgs& a, cudaStream_t s) {
   return EGNN_OK;
 }
 
-// One CTA per SM: 64-column tiles only while twice the CTAs still fit in one
-// wave, else 128-column tiles.
+// One CTA per SM: 64-column tiles while twice the CTAs still fit in one wave;
+// 256-column tiles when 128-column tiles would need a second wave and
+// 256-column ones do not (data GEMMs only: their K is short, so the one-deep
+// raw ring of that shape costs less than the second wave); else 128.
 template <int A_T, int B_T>
 int launch_ab(const GemmArgs& a, cudaStream_t s) {
   const int64_t z = a.ksplit > 1 ? a.ksplit : 1;
-  const int64_t tiles128 = (a.N + 127) / 128 * ((a.M + BMT - 1) / BMT) * z;
-  if (2 * tiles128 <= num_sms_current()) return launch_t<A_T, B_T, 64>(a, s);
+  const int64_t rows = (a.M + BMT - 1) / BMT;
+  const int64_t tiles128 = (a.N + 127) / 128 * rows * z;
+  const int64_t tiles256 = (a.N + 255) / 256 * rows * z;
+  const int sms = num_sms_current();
+  if (2 * tiles128 <= sms) return launch_t<A_T, B_T, 64>(a, s);
+  if (A_T == 0 && z == 1 && a.N > 128 && tiles128 > sms && tiles256 <= sms) return launch_t<A_T, B_T, 256>(a, s);
   return launch_t<A_T, B_T, 128>(a, s);
 }
 

@@ -7,6 +7,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace egnn {
@@ -130,3 +132,31 @@ extern "C" int egnn_kernel_time(const char* name, double* total_ms, int64_t* lau
   *launches = n;
   return EGNN_OK;
 }
+
+namespace egnn {
+
+bool tensor_map_i32_1d(void* map, const int32_t* p, int64_t n, int box) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static std::atomic<Encode> encode{nullptr};
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode.store(reinterpret_cast<Encode>(fn));
+  });
+  Encode f = encode.load();
+  if (!f || !p || n <= 0 || (reinterpret_cast<uintptr_t>(p) & 15u)) return false;
+  const cuuint64_t dim[1] = {(cuuint64_t)n};
+  const cuuint64_t stride[1] = {(cuuint64_t)n * 4};   // not read for rank 1
+  const cuuint32_t boxd[1] = {(cuuint32_t)box};
+  const cuuint32_t estr[1] = {1};
+  return f(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_INT32, 1, const_cast<int32_t*>(p), dim, stride,
+           boxd, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace egnn

@@ -51,6 +51,10 @@ struct TimerScope {
   } while (0)
 
 int num_sms_current();
+// A 1-D tensor map over n int32 elements at p with boxes of `box` elements
+// (TMA loads; elements past n read as zero).  False when p is not 16-byte
+// aligned or the driver cannot encode it (callers then load per thread).
+bool tensor_map_i32_1d(void* map, const int32_t* p, int64_t n, int box);
 // Bit of the current device (for per-device one-time setup flags).
 uint64_t device_bit();
 

@@ -1,6 +1,8 @@
 // Fused EGNN edge kernels (SIMT FFMA path): argument blocks and launchers.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace egnn {
@@ -99,6 +101,12 @@ struct EdgeCommon {
   // to make the give-up path run; the drain wait that precedes freeing the
   // tensor memory always keeps the built-in limit.
   int wait_polls = -1;
+  // Tensor-core kernels: 1-D tensor maps of row_idx and col_idx (int32, box of
+  // 128), for the TMA loads of each chunk's index tiles; use_tma = 0 when the
+  // arrays are not 16-byte aligned (the kernels then load them per thread).
+  CUtensorMap tm_row;
+  CUtensorMap tm_col;
+  int use_tma = 0;
 };
 
 struct EdgeFwdArgs : EdgeCommon {

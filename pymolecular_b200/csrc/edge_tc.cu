@@ -106,6 +106,33 @@ __device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase, int pol
   return true;
 }
 
+// CTA-uniform bounded wait for the next chunk's index tiles (TMA); on
+// timeout the event is counted and thread 0 waits once more (built-in limit)
+// so that no copy is still landing when the CTA leaves.
+__device__ __forceinline__ bool wait_idx(uint64_t* bar, uint32_t& phase) {
+  const bool ok = mbar_wait(bar, phase);
+  if (__syncthreads_or(!ok)) {
+    if (threadIdx.x == 0) {
+      atomicAdd(&g_tc_wait_timeouts, 1);
+      mbar_wait(bar, phase);
+    }
+    __syncthreads();
+    return false;
+  }
+  phase ^= 1;
+  return true;
+}
+
+// Thread 0: the TMA loads of the index tiles of the chunk starting at CSR
+// position c1 (a multiple of 128, so 512-byte aligned) into nrow / ncol.
+template <class Args>
+__device__ __forceinline__ void issue_idx(const Args& a, int64_t c1, int* nrow, int* ncol, uint64_t* ibar) {
+  fence_proxy_async();   // this chunk's generic reads of nrow / ncol precede the async writes
+  mbar_expect_tx_bytes(ibar, 2 * kM * 4);
+  tma_load_1d(nrow, &a.tm_row, (int)c1, ibar);
+  tma_load_1d(ncol, &a.tm_col, (int)c1, ibar);
+}
+
 // Operand writes (generic proxy) and TMEM reads done -> tensor core may go.
 __device__ __forceinline__ void handoff_to_mma() {
   fence_proxy_async();
@@ -281,12 +308,12 @@ struct FwdLayout {
   static constexpr size_t OPEN = XLI + kM * 16;        // float[H + 4]
   static constexpr size_t MISC = OPEN + (H + 4) * 4;   // ints: nseg, open_row, prev_row, warp counts[4]
   static constexpr size_t BAR = MISC + 64;
-  static constexpr size_t END = BAR + 16;
+  static constexpr size_t END = BAR + 32;   // MMA barrier, TMEM base, index-tile barrier
   static constexpr size_t BYTES = END + 1024;
 };
 
 template <int H>
-__global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
+__global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_constant__ EdgeFwdArgs a) {
   using C = TC<H>;
   using L = FwdLayout<H>;
   extern __shared__ __align__(1024) char smem_raw[];
@@ -320,12 +347,16 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
   int* misc = reinterpret_cast<int*>(sm + L::MISC);   // [0] nseg [1] open_row [2] prev_row [4..7] warp counts
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
+  uint64_t* ibar = reinterpret_cast<uint64_t*>(sm + L::BAR + 16);
+  uint32_t iphase = 0;
+  bool idx_pending = false;   // an index-tile copy issued and not yet waited for
 
   const Geo g;
   constexpr uint32_t NCOL = 2 * H;   // D0 | DAGG
   if (g.warp == 0) tmem_alloc(tmem_base_s, NCOL);
   if (g.tid == 0) {
     mbar_init(bar, 1);
+    mbar_init(ibar, 1);
     fence_mbar_init();
   }
   load_weight_tile<H>(W2t, a.W2_src, W2lo);
@@ -467,15 +498,21 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
       for (int kk = 0; kk < H / 16; ++kk)
         mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2lo, H, kk), C::IDESC_FWD, 1u);
       mma_commit(bar);
+      if (a.use_tma && n_next > 0) issue_idx(a, c1, nrow, ncol, ibar);
     }
-    if (prefetcher) {
+    if (a.use_tma && n_next > 0) idx_pending = true;
+    if (prefetcher && !a.use_tma) {
       cp_async4(&nrow[g.e], a.row_idx + c1 + g.e);
       cp_async4(&ncol[g.e], a.col_idx + c1 + g.e);
       cp_async_commit_group();
     }
     if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
+    if (idx_pending) {
+      idx_pending = false;
+      if (!(ok = wait_idx(ibar, iphase))) break;
+    }
     if (prefetcher) {
-      cp_async_wait_all_groups();
+      if (!a.use_tma) cp_async_wait_all_groups();
       cp_async16_ca(&nxi[g.e], a.xp + nrow[g.e]);
       cp_async16_ca(&nxj[g.e], a.xp + ncol[g.e]);
       cp_async_commit_group();
@@ -578,6 +615,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(EdgeFwdArgs a) {
     pref = n_next > 0;
   }
   cp_async_wait_all_groups();   // nothing in flight when the CTA leaves (also after a timeout)
+  if (idx_pending && g.tid == 0) mbar_wait(ibar, iphase);   // an index-tile copy issued before a give-up
   // ---- end of the CTA range: open row -> carry slot, trailing empty rows
   if (ok) {
     const int open_row = misc[1];
@@ -627,12 +665,12 @@ struct BwdLayout {
   static constexpr size_t NXJ = NXI + kM * 16;                        // float4[128]
   static constexpr size_t NGX = NXJ + kM * 16;                        // float4[128] (xyz)
   static constexpr size_t BAR = NGX + kM * 16;
-  static constexpr size_t END = BAR + 16;
+  static constexpr size_t END = BAR + 32;   // MMA barrier, TMEM base, index-tile barrier
   static constexpr size_t BYTES = END + 1024;
 };
 
 template <int H>
-__global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
+__global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(const __grid_constant__ EdgeBwdArgs a) {
   using C = TC<H>;
   using L = BwdLayout<H>;
   extern __shared__ __align__(1024) char smem_raw[];
@@ -662,12 +700,16 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
   float4* stage = reinterpret_cast<float4*>(Mt);   // fp32 row staging over the M | G tiles (64 KB)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
+  uint64_t* ibar = reinterpret_cast<uint64_t*>(sm + L::BAR + 16);
+  uint32_t iphase = 0;
+  bool idx_pending = false;   // an index-tile copy issued and not yet waited for
 
   const Geo g;
   constexpr uint32_t NCOL = 4 * H;   // D0 | fp16 pairs of silu'(a1), silu'(a2) | dWc1 | dW2
   if (g.warp == 0) tmem_alloc(tmem_base_s, NCOL);
   if (g.tid == 0) {
     mbar_init(bar, 1);
+    mbar_init(ibar, 1);
     fence_mbar_init();
   }
   load_weight_tile<H>(W2t, a.W2_src, W2lo);
@@ -763,15 +805,21 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
       for (int kk = 0; kk < H / 16; ++kk)
         mma_bf16(tD0, desc_k(Ut, kM, kk), desc_k(W2lo, H, kk), C::IDESC_FWD, 1u);
       mma_commit(bar);
+      if (a.use_tma && n_next > 0) issue_idx(a, c1, nrow, ncol, ibar);
     }
-    if (prefetcher) {
+    if (a.use_tma && n_next > 0) idx_pending = true;
+    if (prefetcher && !a.use_tma) {
       cp_async4(&nrow[g.e], a.row_idx + c1 + g.e);
       cp_async4(&ncol[g.e], a.col_idx + c1 + g.e);
       cp_async_commit_group();
     }
     if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
+    if (idx_pending) {
+      idx_pending = false;
+      if (!(ok = wait_idx(ibar, iphase))) break;
+    }
     if (prefetcher) {
-      cp_async_wait_all_groups();
+      if (!a.use_tma) cp_async_wait_all_groups();
       const int i = nrow[g.e], j = ncol[g.e];
       cp_async16_ca(&nxi[g.e], a.xp + i);
       cp_async16_ca(&nxj[g.e], a.xp + j);
@@ -945,6 +993,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(EdgeBwdArgs a) {
     pref = n_next > 0;
   }
   cp_async_wait_all_groups();   // nothing in flight when the CTA leaves (also after a timeout)
+  if (idx_pending && g.tid == 0) mbar_wait(ibar, iphase);   // an index-tile copy issued before a give-up
 
   // ---- per-CTA partials: dWc1, dW2 rows from TMEM; column sums over the row quarters
   const int PF = (int)edge_part_floats(H, 0);
@@ -1091,6 +1140,7 @@ template <int H>
 int launch_fwd_tc(const EdgeFwdArgs& a_in, int G, cudaStream_t s) {
   EdgeFwdArgs a = a_in;
   a.wait_polls = debug_wait_polls();
+  a.use_tma = tensor_map_i32_1d(&a.tm_row, a.row_idx, a.E, kM) && tensor_map_i32_1d(&a.tm_col, a.col_idx, a.E, kM);
   constexpr size_t bytes = FwdLayout<H>::BYTES;
   static uint64_t attr_set = 0;
   const uint64_t bit = device_bit();
@@ -1111,6 +1161,7 @@ template <int H>
 int launch_bwd_tc(const EdgeBwdArgs& a_in, int G, cudaStream_t s) {
   EdgeBwdArgs a = a_in;
   a.wait_polls = debug_wait_polls();
+  a.use_tma = tensor_map_i32_1d(&a.tm_row, a.row_idx, a.E, kM) && tensor_map_i32_1d(&a.tm_col, a.col_idx, a.E, kM);
   constexpr size_t bytes = BwdLayout<H>::BYTES;
   static uint64_t attr_set = 0;
   const uint64_t bit = device_bit();

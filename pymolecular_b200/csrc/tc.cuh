@@ -108,6 +108,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// ---- TMA (tensor-map bulk copies; no cluster multicast anywhere) -------------
+// The mbarrier expects `bytes` more bytes in its current phase.
+__device__ __forceinline__ void mbar_expect_tx_bytes(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// Box `x .. x + box - 1` of a 1-D tensor map (global -> shared), its bytes
+// counted on `bar`.  Elements past the tensor's end arrive as zeros.  The
+// coordinate x times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* tmap, int x, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.1d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2}], [%3];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ---- cp.async (4- and 16-byte, per-thread groups) ---------------------------
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");

@@ -106,23 +106,6 @@ __device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase, int pol
   return true;
 }
 
-// CTA-uniform bounded wait for the next chunk's index tiles (TMA); on
-// timeout the event is counted and thread 0 waits once more (built-in limit)
-// so that no copy is still landing when the CTA leaves.
-__device__ __forceinline__ bool wait_idx(uint64_t* bar, uint32_t& phase) {
-  const bool ok = mbar_wait(bar, phase);
-  if (__syncthreads_or(!ok)) {
-    if (threadIdx.x == 0) {
-      atomicAdd(&g_tc_wait_timeouts, 1);
-      mbar_wait(bar, phase);
-    }
-    __syncthreads();
-    return false;
-  }
-  phase ^= 1;
-  return true;
-}
-
 // Thread 0: the TMA loads of the index tiles of the chunk starting at CSR
 // position c1 (a multiple of 128, so 512-byte aligned) into nrow / ncol.
 template <class Args>
@@ -348,8 +331,10 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
   uint64_t* ibar = reinterpret_cast<uint64_t*>(sm + L::BAR + 16);
-  uint32_t iphase = 0;
+  int* idx_abort = reinterpret_cast<int*>(sm + L::BAR + 24);   // a prefetcher gave up on the index tiles
+  uint32_t iphase = 0, idx_last = 0;
   bool idx_pending = false;   // an index-tile copy issued and not yet waited for
+  bool idx_drain = false;     // ... or waited for without success (drain before leaving)
 
   const Geo g;
   constexpr uint32_t NCOL = 2 * H;   // D0 | DAGG
@@ -357,6 +342,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
   if (g.tid == 0) {
     mbar_init(bar, 1);
     mbar_init(ibar, 1);
+    *idx_abort = 0;
     fence_mbar_init();
   }
   load_weight_tile<H>(W2t, a.W2_src, W2lo);
@@ -507,11 +493,19 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
       cp_async_commit_group();
     }
     if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
+    // the prefetchers alone wait for the index tiles; one that gives up skips
+    // its loads and raises the flag the end-of-chunk barrier publishes
+    bool idx_ok = true;
     if (idx_pending) {
       idx_pending = false;
-      if (!(ok = wait_idx(ibar, iphase))) break;
+      idx_last = iphase;
+      iphase ^= 1;
+      if (prefetcher && !mbar_wait(ibar, idx_last)) {
+        idx_ok = false;
+        if (atomicExch(idx_abort, 1) == 0) atomicAdd(&g_tc_wait_timeouts, 1);
+      }
     }
-    if (prefetcher) {
+    if (prefetcher && idx_ok) {
       if (!a.use_tma) cp_async_wait_all_groups();
       cp_async16_ca(&nxi[g.e], a.xp + nrow[g.e]);
       cp_async16_ca(&nxj[g.e], a.xp + ncol[g.e]);
@@ -613,9 +607,17 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
     }
     __syncthreads();
     pref = n_next > 0;
+    if (*idx_abort) {   // read after the barrier: the same value in every thread
+      ok = false;
+      idx_drain = true;
+      break;
+    }
   }
   cp_async_wait_all_groups();   // nothing in flight when the CTA leaves (also after a timeout)
-  if (idx_pending && g.tid == 0) mbar_wait(ibar, iphase);   // an index-tile copy issued before a give-up
+  if (g.tid == 0) {   // no index-tile copy may still be landing when the CTA leaves
+    if (idx_pending) mbar_wait(ibar, iphase);
+    if (idx_drain) mbar_wait(ibar, idx_last);
+  }
   // ---- end of the CTA range: open row -> carry slot, trailing empty rows
   if (ok) {
     const int open_row = misc[1];
@@ -701,8 +703,10 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(const __grid_consta
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(sm + L::BAR + 8);
   uint64_t* ibar = reinterpret_cast<uint64_t*>(sm + L::BAR + 16);
-  uint32_t iphase = 0;
+  int* idx_abort = reinterpret_cast<int*>(sm + L::BAR + 24);   // a prefetcher gave up on the index tiles
+  uint32_t iphase = 0, idx_last = 0;
   bool idx_pending = false;   // an index-tile copy issued and not yet waited for
+  bool idx_drain = false;     // ... or waited for without success (drain before leaving)
 
   const Geo g;
   constexpr uint32_t NCOL = 4 * H;   // D0 | fp16 pairs of silu'(a1), silu'(a2) | dWc1 | dW2
@@ -710,6 +714,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(const __grid_consta
   if (g.tid == 0) {
     mbar_init(bar, 1);
     mbar_init(ibar, 1);
+    *idx_abort = 0;
     fence_mbar_init();
   }
   load_weight_tile<H>(W2t, a.W2_src, W2lo);
@@ -814,11 +819,19 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(const __grid_consta
       cp_async_commit_group();
     }
     if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
+    // the prefetchers alone wait for the index tiles; one that gives up skips
+    // its loads and raises the flag the end-of-chunk barrier publishes
+    bool idx_ok = true;
     if (idx_pending) {
       idx_pending = false;
-      if (!(ok = wait_idx(ibar, iphase))) break;
+      idx_last = iphase;
+      iphase ^= 1;
+      if (prefetcher && !mbar_wait(ibar, idx_last)) {
+        idx_ok = false;
+        if (atomicExch(idx_abort, 1) == 0) atomicAdd(&g_tc_wait_timeouts, 1);
+      }
     }
-    if (prefetcher) {
+    if (prefetcher && idx_ok) {
       if (!a.use_tma) cp_async_wait_all_groups();
       const int i = nrow[g.e], j = ncol[g.e];
       cp_async16_ca(&nxi[g.e], a.xp + i);
@@ -991,9 +1004,17 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(const __grid_consta
     if (prefetcher) cp_async_wait_all_groups();
     __syncthreads();
     pref = n_next > 0;
+    if (*idx_abort) {   // read after the barrier: the same value in every thread
+      ok = false;
+      idx_drain = true;
+      break;
+    }
   }
   cp_async_wait_all_groups();   // nothing in flight when the CTA leaves (also after a timeout)
-  if (idx_pending && g.tid == 0) mbar_wait(ibar, iphase);   // an index-tile copy issued before a give-up
+  if (g.tid == 0) {   // no index-tile copy may still be landing when the CTA leaves
+    if (idx_pending) mbar_wait(ibar, iphase);
+    if (idx_drain) mbar_wait(ibar, idx_last);
+  }
 
   // ---- per-CTA partials: dWc1, dW2 rows from TMEM; column sums over the row quarters
   const int PF = (int)edge_part_floats(H, 0);

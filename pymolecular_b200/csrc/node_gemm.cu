@@ -265,20 +265,33 @@ __global__ void __launch_bounds__(256) wgrad_small_partial_kernel(int64_t R, int
 #pragma unroll
     for (int q = 0; q < kNarrow; ++q) acc[t][q] = 0.f;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per, r1 = min(R, r0 + rows_per);
-  for (int64_t r = r0 + warp; r < r1; r += 8) {
-    float wv[kWideSlots], nv[kNarrow];
+  // rows r and r + 8 of the warp per iteration: both rows' loads in flight
+  // before the first product (the products are added in row order, as one
+  // row per iteration would add them)
+  for (int64_t r = r0 + warp; r < r1; r += 16) {
+    float wv[2][kWideSlots], nv[2][kNarrow];
 #pragma unroll
-    for (int t = 0; t < kWideSlots; ++t) {
-      const int w = lane + 32 * t;
-      wv[t] = (w < wide) ? (lanes_n ? ext_at(X, N, r, w) : G.at(r, w)) : 0.f;
-    }
+    for (int u = 0; u < 2; ++u) {
+      const int64_t ru = r + 8 * u;
+      const bool live = ru < r1;
 #pragma unroll
-    for (int q = 0; q < kNarrow; ++q) nv[q] = (q < narrow) ? (lanes_n ? G.at(r, q) : ext_at(X, N, r, q)) : 0.f;
-#pragma unroll
-    for (int t = 0; t < kWideSlots; ++t)
+      for (int t = 0; t < kWideSlots; ++t) {
+        const int w = lane + 32 * t;
+        wv[u][t] = (live && w < wide) ? (lanes_n ? ext_at(X, N, ru, w) : G.at(ru, w)) : 0.f;
+      }
 #pragma unroll
       for (int q = 0; q < kNarrow; ++q)
-        acc[t][q] = lanes_n ? fmaf(nv[q], wv[t], acc[t][q]) : fmaf(wv[t], nv[q], acc[t][q]);
+        nv[u][q] = (live && q < narrow) ? (lanes_n ? G.at(ru, q) : ext_at(X, N, ru, q)) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (r + 8 * u >= r1) break;
+#pragma unroll
+      for (int t = 0; t < kWideSlots; ++t)
+#pragma unroll
+        for (int q = 0; q < kNarrow; ++q)
+          acc[t][q] = lanes_n ? fmaf(nv[u][q], wv[u][t], acc[t][q]) : fmaf(wv[u][t], nv[u][q], acc[t][q]);
+    }
   }
 #pragma unroll
   for (int t = 0; t < kWideSlots; ++t) {

@@ -281,11 +281,16 @@ class _HaloExchange(torch.autograd.Function):
     owners' rows, summed in increasing source-rank order."""
 
     @staticmethod
-    def forward(ctx, h_own, plan: HaloPlan, group):
+    def forward(ctx, h_own, plan: HaloPlan, group, wire_dtype=None):
         ctx.plan, ctx.group = plan, group
         send = [h_own[idx] if idx.device == h_own.device else h_own[idx.to(h_own.device)]
                 for idx in plan.send_idx]
-        recv = _all_to_all_rows(send, plan.recv_counts, h_own, group)
+        like = h_own
+        if wire_dtype is not None and wire_dtype != h_own.dtype:
+            # rows cross the wire rounded to wire_dtype (bf16 halves the bytes of h)
+            send = [t.to(wire_dtype) for t in send]
+            like = h_own[:0].to(wire_dtype)
+        recv = _all_to_all_rows(send, plan.recv_counts, like, group).to(h_own.dtype)
         return torch.cat([h_own, recv], dim=0)
 
     @staticmethod
@@ -307,7 +312,7 @@ class _HaloExchange(torch.autograd.Function):
             if n:
                 g_own.index_add_(0, plan.send_idx[p].to(g.device, non_blocking=True), back[off:off + n])
             off += n
-        return g_own, None, None
+        return g_own, None, None, None
 
 
 def _all_to_all_rows(send: List[torch.Tensor], recv_counts: List[int], like: torch.Tensor, group):
@@ -323,11 +328,13 @@ def _all_to_all_rows(send: List[torch.Tensor], recv_counts: List[int], like: tor
     return out
 
 
-def halo_exchange(h_own: torch.Tensor, plan: HaloPlan, group=None) -> torch.Tensor:
-    """Autograd-aware halo fetch: returns (n_own + n_halo, F) rows."""
+def halo_exchange(h_own: torch.Tensor, plan: HaloPlan, group=None, wire_dtype=None) -> torch.Tensor:
+    """Autograd-aware halo fetch: returns (n_own + n_halo, F) rows.  With
+    `wire_dtype` (e.g. torch.bfloat16) the halo rows are sent in that type and
+    arrive rounded to it; their gradients return in the rows' own type."""
     if plan.world == 1:
         return h_own
-    return _HaloExchange.apply(h_own, plan, group)
+    return _HaloExchange.apply(h_own, plan, group, wire_dtype)
 
 
 __all__ = ["partition_graphs", "layer_buckets", "GradAllReduce", "node_ranges", "HaloPlan", "build_halo_plan",
@@ -341,13 +348,16 @@ def partitioned_forward(model, h_own: torch.Tensor, x_own: torch.Tensor, csr_loc
     embedding_in on the owned rows; before every layer the halo rows of h
     and x are fetched; each layer runs on the local graph (owned rows plus
     halo rows, edges into owned rows only) and keeps its owned rows;
-    embedding_out on the owned rows.  Returns (h_out_own, x_out_own)."""
+    embedding_out on the owned rows.  In bf16-GEMM mode the halo rows of h
+    travel as bf16 (the coordinates and all gradients stay fp32).  Returns
+    (h_out_own, x_out_own)."""
     from .egnn import linear
     n_own = plan.n_own
     h = linear(h_own, model.embedding_in)
     x = x_own
+    wire = torch.bfloat16 if getattr(model, "precision", "fp32") == "bf16" else None
     for i in range(model.n_layers):
-        h_loc = halo_exchange(h, plan, group)
+        h_loc = halo_exchange(h, plan, group, wire_dtype=wire)
         x_loc = halo_exchange(x, plan, group)
         h_loc, x_loc, _ = model._modules["gcl_%d" % i](h_loc, csr_local, x_loc)
         h, x = h_loc[:n_own], x_loc[:n_own]

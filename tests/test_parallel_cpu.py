@@ -277,3 +277,25 @@ def test_missing_rank_surfaces_as_an_error(mode):
     name, elapsed = survivor[0]
     assert name != "no error", got
     assert elapsed < 60, got
+
+
+def _wire_worker(rank, world):
+    """Halo rows sent as bf16 arrive as the owners' rows rounded to bf16, and
+    their gradients return to the owners in fp32."""
+    row, col, x, h, _, _ = _graph(3)
+    n = x.shape[0]
+    plan = P.build_halo_plan(row, col, n, rank, world)
+    lo, hi = plan.own_lo, plan.own_hi
+    hf = h.float()
+    h_own = hf[lo:hi].clone().requires_grad_(True)
+    got = P.halo_exchange(h_own, plan, wire_dtype=torch.bfloat16)
+    assert got.dtype == torch.float32
+    assert torch.equal(got[:plan.n_own], hf[lo:hi])
+    assert torch.equal(got[plan.n_own:], hf[plan.halo].bfloat16().float())
+    w = torch.arange(got.numel(), dtype=torch.float32).reshape(got.shape)
+    (got * w).sum().backward()
+    assert h_own.grad.dtype == torch.float32 and torch.isfinite(h_own.grad).all()
+
+
+def test_halo_rows_in_bf16_two_ranks():
+    _run(2, _wire_worker)

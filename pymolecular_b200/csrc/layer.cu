@@ -180,13 +180,6 @@ int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_
 int node_gemm(const GemmArgs& g, bool bf, cudaStream_t s) {
   return (bf && gemm_tc_ok(g)) ? gemm_tc(g, s) : gemm(g, s);
 }
-// The node MLP's two chained GEMMs: one launch on the tensor cores when the
-// shapes allow (H = 128), else two.
-int node_mlp(const GemmArgs& g1, const GemmArgs& g2, bool bf, cudaStream_t s) {
-  if (bf && mlp_tc_ok(g1, g2)) return mlp_tc(g1, g2, s);
-  EGNN_TRY(node_gemm(g1, bf, s));
-  return node_gemm(g2, bf, s);
-}
 int node_wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw, float* db, bool bf,
                float* part, cudaStream_t s) {
   return bf ? wgrad_tc(R, M, N, G, X, dW, lddw, db, part, s) : wgrad(R, M, N, G, X, dW, lddw, db, 0, part, s);
@@ -465,6 +458,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n1.bias = p->node_b1; n1.act = ACT_SILU;
   n1.pre = sv.n1pre; n1.ldp = H;
   n1.C = sv.n1; n1.ldc = H;
+  EGNN_TRY(node_gemm(n1, bf, s));
 
   GemmArgs n2;
   n2.M = N; n2.N = H; n2.K = H;
@@ -473,7 +467,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n2.bias = p->node_b2;
   if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = H; }
   n2.C = h_out; n2.ldc = H;
-  EGNN_TRY(node_mlp(n1, n2, bf, s));
+  EGNN_TRY(node_gemm(n2, bf, s));
   return EGNN_OK;
 }
 
@@ -524,6 +518,13 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gn.B = mat(p->node_w2, H); gn.b_t = 0;
     gn.act = ACT_DSILU; gn.aux = sv.n1pre; gn.ldaux = H;
     gn.C = w.g_n1pre; gn.ldc = H;
+    EGNN_TRY(node_gemm(gn, bf, s));
+  }
+  // dW_n1, db_n1 on the side stream once g_n1pre exists
+  EGNN_TRY(stream_fork(s, s2, side->ev[1]));
+  EGNN_TRY(node_wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
+                      gp->node_b1, bf, w.wpart_aux, s2));
+  {
     // [dL/dh (MLP path) + residual | dL/dagg] = g_n1pre Wn1, one N x 2H product
     GemmArgs gh;
     gh.M = N; gh.N = 2 * H; gh.K = H;
@@ -531,14 +532,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.B = mat(p->node_w1, 2 * H); gh.b_t = 0;
     if (residual) { gh.resid = gh_out; gh.ldr = H; gh.resid_cols = H; }
     gh.C = w.ghg; gh.ldc = 2 * H;
-    const bool fused = bf && mlp_tc_ok(gn, gh);
-    if (fused) EGNN_TRY(mlp_tc(gn, gh, s));
-    else EGNN_TRY(node_gemm(gn, bf, s));
-    // dW_n1, db_n1 on the side stream once g_n1pre exists
-    EGNN_TRY(stream_fork(s, s2, side->ev[1]));
-    EGNN_TRY(node_wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
-                        gp->node_b1, bf, w.wpart_aux, s2));
-    if (!fused) EGNN_TRY(node_gemm(gh, bf, s));
+    EGNN_TRY(node_gemm(gh, bf, s));
   }
 
   // ---- edge backward: dst pass, fix-up, partial reduction, src pass

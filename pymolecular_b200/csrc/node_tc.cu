@@ -166,110 +166,6 @@ __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t ph) {
   return !__syncthreads_or(!ok);
 }
 
-// Epilogue, part 1: warp w moves TMEM lanes 32 (w % 4) .. (rows), column
-// quarter w / 4 of a BNT-column accumulator at `tmem`, into the fp32 staging
-// tile [128][BNT + 4] (zeros when the accumulator was never written).
-template <int BNT>
-__device__ __forceinline__ void tmem_to_stage(uint32_t tmem, float* ostage, bool zero) {
-  constexpr int NCW = BNT / 4;       // 64, 32 or 16 columns per warp
-  constexpr int LDO = BNT + 4;       // staging row stride: 65, 33 or 17 16-byte words (odd)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = warp & 3, h = warp >> 2;
-#pragma unroll 1
-  for (int part = 0; part < (NCW > 32 ? NCW / 32 : 1); ++part) {
-    constexpr int W = NCW > 32 ? 32 : NCW;
-    float v[W];
-    if constexpr (W == 32) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + h * NCW + part * 32, v);
-    else tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
-    if (zero) {
-#pragma unroll
-      for (int t = 0; t < W; ++t) v[t] = 0.f;
-    }
-    float* dst = ostage + (q * 32 + lane) * LDO + h * NCW + part * 32;
-#pragma unroll
-    for (int t = 0; t < W; t += 4) *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
-  }
-}
-
-// Epilogue, part 2: whole rows out of the staging tile.  Thread -> (row,
-// 4-column word), consecutive threads on consecutive words of a row, so
-// every global access of a warp is one contiguous run; UR rows per thread
-// have their operand loads in flight together.  With `keep`, the final
-// values also go back into the staging tile (vector path only).
-template <int BNT>
-__device__ __forceinline__ void rows_out(const GemmArgs& a, float* ostage, int64_t m0, int64_t n0, int64_t z,
-                                         float* keep) {
-  constexpr int LDO = BNT + 4;
-  constexpr int G4 = BNT / 4, RPP = NTH / G4, UR = 4;
-  const int tid = threadIdx.x;
-  const int cw = tid % G4, rr = tid / G4;
-  const int64_t n = n0 + 4 * cw;
-  const bool nin = n < a.N, nvec = a.vec && n + 3 < a.N;
-  float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (a.ksplit <= 1 && a.bias && nvec) bb = *reinterpret_cast<const float4*>(a.bias + n);
-#pragma unroll 1
-  for (int rb = 0; rb < BMT; rb += RPP * UR) {
-    float4 acc[UR], aux[UR], rs[UR];
-    int64_t mr[UR];
-#pragma unroll
-    for (int u = 0; u < UR; ++u) {
-      const int row = rb + u * RPP + rr;
-      mr[u] = m0 + row;
-      acc[u] = *reinterpret_cast<const float4*>(ostage + row * LDO + 4 * cw);
-      const bool live = nvec && mr[u] < a.M && a.ksplit <= 1;
-      if (live && a.act == ACT_DSILU) aux[u] = *reinterpret_cast<const float4*>(a.aux + mr[u] * a.ldaux + n);
-      if (live && a.resid && n < a.resid_cols) rs[u] = *reinterpret_cast<const float4*>(a.resid + mr[u] * a.ldr + n);
-    }
-#pragma unroll
-    for (int u = 0; u < UR; ++u) {
-      const int64_t m = mr[u];
-      if (m >= a.M || !nin) continue;
-      if (a.ksplit > 1) {   // raw split-K slice (N % 4 == 0 on this path)
-        *reinterpret_cast<float4*>(a.part + z * a.M * a.N + m * a.N + n) = acc[u];
-        continue;
-      }
-      if (nvec) {
-        float y[4] = {acc[u].x + bb.x, acc[u].y + bb.y, acc[u].z + bb.z, acc[u].w + bb.w};
-        if (a.pre) *reinterpret_cast<float4*>(a.pre + m * a.ldp + n) = make_float4(y[0], y[1], y[2], y[3]);
-        if (a.act == ACT_SILU) {
-#pragma unroll
-          for (int t = 0; t < 4; ++t) y[t] = silu_fast(y[t]);
-        } else if (a.act == ACT_DSILU) {
-          const float zz[4] = {aux[u].x, aux[u].y, aux[u].z, aux[u].w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            float yy, d;
-            silu_grad_fast(zz[t], yy, d);
-            y[t] *= d;
-          }
-        }
-        if (a.resid && n < a.resid_cols) { y[0] += rs[u].x; y[1] += rs[u].y; y[2] += rs[u].z; y[3] += rs[u].w; }
-        *reinterpret_cast<float4*>(a.C + m * a.ldc + n) = make_float4(y[0], y[1], y[2], y[3]);
-        if (keep) *reinterpret_cast<float4*>(keep + (m - m0) * LDO + 4 * cw) = make_float4(y[0], y[1], y[2], y[3]);
-      } else {
-        const float yv[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int64_t nn = n + t;
-          if (nn >= a.N) continue;
-          float y = yv[t];
-          if (a.bias) y += a.bias[nn];
-          if (a.pre) a.pre[m * a.ldp + nn] = y;
-          if (a.act == ACT_SILU) {
-            y = silu_fast(y);
-          } else if (a.act == ACT_DSILU) {
-            float yy, d;
-            silu_grad_fast(a.aux[m * a.ldaux + nn], yy, d);
-            y *= d;
-          }
-          if (a.resid && nn < a.resid_cols) y += a.resid[m * a.ldr + nn];
-          a.C[m * a.ldc + nn] = y;
-        }
-      }
-    }
-  }
-}
-
 template <int A_T, int B_T, int BNT>
 __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
   pdl_enter();
@@ -391,218 +287,103 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
     }
   }
 
-  // ---- epilogue: TMEM -> fp32 staging tile -> whole rows out
-  // the staging tile (128 x (BNT + 4) floats) lies over the idle raw ring, or
-  // for 256-column tiles over the operand tiles and the raw ring together
+  // ---- epilogue.  1: warp w moves TMEM lanes 32 (w % 4) .. (rows), column
+  // quarter w / 4, into an fp32 staging tile over the (idle) raw ring.
+  constexpr int NCW = BNT / 4;       // 64, 32 or 16 columns per warp
+  constexpr int LDO = BNT + 4;       // staging row stride: 65, 33 or 17 16-byte words (odd)
+  // the staging tile (128 x LDO floats) lies over the idle raw ring, or for
+  // 256-column tiles over the operand tiles and the raw ring together
   float* ostage = reinterpret_cast<float*>(sm + (BNT == 256 ? 0 : S::OFF_RAW));
-  static_assert((BNT == 256 ? 0 : S::OFF_RAW) + BMT * (BNT + 4) * 4 <= S::OFF_BAR, "staging fits");
-  tmem_to_stage<BNT>(tmem, ostage, nkc == 0);
+  static_assert((BNT == 256 ? 0 : S::OFF_RAW) + BMT * LDO * 4 <= S::OFF_BAR, "staging fits");
+  {
+    const int q = warp & 3, h = warp >> 2;
+#pragma unroll 1
+    for (int part = 0; part < (NCW > 32 ? NCW / 32 : 1); ++part) {
+      constexpr int W = NCW > 32 ? 32 : NCW;
+      float v[W];
+      if constexpr (W == 32) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + h * NCW + part * 32, v);
+      else tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + h * NCW, v);
+      if (nkc == 0) {   // empty K slice of a split: the accumulator was never written
+#pragma unroll
+        for (int t = 0; t < W; ++t) v[t] = 0.f;
+      }
+      float* dst = ostage + (q * 32 + lane) * LDO + h * NCW + part * 32;
+#pragma unroll
+      for (int t = 0; t < W; t += 4) *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+    }
+  }
   fence_before_sync();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, BNT);
-  rows_out<BNT>(a, ostage, m0, n0, (int64_t)blockIdx.z, nullptr);
-}
-
-// ---- node MLP: two chained GEMMs per 128-row tile --------------------------------
-// C2 = epi2(T B2),  T = epi1(A B1)  (T: 128 columns; B2: 128 x N2, N2 = 128 or 256):
-// the forward's [h, agg] -> n1 -> h' and the backward's dL/dh' -> g_n1pre ->
-// [dL/dh | dL/dagg].  GEMM 1 runs as gemm_tc_kernel<0, 0, 128>; its epilogue
-// writes T (and the pre-activation) to global memory for the weight
-// gradients and also leaves T in the staging tile, which is split into the
-// bf16 hi / lo A tiles of GEMM 2 in place of the operand tiles; GEMM 2
-// streams B2 in 64-row chunks.  One launch and one pass over T instead of two.
-//   shared memory: [0, 64K) GEMM-1 tiles, then T's split A tiles (two 64-column
-//   chunks, hi | lo); [64K, 192K) GEMM-1 raw ring, then T's staging, then B2's
-//   split tiles and raw chunks; GEMM 2's staging over [0, 133K) at the end.
-//   TMEM: GEMM 1 in columns 0..127, GEMM 2 in 128 .. 128 + N2.
-struct MlpArgs {
-  GemmArgs g1, g2;
-};
-
-template <int N2>
-__global__ void __launch_bounds__(NTH, 1) mlp_tc_kernel(MlpArgs args) {
-  pdl_enter();
-  using S = TcShape<128>;
-  const GemmArgs& a = args.g1;
-  const GemmArgs& b = args.g2;
-  constexpr int T_B2 = BKT * N2 * 2, RAW_B2 = BKT * N2 * 4, NRAW2 = N2 == 256 ? 1 : 2;
-  constexpr int OFF_B2 = 64 * 1024, OFF_B2RAW = OFF_B2 + 2 * T_B2;
-  static_assert(OFF_B2RAW + NRAW2 * RAW_B2 <= S::OFF_BAR, "GEMM-2 operands fit");
-  static_assert(64 * 1024 + BMT * 132 * 4 <= S::OFF_BAR && BMT * (N2 + 4) * 4 <= S::OFF_BAR, "staging fits");
-  extern __shared__ __align__(1024) char tsm_raw[];
-  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
-  char* a_hi = sm;
-  char* a_lo = sm + S::T_A;
-  char* b_hi = sm + 2 * S::T_A;
-  char* b_lo = sm + 2 * S::T_A + S::T_B;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + S::OFF_BAR);
-  uint32_t* tmem_s = reinterpret_cast<uint32_t*>(sm + S::OFF_BAR + 16);
-  constexpr uint32_t IDESC1 = make_idesc_bf16(BMT, 128, 0, 1);
-  constexpr uint32_t IDESC2 = make_idesc_bf16(BMT, N2, 0, 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t m0 = (int64_t)blockIdx.x * BMT;
-  const int nkc = (int)((a.K + BKT - 1) / BKT);
-  auto raw_a = [&](int kc) { return reinterpret_cast<float*>(sm + S::OFF_RAW + (kc % S::NRAW) * S::RAW_STAGE); };
-  auto raw_b = [&](int kc) { return raw_a(kc) + S::RAW_A / 4; };
-  const RawCopier<BMT, true> cpa(a.A, m0, a.M);
-  const RawCopier<128, false> cpb(a.B, 0, a.N);
-  auto issue = [&](int kc) {
-    if (kc < nkc) {
-      const int64_t k0 = (int64_t)kc * BKT;
-      cpa.copy(raw_a(kc), a.A, k0, a.K);
-      cpb.copy(raw_b(kc), a.B, k0, a.K);
-    }
-    cp_async_commit();
-  };
-#pragma unroll
-  for (int p = 0; p < S::NRAW - 1; ++p) issue(p);
-  if (warp == 0) tmem_alloc(tmem_s, 512);
-  if (tid == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-  }
-  fence_before_sync();
-  __syncthreads();
-  fence_after_sync();
-  const uint32_t tmem = *tmem_s;
-
-  uint32_t ph = 0;
-  bool pending = false, ok = true;
-  // ---- GEMM 1
+  // 2: whole rows out.  Thread -> (row, 4-column word), consecutive threads on
+  // consecutive words of a row, so every global access of a warp is one
+  // contiguous run; UR rows per thread have their operand loads in flight together.
+  constexpr int G4 = BNT / 4, RPP = NTH / G4, UR = 4;
+  const int cw = tid % G4, rr = tid / G4;
+  const int64_t n = n0 + 4 * cw;
+  const bool nin = n < a.N, nvec = a.vec && n + 3 < a.N;
+  float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (a.ksplit <= 1 && a.bias && nvec) bb = *reinterpret_cast<const float4*>(a.bias + n);
 #pragma unroll 1
-  for (int kc = 0; kc < nkc; ++kc) {
-    issue(kc + S::NRAW - 1);
-    cp_async_wait<S::NRAW - 1>();
-    if (pending) {
-      if (!(ok = wait_all(bar, ph))) break;
-      ph ^= 1u;
-      pending = false;
-      fence_after_sync();
-    } else {
-      __syncthreads();
+  for (int rb = 0; rb < BMT; rb += RPP * UR) {
+    float4 acc[UR], aux[UR], rs[UR];
+    int64_t mr[UR];
+#pragma unroll
+    for (int u = 0; u < UR; ++u) {
+      const int row = rb + u * RPP + rr;
+      mr[u] = m0 + row;
+      acc[u] = *reinterpret_cast<const float4*>(ostage + row * LDO + 4 * cw);
+      const bool live = nvec && mr[u] < a.M && a.ksplit <= 1;
+      if (live && a.act == ACT_DSILU) aux[u] = *reinterpret_cast<const float4*>(a.aux + mr[u] * a.ldaux + n);
+      if (live && a.resid && n < a.resid_cols) rs[u] = *reinterpret_cast<const float4*>(a.resid + mr[u] * a.ldr + n);
     }
-    split_raw<BMT, true>(raw_a(kc), a_hi, a_lo, nullptr);
-    split_raw<128, false>(raw_b(kc), b_hi, b_lo, nullptr);
-    fence_proxy_async();
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    if (tid == 0) {
 #pragma unroll
-      for (int kk = 0; kk < BKT / 16; ++kk) {
-        mma_bf16(tmem, tdesc(a_hi, true, kk), tdesc(b_hi, false, kk), IDESC1, (kc > 0 || kk > 0) ? 1u : 0u);
-        mma_bf16(tmem, tdesc(a_hi, true, kk), tdesc(b_lo, false, kk), IDESC1, 1u);
-        mma_bf16(tmem, tdesc(a_lo, true, kk), tdesc(b_hi, false, kk), IDESC1, 1u);
+    for (int u = 0; u < UR; ++u) {
+      const int64_t m = mr[u];
+      if (m >= a.M || !nin) continue;
+      if (a.ksplit > 1) {   // raw split-K slice (N % 4 == 0 on this path)
+        *reinterpret_cast<float4*>(a.part + (int64_t)blockIdx.z * a.M * a.N + m * a.N + n) = acc[u];
+        continue;
       }
-      mma_commit(bar);
-    }
-    pending = true;
-  }
-  cp_async_wait<0>();
-  if (ok && pending) {
-    ok = wait_all(bar, ph);
-    if (ok) { ph ^= 1u; pending = false; }
-  }
-  if (ok) {
-    fence_after_sync();
-    // ---- epilogue 1: T to global memory, and kept in the staging tile
-    float* st1 = reinterpret_cast<float*>(sm + 64 * 1024);
-    tmem_to_stage<128>(tmem, st1, nkc == 0);
-    fence_before_sync();
-    __syncthreads();
-    rows_out<128>(a, st1, m0, 0, 0, st1);
-    __syncthreads();
-    // T -> bf16 hi / lo K-major A tiles of GEMM 2 (two 64-column chunks)
+      if (nvec) {
+        float y[4] = {acc[u].x + bb.x, acc[u].y + bb.y, acc[u].z + bb.z, acc[u].w + bb.w};
+        if (a.pre) *reinterpret_cast<float4*>(a.pre + m * a.ldp + n) = make_float4(y[0], y[1], y[2], y[3]);
+        if (a.act == ACT_SILU) {
 #pragma unroll
-    for (int q = 0; q < BMT * 128 / 8 / NTH; ++q) {
-      const int idx = tid + NTH * q, r = idx >> 4, c8 = (idx & 15) * 8;
-      const float4 x0 = *reinterpret_cast<const float4*>(st1 + r * 132 + c8);
-      const float4 x1 = *reinterpret_cast<const float4*>(st1 + r * 132 + c8 + 4);
-      const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      uint32_t hw[4], lw[4];
+          for (int t = 0; t < 4; ++t) y[t] = silu_fast(y[t]);
+        } else if (a.act == ACT_DSILU) {
+          const float z[4] = {aux[u].x, aux[u].y, aux[u].z, aux[u].w};
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const __nv_bfloat162 hp = __floats2bfloat162_rn(x[2 * t], x[2 * t + 1]);
-        const float2 hf = __bfloat1622float2(hp);
-        const __nv_bfloat162 lp = __floats2bfloat162_rn(x[2 * t] - hf.x, x[2 * t + 1] - hf.y);
-        hw[t] = *reinterpret_cast<const uint32_t*>(&hp);
-        lw[t] = *reinterpret_cast<const uint32_t*>(&lp);
-      }
-      char* chunk = sm + (c8 >> 6) * 2 * S::T_A;
-      const uint32_t off = sw128_offset(r, c8 & 63, BMT);
-      *reinterpret_cast<uint4*>(chunk + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(chunk + S::T_A + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    }
-    fence_proxy_async();
-    __syncthreads();
-
-    // ---- GEMM 2: A from the split T tiles, B2 streamed in 64-row chunks
-    char* b2_hi = sm + OFF_B2;
-    char* b2_lo = sm + OFF_B2 + T_B2;
-    auto raw_b2 = [&](int kc) { return reinterpret_cast<float*>(sm + OFF_B2RAW + (kc % NRAW2) * RAW_B2); };
-    const RawCopier<N2, false> cpb2(b.B, 0, b.N);
-    const int nkc2 = (int)((b.K + BKT - 1) / BKT);
-    auto issue2 = [&](int kc) {
-      if (kc < nkc2) cpb2.copy(raw_b2(kc), b.B, (int64_t)kc * BKT, b.K);
-      cp_async_commit();
-    };
-#pragma unroll
-    for (int p = 0; p < NRAW2 - 1; ++p) issue2(p);
-    const uint32_t tacc2 = tmem + 128;
-#pragma unroll 1
-    for (int kc = 0; kc < nkc2; ++kc) {
-      issue2(kc + NRAW2 - 1);
-      cp_async_wait<NRAW2 - 1>();
-      if (pending) {
-        if (!(ok = wait_all(bar, ph))) break;
-        ph ^= 1u;
-        pending = false;
-        fence_after_sync();
-      } else {
-        __syncthreads();
-      }
-      split_raw<N2, false>(raw_b2(kc), b2_hi, b2_lo, nullptr);
-      fence_proxy_async();
-      fence_before_sync();
-      __syncthreads();
-      fence_after_sync();
-      if (tid == 0) {
-        char* ah = sm + kc * 2 * S::T_A;
-        char* al = ah + S::T_A;
-#pragma unroll
-        for (int kk = 0; kk < BKT / 16; ++kk) {
-          mma_bf16(tacc2, tdesc(ah, true, kk), tdesc(b2_hi, false, kk), IDESC2, (kc > 0 || kk > 0) ? 1u : 0u);
-          mma_bf16(tacc2, tdesc(ah, true, kk), tdesc(b2_lo, false, kk), IDESC2, 1u);
-          mma_bf16(tacc2, tdesc(al, true, kk), tdesc(b2_hi, false, kk), IDESC2, 1u);
+          for (int t = 0; t < 4; ++t) {
+            float yy, d;
+            silu_grad_fast(z[t], yy, d);
+            y[t] *= d;
+          }
         }
-        mma_commit(bar);
+        if (a.resid && n < a.resid_cols) { y[0] += rs[u].x; y[1] += rs[u].y; y[2] += rs[u].z; y[3] += rs[u].w; }
+        *reinterpret_cast<float4*>(a.C + m * a.ldc + n) = make_float4(y[0], y[1], y[2], y[3]);
+      } else {
+        const float yv[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int64_t nn = n + t;
+          if (nn >= a.N) continue;
+          float y = yv[t];
+          if (a.bias) y += a.bias[nn];
+          if (a.pre) a.pre[m * a.ldp + nn] = y;
+          if (a.act == ACT_SILU) {
+            y = silu_fast(y);
+          } else if (a.act == ACT_DSILU) {
+            float yy, d;
+            silu_grad_fast(a.aux[m * a.ldaux + nn], yy, d);
+            y *= d;
+          }
+          if (a.resid && nn < a.resid_cols) y += a.resid[m * a.ldr + nn];
+          a.C[m * a.ldc + nn] = y;
+        }
       }
-      pending = true;
-    }
-    cp_async_wait<0>();
-    if (ok && pending) {
-      ok = wait_all(bar, ph);
-      if (ok) pending = false;
     }
   }
-  if (!ok) {
-    if (tid == 0) {
-      atomicAdd(&g_node_tc_timeouts, 1);
-      if (pending) mbar_wait(bar, ph);
-    }
-    fence_before_sync();
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 512);
-    return;
-  }
-  fence_after_sync();
-  // ---- epilogue 2
-  float* st2 = reinterpret_cast<float*>(sm);
-  tmem_to_stage<N2>(tmem + 128, st2, false);
-  fence_before_sync();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 512);
-  rows_out<N2>(b, st2, m0, 0, 0, nullptr);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -662,54 +443,15 @@ bool gemm_tc_ok(const GemmArgs& a) {
   return true;
 }
 
-namespace {
-// The epilogue may move four columns at a time.
-int vec_ok(const GemmArgs& a) {
-  return (a.N % 4 == 0 && a.ldc % 4 == 0 && aligned16(a.C) && (!a.bias || aligned16(a.bias)) &&
-          (!a.pre || (a.ldp % 4 == 0 && aligned16(a.pre))) &&
-          (a.act != ACT_DSILU || (a.ldaux % 4 == 0 && aligned16(a.aux))) &&
-          (!a.resid || (a.ldr % 4 == 0 && aligned16(a.resid) &&
-                        (a.resid_cols == INT64_MAX || a.resid_cols % 4 == 0)))) ? 1 : 0;
-}
-
-template <int N2>
-int launch_mlp(const MlpArgs& m, cudaStream_t s) {
-  static uint64_t attr_set = 0;
-  constexpr size_t bytes = TcShape<128>::SMEM_BYTES;
-  const uint64_t bit = device_bit();
-  if (!(attr_set & bit)) {
-    EGNN_CHECK_CUDA(cudaFuncSetAttribute(mlp_tc_kernel<N2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-    attr_set |= bit;
-  }
-  const dim3 grid((unsigned)((m.g1.M + BMT - 1) / BMT));
-  TimerScope ts("node_gemm", s);
-  EGNN_CHECK_CUDA(launch_pdl(mlp_tc_kernel<N2>, grid, dim3(NTH), bytes, s, m));
-  EGNN_CHECK_LAUNCH();
-  return EGNN_OK;
-}
-}  // namespace
-
-bool mlp_tc_ok(const GemmArgs& g1, const GemmArgs& g2) {
-  if (!gemm_tc_ok(g1) || !gemm_tc_ok(g2)) return false;
-  if (g1.a_t != 0 || g1.b_t != 0 || g2.a_t != 0 || g2.b_t != 0 || g1.ksplit > 1 || g2.ksplit > 1) return false;
-  if (g1.N != 128 || g2.K != 128 || g1.M != g2.M || (g2.N != 128 && g2.N != 256)) return false;
-  return vec_ok(g1) && vec_ok(g2);   // GEMM 2's operand is taken from the vector epilogue of GEMM 1
-}
-
-int mlp_tc(const GemmArgs& g1, const GemmArgs& g2, cudaStream_t s) {
-  if (g1.M <= 0) return EGNN_OK;
-  if (!mlp_tc_ok(g1, g2)) return fail(EGNN_ERR_UNSUPPORTED, "mlp_tc: operand layout not supported");
-  MlpArgs m{g1, g2};
-  m.g1.vec = 1;
-  m.g2.vec = 1;
-  return g2.N == 256 ? launch_mlp<256>(m, s) : launch_mlp<128>(m, s);
-}
-
 int gemm_tc(const GemmArgs& a_in, cudaStream_t s) {
   if (a_in.M <= 0 || a_in.N <= 0) return EGNN_OK;
   if (!gemm_tc_ok(a_in)) return fail(EGNN_ERR_UNSUPPORTED, "gemm_tc: operand layout not supported");
   GemmArgs a = a_in;
-  a.vec = vec_ok(a);
+  a.vec = (a.N % 4 == 0 && a.ldc % 4 == 0 && aligned16(a.C) && (!a.bias || aligned16(a.bias)) &&
+           (!a.pre || (a.ldp % 4 == 0 && aligned16(a.pre))) &&
+           (a.act != ACT_DSILU || (a.ldaux % 4 == 0 && aligned16(a.aux))) &&
+           (!a.resid || (a.ldr % 4 == 0 && aligned16(a.resid) &&
+                         (a.resid_cols == INT64_MAX || a.resid_cols % 4 == 0)))) ? 1 : 0;
   if (a.a_t == 0 && a.b_t == 0) EGNN_TRY((launch_ab<0, 0>(a, s)));
   else if (a.a_t == 0 && a.b_t == 1) EGNN_TRY((launch_ab<0, 1>(a, s)));
   else if (a.a_t == 1 && a.b_t == 0) EGNN_TRY((launch_ab<1, 0>(a, s)));

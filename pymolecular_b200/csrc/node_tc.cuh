@@ -15,13 +15,6 @@ bool gemm_tc_ok(const GemmArgs& a);
 // are added by the same ordered reduction as gemm().
 int gemm_tc(const GemmArgs& a, cudaStream_t s);
 
-// The node MLP's two chained GEMMs in one launch: C2 = epi2(epi1(A B1) B2),
-// with T = epi1(A B1) also written (g1.C, and g1.pre); g1.N = g2.K = 128,
-// g2.N = 128 or 256, both operand layouts row-major as gemm_tc_ok() takes.
-// g2.A is not read (GEMM 2's operand is T).
-bool mlp_tc_ok(const GemmArgs& g1, const GemmArgs& g2);
-int mlp_tc(const GemmArgs& g1, const GemmArgs& g2, cudaStream_t s);
-
 // Split-K count of wgrad_tc() for R rows: about one wave of 128 x 128 output
 // tiles, at least two 64-row chunks per slice, at most 64 slices.  The
 // split-K workspace holds that many slices of M x N (+ M for the bias).

@@ -67,13 +67,19 @@ enum {
 /* GEMM input precision. Accumulation and coordinates are always float32. */
 enum { EGNN_PREC_FP32 = 0, EGNN_PREC_BF16 = 1 };
 
+/* E_GCL(input_nf = I, output_nf = O, hidden_nf = H, edges_in_d = d)
+ * (egnn_clean.py:11-47).  EGNN builds every layer with I = O = H
+ * (egnn_clean.py:136); I and O may differ from H (0 means H), and the
+ * residual (h' = h + ...) needs I = O. */
 typedef struct {
   int64_t n_nodes;        /* N */
   int64_t n_edges;        /* E (< 2^31) */
-  int32_t hidden;         /* H = input_nf = output_nf = hidden_nf; multiple of 32, <= 256 */
+  int32_t hidden;         /* H = hidden_nf: 32, 64, 128 or 256 */
   int32_t edge_attr_dim;  /* edges_in_d (0..16) */
   int32_t flags;          /* EGNN_FLAG_* */
   int32_t precision;      /* EGNN_PREC_* */
+  int32_t in_dim;         /* I = input_nf, columns of h (1..1024; 0 = H) */
+  int32_t out_dim;        /* O = output_nf, columns of h_out (1..1024; 0 = H) */
 } egnn_layer_desc;
 
 /* A destination-sorted CSR and its transpose (built by egnn_csr_build /
@@ -89,10 +95,10 @@ typedef struct {
 
 /* Parameters of one E_GCL (nn.Linear layout, float32). */
 typedef struct {
-  const float* edge_w1;  const float* edge_b1;   /* edge_mlp.0: (H, 2H+1+d), (H) */
+  const float* edge_w1;  const float* edge_b1;   /* edge_mlp.0: (H, 2I+1+d), (H) */
   const float* edge_w2;  const float* edge_b2;   /* edge_mlp.2: (H, H), (H)      */
-  const float* node_w1;  const float* node_b1;   /* node_mlp.0: (H, 2H), (H)     */
-  const float* node_w2;  const float* node_b2;   /* node_mlp.2: (H, H), (H)      */
+  const float* node_w1;  const float* node_b1;   /* node_mlp.0: (H, I+H), (H)    */
+  const float* node_w2;  const float* node_b2;   /* node_mlp.2: (O, H), (O)      */
   const float* coord_w1; const float* coord_b1;  /* coord_mlp.0: (H, H), (H)     */
   const float* coord_w2;                         /* coord_mlp.2: (1, H), no bias */
   const float* att_w;    const float* att_b;     /* att_mlp.0: (1, H), (1); attention only */
@@ -225,7 +231,7 @@ EGNN_API size_t egnn_saved_size(const egnn_layer_desc* d);
  * (EGNN_WS_BWD) on a device with `num_sms` SMs (0 = current device). */
 EGNN_API size_t egnn_workspace_size(const egnn_layer_desc* d, int which, int num_sms);
 
-/* E_GCL.forward (egnn_clean.py:95-103): h_out (N,H), x_out (N,3).
+/* E_GCL.forward (egnn_clean.py:95-103): h (N,I) -> h_out (N,O), x_out (N,3).
  * edge_attr may be NULL iff d->edge_attr_dim == 0.  `saved` (may be NULL in
  * inference) receives egnn_saved_size(d) bytes for the backward. */
 EGNN_API int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, const egnn_layer_params* p,

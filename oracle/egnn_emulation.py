@@ -44,10 +44,11 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     d = torch.float64
     h, x, gh, gx = h.to(d), x.to(d), gh.to(d), gx.to(d)
     p = {k: v.to(d) for k, v in p.items()}
-    N, H = h.shape
+    N, I = h.shape                      # I = input_nf
     W1 = p["edge_mlp.0.weight"]
-    Wa, Wb, wr = W1[:, :H], W1[:, H:2 * H], W1[:, 2 * H]
-    We = W1[:, 2 * H + 1:]
+    H = W1.shape[0]                     # hidden_nf
+    Wa, Wb, wr = W1[:, :I], W1[:, I:2 * I], W1[:, 2 * I]
+    We = W1[:, 2 * I + 1:]
     b1, W2, b2 = p["edge_mlp.0.bias"], p["edge_mlp.2.weight"], p["edge_mlp.2.bias"]
     Wn1, bn1, Wn2, bn2 = p["node_mlp.0.weight"], p["node_mlp.0.bias"], p["node_mlp.2.weight"], p["node_mlp.2.bias"]
     Wc1, bc1, wc2 = p["coord_mlp.0.weight"], p["coord_mlp.0.bias"], p["coord_mlp.2.weight"][0]
@@ -101,8 +102,8 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     g_n1pre = (gh @ Wn2) * dn1
     g["node_mlp.0.weight"] = g_n1pre.t() @ cat
     g["node_mlp.0.bias"] = g_n1pre.sum(0)
-    gh_acc = g_n1pre @ Wn1[:, :H] + (gh if residual else 0.0)
-    g_agg = g_n1pre @ Wn1[:, H:]
+    gh_acc = g_n1pre @ Wn1[:, :I] + (gh if residual else 0.0)
+    g_agg = g_n1pre @ Wn1[:, I:]
 
     g_trans = gx[row] * scale[row][:, None]
     gphi = (g_trans * dlt).sum(1) * inv
@@ -137,11 +138,11 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     grad_x = gx + segment_sum(gdl, row, N) - segment_sum(gdl, col, N)
     grad_h = gh_acc + S_dst @ Wa + S_src @ Wb
     gW1 = torch.zeros_like(W1)
-    gW1[:, :H] = S_dst.t() @ h
-    gW1[:, H:2 * H] = S_src.t() @ h
-    gW1[:, 2 * H] = (g_a1 * r[:, None]).sum(0)
+    gW1[:, :I] = S_dst.t() @ h
+    gW1[:, I:2 * I] = S_src.t() @ h
+    gW1[:, 2 * I] = (g_a1 * r[:, None]).sum(0)
     if edge_attr is not None and edge_attr.shape[1]:
-        gW1[:, 2 * H + 1:] = g_a1.t() @ edge_attr.to(d)
+        gW1[:, 2 * I + 1:] = g_a1.t() @ edge_attr.to(d)
     g["edge_mlp.0.weight"] = gW1
     g["edge_mlp.0.bias"] = S_dst.sum(0)
     return h_out, x_out, grad_h, grad_x, g

@@ -53,7 +53,8 @@ class EgnnError(RuntimeError):
 
 class LayerDesc(C.Structure):
     _fields_ = [("n_nodes", C.c_int64), ("n_edges", C.c_int64), ("hidden", C.c_int32),
-                ("edge_attr_dim", C.c_int32), ("flags", C.c_int32), ("precision", C.c_int32)]
+                ("edge_attr_dim", C.c_int32), ("flags", C.c_int32), ("precision", C.c_int32),
+                ("in_dim", C.c_int32), ("out_dim", C.c_int32)]   # 0: hidden
 
 
 class Graph(C.Structure):

@@ -928,7 +928,8 @@ __global__ void src_pass_kernel(int64_t N, const int32_t* __restrict__ src_ptr,
 // of the CTA partials (eight loads in flight), and warp 0 adds the 8 sums in
 // warp order (a fixed association: bit-reproducible).
 __global__ void __launch_bounds__(256) part_reduce_kernel(int H, int d, int att, int G, int64_t PF,
-                                                          const float* part, egnn_layer_grads gp, int64_t ld_w1) {
+                                                          const float* part, egnn_layer_grads gp, int64_t ld_w1,
+                                                          int64_t c_r) {
   pdl_enter();
   __shared__ float red[8][33];
   const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
@@ -962,11 +963,11 @@ __global__ void __launch_bounds__(256) part_reduce_kernel(int H, int d, int att,
     if (v2 < H) gp.coord_b1[v2] = s;
     else if (v2 < 2 * H) gp.edge_b2[v2 - H] = s;
     else if (v2 < 3 * H) gp.coord_w2[v2 - 2 * H] = s;
-    else if (v2 < 4 * H) gp.edge_w1[(v2 - 3 * H) * ld_w1 + 2 * H] = s;
+    else if (v2 < 4 * H) gp.edge_w1[(v2 - 3 * H) * ld_w1 + c_r] = s;
     else if (v2 < 4 * H + (int64_t)H * d) {
       const int64_t w = v2 - 4 * H;
       const int64_t f = w / d, t = w % d;
-      gp.edge_w1[f * ld_w1 + 2 * H + 1 + t] = s;
+      gp.edge_w1[f * ld_w1 + c_r + 1 + t] = s;
     } else {
       const int64_t w = v2 - 4 * H - (int64_t)H * d;
       if (w < H) gp.att_w[w] = s;
@@ -1138,12 +1139,12 @@ int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_e
 }
 
 int edge_part_reduce(int H, int d, bool att, int G, const float* part, const egnn_layer_grads* gp,
-                     int64_t ld_w1, cudaStream_t s) {
+                     int64_t ld_w1, int64_t c_r, cudaStream_t s) {
   const int64_t total = edge_part_att(H, d) + (att ? H + 1 : 0);
   const int blocks = (int)((total + 31) / 32);
   TimerScope ts("part_reduce", s);
   EGNN_CHECK_CUDA(launch_pdl(part_reduce_kernel, dim3(blocks), dim3(256), 0, s, H, d, att ? 1 : 0, G,
-                             edge_part_floats(H, d), part, *gp, ld_w1));
+                             edge_part_floats(H, d), part, *gp, ld_w1, c_r));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }

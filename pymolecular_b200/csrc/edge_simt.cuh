@@ -161,8 +161,9 @@ int edge_src_pass(int H, int64_t N, const int32_t* src_ptr, const int32_t* src_e
                   const float* gxd, float* S_src, float* gx, cudaStream_t s);
 
 // Reduce the G per-CTA partials in CTA order and scatter them into the
-// parameter-gradient outputs.
+// parameter-gradient outputs.  edge_mlp.0.weight has row stride ld_w1; its
+// radial column is c_r (= 2 input_nf), the edge-attribute columns follow.
 int edge_part_reduce(int H, int d, bool att, int G, const float* part, const egnn_layer_grads* gp,
-                     int64_t ld_w1, cudaStream_t s);
+                     int64_t ld_w1, int64_t c_r, cudaStream_t s);
 
 }  // namespace egnn

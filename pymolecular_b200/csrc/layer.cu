@@ -37,6 +37,10 @@ namespace {
 
 bool valid_hidden(int H) { return H == 32 || H == 64 || H == 128 || H == 256; }
 
+// input_nf and output_nf of the layer (0 in the descriptor: hidden_nf)
+int in_dim(const egnn_layer_desc* d) { return d->in_dim ? d->in_dim : d->hidden; }
+int out_dim(const egnn_layer_desc* d) { return d->out_dim ? d->out_dim : d->hidden; }
+
 int check_desc(const egnn_layer_desc* d) {
   if (!d) return fail(EGNN_ERR_INVALID_ARG, "null layer descriptor");
   if (d->n_nodes < 0 || d->n_edges < 0 || d->n_nodes >= INT32_MAX || d->n_edges >= INT32_MAX)
@@ -49,6 +53,12 @@ int check_desc(const egnn_layer_desc* d) {
   if (d->flags & ~31) return fail(EGNN_ERR_INVALID_ARG, "unknown flag bits 0x%x", d->flags);
   if (d->precision != EGNN_PREC_FP32 && d->precision != EGNN_PREC_BF16)
     return fail(EGNN_ERR_INVALID_ARG, "unknown precision %d", d->precision);
+  if (d->in_dim < 0 || d->in_dim > 1024 || d->out_dim < 0 || d->out_dim > 1024)
+    return fail(EGNN_ERR_UNSUPPORTED, "in_dim %d / out_dim %d not built (1..1024, 0 = hidden)", d->in_dim,
+                d->out_dim);
+  if ((d->flags & EGNN_FLAG_RESIDUAL) && in_dim(d) != out_dim(d))
+    return fail(EGNN_ERR_INVALID_ARG, "the residual h + out needs in_dim == out_dim (%d, %d)", in_dim(d),
+                out_dim(d));
   return EGNN_OK;
 }
 
@@ -62,20 +72,21 @@ int64_t max_ctas(int64_t E, int H, int num_sms) {
   return std::min<int64_t>(chunks, (int64_t)num_sms * 8);
 }
 
-// Prepared operands shared by the forward and the backward.
+// Prepared operands shared by the forward and the backward (I = input_nf,
+// O = output_nf).
 struct Prep {
   float4* xp; float* bias2; float* W2T; float* Wc1T; float* W2r; float* Wc1r; float* wr; float* We;
-  float* WPQ;   // (2H, H): rows of edge_mlp.0 restricted to the h_i and h_j columns, contiguous
+  float* WPQ;   // (2H, I): rows of edge_mlp.0 restricted to the h_i and h_j columns, contiguous
   // forward only: transposed weights (in x out), so that the forward node
   // GEMMs read their weight operand k-major like the backward ones
-  float* Wn2T;  // (H, H):  node_mlp.2.weight^T
-  float* Wn1T;  // (2H, H): node_mlp.0.weight^T
-  float* WPQT;  // (H, 2H): WPQ^T
+  float* Wn2T;  // (H, O):     node_mlp.2.weight^T
+  float* Wn1T;  // (I + H, H): node_mlp.0.weight^T
+  float* WPQT;  // (I, 2H):    WPQ^T
 };
 
 // `tc`: the tensor-core edge kernels read W2 and W_c1 as given, so the SIMT
 // kernels' transposed / rounded copies are not made.
-Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd, bool tc) {
+Prep carve_prep(Carver& c, int64_t N, int H, int I, int O, int d, bool bwd, bool tc) {
   Prep p{};
   p.xp = c.take<float4>(std::max<int64_t>(N, 1));
   p.bias2 = c.take<float>(2 * H);
@@ -85,14 +96,16 @@ Prep carve_prep(Carver& c, int64_t N, int H, int d, bool bwd, bool tc) {
   p.Wc1r = (bwd && !tc) ? c.take<float>((size_t)H * H) : nullptr;
   p.wr = c.take<float>(H);
   p.We = c.take<float>((size_t)H * std::max(d, 1));
-  p.WPQ = c.take<float>((size_t)2 * H * H);
-  p.Wn2T = bwd ? nullptr : c.take<float>((size_t)H * H);
-  p.Wn1T = bwd ? nullptr : c.take<float>((size_t)2 * H * H);
-  p.WPQT = bwd ? nullptr : c.take<float>((size_t)2 * H * H);
+  p.WPQ = c.take<float>((size_t)2 * H * I);
+  p.Wn2T = bwd ? nullptr : c.take<float>((size_t)H * O);
+  p.Wn1T = bwd ? nullptr : c.take<float>((size_t)(I + H) * H);
+  p.WPQT = bwd ? nullptr : c.take<float>((size_t)2 * H * I);
   return p;
 }
 
-__host__ __device__ inline int64_t prep_transposes(const Prep& o, int H) { return o.Wn2T ? 5LL * H * H : 0; }
+__host__ __device__ inline int64_t prep_transposes(const Prep& o, int H, int I, int O) {
+  return o.Wn2T ? (int64_t)H * O + (int64_t)(I + H) * H + 2LL * H * I : 0;
+}
 // The H x H copies of W2 / W_c1 the layout asks for: W2T, Wc1T, W2r, Wc1r in
 // this order, the absent ones left out; sel[] lists the present ones.
 __host__ __device__ inline int prep_copies(const Prep& o, int* sel) {
@@ -103,46 +116,48 @@ __host__ __device__ inline int prep_copies(const Prep& o, int* sel) {
   if (o.Wc1r) sel[n++] = 3;
   return n;
 }
-__host__ __device__ inline int64_t prep_total(int64_t N, int H, int d, const Prep& o) {
+__host__ __device__ inline int64_t prep_total(int64_t N, int H, int I, int O, int d, const Prep& o) {
   int sel[4];
   const int64_t HH = (int64_t)H * H;
-  return N + 2 * H + prep_copies(o, sel) * HH + H + (int64_t)H * d + 2 * HH + prep_transposes(o, H);
+  return N + 2 * H + prep_copies(o, sel) * HH + H + (int64_t)H * d + 2LL * H * I + prep_transposes(o, H, I, O);
 }
 
-__global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_layer_params p,
+// edge_mlp.0.weight (H, ld1 = 2I + 1 + d) columns: [0, I) h_i, [I, 2I) h_j,
+// 2I the radial term, then the edge attributes.
+__global__ void prep_kernel(int64_t N, int H, int I, int O, int d, int64_t ld1, int bf, egnn_layer_params p,
                             const float* x, Prep o) {
   pdl_enter();
-  const int64_t HH = (int64_t)H * H;
+  const int64_t HH = (int64_t)H * H, HI = (int64_t)H * I, HO = (int64_t)H * O, IHH = (int64_t)(I + H) * H;
   int sel[4];
   const int ncopy = prep_copies(o, sel);
-  const int64_t total = prep_total(N, H, d, o);
+  const int64_t total = prep_total(N, H, I, O, d, o);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     int64_t t = idx;
     if (o.Wn2T) {
-      if (t < HH) {   // Wn2T[n][k] = node_w2[k][n]
-        o.Wn2T[t] = p.node_w2[(t % H) * H + t / H];
+      if (t < HO) {   // Wn2T[k][n] = node_w2[n][k], node_w2 is (O, H)
+        o.Wn2T[t] = p.node_w2[(t % O) * H + t / O];
         continue;
       }
-      t -= HH;
-      if (t < 2 * HH) {   // Wn1T[n][k] = node_w1[k][n], node_w1 is (H, 2H)
-        o.Wn1T[t] = p.node_w1[(t % H) * 2 * H + t / H];
+      t -= HO;
+      if (t < IHH) {   // Wn1T[k][n] = node_w1[n][k], node_w1 is (H, I + H)
+        o.Wn1T[t] = p.node_w1[(t % H) * (I + H) + t / H];
         continue;
       }
-      t -= 2 * HH;
-      if (t < 2 * HH) {   // WPQT[n][k] = WPQ[k][n], n < H, k < 2H
-        const int64_t n = t / (2 * H), k = t % (2 * H);
-        o.WPQT[t] = k < H ? p.edge_w1[k * ld1 + n] : p.edge_w1[(k - H) * ld1 + H + n];
+      t -= IHH;
+      if (t < 2 * HI) {   // WPQT[k][n] = WPQ[n][k], k < I, n < 2H
+        const int64_t k = t / (2 * H), n = t % (2 * H);
+        o.WPQT[t] = n < H ? p.edge_w1[n * ld1 + k] : p.edge_w1[(n - H) * ld1 + I + k];
         continue;
       }
-      t -= 2 * HH;
+      t -= 2 * HI;
     }
-    if (t < 2 * HH) {
-      const int64_t r = t / H, c = t % H;   // WPQ[r][c]: r < H -> Wa, else Wb
-      o.WPQ[t] = r < H ? p.edge_w1[r * ld1 + c] : p.edge_w1[(r - H) * ld1 + H + c];
+    if (t < 2 * HI) {
+      const int64_t r = t / I, c = t % I;   // WPQ[r][c]: r < H -> Wa, else Wb
+      o.WPQ[t] = r < H ? p.edge_w1[r * ld1 + c] : p.edge_w1[(r - H) * ld1 + I + c];
       continue;
     }
-    t -= 2 * HH;
+    t -= 2 * HI;
     if (t < N) { o.xp[t] = make_float4(x[t * 3], x[t * 3 + 1], x[t * 3 + 2], 0.f); continue; }
     t -= N;
     if (t < 2 * H) { o.bias2[t] = t < H ? p.edge_b1[t] : 0.f; continue; }
@@ -160,18 +175,19 @@ __global__ void prep_kernel(int64_t N, int H, int d, int64_t ld1, int bf, egnn_l
       continue;
     }
     t -= ncopy * HH;
-    if (t < H) { o.wr[t] = p.edge_w1[t * ld1 + 2 * H]; continue; }
+    if (t < H) { o.wr[t] = p.edge_w1[t * ld1 + 2 * I]; continue; }
     t -= H;
-    { const int64_t f = t / d, a = t % d; o.We[f * d + a] = p.edge_w1[f * ld1 + 2 * H + 1 + a]; }
+    { const int64_t f = t / d, a = t % d; o.We[f * d + a] = p.edge_w1[f * ld1 + 2 * I + 1 + a]; }
   }
 }
 
-int launch_prep(int64_t N, int H, int d, int64_t ld1, bool bf, const egnn_layer_params* p,
+int launch_prep(int64_t N, int H, int I, int O, int d, int64_t ld1, bool bf, const egnn_layer_params* p,
                 const float* x, const Prep& o, cudaStream_t s) {
-  const int64_t total = prep_total(N, H, d, o);
+  const int64_t total = prep_total(N, H, I, O, d, o);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
   TimerScope ts("prep", s);
-  EGNN_CHECK_CUDA(launch_pdl(prep_kernel, dim3(blocks), dim3(256), 0, s, N, H, d, ld1, bf ? 1 : 0, *p, x, o));
+  EGNN_CHECK_CUDA(launch_pdl(prep_kernel, dim3(blocks), dim3(256), 0, s, N, H, I, O, d, ld1, bf ? 1 : 0, *p, x,
+                             o));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
@@ -185,11 +201,11 @@ int node_wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t
   return bf ? wgrad_tc(R, M, N, G, X, dW, lddw, db, part, s) : wgrad(R, M, N, G, X, dW, lddw, db, 0, part, s);
 }
 
-int gemm_pq(int64_t N, int H, const float* h, const float* WPQT, const float* bias2, float* PQ, bool bf,
+int gemm_pq(int64_t N, int H, int I, const float* h, const float* WPQT, const float* bias2, float* PQ, bool bf,
             cudaStream_t s) {
   GemmArgs g;
-  g.M = N; g.N = 2 * H; g.K = H;
-  g.A = mat(h, H);
+  g.M = N; g.N = 2 * H; g.K = I;
+  g.A = mat(h, I);
   g.B = mat(WPQT, 2 * H); g.b_t = 0;
   g.bias = bias2;
   g.C = PQ; g.ldc = 2 * H;
@@ -223,7 +239,7 @@ FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int H = d->hidden;
   FwdWs w;
   const bool rows = edge_rows_supported(H, d->edge_attr_dim, d->flags, d->precision);
-  w.prep = carve_prep(c, N, H, d->edge_attr_dim, false,
+  w.prep = carve_prep(c, N, H, in_dim(d), out_dim(d), d->edge_attr_dim, false,
                       rows || edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
   const int64_t G = max_ctas(E, H, num_sms);
   w.carry = c.take<float>((size_t)G * 2 * (H + 4));
@@ -235,8 +251,14 @@ FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   return w;
 }
 
+// dL/dh from the node MLP and dL/dagg: one (N, I + H) product into ghg when
+// I % 4 == 0; otherwise dL/dh (N, I) in ghg and dL/dagg (N, H) in gagg, so
+// that the dL/dagg rows the edge kernels read 16 bytes at a time stay
+// 16-byte aligned.
+bool ghg_joint(int I) { return I % 4 == 0; }
+
 struct BwdWs {
-  Prep prep; float* g_n1pre; float* ghg;   // ghg: (N, 2H) = [dL/dh from the node MLP | dL/dagg]
+  Prep prep; float* g_n1pre; float* ghg; float* gagg;
   float* S_dst; float* S_src; float* gxd; float* gstore; float4* gdstore; float* carry;
   int32_t* carry_row; float* part; float* wpart;
   float* wpart_aux;   // split-K scratch of the weight gradients run on the side stream
@@ -244,23 +266,28 @@ struct BwdWs {
   RowsBufs rows;      // edge-row GEMM path only
 };
 
-int64_t wpart_floats(int64_t N, int H) {
+// Split-K scratch of the layer's weight gradients: dW_n1 (H x (I + H)),
+// dW_n2 (O x H), dW_a and dW_b (H x I).
+int64_t wpart_floats(int64_t N, int H, int I, int O) {
   // slices of the FFMA split (wgrad) or of the tensor-core split (wgrad_tc)
-  int64_t a = std::max(wgrad_splits(N, H, 2 * H), wgrad_tc_splits(N, H, 2 * H)) * ((int64_t)H * 2 * H + H);
-  int64_t b = std::max(wgrad_splits(N, H, H), wgrad_tc_splits(N, H, H)) * ((int64_t)H * H + H);
-  int64_t c = colsum_splits(N) * (int64_t)2 * H;
-  return std::max<int64_t>({a, b, c, 1});
+  auto need = [&](int64_t M, int64_t K) {
+    return std::max(wgrad_splits(N, M, K), wgrad_tc_splits(N, M, K)) * (M * K + M);
+  };
+  const int64_t c = colsum_splits(N) * (int64_t)std::max(I + H, O);
+  return std::max<int64_t>({need(H, I + H), need(O, H), need(H, I), c, 1});
 }
 
 BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int64_t N = std::max<int64_t>(d->n_nodes, 1), E = d->n_edges;
   const int H = d->hidden;
   BwdWs w;
+  const int I = in_dim(d), O = out_dim(d);
   const bool rows = edge_rows_supported(H, d->edge_attr_dim, d->flags, d->precision);
-  w.prep = carve_prep(c, N, H, d->edge_attr_dim, true,
+  w.prep = carve_prep(c, N, H, I, O, d->edge_attr_dim, true,
                       rows || edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
   w.g_n1pre = c.take<float>((size_t)N * H);
-  w.ghg = c.take<float>((size_t)N * 2 * H);
+  w.ghg = c.take<float>((size_t)N * (ghg_joint(I) ? I + H : I));
+  w.gagg = ghg_joint(I) ? w.ghg + I : c.take<float>((size_t)N * H);
   w.S_dst = c.take<float>((size_t)N * H);
   w.S_src = c.take<float>((size_t)N * H);
   w.gxd = c.take<float>((size_t)N * 3);
@@ -271,8 +298,8 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   w.carry_row = c.take<int32_t>((size_t)G * 2);
   // the edge-row path keeps its per-CTA partials in w.rows.part
   w.part = rows ? nullptr : c.take<float>((size_t)G * edge_part_floats(H, d->edge_attr_dim));
-  w.wpart = c.take<float>((size_t)wpart_floats(N, H));
-  w.wpart_aux = c.take<float>((size_t)wpart_floats(N, H));
+  w.wpart = c.take<float>((size_t)wpart_floats(N, H, I, O));
+  w.wpart_aux = c.take<float>((size_t)wpart_floats(N, H, I, O));
   w.att_scr = (d->flags & EGNN_FLAG_ATTENTION) ? c.take<float>((size_t)(G * edge_att_scratch_floats(H))) : nullptr;
   if (rows) w.rows = carve_rows(c, E, H, true, num_sms);
   return w;
@@ -417,7 +444,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(check_desc(d));
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t N = d->n_nodes, E = d->n_edges;
-  const int H = d->hidden, dd = d->edge_attr_dim;
+  const int H = d->hidden, dd = d->edge_attr_dim, I = in_dim(d), O = out_dim(d);
   const bool bf = d->precision == EGNN_PREC_BF16;
   if (N == 0) return EGNN_OK;
   if (missing_params(p, d->flags) || missing_graph(g, false, dd > 0, E) || !h || !x || !h_out || !x_out ||
@@ -430,13 +457,13 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
     return fail(EGNN_ERR_WORKSPACE, "egnn_layer_fwd: workspace %zu < %zu bytes", ws_bytes, probe.size());
   Carver c(ws);
   FwdWs w = carve_fwd(c, d, sms);
-  const int64_t ld1 = 2 * H + 1 + dd;
+  const int64_t ld1 = 2 * I + 1 + dd;
   Carver sc(saved ? saved : static_cast<void*>(w.saved_tmp));
   const Saved sv = carve_saved(sc, N, H);
   float* agg = sv.agg;
 
-  EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, h, w.prep.WPQT, w.prep.bias2, sv.PQ, bf, s));
+  EGNN_TRY(launch_prep(N, H, I, O, dd, ld1, bf, p, x, w.prep, s));
+  EGNN_TRY(gemm_pq(N, H, I, h, w.prep.WPQT, w.prep.bias2, sv.PQ, bf, s));
 
   const bool rows = edge_rows_supported(H, dd, d->flags, d->precision);
   const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
@@ -452,8 +479,8 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   else EGNN_TRY(edge_fwd(H, bf, a, eg, s));
 
   GemmArgs n1;
-  n1.M = N; n1.N = H; n1.K = 2 * H;
-  n1.A = mat_cols(h, H, H, agg, H);
+  n1.M = N; n1.N = H; n1.K = I + H;
+  n1.A = mat_cols(h, I, I, agg, H);
   n1.B = mat(w.prep.Wn1T, H); n1.b_t = 0;
   n1.bias = p->node_b1; n1.act = ACT_SILU;
   n1.pre = sv.n1pre; n1.ldp = H;
@@ -461,12 +488,12 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(node_gemm(n1, bf, s));
 
   GemmArgs n2;
-  n2.M = N; n2.N = H; n2.K = H;
+  n2.M = N; n2.N = O; n2.K = H;
   n2.A = mat(sv.n1, H);
-  n2.B = mat(w.prep.Wn2T, H); n2.b_t = 0;
+  n2.B = mat(w.prep.Wn2T, O); n2.b_t = 0;
   n2.bias = p->node_b2;
-  if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = H; }
-  n2.C = h_out; n2.ldc = H;
+  if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = I; }   // I == O
+  n2.C = h_out; n2.ldc = O;
   EGNN_TRY(node_gemm(n2, bf, s));
   return EGNN_OK;
 }
@@ -478,7 +505,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(check_desc(d));
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t N = d->n_nodes, E = d->n_edges;
-  const int H = d->hidden, dd = d->edge_attr_dim;
+  const int H = d->hidden, dd = d->edge_attr_dim, I = in_dim(d), O = out_dim(d);
   const bool bf = d->precision == EGNN_PREC_BF16;
   const bool residual = d->flags & EGNN_FLAG_RESIDUAL;
   if (missing_params(p, d->flags) || missing_graph(g, true, dd > 0, E) || !h || !x || !saved || !gh_out ||
@@ -495,13 +522,13 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     return fail(EGNN_ERR_WORKSPACE, "egnn_layer_bwd: workspace %zu < %zu bytes", ws_bytes, probe.size());
   Carver c(ws);
   BwdWs w = carve_bwd(c, d, sms);
-  const int64_t ld1 = 2 * H + 1 + dd;
+  const int64_t ld1 = 2 * I + 1 + dd;
   Carver sc(const_cast<void*>(saved));
   const Saved sv = carve_saved(sc, N, H);
   const float* agg = sv.agg;
   if (N == 0) return EGNN_OK;
 
-  EGNN_TRY(launch_prep(N, H, dd, ld1, bf, p, x, w.prep, s));
+  EGNN_TRY(launch_prep(N, H, I, O, dd, ld1, bf, p, x, w.prep, s));
   SideStream* side = nullptr;
   EGNN_TRY(side_stream(s, &side));
   const cudaStream_t s2 = side->stream;
@@ -510,11 +537,11 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   // ---- node MLP backward: h' = [h +] Wn2 silu(Wn1 [h, agg] + bn1) + bn2
   // dW_n2, db_n2 on the side stream (inputs ready at entry)
   EGNN_TRY(stream_fork(s, s2, side->ev[0]));
-  EGNN_TRY(node_wgrad(N, H, H, mat(gh_out, H), mat(sv.n1, H), gp->node_w2, H, gp->node_b2, bf, w.wpart_aux, s2));
+  EGNN_TRY(node_wgrad(N, O, H, mat(gh_out, O), mat(sv.n1, H), gp->node_w2, H, gp->node_b2, bf, w.wpart_aux, s2));
   {
     GemmArgs gn;
-    gn.M = N; gn.N = H; gn.K = H;
-    gn.A = mat(gh_out, H);
+    gn.M = N; gn.N = H; gn.K = O;
+    gn.A = mat(gh_out, O);
     gn.B = mat(p->node_w2, H); gn.b_t = 0;
     gn.act = ACT_DSILU; gn.aux = sv.n1pre; gn.ldaux = H;
     gn.C = w.g_n1pre; gn.ldc = H;
@@ -522,17 +549,28 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   }
   // dW_n1, db_n1 on the side stream once g_n1pre exists
   EGNN_TRY(stream_fork(s, s2, side->ev[1]));
-  EGNN_TRY(node_wgrad(N, H, 2 * H, mat(w.g_n1pre, H), mat_cols(h, H, H, agg, H), gp->node_w1, 2 * H,
+  EGNN_TRY(node_wgrad(N, H, I + H, mat(w.g_n1pre, H), mat_cols(h, I, I, agg, H), gp->node_w1, I + H,
                       gp->node_b1, bf, w.wpart_aux, s2));
+  const bool joint = ghg_joint(I);
+  const int64_t ld_ghg = joint ? I + H : I;
   {
-    // [dL/dh (MLP path) + residual | dL/dagg] = g_n1pre Wn1, one N x 2H product
+    // [dL/dh (MLP path) + residual | dL/dagg] = g_n1pre Wn1: one N x (I + H)
+    // product, or its dL/dh columns here and the dL/dagg columns below
     GemmArgs gh;
-    gh.M = N; gh.N = 2 * H; gh.K = H;
+    gh.M = N; gh.N = joint ? I + H : I; gh.K = H;
     gh.A = mat(w.g_n1pre, H);
-    gh.B = mat(p->node_w1, 2 * H); gh.b_t = 0;
-    if (residual) { gh.resid = gh_out; gh.ldr = H; gh.resid_cols = H; }
-    gh.C = w.ghg; gh.ldc = 2 * H;
+    gh.B = mat(p->node_w1, I + H); gh.b_t = 0;
+    if (residual) { gh.resid = gh_out; gh.ldr = O; gh.resid_cols = I; }   // I == O
+    gh.C = w.ghg; gh.ldc = ld_ghg;
     EGNN_TRY(node_gemm(gh, bf, s));
+  }
+  if (!joint) {
+    GemmArgs ga;
+    ga.M = N; ga.N = H; ga.K = H;
+    ga.A = mat(w.g_n1pre, H);
+    ga.B = mat(p->node_w1 + I, I + H); ga.b_t = 0;
+    ga.C = w.gagg; ga.ldc = H;
+    EGNN_TRY(node_gemm(ga, bf, s));
   }
 
   // ---- edge backward: dst pass, fix-up, partial reduction, src pass
@@ -546,7 +584,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   a.carry = w.carry; a.carry_row = w.carry_row;
   a.W2 = bf ? w.prep.W2r : p->edge_w2;
   a.Wc1 = bf ? w.prep.Wc1r : p->coord_w1;
-  a.gx_out = gx_out; a.g_agg = w.ghg + H; a.ld_gagg = 2 * H;
+  a.gx_out = gx_out; a.g_agg = w.gagg; a.ld_gagg = joint ? I + H : H;
   a.S_dst = w.S_dst; a.gxd = w.gxd; a.gstore = w.gstore; a.gdstore = w.gdstore; a.part = w.part;
   a.att_scr = w.att_scr;
   if (rows) {
@@ -554,13 +592,13 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     // dW_c1, dW_2 and the partial reduction on the side stream
     EGNN_TRY(stream_fork(s, s2, side->ev[2]));
     EGNN_TRY(edge_wgrad_rows(E, w.rows, s2));
-    EGNN_TRY(edge_part_reduce(H, dd, false, w.rows.G, w.rows.part, gp, ld1, s2));
+    EGNN_TRY(edge_part_reduce(H, dd, false, w.rows.G, w.rows.part, gp, ld1, 2 * I, s2));
   } else {
     if (tc) EGNN_TRY(edge_bwd_tc(H, a, eg, s));
     else EGNN_TRY(edge_bwd(H, bf, a, eg, s));
     // per-CTA weight-gradient partials -> parameter gradients, on the side stream
     EGNN_TRY(stream_fork(s, s2, side->ev[2]));
-    EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, s2));
+    EGNN_TRY(edge_part_reduce(H, dd, (d->flags & EGNN_FLAG_ATTENTION) != 0, eg.G, w.part, gp, ld1, 2 * I, s2));
   }
   if (tc || rows)
     EGNN_TRY(edge_node_pass_tc(H, N, g->row_ptr, g->src_ptr, g->src_edge, w.gstore, w.gdstore, gx_out, w.S_dst,
@@ -572,16 +610,16 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
   // ---- dL/dh = gh_acc + S_dst Wa + S_src Wb here; dWa, db1 and dWb on the two side streams
   EGNN_TRY(stream_fork(s, s2, side->ev[3]));
   EGNN_TRY(stream_fork(s, side->stream2, side->ev[4]));
-  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_src, H), mat(h, H), gp->edge_w1 + H, ld1, nullptr, bf, w.wpart,
+  EGNN_TRY(node_wgrad(N, H, I, mat(w.S_src, H), mat(h, I), gp->edge_w1 + I, ld1, nullptr, bf, w.wpart,
                       side->stream2));
-  EGNN_TRY(node_wgrad(N, H, H, mat(w.S_dst, H), mat(h, H), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart_aux, s2));
+  EGNN_TRY(node_wgrad(N, H, I, mat(w.S_dst, H), mat(h, I), gp->edge_w1, ld1, gp->edge_b1, bf, w.wpart_aux, s2));
   {
     GemmArgs gh;
-    gh.M = N; gh.N = H; gh.K = 2 * H;
+    gh.M = N; gh.N = I; gh.K = 2 * H;
     gh.A = mat_cols(w.S_dst, H, H, w.S_src, H);
-    gh.B = mat(w.prep.WPQ, H); gh.b_t = 0;
-    gh.resid = w.ghg; gh.ldr = 2 * H;
-    gh.C = grad_h; gh.ldc = H;
+    gh.B = mat(w.prep.WPQ, I); gh.b_t = 0;
+    gh.resid = w.ghg; gh.ldr = ld_ghg;
+    gh.C = grad_h; gh.ldc = I;
     EGNN_TRY(node_gemm(gh, bf, s));
   }
   return EGNN_OK;

@@ -19,10 +19,16 @@ Parameters keep the reference ``state_dict`` names, so checkpoints move both
 ways.  One extra keyword, ``precision='fp32' | 'bf16'``, selects fp32 GEMMs
 (default) or bf16 GEMM inputs with fp32 accumulation.
 
+``E_GCL`` takes any ``input_nf`` / ``output_nf`` next to ``hidden_nf`` (as
+the reference constructor does; ``EGNN`` builds every layer with all three
+equal, egnn_clean.py:136).
+
 Differences that raise instead of silently diverging:
-``act_fn`` other than SiLU, ``input_nf != output_nf != hidden_nf`` in
-``E_GCL``, ``node_attr`` (the reference node_mlp width ignores it,
-egnn_clean.py:29 vs :63-64), CPU tensors.
+``act_fn`` other than SiLU, ``residual=True`` with ``input_nf != output_nf``
+(the reference's ``h + out`` fails on the shapes, or broadcasts when one of
+them is 1; here it always raises, NotImplementedError being a RuntimeError),
+``node_attr`` (the reference node_mlp width ignores it, egnn_clean.py:29 vs
+:63-64), CPU tensors.
 """
 from __future__ import annotations
 
@@ -62,11 +68,11 @@ class _LayerFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, h, x, edge_attr, csr: CSR, cfg, *params):
-        flags, precision, d = cfg
-        N, H = h.shape
-        desc = nat.LayerDesc(N, csr.n_edges, H, d, flags, precision)
+        flags, precision, d, H, O = cfg
+        N, I = h.shape
+        desc = nat.LayerDesc(N, csr.n_edges, H, d, flags, precision, I, O)
         lib = nat.lib()
-        h_out = torch.empty_like(h)
+        h_out = torch.empty(N, O, dtype=torch.float32, device=h.device)
         x_out = torch.empty_like(x)
         saved = torch.empty(max(lib.egnn_saved_size(C.byref(desc)) // 4, 1), dtype=torch.float32,
                             device=h.device)
@@ -89,12 +95,12 @@ class _LayerFn(torch.autograd.Function):
         h, x, edge_attr, saved, *params = ctx.saved_tensors
         if not ctx.has_attr:
             edge_attr = None
-        flags, precision, d = ctx.cfg
+        flags, precision, d, H, O = ctx.cfg
         csr = ctx.csr
-        N, H = h.shape
-        gh = torch.zeros_like(h) if gh is None else gh.contiguous().float()
+        N, I = h.shape
+        gh = h.new_zeros(N, O) if gh is None else gh.contiguous().float()
         gx = torch.zeros_like(x) if gx is None else gx.contiguous().float()
-        desc = nat.LayerDesc(N, csr.n_edges, H, d, flags, precision)
+        desc = nat.LayerDesc(N, csr.n_edges, H, d, flags, precision, I, O)
         lib = nat.lib()
         grad_h = torch.empty_like(h)
         grad_x = torch.empty_like(x)
@@ -157,14 +163,12 @@ class E_GCL(nn.Module):
         super().__init__()
         if not isinstance(act_fn, nn.SiLU):
             raise NotImplementedError("only act_fn=nn.SiLU() is built (the reference default)")
-        if not (input_nf == output_nf == hidden_nf):
-            raise NotImplementedError("the fused layer needs input_nf == output_nf == hidden_nf "
-                                      "(as every E_GCL inside EGNN has, egnn_clean.py:136)")
         if coords_agg not in ("mean", "sum"):
             raise Exception('Wrong coords_agg parameter %s' % coords_agg)
         if precision not in _PRECISIONS:
             raise ValueError(f"precision must be one of {sorted(_PRECISIONS)}")
         input_edge = input_nf * 2
+        self.input_nf, self.output_nf, self.hidden_nf = input_nf, output_nf, hidden_nf
         self.residual = residual
         self.attention = attention
         self.normalize = normalize
@@ -213,10 +217,16 @@ class E_GCL(nn.Module):
         if node_attr is not None:
             raise NotImplementedError("node_attr is not supported (the reference node_mlp input "
                                       "width does not include it, egnn_clean.py:29, 63-64)")
+        if self.residual and self.input_nf != self.output_nf:
+            raise NotImplementedError(f"residual=True needs input_nf == output_nf (got {self.input_nf}, "
+                                      f"{self.output_nf}): the residual adds h to the node MLP output "
+                                      "(egnn_clean.py:68-69)")
         h = _check_tensor(h, "h")
         coord = _check_tensor(coord, "coord")
         if coord.dim() != 2 or coord.shape[1] != 3:
             raise ValueError("coord must be (N, 3)")
+        if h.dim() != 2 or h.shape[1] != self.input_nf:
+            raise ValueError(f"h must be (N, {self.input_nf})")
         csr = as_csr(edge_index, h.shape[0], h.device)
         d = self.edges_in_d
         if d == 0 and edge_attr is not None:
@@ -227,7 +237,7 @@ class E_GCL(nn.Module):
             edge_attr = _check_tensor(edge_attr, "edge_attr")
             if edge_attr.shape != (csr.n_edges, d):
                 raise ValueError(f"edge_attr must be ({csr.n_edges}, {d})")
-        cfg = (self._flags(), _PRECISIONS[self.precision], d)
+        cfg = (self._flags(), _PRECISIONS[self.precision], d, self.hidden_nf, self.output_nf)
         h_out, x_out = _LayerFn.apply(h, coord, edge_attr, csr, cfg, *self._params())
         return h_out, x_out, edge_attr
 

@@ -69,21 +69,25 @@ def _random_graph(g, n, n_edges, hub=None, isolated=(), self_loop=True, duplicat
     return row.long(), col.long()
 
 
-def case_layer(ref, name, seed, n, n_edges, hidden, edges_in_d=0, **flags):
-    """One E_GCL with random upstream gradients on an unsorted, ragged graph."""
+def case_layer(ref, name, seed, n, n_edges, hidden, edges_in_d=0, input_nf=None, output_nf=None, **flags):
+    """One E_GCL with random upstream gradients on an unsorted, ragged graph
+    (input_nf / output_nf default to hidden, as inside EGNN)."""
+    input_nf = hidden if input_nf is None else input_nf
+    output_nf = hidden if output_nf is None else output_nf
     g = torch.Generator().manual_seed(seed)
     row, col = _random_graph(g, n, n_edges, hub=3, isolated=(n - 1, n - 2))
     E = row.numel()
     torch.manual_seed(seed)
-    layer = ref.E_GCL(hidden, hidden, hidden, edges_in_d=edges_in_d, **flags).double()
-    h = torch.randn(n, hidden, generator=g, dtype=torch.float64).requires_grad_(True)
+    layer = ref.E_GCL(input_nf, output_nf, hidden, edges_in_d=edges_in_d, **flags).double()
+    h = torch.randn(n, input_nf, generator=g, dtype=torch.float64).requires_grad_(True)
     x = (torch.randn(n, 3, generator=g, dtype=torch.float64) * 1.5).requires_grad_(True)
     ea = torch.randn(E, edges_in_d, generator=g, dtype=torch.float64) if edges_in_d else None
-    gh = torch.randn(n, hidden, generator=g, dtype=torch.float64)
+    gh = torch.randn(n, output_nf, generator=g, dtype=torch.float64)
     gx = torch.randn(n, 3, generator=g, dtype=torch.float64)
     ho, xo, _ = layer(h, [row, col], x, edge_attr=ea)
     torch.autograd.backward([ho, xo], [gh, gx])
-    return dict(kind="layer", hidden=hidden, edges_in_d=edges_in_d, flags=flags,
+    return dict(kind="layer", hidden=hidden, input_nf=input_nf, output_nf=output_nf,
+                edges_in_d=edges_in_d, flags=flags,
                 h=h.detach(), x=x.detach(), row=row, col=col, edge_attr=ea, gh=gh, gx=gx,
                 state_dict={k: v.clone() for k, v in layer.state_dict().items()},
                 h_out=ho.detach(), x_out=xo.detach(), grads=_grads(layer),
@@ -122,6 +126,11 @@ CASES = {
                                                       tanh=True, coords_agg="sum"),
     "model_attention_molecules": lambda r: case_model(r, "model_attention_molecules", 7, 5, 3, 7, 32, 2,
                                                       attention=True),
+    # E_GCL with input_nf / output_nf other than hidden_nf (egnn_clean.py:11-31)
+    "layer_dims_i16_o8_h32": lambda r: case_layer(r, "layer_dims_i16_o8_h32", 8, 40, 160, 32, edges_in_d=2,
+                                                  input_nf=16, output_nf=8, residual=False),
+    "layer_dims_i12_h64": lambda r: case_layer(r, "layer_dims_i12_h64", 9, 48, 200, 64, input_nf=12,
+                                               output_nf=12, attention=True),
 }
 
 

@@ -123,11 +123,38 @@ def test_state_dict_names_and_seeded_init_match_reference():
     m.load_state_dict({k: v.float() for k, v in c["state_dict"].items()})
 
 
+@pytest.mark.parametrize("name", ["layer_dims_i16_o8_h32", "layer_dims_i12_h64"])
+def test_other_input_output_widths_match_reference_shapes_and_init(name):
+    """E_GCL(input_nf, output_nf, hidden_nf) with widths other than hidden_nf:
+    the same parameter names, shapes and seeded initial values as the
+    reference module the fixture was made from."""
+    c = load_golden(name)
+    torch.manual_seed(int(c["name"] == "layer_dims_i12_h64") + 8)   # the fixtures' seeds: 8, 9
+    layer = E_GCL(c["input_nf"], c["output_nf"], c["hidden"], edges_in_d=c["edges_in_d"], **c["flags"])
+    sd = layer.state_dict()
+    assert list(sd) == list(c["state_dict"])
+    for k, v in sd.items():
+        assert torch.equal(v.double(), c["state_dict"][k]), k
+
+
+def test_widths_in_the_layer_descriptor():
+    lib = nat.lib()
+    same = nat.LayerDesc(1000, 20000, 64, 0, 0, nat.PREC_FP32)
+    wide = nat.LayerDesc(1000, 20000, 64, 0, 0, nat.PREC_FP32, 200, 300)
+    assert lib.egnn_workspace_size(C.byref(wide), nat.WS_BWD, 148) > lib.egnn_workspace_size(
+        C.byref(same), nat.WS_BWD, 148)
+    # the residual needs input_nf == output_nf; widths above 1024 are not built
+    for d in [nat.LayerDesc(10, 10, 64, 0, nat.FLAG_RESIDUAL, 0, 16, 8),
+              nat.LayerDesc(10, 10, 64, 0, 0, 0, 2000, 8)]:
+        assert lib.egnn_workspace_size(C.byref(d), nat.WS_FWD, 148) == 0
+    layer = E_GCL(16, 8, 32)       # residual=True by default, as in the reference
+    with pytest.raises(NotImplementedError, match="input_nf == output_nf"):
+        layer(torch.zeros(4, 16), [torch.tensor([0]), torch.tensor([1])], torch.zeros(4, 3))
+
+
 def test_e_gcl_signature_guards():
     with pytest.raises(NotImplementedError):
         E_GCL(32, 32, 32, act_fn=nn.ReLU())
-    with pytest.raises(NotImplementedError):
-        E_GCL(16, 32, 32)
     with pytest.raises(Exception):
         E_GCL(32, 32, 32, coords_agg="max")
     with pytest.raises(ValueError):
@@ -155,7 +182,7 @@ def test_flag_bits_match_header():
                       ("EGNN_FLAG_NORMALIZE", nat.FLAG_NORMALIZE), ("EGNN_FLAG_TANH", nat.FLAG_TANH),
                       ("EGNN_FLAG_COORDS_SUM", nat.FLAG_COORDS_SUM)]:
         assert re.search(rf"{name}\s*=\s*{val}\b", text), name
-    assert len(nat.LayerDesc._fields_) == 6 and C.sizeof(nat.LayerDesc) == 32
+    assert len(nat.LayerDesc._fields_) == 8 and C.sizeof(nat.LayerDesc) == 40
     assert C.sizeof(nat.Graph) == 6 * 8
     assert C.sizeof(nat.LayerParams) == 13 * 8
 

@@ -27,8 +27,9 @@ pytestmark = pytest.mark.gpu
 TOL = {"fp32": 1e-5, "bf16": 2e-2}
 
 
-def _layer_from_state(sd, hidden, precision, dev, edges_in_d=0, **flags):
-    layer = E_GCL(hidden, hidden, hidden, edges_in_d=edges_in_d, precision=precision, **flags).to(dev)
+def _layer_from_state(sd, hidden, precision, dev, edges_in_d=0, input_nf=None, output_nf=None, **flags):
+    layer = E_GCL(input_nf or hidden, output_nf or hidden, hidden, edges_in_d=edges_in_d, precision=precision,
+                  **flags).to(dev)
     layer.load_state_dict({k: v.float() for k, v in sd.items()})
     return layer
 
@@ -62,7 +63,8 @@ def test_golden_fixture_fp32(name, cuda_device):
     dev = cuda_device
     if c["kind"] == "layer":
         flags = dict(c.get("flags", {}))
-        layer = _layer_from_state(c["state_dict"], c["hidden"], "fp32", dev, c["edges_in_d"], **flags)
+        layer = _layer_from_state(c["state_dict"], c["hidden"], "fp32", dev, c["edges_in_d"],
+                                  c.get("input_nf"), c.get("output_nf"), **flags)
         csr = CSR.from_edges(c["row"], c["col"], n_nodes=c["h"].shape[0], device=dev)
         ea = c["edge_attr"].float().to(dev) if c["edge_attr"] is not None else None
         res = _run_layer(layer, c["h"].float().to(dev), c["x"].float().to(dev), csr,
@@ -174,6 +176,51 @@ def test_layer_matches_oracle(H, precision, N, E, d, flags, cuda_device):
                      gx.float().to(dev), ea.float().to(dev) if ea is not None else None)
     got, refd = as_dict(res), as_dict(ref)
     what = f"H={H} {precision} d={d} {flags}"
+    if precision == "fp32":
+        check_tensors(got, refd, _fp32_tol(p, h, row, col, x, gh, gx, ea, ref, flags), what)
+        return
+    emu = as_dict(EM.layer_fwd_bwd(p, h, row, col, x, gh, gx, ea, precision="bf16", **flags))
+    check_bf16(got, refd, emu, what)
+
+
+# E_GCL(input_nf, output_nf, hidden_nf) with input_nf / output_nf other than
+# hidden_nf (egnn_clean.py:11-31; EGNN itself always builds them equal)
+DIM_CASES = [
+    # (input_nf, output_nf, H, precision, N, E, edges_in_d, flags)
+    (16, 16, 128, "bf16", 1500, 30000, 0, {}),                          # fused tensor-core edge kernels
+    (40, 7, 256, "bf16", 600, 12000, 0, {"residual": False}),           # edge-row GEMMs
+    (5, 1, 64, "fp32", 500, 8000, 0, {"residual": False}),
+    (128, 32, 128, "fp32", 400, 6000, 2, {"residual": False, "attention": True}),
+    (20, 20, 32, "bf16", 300, 4000, 0, {"normalize": True}),
+    (3, 3, 128, "fp32", 700, 9000, 0, {"coords_agg": "sum"}),
+]
+
+
+@pytest.mark.parametrize("nin,nout,H,precision,N,E,d,flags", DIM_CASES)
+def test_layer_with_other_input_output_widths(nin, nout, H, precision, N, E, d, flags, cuda_device):
+    dev = cuda_device
+    seed = nin * 31 + nout * 7 + H
+    g = torch.Generator().manual_seed(seed)
+    row = torch.randint(0, N, (E,), generator=g)
+    col = torch.randint(0, N, (E,), generator=g)
+    row[: E // 3] = 0
+    torch.manual_seed(seed)
+    cpu_layer = E_GCL(nin, nout, H, edges_in_d=d, **flags)      # the reference's shapes and init order
+    p = {k: v.detach().double() for k, v in cpu_layer.state_dict().items()}
+    p["coord_mlp.2.weight"] = p["coord_mlp.2.weight"] * 300.0
+    h = torch.randn(N, nin, generator=g, dtype=torch.float64)
+    x = torch.randn(N, 3, generator=g, dtype=torch.float64) * 1.5
+    ea = torch.randn(E, d, generator=g, dtype=torch.float64) if d else None
+    gh = torch.randn(N, nout, generator=g, dtype=torch.float64)
+    gx = torch.randn(N, 3, generator=g, dtype=torch.float64)
+    ref = O.layer_grads(p, "", h, row, col, x, gh, gx, ea, **flags)
+    layer = _layer_from_state(p, H, precision, dev, d, nin, nout, **flags)
+    csr = CSR.from_edges(row, col, n_nodes=N, device=dev)
+    res = _run_layer(layer, h.float().to(dev), x.float().to(dev), csr, gh.float().to(dev),
+                     gx.float().to(dev), ea.float().to(dev) if ea is not None else None)
+    assert res[0].shape == (N, nout) and res[2].shape == (N, nin)
+    got, refd = as_dict(res), as_dict(ref)
+    what = f"in={nin} out={nout} H={H} {precision} d={d} {flags}"
     if precision == "fp32":
         check_tensors(got, refd, _fp32_tol(p, h, row, col, x, gh, gx, ea, ref, flags), what)
         return

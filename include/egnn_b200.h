@@ -248,6 +248,28 @@ EGNN_API int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, const
                    float* grad_h, float* grad_x, const egnn_layer_grads* gp,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- graph-level loss of the training step ----------------------------- */
+
+/* The benchmark objective around EGNN.forward (egnn_clean.py:141-146): the
+ * per-graph sum of one node value (h_out[:, 0]) regressed on one target per
+ * graph.  Graphs are contiguous node ranges: graph g holds nodes
+ * graph_ptr[g] .. graph_ptr[g+1]-1 (graph_ptr: G+1 int64 offsets, 0 .. N).
+ *   pred_g = sum_{i in g} values[i * ld],  loss = (1/G) sum_g (pred_g - target_g)^2
+ * Deterministic: every sum is added in a fixed order (bit-identical reruns).
+ * A malformed graph_ptr gives wrong sums, never an out-of-range access. */
+EGNN_API size_t egnn_graph_mse_workspace_size(int64_t n_nodes);
+
+/* Writes pred (G floats) and *loss (device). */
+EGNN_API int egnn_graph_mse_fwd(int64_t n_nodes, int64_t n_graphs, const float* values, int64_t ld,
+                                const int64_t* graph_ptr, const float* target, float* pred, float* loss,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* grad_values[i * ld] = grad_loss[0] * 2 (pred_g - target_g) / G for node i of
+ * graph g (grad_loss: one device float). */
+EGNN_API int egnn_graph_mse_bwd(int64_t n_nodes, int64_t n_graphs, const int64_t* graph_ptr, const float* pred,
+                                const float* target, const float* grad_loss, float* grad_values, int64_t ld,
+                                void* stream);
+
 /* ---- node linear (embedding_in / embedding_out, egnn_clean.py:133-134) --- */
 
 /* y (M,O) = x (M,K) W^T + b  (b may be NULL). */

@@ -105,6 +105,9 @@ _SIGNATURES = {
     "egnn_layer_bwd": (C.c_int, [C.POINTER(LayerDesc), C.POINTER(Graph), C.POINTER(LayerParams),
                                  VP, VP, VP, VP, VP, VP, VP, VP, C.POINTER(LayerGrads), VP,
                                  C.c_size_t, VP]),
+    "egnn_graph_mse_workspace_size": (C.c_size_t, [C.c_int64]),
+    "egnn_graph_mse_fwd": (C.c_int, [C.c_int64, C.c_int64, VP, C.c_int64, VP, VP, VP, VP, VP, C.c_size_t, VP]),
+    "egnn_graph_mse_bwd": (C.c_int, [C.c_int64, C.c_int64, VP, VP, VP, VP, VP, C.c_int64, VP]),
     "egnn_linear_fwd": (C.c_int, [C.c_int64, C.c_int32, C.c_int32, VP, VP, VP, VP, VP]),
     "egnn_linear_workspace_size": (C.c_size_t, [C.c_int64, C.c_int32, C.c_int32]),
     "egnn_linear_bwd": (C.c_int, [C.c_int64, C.c_int32, C.c_int32, VP, VP, VP, VP, VP, VP, VP,

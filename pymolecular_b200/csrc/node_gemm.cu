@@ -240,78 +240,39 @@ __global__ void linear_n1_kernel(int64_t M, int K, const float* __restrict__ x, 
 // ---- weight gradients with one narrow side (the embeddings) -----------------------
 // dW (M x N) = sum_r G[r][i] X[r][j] and db (M) = sum_r G[r][i], computed as
 // one product with X extended by a column of ones (db = its last column).
-// Block z sums rows [z rows_per, ...): warp w takes every 8th row from w, a
-// lane owns the wide indices lane + 32 t and every narrow one; warp
-// partials are added in warp order, then the block slices in block order.
-constexpr int kNarrow = 9;            // narrow side incl. the ones column
+// The wide side (max(M, N + 1) <= 288) runs over the lanes, the narrow side
+// (min(M, N + 1) <= 45) in groups of 9, one group per grid row.  Block z
+// streams rows [z rows_per, ...) through a ring of shared-memory stages of 32
+// rows filled by cp.async two stages ahead; warp w takes rows w, w + 8,
+// w + 16, w + 24 of every stage (each warp adds its rows in row order), a lane
+// owns the wide indices lane + 32 t; warp partials are added in warp order,
+// then the block slices in block order (wgrad_small_reduce_kernel).
+constexpr int kNarrow = 9;            // narrow indices per group
+constexpr int kNarrowMax = 45;        // narrow side incl. the ones column: 5 groups
 constexpr int kWideSlots = 9;         // wide side up to 288 (with the ones column)
-constexpr int kSmallOut = 1040;       // M (N + 1) outputs at most
+constexpr int kStageRows = 32, kStages = 3;
 
-__device__ __forceinline__ float ext_at(const Mat& X, int N, int64_t r, int j) {
-  return j < N ? X.at(r, j) : 1.f;
-}
-
-__global__ void __launch_bounds__(256) wgrad_small_partial_kernel(int64_t R, int M, int N, Mat G, Mat X,
-                                                                  int64_t rows_per, float* part) {
-  pdl_enter();
-  __shared__ float red[8][kSmallOut];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+struct SmallShape {
+  int lanes_n;     // lanes over the extended columns of X (else over the rows i of dW)
+  int wide, narrow;
+  int wide_data;   // staged wide values (the ones column is implied)
+  int groups, slots;
+};
+__host__ __device__ inline SmallShape small_shape(int M, int N) {
+  SmallShape s;
   const int N1 = N + 1;
-  const bool lanes_n = N1 >= M;            // lanes over the extended columns, else over the rows i
-  const int wide = lanes_n ? N1 : M, narrow = lanes_n ? M : N1;
-  float acc[kWideSlots][kNarrow];
-#pragma unroll
-  for (int t = 0; t < kWideSlots; ++t)
-#pragma unroll
-    for (int q = 0; q < kNarrow; ++q) acc[t][q] = 0.f;
-  const int64_t r0 = (int64_t)blockIdx.x * rows_per, r1 = min(R, r0 + rows_per);
-  // rows r and r + 8 of the warp per iteration: both rows' loads in flight
-  // before the first product (the products are added in row order, as one
-  // row per iteration would add them)
-  for (int64_t r = r0 + warp; r < r1; r += 16) {
-    float wv[2][kWideSlots], nv[2][kNarrow];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int64_t ru = r + 8 * u;
-      const bool live = ru < r1;
-#pragma unroll
-      for (int t = 0; t < kWideSlots; ++t) {
-        const int w = lane + 32 * t;
-        wv[u][t] = (live && w < wide) ? (lanes_n ? ext_at(X, N, ru, w) : G.at(ru, w)) : 0.f;
-      }
-#pragma unroll
-      for (int q = 0; q < kNarrow; ++q)
-        nv[u][q] = (live && q < narrow) ? (lanes_n ? G.at(ru, q) : ext_at(X, N, ru, q)) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      if (r + 8 * u >= r1) break;
-#pragma unroll
-      for (int t = 0; t < kWideSlots; ++t)
-#pragma unroll
-        for (int q = 0; q < kNarrow; ++q)
-          acc[t][q] = lanes_n ? fmaf(nv[u][q], wv[u][t], acc[t][q]) : fmaf(wv[u][t], nv[u][q], acc[t][q]);
-    }
-  }
-#pragma unroll
-  for (int t = 0; t < kWideSlots; ++t) {
-    const int w = lane + 32 * t;
-    if (w >= wide) continue;
-#pragma unroll
-    for (int q = 0; q < kNarrow; ++q) {
-      if (q >= narrow) continue;
-      const int i = lanes_n ? q : w, j = lanes_n ? w : q;
-      red[warp][i * N1 + j] = acc[t][q];
-    }
-  }
-  __syncthreads();
-  const int O = M * N1;
-  for (int o = threadIdx.x; o < O; o += blockDim.x) {
-    float v = red[0][o];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) v += red[w][o];
-    part[(int64_t)blockIdx.x * O + o] = v;
-  }
+  s.lanes_n = N1 >= M;
+  s.wide = s.lanes_n ? N1 : M;
+  s.narrow = s.lanes_n ? M : N1;
+  s.wide_data = s.lanes_n ? N : M;
+  s.groups = (s.narrow + kNarrow - 1) / kNarrow;
+  s.slots = (s.wide + 31) / 32;
+  return s;
+}
+size_t small_smem_bytes(int slots) {
+  const size_t ring = (size_t)kStages * kStageRows * (32 * slots + kNarrow) * 4;
+  const size_t red = (size_t)8 * 32 * slots * kNarrow * 4;
+  return std::max(ring, red);
 }
 
 __global__ void wgrad_small_reduce_kernel(int M, int N, int S, const float* part, float* dW, int64_t lddw,
@@ -361,6 +322,120 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 __device__ __forceinline__ const float* mat_ptr(const Mat& A, int64_t r, int64_t c) {
   if (A.split_rows) return r < A.split ? A.p0 + r * A.ld0 + c : A.p1 + (r - A.split) * A.ld1 + c;
   return c < A.split ? A.p0 + r * A.ld0 + c : A.p1 + r * A.ld1 + (c - A.split);
+}
+
+// Zero-filling 4-byte asynchronous copy (any alignment).
+__device__ __forceinline__ void cp_async4z(float* dst, const float* src, bool ok) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sptr(dst)), "l"(src), "r"(ok ? 4 : 0)
+               : "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait_n() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <int WS>
+__global__ void __launch_bounds__(256) wgrad_small_partial_kernel(int64_t R, int M, int N, Mat G, Mat X,
+                                                                  int64_t rows_per, int vec_w, float* part) {
+  pdl_enter();
+  extern __shared__ __align__(16) float wsm[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const SmallShape sh = small_shape(M, N);
+  const int N1 = N + 1;
+  const int q0 = blockIdx.y * kNarrow;                 // first narrow index of this group
+  const int nq = min(kNarrow, sh.narrow - q0);
+  constexpr int LDW = 32 * WS;                         // staged wide row (floats)
+  float* ring_w = wsm;                                 // [kStages][kStageRows][LDW]
+  float* ring_n = wsm + kStages * kStageRows * LDW;    // [kStages][kStageRows][kNarrow]
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per, r1 = min(R, r0 + rows_per);
+  const int64_t nrows = r1 > r0 ? r1 - r0 : 0;
+  const int nstage = (int)((nrows + kStageRows - 1) / kStageRows);
+  const Mat& Wm = sh.lanes_n ? X : G;                  // wide operand
+  const Mat& Nm = sh.lanes_n ? G : X;                  // narrow operand
+  const int narrow_data = sh.lanes_n ? M : N;          // narrow index N of X is the ones column
+
+  auto issue = [&](int st) {
+    if (st < nstage) {
+      float* dw = ring_w + (st % kStages) * kStageRows * LDW;
+      float* dn = ring_n + (st % kStages) * kStageRows * kNarrow;
+      const int64_t rs = r0 + (int64_t)st * kStageRows;
+      if (vec_w) {   // aligned rows, wide_data % 4 == 0: 16-byte words
+        const int words = sh.wide_data / 4;
+        for (int c = threadIdx.x; c < kStageRows * words; c += 256) {
+          const int rl = c / words, w4 = (c % words) * 4;
+          const int64_t r = rs + rl;
+          const bool ok = r < r1;
+          cp_async16(dw + rl * LDW + w4, ok ? mat_ptr(Wm, r, w4) : Wm.p0, ok);
+        }
+      } else {
+        for (int c = threadIdx.x; c < kStageRows * sh.wide_data; c += 256) {
+          const int rl = c / sh.wide_data, w = c % sh.wide_data;
+          const int64_t r = rs + rl;
+          const bool ok = r < r1;
+          cp_async4z(dw + rl * LDW + w, ok ? mat_ptr(Wm, r, w) : Wm.p0, ok);
+        }
+      }
+      for (int c = threadIdx.x; c < kStageRows * nq; c += 256) {
+        const int rl = c / nq, q = c % nq, j = q0 + q;
+        const int64_t r = rs + rl;
+        const bool ok = r < r1 && j < narrow_data;
+        cp_async4z(dn + rl * kNarrow + q, ok ? mat_ptr(Nm, r, j) : Nm.p0, ok);
+      }
+    }
+    cp_async_commit();   // empty groups keep the count uniform
+  };
+
+  float acc[WS][kNarrow];
+#pragma unroll
+  for (int t = 0; t < WS; ++t)
+#pragma unroll
+    for (int q = 0; q < kNarrow; ++q) acc[t][q] = 0.f;
+#pragma unroll
+  for (int p = 0; p < kStages - 1; ++p) issue(p);
+#pragma unroll 1
+  for (int st = 0; st < nstage; ++st) {
+    cp_async_wait_n<kStages - 2>();   // this thread's copies of stage st have landed
+    __syncthreads();                  // everyone's have; stage st - 1 is consumed
+    issue(st + kStages - 1);
+    const float* sw = ring_w + (st % kStages) * kStageRows * LDW;
+    const float* sn = ring_n + (st % kStages) * kStageRows * kNarrow;
+    const int64_t left = r1 - (r0 + (int64_t)st * kStageRows);
+    const int live = left < kStageRows ? (int)left : kStageRows;
+#pragma unroll 1
+    for (int u = 0; u < kStageRows / 8; ++u) {
+      const int rl = warp + 8 * u;
+      if (rl >= live) break;
+      float wv[WS], nv[kNarrow];
+#pragma unroll
+      for (int t = 0; t < WS; ++t) {
+        const int w = lane + 32 * t;
+        wv[t] = w < sh.wide_data ? sw[rl * LDW + w] : (w < sh.wide ? 1.f : 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < kNarrow; ++q) nv[q] = q < nq ? (q0 + q < narrow_data ? sn[rl * kNarrow + q] : 1.f) : 0.f;
+#pragma unroll
+      for (int t = 0; t < WS; ++t)
+#pragma unroll
+        for (int q = 0; q < kNarrow; ++q) acc[t][q] = fmaf(wv[t], nv[q], acc[t][q]);
+    }
+  }
+  cp_async_wait_n<0>();
+  __syncthreads();   // the ring is free for the warp partials
+  float* red = wsm;  // [8 warps][32 WS wide][kNarrow]
+  constexpr int PER = 32 * WS * kNarrow;
+#pragma unroll
+  for (int t = 0; t < WS; ++t)
+#pragma unroll
+    for (int q = 0; q < kNarrow; ++q) red[warp * PER + (t * 32 + lane) * kNarrow + q] = acc[t][q];
+  __syncthreads();
+  for (int o = threadIdx.x; o < PER; o += 256) {
+    const int wi = o / kNarrow, q = o % kNarrow;
+    if (wi >= sh.wide || q >= nq) continue;
+    float v = red[o];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) v += red[w * PER + o];
+    const int ni = q0 + q;
+    const int i = sh.lanes_n ? ni : wi, j = sh.lanes_n ? wi : ni;
+    part[(int64_t)blockIdx.x * M * N1 + (int64_t)i * N1 + j] = v;
+  }
 }
 
 __device__ __forceinline__ void thread_grid(int& tx, int& ty) {
@@ -683,16 +758,40 @@ int gemm_reduce(const GemmArgs& a_in, cudaStream_t s) {
   return EGNN_OK;
 }
 
+bool wgrad_small_ok(int64_t M, int64_t N) {
+  const int64_t n1 = N + 1;
+  return M >= 1 && std::min(M, n1) <= kNarrowMax && std::max(M, n1) <= 32 * kWideSlots;
+}
+
+// Row slices of a weight gradient: for the narrow-side kernel about two
+// blocks per SM over all narrow groups with at least 256 rows each, for the
+// split-K GEMM about one wave of tiles with at least 128 rows each.
 int64_t wgrad_splits(int64_t K, int64_t M, int64_t N) {
+  if (wgrad_small_ok(M, N)) {
+    const SmallShape sh = small_shape((int)M, (int)N);
+    return std::max<int64_t>(1, std::min<int64_t>(K / 256, std::max(1, 296 / sh.groups)));
+  }
   int64_t tiles = ((M + 63) / 64) * ((N + 127) / 128);
   int64_t want = (148 + tiles - 1) / tiles;               // about one wave of CTAs
   int64_t by_len = std::max<int64_t>(1, K / 128);         // at least 128 rows per slice
   return std::max<int64_t>(1, std::min<int64_t>({want, by_len, 64}));
 }
 
-bool wgrad_small_ok(int64_t M, int64_t N) {
-  const int64_t n1 = N + 1;
-  return std::min(M, n1) <= kNarrow && std::max(M, n1) <= 32 * kWideSlots && M * n1 <= kSmallOut;
+template <int WS>
+int launch_small(int64_t R, int M, int N, const Mat& G, const Mat& X, int64_t S, int64_t rows_per, int vec_w,
+                 float* part, cudaStream_t s) {
+  static uint64_t attr_set = 0;
+  const size_t bytes = small_smem_bytes(WS);
+  const uint64_t bit = device_bit();
+  if (!(attr_set & bit)) {
+    EGNN_CHECK_CUDA(cudaFuncSetAttribute(wgrad_small_partial_kernel<WS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)bytes));
+    attr_set |= bit;
+  }
+  const dim3 grid((unsigned)S, (unsigned)small_shape(M, N).groups);
+  EGNN_CHECK_CUDA(launch_pdl(wgrad_small_partial_kernel<WS>, grid, dim3(256), bytes, s, R, M, N, G, X, rows_per,
+                             vec_w, part));
+  return EGNN_OK;
 }
 
 int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw,
@@ -702,9 +801,21 @@ int wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t lddw
     // (S (M N + M) floats) holds the slices
     const int64_t S = wgrad_splits(R, M, N);
     const int64_t rows_per = (R + S - 1) / S;
+    const SmallShape sh = small_shape((int)M, (int)N);
+    const Mat& Wm = sh.lanes_n ? X : G;
+    const int vec_w = (sh.wide_data % 4 == 0 && !Wm.split_rows && !Wm.p1 && aligned16(Wm.p0) && Wm.ld0 % 4 == 0);
     TimerScope ts("wgrad_small", s);
-    EGNN_CHECK_CUDA(launch_pdl(wgrad_small_partial_kernel, dim3((unsigned)S), dim3(256), 0, s, R, (int)M, (int)N, G,
-                               X, rows_per, part));
+    switch (sh.slots) {
+      case 1: EGNN_TRY(launch_small<1>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      case 2: EGNN_TRY(launch_small<2>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      case 3: EGNN_TRY(launch_small<3>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      case 4: EGNN_TRY(launch_small<4>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      case 5: EGNN_TRY(launch_small<5>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      case 6: EGNN_TRY(launch_small<6>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      case 7: EGNN_TRY(launch_small<7>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      case 8: EGNN_TRY(launch_small<8>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+      default: EGNN_TRY(launch_small<9>(R, (int)M, (int)N, G, X, S, rows_per, vec_w, part, s)); break;
+    }
     EGNN_CHECK_LAUNCH();
     const int O = (int)(M * (N + 1));
     EGNN_CHECK_CUDA(launch_pdl(wgrad_small_reduce_kernel, dim3((unsigned)((O + 255) / 256)), dim3(256), 0, s, (int)M,

@@ -13,7 +13,12 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("m,k,o", [(1000, 64, 128), (777, 96, 256), (10000, 128, 32), (9939, 5, 128),
                                    (4097, 128, 1), (130, 256, 128), (33, 40, 64), (300, 1, 7), (5000, 8, 1),
-                                   (65, 3, 300)])
+                                   (65, 3, 300),
+                                   # weight gradients with one narrow side at many stages of rows: the
+                                   # embeddings of configs 3-5 (narrow groups of 9, 16-byte and 4-byte
+                                   # staging of the wide side)
+                                   (200000, 16, 128), (300000, 128, 1), (50000, 40, 256), (20000, 20, 128),
+                                   (7000, 44, 100), (7000, 44, 99)])
 def test_linear_fwd_bwd_fp32_accuracy(m, k, o, cuda_device):
     g = torch.Generator(device=cuda_device).manual_seed(m + k + o)
     x = torch.randn(m, k, device=cuda_device, generator=g)

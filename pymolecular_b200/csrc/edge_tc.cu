@@ -8,7 +8,10 @@
 //
 //   forward  u1 = silu(P_i + Q_j + w_r r)        CUDA cores -> bf16 tile U
 //            a2 = U W2hi^T + U W2lo^T             tcgen05 -> TMEM
+//            (edge attributes: a1 += We attr[edge_id], forward only)
 //            m  = silu(a2 + b2)                   -> bf16 tile M, fp32 staging
+//                 [attention: m *= sigmoid(wa . m + ba), the dot over the
+//                  four column slices of the edge's row]
 //            c1 = M Wc1^T                         tcgen05 -> TMEM
 //            phi = wc2 . silu(c1 + bc1)           per thread
 //            agg, x' : row walk over the staging (as in the SIMT kernel)
@@ -204,14 +207,19 @@ __device__ __forceinline__ void gather_a1(float4* stage, const float* __restrict
 // Forward variant: u1 = silu(a1) rounded to bf16 straight into row e of the
 // SW128 tile U (lane = features 4 lane .. + 3, one 8-byte store); invalid
 // edges get zero rows.  Same arithmetic and rounding as staging a1 first.
+// Edge attributes (d > 0): a1 += We a_e with a_e = attr[edge_id] (lane k < d
+// loads feature k, broadcast by shuffles) and s_WeT[k][f] = We[f][k].
 template <int GB>
 __device__ __forceinline__ void gather_u(char* Ut, const float* __restrict__ PQ, const int* rows, const int* cols,
-                                         const float4* geo, const float* s_wr, int n, int warp, int lane) {
+                                         const float4* geo, const float* s_wr, int n, int warp, int lane,
+                                         const float* __restrict__ attr, const int* eids, const float* s_WeT,
+                                         int d) {
   constexpr int H = 128;
   const float4 wr4 = *reinterpret_cast<const float4*>(s_wr + 4 * lane);
 #pragma unroll
   for (int b = 0; b < 8; b += GB) {
     float4 p[GB], q[GB];
+    float av[GB];
 #pragma unroll
     for (int t = 0; t < GB; ++t) {
       const int e = warp * 8 + b + t;
@@ -221,17 +229,24 @@ __device__ __forceinline__ void gather_u(char* Ut, const float* __restrict__ PQ,
       } else {
         p[t] = q[t] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      av[t] = (d > 0 && e < n && lane < d) ? __ldg(attr + (int64_t)eids[e] * d + lane) : 0.f;
     }
 #pragma unroll
     for (int t = 0; t < GB; ++t) {
       const int e = warp * 8 + b + t;
       float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
+      float4 x4 = make_float4(p[t].x + q[t].x, p[t].y + q[t].y, p[t].z + q[t].z, p[t].w + q[t].w);
+      for (int k = 0; k < d; ++k) {   // uniform trip count: every lane takes part in the shuffles
+        const float ak = __shfl_sync(0xffffffffu, av[t], k);
+        const float4 w = *reinterpret_cast<const float4*>(s_WeT + k * H + 4 * lane);
+        x4 = make_float4(fmaf(w.x, ak, x4.x), fmaf(w.y, ak, x4.y), fmaf(w.z, ak, x4.z), fmaf(w.w, ak, x4.w));
+      }
       if (e < n) {
         const float r = geo[e].w;
-        u0 = silu_edge(fmaf(wr4.x, r, p[t].x + q[t].x));
-        u1 = silu_edge(fmaf(wr4.y, r, p[t].y + q[t].y));
-        u2 = silu_edge(fmaf(wr4.z, r, p[t].z + q[t].z));
-        u3 = silu_edge(fmaf(wr4.w, r, p[t].w + q[t].w));
+        u0 = silu_edge(fmaf(wr4.x, r, x4.x));
+        u1 = silu_edge(fmaf(wr4.y, r, x4.y));
+        u2 = silu_edge(fmaf(wr4.z, r, x4.z));
+        u3 = silu_edge(fmaf(wr4.w, r, x4.w));
       }
       const __nv_bfloat162 h01 = __floats2bfloat162_rn(u0, u1);
       const __nv_bfloat162 h23 = __floats2bfloat162_rn(u2, u3);
@@ -273,8 +288,8 @@ struct FwdLayout {
   static constexpr size_t U = WC1 + TC<H>::WT;         // u1, then bf16(m - bf16(m))
   static constexpr size_t M = U + TC<H>::TILE;
   static constexpr size_t S = M + TC<H>::TILE;         // 0/1 segment matrix [slot][edge]
-  static constexpr size_t VEC = S + TC<H>::TILE;       // wr, b2, bc1, wc2
-  static constexpr size_t PART = VEC + 4 * H * 4;      // float[4][128]
+  static constexpr size_t VEC = S + TC<H>::TILE;       // wr, b2, bc1, wc2, wa
+  static constexpr size_t PART = VEC + 5 * H * 4;      // float[4][128]
   static constexpr size_t DL = PART + 4 * kM * 4;      // float4[128]: dn.xyz, r
   static constexpr size_t SEGX = DL + kM * 16;         // float4[128]: coordinate sums per segment
   static constexpr size_t NXI = SEGX + kM * 16;        // float4[128]: next chunk's x_i (prefetch)
@@ -288,7 +303,9 @@ struct FwdLayout {
   static constexpr size_t SEGSTART = SEGROW + (kM + 4) * 4;
   static constexpr size_t SEGRP = SEGSTART + (kM + 4) * 4;   // int[128][2]: row_ptr[r], row_ptr[r + 1] of segment rows
   static constexpr size_t XLI = SEGRP + kM * 8;        // float4[128]: x_i of each edge
-  static constexpr size_t OPEN = XLI + kM * 16;        // float[H + 4]
+  static constexpr size_t EIDL = XLI + kM * 16;        // int[128]: edge ids (edge attributes only)
+  static constexpr size_t WET = EIDL + kM * 4;         // float[16][H]: We^T (edge attributes only)
+  static constexpr size_t OPEN = WET + 16 * H * 4;     // float[H + 4]
   static constexpr size_t MISC = OPEN + (H + 4) * 4;   // ints: nseg, open_row, prev_row, warp counts[4]
   static constexpr size_t BAR = MISC + 64;
   static constexpr size_t END = BAR + 32;   // MMA barrier, TMEM base, index-tile barrier
@@ -312,6 +329,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
   float* s_b2 = s_wr + H;
   float* s_bc1 = s_b2 + H;
   float* s_wc2 = s_bc1 + H;
+  float* s_wa = s_wc2 + H;   // att_mlp.0.weight (attention only)
   float* part = reinterpret_cast<float*>(sm + L::PART);
   float4* dl = reinterpret_cast<float4*>(sm + L::DL);
   float4* segx = reinterpret_cast<float4*>(sm + L::SEGX);
@@ -326,6 +344,8 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
   int* segstart = reinterpret_cast<int*>(sm + L::SEGSTART);
   int* segrp = reinterpret_cast<int*>(sm + L::SEGRP);
   float4* xli = reinterpret_cast<float4*>(sm + L::XLI);
+  int* eidl = reinterpret_cast<int*>(sm + L::EIDL);
+  float* s_WeT = reinterpret_cast<float*>(sm + L::WET);
   float* open = reinterpret_cast<float*>(sm + L::OPEN);
   int* misc = reinterpret_cast<int*>(sm + L::MISC);   // [0] nseg [1] open_row [2] prev_row [4..7] warp counts
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
@@ -347,9 +367,13 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
   }
   load_weight_tile<H>(W2t, a.W2_src, W2lo);
   load_weight_tile<H>(Wc1t, a.Wc1_src);
+  const bool att = a.flags & EGNN_FLAG_ATTENTION;
   for (int c = g.tid; c < H; c += kNT) {
     s_wr[c] = a.wr[c]; s_b2[c] = a.b2[c]; s_bc1[c] = a.bc1[c]; s_wc2[c] = a.wc2[c];
+    s_wa[c] = att ? a.wa[c] : 0.f;
   }
+  for (int c = g.tid; c < H * a.d; c += kNT) s_WeT[(c % a.d) * H + c / a.d] = a.We[c];   // We is (H, d)
+  const float ba = att ? a.ba[0] : 0.f;
   pdl_enter();   // everything below reads the predecessor's output (P, Q) or writes
   const int cta = blockIdx.x, G = gridDim.x;
   const int64_t eb = std::min<int64_t>(a.E, (int64_t)cta * a.epc);
@@ -434,6 +458,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
         coll[g.e] = j;
         dl[g.e] = make_float4(dx * inv, dy * inv, dz * inv, r);
         xli[g.e] = xi;
+        if (a.d > 0) eidl[g.e] = a.edge_id[c0 + g.e];
       } else {
         rowl[g.e] = INT_MAX;
         coll[g.e] = 0;
@@ -447,7 +472,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
     }
     __syncthreads();
     // ---- u1 = silu(a1) rows -> tile U (coalesced P / Q rows, one warp per edge)
-    gather_u<4>(Ut, a.PQ, rowl, coll, dl, s_wr, n, g.warp, g.lane);
+    gather_u<4>(Ut, a.PQ, rowl, coll, dl, s_wr, n, g.warp, g.lane, a.attr, eidl, s_WeT, a.d);
     // ---- segments of the chunk (runs of equal destination rows)
     if (g.cg == 0) {
       const int r = rowl[g.e];
@@ -512,16 +537,24 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
       cp_async_commit_group();
     }
 
-    // ---- m = silu(a2 + b2) -> tiles M (bf16) and MLO (bf16 residual)
+    // ---- m = silu(a2 + b2) [* sigmoid(wa . m + ba)] -> tiles M (bf16) and MLO (bf16 residual)
     {
       float v[32], lo[32];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        const float m = silu_edge(v[q] + s_b2[g.col0 + q]);
-        v[q] = m;
-        lo[q] = m - __bfloat162float(__float2bfloat16_rn(m));
+      for (int q = 0; q < 32; ++q) v[q] = silu_edge(v[q] + s_b2[g.col0 + q]);
+      if (att) {   // the gate's dot product over the edge's four column slices (uniform branch)
+        float pa = 0.f;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) pa = fmaf(v[q], s_wa[g.col0 + q], pa);
+        part[g.cg * kM + g.e] = pa;
+        __syncthreads();
+        const float gate = sigmoidf_(part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e] + ba);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) v[q] *= gate;
       }
+#pragma unroll
+      for (int q = 0; q < 32; ++q) lo[q] = v[q] - __bfloat162float(__float2bfloat16_rn(v[q]));
       st_row32_bf16(Mt, g.e, g.col0, v);
       st_row32_bf16(Mlo, g.e, g.col0, lo);
     }
@@ -1202,8 +1235,13 @@ int launch_bwd_tc(const EdgeBwdArgs& a_in, int G, cudaStream_t s) {
 }  // namespace
 
 bool edge_tc_supported(int H, int d, int flags, int precision) {
-  // the attention gate runs on the SIMT kernels only
+  // the backward of the attention gate runs on the SIMT kernels: the ungated
+  // messages it needs would take TMEM columns the backward does not have
   return precision == EGNN_PREC_BF16 && H == 128 && d == 0 && !(flags & EGNN_FLAG_ATTENTION);
+}
+
+bool edge_tc_fwd_supported(int H, int d, int flags, int precision) {
+  return precision == EGNN_PREC_BF16 && H == 128 && d <= 16;
 }
 
 EdgeGrid edge_tc_grid(int64_t E, int num_sms) {

@@ -7,6 +7,8 @@ namespace egnn {
 
 // True when the tensor-core kernels cover this layer configuration.
 bool edge_tc_supported(int H, int d, int flags, int precision);
+// The forward also runs the attention gate and edge attributes (d <= 16).
+bool edge_tc_fwd_supported(int H, int d, int flags, int precision);
 
 // CTA count and edges per CTA (a multiple of the 128-edge chunk).
 EdgeGrid edge_tc_grid(int64_t E, int num_sms);

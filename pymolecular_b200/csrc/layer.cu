@@ -240,7 +240,7 @@ FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   FwdWs w;
   const bool rows = edge_rows_supported(H, d->edge_attr_dim, d->flags, d->precision);
   w.prep = carve_prep(c, N, H, in_dim(d), out_dim(d), d->edge_attr_dim, false,
-                      rows || edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
+                      rows || edge_tc_fwd_supported(H, d->edge_attr_dim, d->flags, d->precision));
   const int64_t G = max_ctas(E, H, num_sms);
   w.carry = c.take<float>((size_t)G * 2 * (H + 4));
   w.carry_row = c.take<int32_t>((size_t)G * 2);
@@ -466,7 +466,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   EGNN_TRY(gemm_pq(N, H, I, h, w.prep.WPQT, w.prep.bias2, sv.PQ, bf, s));
 
   const bool rows = edge_rows_supported(H, dd, d->flags, d->precision);
-  const bool tc = edge_tc_supported(H, dd, d->flags, d->precision);
+  const bool tc = edge_tc_fwd_supported(H, dd, d->flags, d->precision);
   EdgeGrid eg{1, 0};
   if (tc) eg = edge_tc_grid(E, sms);
   else if (!rows) EGNN_TRY(edge_grid(H, false, bf, E, sms, &eg));

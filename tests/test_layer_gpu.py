@@ -143,13 +143,16 @@ LAYER_CASES = [
     (64, "bf16", 500, 12000, 0, {}),
     (128, "bf16", 700, 20000, 0, {}),
     (256, "bf16", 400, 9000, 0, {}),
-    (128, "bf16", 300, 5000, 2, {"normalize": True}),
+    (128, "bf16", 300, 5000, 2, {"normalize": True}),            # tensor-core forward, SIMT backward
+    (128, "bf16", 2000, 40000, 16, {"attention": True, "tanh": True}),
     # attention gate (SIMT path for every H and precision)
     (32, "fp32", 300, 4000, 2, {"attention": True, "tanh": True}),
     (128, "fp32", 700, 20000, 0, {"attention": True}),
     (256, "fp32", 400, 9000, 0, {"attention": True, "normalize": True}),
     (64, "bf16", 500, 12000, 0, {"attention": True, "coords_agg": "sum"}),
-    (128, "bf16", 2000, 60000, 0, {"attention": True}),
+    (128, "bf16", 2000, 60000, 0, {"attention": True}),       # tensor-core forward, SIMT backward
+    (128, "bf16", 3000, 100000, 0, {"attention": True, "normalize": True, "tanh": True, "coords_agg": "sum",
+                                    "residual": False}),
     (256, "bf16", 400, 9000, 0, {"attention": True}),
     # tensor-core paths (bf16, no edge attributes): fused edge kernels at H = 128,
     # edge-row GEMMs at H = 256 (fewer edges than one tile; several tiles per CTA)

@@ -82,11 +82,33 @@ struct Prep {
   float* Wn2T;  // (H, O):     node_mlp.2.weight^T
   float* Wn1T;  // (I + H, H): node_mlp.0.weight^T
   float* WPQT;  // (I, 2H):    WPQ^T
+  // bf16 mode: the weight operands of the call's node GEMMs as split bf16
+  // tile images (forward: WPQT, Wn1T, Wn2T; backward: node_mlp.2.weight,
+  // node_mlp.0.weight, WPQ), built by prep_kernel
+  BImage img[3];
 };
+
+enum { IMG_WPQT = 0, IMG_WN1T = 1, IMG_WN2T = 2, IMG_NW2 = 3, IMG_NW1 = 4, IMG_WPQ = 5 };
+
+// Element (k, n) of the B operand an image holds (see Prep::img).
+__device__ __forceinline__ float image_src(int kind, int64_t k, int64_t n, const egnn_layer_params& p, int H, int I,
+                                           int64_t ld1) {
+  switch (kind) {
+    case IMG_WPQT: return n < H ? p.edge_w1[n * ld1 + k] : p.edge_w1[(n - H) * ld1 + I + k];
+    case IMG_WN1T: return p.node_w1[n * (I + H) + k];
+    case IMG_WN2T: return p.node_w2[n * H + k];
+    case IMG_NW2: return p.node_w2[k * H + n];
+    case IMG_NW1: return p.node_w1[k * (I + H) + n];
+    default: return k < H ? p.edge_w1[k * ld1 + n] : p.edge_w1[(k - H) * ld1 + I + n];
+  }
+}
+
+// 16-byte chunks (8 consecutive n) of the three images, in image order.
+__host__ __device__ inline int64_t image_chunks(const BImage& b) { return b.base ? b.nkc * 64 * b.nb * 8 : 0; }
 
 // `tc`: the tensor-core edge kernels read W2 and W_c1 as given, so the SIMT
 // kernels' transposed / rounded copies are not made.
-Prep carve_prep(Carver& c, int64_t N, int H, int I, int O, int d, bool bwd, bool tc) {
+Prep carve_prep(Carver& c, int64_t N, int H, int I, int O, int d, bool bwd, bool tc, bool bf) {
   Prep p{};
   p.xp = c.take<float4>(std::max<int64_t>(N, 1));
   p.bias2 = c.take<float>(2 * H);
@@ -100,6 +122,14 @@ Prep carve_prep(Carver& c, int64_t N, int H, int I, int O, int d, bool bwd, bool
   p.Wn2T = bwd ? nullptr : c.take<float>((size_t)H * O);
   p.Wn1T = bwd ? nullptr : c.take<float>((size_t)(I + H) * H);
   p.WPQT = bwd ? nullptr : c.take<float>((size_t)2 * H * I);
+  if (bf) {
+    const int64_t KN[3][2] = {{bwd ? O : I, bwd ? H : 2 * H}, {bwd ? H : I + H, bwd ? I + H : H},
+                              {bwd ? 2 * H : H, bwd ? I : O}};
+    for (int i = 0; i < 3; ++i) {
+      p.img[i] = bimage_shape(KN[i][0], KN[i][1]);
+      p.img[i].base = c.take<char>((size_t)p.img[i].bytes());
+    }
+  }
   return p;
 }
 
@@ -127,6 +157,39 @@ __host__ __device__ inline int64_t prep_total(int64_t N, int H, int I, int O, in
 __global__ void prep_kernel(int64_t N, int H, int I, int O, int d, int64_t ld1, int bf, egnn_layer_params p,
                             const float* x, Prep o) {
   pdl_enter();
+  // the split bf16 images of the node GEMMs' weight operands
+  {
+    const int kind0 = o.Wn2T ? IMG_WPQT : IMG_NW2;
+    const int64_t c0 = image_chunks(o.img[0]), c1 = image_chunks(o.img[1]), c2 = image_chunks(o.img[2]);
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < c0 + c1 + c2;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+      int which = 0;
+      int64_t t = idx;
+      if (t >= c0) { t -= c0; which = 1; if (t >= c1) { t -= c1; which = 2; } }
+      const BImage& b = o.img[which];
+      const int64_t k = t / (b.nb * 8), n0 = (t % (b.nb * 8)) * 8;
+      const int64_t kc = k >> 6, kr = k & 63, nb = n0 >> 6, nc = n0 & 63;
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int64_t n = n0 + 2 * q + u;
+          v[u] = (k < b.K && n < b.N) ? image_src(kind0 + which, k, n, p, H, I, ld1) : 0.f;
+        }
+        const __nv_bfloat162 hp = __floats2bfloat162_rn(v[0], v[1]);
+        const float2 hf = __bfloat1622float2(hp);
+        const __nv_bfloat162 lp = __floats2bfloat162_rn(v[0] - hf.x, v[1] - hf.y);
+        hw[q] = *reinterpret_cast<const uint32_t*>(&hp);
+        lw[q] = *reinterpret_cast<const uint32_t*>(&lp);
+      }
+      // 128-byte swizzle: 16-byte chunk (nc / 8) of row kr at (nc / 8) ^ (kr % 8)
+      const int64_t off = (kc * b.nb + nb) * 8192 + kr * 128 + (((nc >> 3) ^ (kr & 7)) << 4);
+      *reinterpret_cast<uint4*>(b.base + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(b.base + b.part_bytes() + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+  }
   const int64_t HH = (int64_t)H * H, HI = (int64_t)H * I, HO = (int64_t)H * O, IHH = (int64_t)(I + H) * H;
   int sel[4];
   const int ncopy = prep_copies(o, sel);
@@ -183,7 +246,8 @@ __global__ void prep_kernel(int64_t N, int H, int I, int O, int d, int64_t ld1, 
 
 int launch_prep(int64_t N, int H, int I, int O, int d, int64_t ld1, bool bf, const egnn_layer_params* p,
                 const float* x, const Prep& o, cudaStream_t s) {
-  const int64_t total = prep_total(N, H, I, O, d, o);
+  const int64_t total = std::max(prep_total(N, H, I, O, d, o),
+                                 image_chunks(o.img[0]) + image_chunks(o.img[1]) + image_chunks(o.img[2]));
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 4096));
   TimerScope ts("prep", s);
   EGNN_CHECK_CUDA(launch_pdl(prep_kernel, dim3(blocks), dim3(256), 0, s, N, H, I, O, d, ld1, bf ? 1 : 0, *p, x,
@@ -202,8 +266,9 @@ int node_wgrad(int64_t R, int64_t M, int64_t N, Mat G, Mat X, float* dW, int64_t
 }
 
 int gemm_pq(int64_t N, int H, int I, const float* h, const float* WPQT, const float* bias2, float* PQ, bool bf,
-            cudaStream_t s) {
+            const BImage& img, cudaStream_t s) {
   GemmArgs g;
+  gemm_use_image(g, img);
   g.M = N; g.N = 2 * H; g.K = I;
   g.A = mat(h, I);
   g.B = mat(WPQT, 2 * H); g.b_t = 0;
@@ -240,7 +305,8 @@ FwdWs carve_fwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   FwdWs w;
   const bool rows = edge_rows_supported(H, d->edge_attr_dim, d->flags, d->precision);
   w.prep = carve_prep(c, N, H, in_dim(d), out_dim(d), d->edge_attr_dim, false,
-                      rows || edge_tc_fwd_supported(H, d->edge_attr_dim, d->flags, d->precision));
+                      rows || edge_tc_fwd_supported(H, d->edge_attr_dim, d->flags, d->precision),
+                      d->precision == EGNN_PREC_BF16);
   const int64_t G = max_ctas(E, H, num_sms);
   w.carry = c.take<float>((size_t)G * 2 * (H + 4));
   w.carry_row = c.take<int32_t>((size_t)G * 2);
@@ -284,7 +350,8 @@ BwdWs carve_bwd(Carver& c, const egnn_layer_desc* d, int num_sms) {
   const int I = in_dim(d), O = out_dim(d);
   const bool rows = edge_rows_supported(H, d->edge_attr_dim, d->flags, d->precision);
   w.prep = carve_prep(c, N, H, I, O, d->edge_attr_dim, true,
-                      rows || edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision));
+                      rows || edge_tc_supported(H, d->edge_attr_dim, d->flags, d->precision),
+                      d->precision == EGNN_PREC_BF16);
   w.g_n1pre = c.take<float>((size_t)N * H);
   w.ghg = c.take<float>((size_t)N * (ghg_joint(I) ? I + H : I));
   w.gagg = ghg_joint(I) ? w.ghg + I : c.take<float>((size_t)N * H);
@@ -463,7 +530,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   float* agg = sv.agg;
 
   EGNN_TRY(launch_prep(N, H, I, O, dd, ld1, bf, p, x, w.prep, s));
-  EGNN_TRY(gemm_pq(N, H, I, h, w.prep.WPQT, w.prep.bias2, sv.PQ, bf, s));
+  EGNN_TRY(gemm_pq(N, H, I, h, w.prep.WPQT, w.prep.bias2, sv.PQ, bf, w.prep.img[0], s));
 
   const bool rows = edge_rows_supported(H, dd, d->flags, d->precision);
   const bool tc = edge_tc_fwd_supported(H, dd, d->flags, d->precision);
@@ -485,6 +552,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n1.bias = p->node_b1; n1.act = ACT_SILU;
   n1.pre = sv.n1pre; n1.ldp = H;
   n1.C = sv.n1; n1.ldc = H;
+  gemm_use_image(n1, w.prep.img[1]);
   EGNN_TRY(node_gemm(n1, bf, s));
 
   GemmArgs n2;
@@ -494,6 +562,7 @@ extern "C" int egnn_layer_fwd(const egnn_layer_desc* d, const egnn_graph* g, con
   n2.bias = p->node_b2;
   if (d->flags & EGNN_FLAG_RESIDUAL) { n2.resid = h; n2.ldr = I; }   // I == O
   n2.C = h_out; n2.ldc = O;
+  gemm_use_image(n2, w.prep.img[2]);
   EGNN_TRY(node_gemm(n2, bf, s));
   return EGNN_OK;
 }
@@ -545,6 +614,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gn.B = mat(p->node_w2, H); gn.b_t = 0;
     gn.act = ACT_DSILU; gn.aux = sv.n1pre; gn.ldaux = H;
     gn.C = w.g_n1pre; gn.ldc = H;
+    gemm_use_image(gn, w.prep.img[0]);
     EGNN_TRY(node_gemm(gn, bf, s));
   }
   // dW_n1, db_n1 on the side stream once g_n1pre exists
@@ -562,6 +632,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.B = mat(p->node_w1, I + H); gh.b_t = 0;
     if (residual) { gh.resid = gh_out; gh.ldr = O; gh.resid_cols = I; }   // I == O
     gh.C = w.ghg; gh.ldc = ld_ghg;
+    gemm_use_image(gh, w.prep.img[1]);   // its columns start at the image's first block
     EGNN_TRY(node_gemm(gh, bf, s));
   }
   if (!joint) {
@@ -620,6 +691,7 @@ extern "C" int egnn_layer_bwd(const egnn_layer_desc* d, const egnn_graph* g, con
     gh.B = mat(w.prep.WPQ, I); gh.b_t = 0;
     gh.resid = w.ghg; gh.ldr = ld_ghg;
     gh.C = grad_h; gh.ldc = I;
+    gemm_use_image(gh, w.prep.img[2]);
     EGNN_TRY(node_gemm(gh, bf, s));
   }
   return EGNN_OK;

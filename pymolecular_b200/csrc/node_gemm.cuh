@@ -60,7 +60,37 @@ struct GemmArgs {
   float* db = nullptr;
   float* db_part = nullptr;
   int vec = 0;   // set by gemm(): the epilogue may move four columns at a time
+  // bf16 mode: B (K x N, b_t = 0) already split into bf16 hi / lo parts laid
+  // out as the GEMM's shared-memory tiles (see BImage); nullptr: split per CTA
+  const char* b_img = nullptr;
+  int64_t b_img_nb = 0;          // 64-column blocks per 64-row chunk of the image
+  int64_t b_img_part = 0;        // bytes from the hi part to the lo part
 };
+
+// A weight operand B (K x N, element (k, n)) as bf16 hi = bf16(B) and
+// lo = bf16(B - hi) images: for each 64-row chunk kc of k and each 64-column
+// block nb of n an 8 KB block of 64 k-rows x 128 bytes in the 128-byte
+// swizzle of an MN-major tcgen05 operand (16-byte chunk c of row r at
+// c ^ (r % 8)), block (kc, nb) at byte (kc NB + nb) 8192, the lo part at
+// NKC NB 8192.  Padding rows and columns are zero.  NB is even, so a
+// 128-column tile is one contiguous 16 KB piece per part.
+struct BImage {
+  char* base = nullptr;
+  int64_t K = 0, N = 0, nkc = 0, nb = 0;
+  __host__ __device__ int64_t part_bytes() const { return nkc * nb * 8192; }
+  __host__ __device__ int64_t bytes() const { return 2 * part_bytes(); }
+};
+inline BImage bimage_shape(int64_t K, int64_t N) {
+  BImage b;
+  b.K = K; b.N = N;
+  b.nkc = (K + 63) / 64;
+  b.nb = ((N + 63) / 64 + 1) / 2 * 2;
+  return b;
+}
+inline void gemm_use_image(GemmArgs& g, const BImage& b) {
+  if (!b.base) return;
+  g.b_img = b.base; g.b_img_nb = b.nb; g.b_img_part = b.part_bytes();
+}
 
 int gemm(const GemmArgs& a, cudaStream_t s);
 

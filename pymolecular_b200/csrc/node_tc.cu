@@ -33,19 +33,22 @@ using namespace tc;
 
 constexpr int BMT = 128, BKT = 64, NTH = 512, NDB = NTH / 16;
 
-template <int BN>
+// IMG: B arrives as bf16 hi / lo tiles from a prepared image (BImage) by
+// bulk copies into two tile buffers; the raw ring then holds A alone and
+// runs deeper (the data GEMMs, B = a weight; no db).
+template <int BN, bool IMG = false>
 struct TcShape {
-  static constexpr int NRAW = BN == 64 ? 3 : (BN == 128 ? 2 : 1);   // raw fp32 ring depth
+  static constexpr int NRAW = IMG ? (BN == 64 ? 5 : 4) : (BN == 64 ? 3 : (BN == 128 ? 2 : 1));   // raw ring depth
   static constexpr int RAW_A = BMT * BKT * 4;          // 32 KB
-  static constexpr int RAW_B = BN * BKT * 4;
+  static constexpr int RAW_B = IMG ? 0 : BN * BKT * 4;
   static constexpr int RAW_STAGE = RAW_A + RAW_B;
   static constexpr int T_A = BMT * BKT * 2;            // one bf16 part of the A chunk: 16 KB
   static constexpr int T_B = BN * BKT * 2;
-  static constexpr int TILES = 2 * T_A + 2 * T_B;      // A hi, A lo, B hi, B lo
+  static constexpr int TILES = 2 * T_A + (IMG ? 4 : 2) * T_B;   // A hi, A lo, B hi, B lo (two B buffers with IMG)
   static constexpr int OFF_RAW = TILES;
   static constexpr int OFF_BAR = OFF_RAW + NRAW * RAW_STAGE;
-  static constexpr int OFF_DB = OFF_BAR + 64;          // float[NDB][128]
-  static constexpr size_t SMEM_BYTES = OFF_DB + NDB * BMT * 4 + 1024;
+  static constexpr int OFF_DB = OFF_BAR + 64;          // float[NDB][128] (weight gradients only)
+  static constexpr size_t SMEM_BYTES = OFF_DB + (IMG ? 0 : NDB * BMT * 4) + 1024;
 };
 
 __device__ __forceinline__ const float* mat_at(const Mat& X, int64_t r, int64_t c) {
@@ -166,10 +169,11 @@ __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t ph) {
   return !__syncthreads_or(!ok);
 }
 
-template <int A_T, int B_T, int BNT>
+template <int A_T, int B_T, int BNT, bool IMG = false>
 __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
   pdl_enter();
-  using S = TcShape<BNT>;
+  using S = TcShape<BNT, IMG>;
+  static_assert(!IMG || (A_T == 0 && B_T == 0 && BNT <= 128), "image path: data GEMMs, MN-major B");
   extern __shared__ __align__(1024) char tsm_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
   char* a_hi = sm;
@@ -178,6 +182,9 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
   char* b_lo = sm + 2 * S::T_A + S::T_B;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + S::OFF_BAR);
   uint32_t* tmem_s = reinterpret_cast<uint32_t*>(sm + S::OFF_BAR + 16);
+  uint64_t* bbar = reinterpret_cast<uint64_t*>(sm + S::OFF_BAR + 24);   // [2]: B tile buffers (IMG)
+  int* babort = reinterpret_cast<int*>(sm + S::OFF_BAR + 40);          // a B wait gave up (IMG)
+  auto b_buf = [&](int buf) { return sm + 2 * S::T_A + buf * 2 * S::T_B; };   // hi, then lo
   float* dbred = reinterpret_cast<float*>(sm + S::OFF_DB);      // [NDB][128]
   constexpr bool AK = A_T == 0, BK = B_T == 1;   // K-major operand tiles
   constexpr uint32_t IDESC = make_idesc_bf16(BMT, BNT, AK ? 0 : 1, BK ? 0 : 1);
@@ -199,9 +206,23 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
     if (kc < nkc) {
       const int64_t k0 = kbeg + (int64_t)kc * BKT;
       cpa.copy(raw_a(kc), a.A, k0, kend);
-      cpb.copy(raw_b(kc), a.B, k0, kend);
+      if constexpr (!IMG) cpb.copy(raw_b(kc), a.B, k0, kend);
     }
     cp_async_commit();   // empty groups keep the group count uniform
+  };
+  // IMG, thread 0: the hi and lo tiles of chunk kc (its 64-column blocks are
+  // contiguous in the image) into buffer kc & 1
+  const int64_t nb0 = (int64_t)blockIdx.x * (BNT / 64);
+  bool b_pend[2] = {false, false};   // thread 0: a copy into the buffer not yet waited for
+  int b_last[2] = {0, 0};            // thread 0: the chunk last copied into the buffer
+  auto issue_b = [&](int kc) {
+    const int buf = kc & 1;
+    const char* src = a.b_img + ((int64_t)kc * a.b_img_nb + nb0) * 8192;
+    mbar_expect_tx_bytes(&bbar[buf], 2 * S::T_B);
+    bulk_copy_g2s(b_buf(buf), src, S::T_B, &bbar[buf]);
+    bulk_copy_g2s(b_buf(buf) + S::T_B, src + a.b_img_part, S::T_B, &bbar[buf]);
+    b_pend[buf] = true;
+    b_last[buf] = kc;
   };
 
   // raw chunks in flight while the TMEM and barrier set-up runs
@@ -210,7 +231,16 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
   if (warp == 0) tmem_alloc(tmem_s, BNT);
   if (tid == 0) {
     mbar_init(bar, 1);
+    if constexpr (IMG) {
+      mbar_init(&bbar[0], 1);
+      mbar_init(&bbar[1], 1);
+      *babort = 0;
+    }
     fence_mbar_init();
+    if constexpr (IMG) {
+      if (nkc > 0) issue_b(0);
+      if (nkc > 1) issue_b(1);
+    }
   }
   fence_before_sync();
   __syncthreads();
@@ -233,21 +263,40 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
       ph ^= 1u;
       pending = false;
       fence_after_sync();
+      if constexpr (IMG) {
+        if (*babort) {              // set before the commit waited for above: the same in every thread
+          ok = false;
+          break;
+        }
+        if (tid == 0 && kc + 1 < nkc) issue_b(kc + 1);   // its buffer's last reader has completed
+      }
     } else {
       __syncthreads();
     }
     split_raw<BMT, AK>(raw_a(kc), a_hi, a_lo, do_db ? colsum : nullptr);
-    split_raw<BNT, BK>(raw_b(kc), b_hi, b_lo, nullptr);
+    if constexpr (!IMG) split_raw<BNT, BK>(raw_b(kc), b_hi, b_lo, nullptr);
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();   // tiles complete; raw chunk kc free for chunk kc + NRAW
     fence_after_sync();
     if (tid == 0) {
+      bool go = true;
+      const char* bh = b_hi;
+      const char* bl = b_lo;
+      if constexpr (IMG) {
+        const int buf = kc & 1;
+        go = mbar_wait(&bbar[buf], (uint32_t)((kc >> 1) & 1));
+        if (go) b_pend[buf] = false; else *babort = 1;
+        bh = b_buf(buf);
+        bl = bh + S::T_B;
+      }
+      if (go) {
 #pragma unroll
-      for (int kk = 0; kk < BKT / 16; ++kk) {
-        mma_bf16(tmem, tdesc(a_hi, AK, kk), tdesc(b_hi, BK, kk), IDESC, (kc > 0 || kk > 0) ? 1u : 0u);
-        mma_bf16(tmem, tdesc(a_hi, AK, kk), tdesc(b_lo, BK, kk), IDESC, 1u);
-        mma_bf16(tmem, tdesc(a_lo, AK, kk), tdesc(b_hi, BK, kk), IDESC, 1u);
+        for (int kk = 0; kk < BKT / 16; ++kk) {
+          mma_bf16(tmem, tdesc(a_hi, AK, kk), tdesc(bh, BK, kk), IDESC, (kc > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16(tmem, tdesc(a_hi, AK, kk), tdesc(bl, BK, kk), IDESC, 1u);
+          mma_bf16(tmem, tdesc(a_lo, AK, kk), tdesc(bh, BK, kk), IDESC, 1u);
+        }
       }
       mma_commit(bar);
     }
@@ -258,10 +307,18 @@ __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
     ok = wait_all(bar, ph);
     if (ok) pending = false;
   }
+  if constexpr (IMG) {
+    if (ok && *babort) ok = false;
+  }
   if (!ok) {
     if (tid == 0) {
       atomicAdd(&g_node_tc_timeouts, 1);
       if (pending) mbar_wait(bar, ph);
+      if constexpr (IMG) {   // no bulk copy may still be landing when the CTA leaves
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+          if (b_pend[b]) mbar_wait(&bbar[b], (uint32_t)((b_last[b] >> 1) & 1));
+      }
     }
     fence_before_sync();
     __syncthreads();
@@ -397,20 +454,21 @@ bool words_ok(const Mat& X, int64_t contiguous_extent) {
   return true;
 }
 
-template <int A_T, int B_T, int BNT>
+template <int A_T, int B_T, int BNT, bool IMG = false>
 int launch_t(const GemmArgs& a, cudaStream_t s) {
   static uint64_t attr_set = 0;
-  constexpr size_t bytes = TcShape<BNT>::SMEM_BYTES;
+  constexpr size_t bytes = TcShape<BNT, IMG>::SMEM_BYTES;
+  static_assert(bytes <= 232448, "shared memory per CTA");
   const uint64_t bit = device_bit();
   if (!(attr_set & bit)) {
-    EGNN_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<A_T, B_T, BNT>,
+    EGNN_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<A_T, B_T, BNT, IMG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     attr_set |= bit;
   }
   const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
   const dim3 grid((unsigned)((a.N + BNT - 1) / BNT), (unsigned)((a.M + BMT - 1) / BMT), z);
   TimerScope ts("node_gemm", s);
-  EGNN_CHECK_CUDA(launch_pdl(gemm_tc_kernel<A_T, B_T, BNT>, grid, dim3(NTH), bytes, s, a));
+  EGNN_CHECK_CUDA(launch_pdl(gemm_tc_kernel<A_T, B_T, BNT, IMG>, grid, dim3(NTH), bytes, s, a));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;
 }
@@ -452,6 +510,13 @@ int gemm_tc(const GemmArgs& a_in, cudaStream_t s) {
            (a.act != ACT_DSILU || (a.ldaux % 4 == 0 && aligned16(a.aux))) &&
            (!a.resid || (a.ldr % 4 == 0 && aligned16(a.resid) &&
                          (a.resid_cols == INT64_MAX || a.resid_cols % 4 == 0)))) ? 1 : 0;
+  if (a.b_img && a.a_t == 0 && a.b_t == 0 && a.ksplit <= 1) {
+    // B from its prepared image: 64-column tiles while twice the CTAs fit in one wave, else 128
+    const int64_t tiles128 = (a.N + 127) / 128 * ((a.M + BMT - 1) / BMT);
+    if (2 * tiles128 <= num_sms_current()) EGNN_TRY((launch_t<0, 0, 64, true>(a, s)));
+    else EGNN_TRY((launch_t<0, 0, 128, true>(a, s)));
+    return EGNN_OK;
+  }
   if (a.a_t == 0 && a.b_t == 0) EGNN_TRY((launch_ab<0, 0>(a, s)));
   else if (a.a_t == 0 && a.b_t == 1) EGNN_TRY((launch_ab<0, 1>(a, s)));
   else if (a.a_t == 1 && a.b_t == 0) EGNN_TRY((launch_ab<1, 0>(a, s)));

@@ -124,6 +124,14 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (both 16-byte aligned, size a multiple
+// of 16 bytes), its bytes counted on `bar`.  Never a peer's memory as source.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // ---- cp.async (4- and 16-byte, per-thread groups) ---------------------------
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");

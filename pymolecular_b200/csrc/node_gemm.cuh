@@ -72,8 +72,8 @@ struct GemmArgs {
 // block nb of n an 8 KB block of 64 k-rows x 128 bytes in the 128-byte
 // swizzle of an MN-major tcgen05 operand (16-byte chunk c of row r at
 // c ^ (r % 8)), block (kc, nb) at byte (kc NB + nb) 8192, the lo part at
-// NKC NB 8192.  Padding rows and columns are zero.  NB is even, so a
-// 128-column tile is one contiguous 16 KB piece per part.
+// NKC NB 8192.  Padding rows and columns are zero.  NB is a multiple of 4,
+// so a 128- or 256-column tile is one contiguous 16 or 32 KB piece per part.
 struct BImage {
   char* base = nullptr;
   int64_t K = 0, N = 0, nkc = 0, nb = 0;
@@ -84,7 +84,7 @@ inline BImage bimage_shape(int64_t K, int64_t N) {
   BImage b;
   b.K = K; b.N = N;
   b.nkc = (K + 63) / 64;
-  b.nb = ((N + 63) / 64 + 1) / 2 * 2;
+  b.nb = ((N + 63) / 64 + 3) / 4 * 4;
   return b;
 }
 inline void gemm_use_image(GemmArgs& g, const BImage& b) {

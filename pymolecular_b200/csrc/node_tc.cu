@@ -38,7 +38,7 @@ constexpr int BMT = 128, BKT = 64, NTH = 512, NDB = NTH / 16;
 // runs deeper (the data GEMMs, B = a weight; no db).
 template <int BN, bool IMG = false>
 struct TcShape {
-  static constexpr int NRAW = IMG ? (BN == 64 ? 5 : 4) : (BN == 64 ? 3 : (BN == 128 ? 2 : 1));   // raw ring depth
+  static constexpr int NRAW = IMG ? (BN == 64 ? 5 : (BN == 128 ? 4 : 2)) : (BN == 64 ? 3 : (BN == 128 ? 2 : 1));
   static constexpr int RAW_A = BMT * BKT * 4;          // 32 KB
   static constexpr int RAW_B = IMG ? 0 : BN * BKT * 4;
   static constexpr int RAW_STAGE = RAW_A + RAW_B;
@@ -173,7 +173,7 @@ template <int A_T, int B_T, int BNT, bool IMG = false>
 __global__ void __launch_bounds__(NTH, 1) gemm_tc_kernel(GemmArgs a) {
   pdl_enter();
   using S = TcShape<BNT, IMG>;
-  static_assert(!IMG || (A_T == 0 && B_T == 0 && BNT <= 128), "image path: data GEMMs, MN-major B");
+  static_assert(!IMG || (A_T == 0 && B_T == 0), "image path: data GEMMs, MN-major B");
   extern __shared__ __align__(1024) char tsm_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
   char* a_hi = sm;
@@ -511,9 +511,12 @@ int gemm_tc(const GemmArgs& a_in, cudaStream_t s) {
            (!a.resid || (a.ldr % 4 == 0 && aligned16(a.resid) &&
                          (a.resid_cols == INT64_MAX || a.resid_cols % 4 == 0)))) ? 1 : 0;
   if (a.b_img && a.a_t == 0 && a.b_t == 0 && a.ksplit <= 1) {
-    // B from its prepared image: 64-column tiles while twice the CTAs fit in one wave, else 128
-    const int64_t tiles128 = (a.N + 127) / 128 * ((a.M + BMT - 1) / BMT);
-    if (2 * tiles128 <= num_sms_current()) EGNN_TRY((launch_t<0, 0, 64, true>(a, s)));
+    // B from its prepared image; tile width chosen as in launch_ab
+    const int64_t rows = (a.M + BMT - 1) / BMT;
+    const int64_t tiles128 = (a.N + 127) / 128 * rows, tiles256 = (a.N + 255) / 256 * rows;
+    const int sms = num_sms_current();
+    if (2 * tiles128 <= sms) EGNN_TRY((launch_t<0, 0, 64, true>(a, s)));
+    else if (a.N > 128 && tiles128 > sms && tiles256 <= sms) EGNN_TRY((launch_t<0, 0, 256, true>(a, s)));
     else EGNN_TRY((launch_t<0, 0, 128, true>(a, s)));
     return EGNN_OK;
   }

@@ -554,22 +554,28 @@ def roofline(prob, m, peaks, clk, dev):
     tensor("node_gemm", 30.0 * H * H * N * L, _per_step(kt, node_names, n),
            sum(kt[x][1] for x in node_names), on_tc=bf,
            extra={"kernels": node_names, "operands": "split bf16 (hi*hi + hi*lo + lo*hi)" if bf else "fp32 FFMA"})
-    # node pass (tensor-core paths): per node, the bf16 dL/da1 rows of its
-    # in-edges and out-edges (2 x 2H bytes per edge), their g_d (2 x 16),
-    # the transpose-CSR positions (4), and per node the row pointers, dL/dx',
-    # S_dst, S_src (2 x 4H) and dL/dx
+    # HBM groups count unique bytes: data a launch must move at least once
+    # (gathered node rows and second reads are L2 or DRAM traffic, which the
+    # ncu `traffic` figures show).
+    # node pass (tensor-core paths): the bf16 dL/da1 row of every edge (2H;
+    # read for its destination and again for its source), its g_d (16), the
+    # transpose-CSR position (4); per node the row pointers, dL/dx', S_dst,
+    # S_src (2 x 4H) and dL/dx
     if kt["node_pass"][1]:
-        memory("node_pass", (E * (4 * H + 32 + 4) + N * (8 * H + 8 + 24)) * L,
+        memory("node_pass", (E * (2 * H + 16 + 4) + N * (8 * H + 8 + 24)) * L,
                _per_step(kt, ["node_pass"], n), kt["node_pass"][1],
-               "E (4H + 36) + N (8H + 32) per layer")
+               "E (2H + 20) + N (8H + 32) per layer (unique bytes)")
     if kt["src_pass"][1]:
         memory("src_pass", (E * (4 * H + 16 + 4) + N * (4 * H + 8 + 24)) * L,
                _per_step(kt, ["src_pass"], n), kt["src_pass"][1], "E (4H + 20) + N (4H + 32) per layer")
     if rows_path:
-        # gather: indices, P/Q rows (2 x 4H), u1 tile row (2H), geometry,
-        # backward also silu'(a1) fp16 (2H) and the gradient factors
-        memory("edge_rows_u", E * ((8 + 8 * H + 2 * H + 16) * 2 + 2 * H + 16) * L,
-               _per_step(kt, ["edge_rows_u"], n), kt["edge_rows_u"][1], "E (18H + 48) + E (2H + 16) per layer")
+        # gather, forward and backward launch: indices (8 per launch), the u1
+        # tile row (2H per launch), backward also silu'(a1) fp16 (2H) and the
+        # gradient factors (16); per launch the P|Q table (8H per node) and
+        # the coordinates (16 per node) once
+        memory("edge_rows_u", (E * (16 + 4 * H + 2 * H + 16) + N * 2 * (8 * H + 16)) * L,
+               _per_step(kt, ["edge_rows_u"], n), kt["edge_rows_u"][1],
+               "E (6H + 32) + N (16H + 32) per layer (unique bytes)")
         memory("edge_rows_agg", (E * (4 * H + 20) + N * (4 * H + 24)) * L,
                _per_step(kt, ["edge_rows_agg"], n), kt["edge_rows_agg"][1], "E (4H + 20) + N (4H + 24) per layer")
     if rows_path:

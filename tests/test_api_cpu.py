@@ -192,3 +192,22 @@ def test_no_oracle_import_in_product():
     pat = re.compile(r"^\s*(from\s+oracle|import\s+oracle)", re.M)
     for p in (ROOT / "pymolecular_b200").rglob("*.py"):
         assert not pat.search(p.read_text()), p
+
+
+def test_graph_mse_entry_points_validate_before_any_launch():
+    """The loss entry points reject bad shapes and null pointers with an
+    error status (no GPU needed: nothing is launched)."""
+    lib = nat.lib()
+    assert lib.egnn_graph_mse_workspace_size(0) > 0
+    assert lib.egnn_graph_mse_workspace_size(10_000_000) >= 2 * 4 * (10_000_000 // 2048)
+    # nodes without graphs, negative sizes, null pointers
+    assert lib.egnn_graph_mse_fwd(10, 0, 1, 1, 1, 1, 1, 1, 1, 1 << 20, None) == nat.EGNN_ERR_INVALID_ARG
+    assert lib.egnn_graph_mse_fwd(-1, 1, 1, 1, 1, 1, 1, 1, 1, 1 << 20, None) == nat.EGNN_ERR_INVALID_ARG
+    assert lib.egnn_graph_mse_fwd(10, 2, None, 1, 1, 1, 1, 1, 1, 1 << 20, None) == nat.EGNN_ERR_INVALID_ARG
+    assert lib.egnn_graph_mse_fwd(10, 2, 1, 1, 1, 1, 1, 1, 1, 0, None) == nat.EGNN_ERR_WORKSPACE
+    assert lib.egnn_graph_mse_bwd(10, 0, 1, 1, 1, 1, 1, 1, None) == nat.EGNN_ERR_INVALID_ARG
+    assert lib.egnn_graph_mse_bwd(10, 2, 1, None, 1, 1, 1, 1, None) == nat.EGNN_ERR_INVALID_ARG
+    assert lib.egnn_graph_mse_bwd(0, 0, None, None, None, None, None, 1, None) == nat.EGNN_OK
+    with pytest.raises(ValueError, match="CUDA"):
+        from pymolecular_b200 import graph_sum_mse
+        graph_sum_mse(torch.zeros(4), torch.tensor([0, 4]), torch.zeros(1))

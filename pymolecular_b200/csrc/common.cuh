@@ -4,7 +4,6 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
-#include <cuda_fp16.h>
 #include <stdint.h>
 #include <stddef.h>
 #include <string>
@@ -146,25 +145,6 @@ __device__ __forceinline__ void silu_grad_edge(float a, float& y, float& dy) {
   const float s = sigmoid_edge(a);
   y = a * s;
   dy = s * (1.0f + a * (1.0f - s));
-}
-
-// Two sigmoids per MUFU operation: sigmoid(x) = 1/2 + tanh(x/2)/2 with the
-// hardware's packed fp16 tanh.approx (x/2 rounded to fp16, a tanh accurate to
-// about 2^-10.7 relative); for activations that are rounded to bf16 (an 8-bit
-// mantissa) or summed over many edges downstream.
-__device__ __forceinline__ void sigmoid2_edge(float a, float b, float& sa, float& sb) {
-  const __half2 h = __floats2half2_rn(0.5f * a, 0.5f * b);
-  uint32_t t;
-  asm("tanh.approx.f16x2 %0, %1;" : "=r"(t) : "r"(*reinterpret_cast<const uint32_t*>(&h)));
-  const float2 tf = __half22float2(*reinterpret_cast<const __half2*>(&t));
-  sa = fmaf(0.5f, tf.x, 0.5f);
-  sb = fmaf(0.5f, tf.y, 0.5f);
-}
-__device__ __forceinline__ void silu2_edge(float& a, float& b) {
-  float sa, sb;
-  sigmoid2_edge(a, b, sa, sb);
-  a *= sa;
-  b *= sb;
 }
 
 // Round-to-nearest-even to the bf16 grid, kept in a float register.

@@ -243,12 +243,10 @@ __device__ __forceinline__ void gather_u(char* Ut, const float* __restrict__ PQ,
       }
       if (e < n) {
         const float r = geo[e].w;
-        u0 = fmaf(wr4.x, r, x4.x);
-        u1 = fmaf(wr4.y, r, x4.y);
-        u2 = fmaf(wr4.z, r, x4.z);
-        u3 = fmaf(wr4.w, r, x4.w);
-        silu2_edge(u0, u1);
-        silu2_edge(u2, u3);
+        u0 = silu_edge(fmaf(wr4.x, r, x4.x));
+        u1 = silu_edge(fmaf(wr4.y, r, x4.y));
+        u2 = silu_edge(fmaf(wr4.z, r, x4.z));
+        u3 = silu_edge(fmaf(wr4.w, r, x4.w));
       }
       const __nv_bfloat162 h01 = __floats2bfloat162_rn(u0, u1);
       const __nv_bfloat162 h23 = __floats2bfloat162_rn(u2, u3);
@@ -544,11 +542,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
       float v[32], lo[32];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
 #pragma unroll
-      for (int q = 0; q < 32; q += 2) {
-        v[q] += s_b2[g.col0 + q];
-        v[q + 1] += s_b2[g.col0 + q + 1];
-        silu2_edge(v[q], v[q + 1]);
-      }
+      for (int q = 0; q < 32; ++q) v[q] = silu_edge(v[q] + s_b2[g.col0 + q]);
       if (att) {   // the gate's dot product over the edge's four column slices (uniform branch)
         float pa = 0.f;
 #pragma unroll
@@ -586,12 +580,7 @@ __global__ void __launch_bounds__(kNT, 1) edge_fwd_tc_kernel(const __grid_consta
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
       float p = 0.f;
 #pragma unroll
-      for (int q = 0; q < 32; q += 2) {
-        float y0 = v[q] + s_bc1[g.col0 + q], y1 = v[q + 1] + s_bc1[g.col0 + q + 1];
-        silu2_edge(y0, y1);
-        p = fmaf(y0, s_wc2[g.col0 + q], p);
-        p = fmaf(y1, s_wc2[g.col0 + q + 1], p);
-      }
+      for (int q = 0; q < 32; ++q) p = fmaf(silu_edge(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
       part[g.cg * kM + g.e] = p;
     }
     if (g.cg == 0) cp_async_wait_all_groups();   // segment heads: row pointers landed

@@ -897,28 +897,50 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(const __grid_consta
     }
     if (!(ok = wait_mma(bar, phase, a.wait_polls))) break;
 
-    // ---- phi and its gradient (row sums across the four column slices)
-    {
-      float v[32];
+    // ---- phi = wc2 . silu(c1 + bc1) (row sums across the four column slices)
+    // and g_c1 = gphi' wc2 silu'(c1) -> tile G, with column sums.  Without
+    // tanh, gphi' = (dL/dx'_i / deg_i) . d (x 1/|d| when normalising) does not
+    // depend on phi: one pass over c1 gives both, and phi is summed later.
+    if (!tanh_) {
+      const float4 d = dl[g.e], gt = gtr[g.e];
+      float gp = gt.x * d.x + gt.y * d.y + gt.z * d.z;
+      if (normalize) gp *= gt.w;
+      if (!valid) gp = 0.f;
+      float v[32], gc[32];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
       float p = 0.f;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) p = fmaf(silu_edge(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
+      for (int q = 0; q < 32; ++q) {
+        float y, dy;
+        silu_grad_edge(v[q] + s_bc1[g.col0 + q], y, dy);
+        p = fmaf(y, s_wc2[g.col0 + q], p);
+        gc[q] = gp * s_wc2[g.col0 + q] * dy;
+        v[q] = gp * y;
+      }
       part[g.cg * kM + g.e] = p;
-    }
-    __syncthreads();
-    if (g.cg == 0) {
-      const float p = part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e];
-      const float4 d = dl[g.e], gt = gtr[g.e];
-      const float ph = tanh_ ? tanhf(p) : p;
-      float gp = gt.x * d.x + gt.y * d.y + gt.z * d.z;
-      if (normalize) gp *= gt.w;
-      if (tanh_) gp *= (1.f - ph * ph);
-      phis[g.e] = valid ? make_float2(ph, gp) : make_float2(0.f, 0.f);
-    }
-    __syncthreads();
-    // ---- g_c1 = gphi' wc2 silu'(c1) -> tile G ; column sums
-    {
+      st_row32_bf16(Gt, g.e, g.col0, gc);
+      r_bc1 += warp_colsum32(gc);
+      r_wc2 += warp_colsum32(v);
+    } else {
+      {
+        float v[32];
+        tmem_ld32(tD0 + g.lane_base + g.col0, v);
+        float p = 0.f;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) p = fmaf(silu_edge(v[q] + s_bc1[g.col0 + q]), s_wc2[g.col0 + q], p);
+        part[g.cg * kM + g.e] = p;
+      }
+      __syncthreads();
+      if (g.cg == 0) {
+        const float p = part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e];
+        const float4 d = dl[g.e], gt = gtr[g.e];
+        const float ph = tanhf(p);
+        float gp = gt.x * d.x + gt.y * d.y + gt.z * d.z;
+        if (normalize) gp *= gt.w;
+        gp *= (1.f - ph * ph);
+        phis[g.e] = valid ? make_float2(ph, gp) : make_float2(0.f, 0.f);
+      }
+      __syncthreads();
       const float gp = phis[g.e].y;
       float v[32], gc[32];
       tmem_ld32(tD0 + g.lane_base + g.col0, v);
@@ -942,6 +964,10 @@ __global__ void __launch_bounds__(kNT, 1) edge_bwd_tc_kernel(const __grid_consta
       for (int kk = 0; kk < H / 16; ++kk)
         mma_bf16(tD0, desc_k(Gt, kM, kk), desc_mn(Wc1t, H, kk), C::IDESC_DGRAD, kk > 0);
       mma_commit(bar);
+    }
+    if (!tanh_ && g.cg == 0) {   // phi of the one-pass path (its parts are complete after the handoff)
+      const float p = part[g.e] + part[kM + g.e] + part[2 * kM + g.e] + part[3 * kM + g.e];
+      phis[g.e] = make_float2(valid ? p : 0.f, 0.f);
     }
     // g_agg[i] slice of edge e: loads issued before the wait, used after it
     float4 gagg[8];

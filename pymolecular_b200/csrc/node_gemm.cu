@@ -446,11 +446,13 @@ __device__ __forceinline__ void thread_grid(int& tx, int& ty) {
 
 // 64 x 128 tiles (TM = 4): on B200 the 128 x 128 tile (TM = 8) measured no
 // faster on these shapes (K = 128..256) and quantises worse over 148 SMs.
+// 64 x 64 tiles (NBN = 1 column group) when 128-column tiles would leave
+// more than half the SMs idle (small row counts, N <= 64).
 constexpr int TBN = 128, TBK = 16, TTM = 4;
 
-template <int BM>
+template <int BM, int BN>
 constexpr size_t tiled_smem_bytes() {
-  return (size_t)2 * TBK * ((BM + 4) + (TBN + 4)) * sizeof(float);
+  return (size_t)2 * TBK * ((BM + 4) + (BN + 4)) * sizeof(float);
 }
 
 // One operand slice: ROWS rows (m or n) x 16 k into s[k][row] (leading
@@ -514,18 +516,20 @@ __device__ __forceinline__ float4 epi_act(float4 v, int act, const float* aux) {
   return v;
 }
 
-template <int TM, int A_T, int B_T>
+template <int TM, int A_T, int B_T, int NBN = 2>
 __global__ void __launch_bounds__(256, 2) gemm_tiled_kernel(GemmArgs a) {
   static_assert(TM == 4, "fragment loads below cover 4 rows per thread");
+  static_assert(NBN == 1 || NBN == 2, "one or two 64-column groups per thread");
   pdl_enter();
-  constexpr int BM = 16 * TM, LDA = BM + 4, LDB = TBN + 4;
+  constexpr int BNT = 64 * NBN;   // tile columns
+  constexpr int BM = 16 * TM, LDA = BM + 4, LDB = BNT + 4;
   constexpr int SA = TBK * LDA, SB = TBK * LDB;
   extern __shared__ __align__(16) float tsm[];
   float* As = tsm;
   float* Bs = tsm + 2 * SA;
   int tx, ty;
   thread_grid(tx, ty);
-  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * TBN;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BNT;
   int64_t kbeg = 0, kend = a.K;
   if (a.ksplit > 1) {
     int64_t kc = (a.K + a.ksplit - 1) / a.ksplit;
@@ -535,13 +539,13 @@ __global__ void __launch_bounds__(256, 2) gemm_tiled_kernel(GemmArgs a) {
   }
   const int64_t nk = (kend - kbeg + TBK - 1) / TBK;
   Slice<BM, A_T> sa;
-  Slice<TBN, 1 - B_T> sb;
+  Slice<BNT, 1 - B_T> sb;
 
-  float acc[TM][8];
+  float acc[TM][4 * NBN];
 #pragma unroll
   for (int i = 0; i < TM; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4 * NBN; ++j) acc[i][j] = 0.f;
   // db[m] = sum_k A(m, k): taken by the tx == 0 threads of the first column tile
   const bool do_db = A_T == 1 && a.db != nullptr && blockIdx.x == 0 && tx == 0;
   float dbacc[TM];
@@ -570,17 +574,18 @@ __global__ void __launch_bounds__(256, 2) gemm_tiled_kernel(GemmArgs a) {
     const float* bs = Bs + cur * SB + tx * 4;
 #pragma unroll
     for (int k = 0; k < TBK; ++k) {
-      float av[TM], bv[8];
-      const float4 b0 = *reinterpret_cast<const float4*>(bs + k * LDB);
-      const float4 b1 = *reinterpret_cast<const float4*>(bs + k * LDB + 64);
-      bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
-      bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+      float av[TM], bv[4 * NBN];
+#pragma unroll
+      for (int jj = 0; jj < NBN; ++jj) {
+        const float4 b = *reinterpret_cast<const float4*>(bs + k * LDB + 64 * jj);
+        bv[4 * jj] = b.x; bv[4 * jj + 1] = b.y; bv[4 * jj + 2] = b.z; bv[4 * jj + 3] = b.w;
+      }
       const float4 a0 = *reinterpret_cast<const float4*>(as + k * LDA);
       av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
 #pragma unroll
       for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 4 * NBN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
       if (do_db) {
 #pragma unroll
         for (int i = 0; i < TM; ++i) dbacc[i] += av[i];
@@ -610,7 +615,7 @@ __global__ void __launch_bounds__(256, 2) gemm_tiled_kernel(GemmArgs a) {
     const int64_t m = row_of(i);
     if (m >= a.M) continue;
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
+    for (int jj = 0; jj < NBN; ++jj) {
       const int64_t n = n0 + jj * 64 + tx * 4;
       const float* v4 = &acc[i][jj * 4];
       if (a.ksplit > 1) {
@@ -679,27 +684,36 @@ int vec_epilogue(const GemmArgs& a) {
   return 1;
 }
 
-template <int TM, int A_T, int B_T>
+template <int TM, int A_T, int B_T, int NBN>
 int launch_tiled_t(const GemmArgs& a, cudaStream_t s) {
   static uint64_t attr_set = 0;
-  constexpr size_t bytes = tiled_smem_bytes<16 * TM>();
+  constexpr int BNT = 64 * NBN;
+  constexpr size_t bytes = tiled_smem_bytes<16 * TM, BNT>();
   const uint64_t bit = device_bit();
   if (!(attr_set & bit)) {
-    EGNN_CHECK_CUDA(cudaFuncSetAttribute(gemm_tiled_kernel<TM, A_T, B_T>,
+    EGNN_CHECK_CUDA(cudaFuncSetAttribute(gemm_tiled_kernel<TM, A_T, B_T, NBN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     attr_set |= bit;
   }
   const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
-  const dim3 grid((unsigned)((a.N + TBN - 1) / TBN), (unsigned)((a.M + 16 * TM - 1) / (16 * TM)), z);
-  EGNN_CHECK_CUDA(launch_pdl(gemm_tiled_kernel<TM, A_T, B_T>, grid, dim3(256), bytes, s, a));
+  const dim3 grid((unsigned)((a.N + BNT - 1) / BNT), (unsigned)((a.M + 16 * TM - 1) / (16 * TM)), z);
+  EGNN_CHECK_CUDA(launch_pdl(gemm_tiled_kernel<TM, A_T, B_T, NBN>, grid, dim3(256), bytes, s, a));
   return EGNN_OK;
 }
 
+template <int A_T, int B_T>
+int launch_tiled_ab(const GemmArgs& a, cudaStream_t s) {
+  const int64_t z = a.ksplit > 1 ? a.ksplit : 1;
+  const int64_t tiles128 = (a.N + TBN - 1) / TBN * ((a.M + 16 * TTM - 1) / (16 * TTM)) * z;
+  if (a.N <= 64 || 2 * tiles128 <= num_sms_current()) return launch_tiled_t<TTM, A_T, B_T, 1>(a, s);
+  return launch_tiled_t<TTM, A_T, B_T, 2>(a, s);
+}
+
 int launch_tiled(const GemmArgs& a, cudaStream_t s) {
-  if (a.a_t == 0 && a.b_t == 0) return launch_tiled_t<TTM, 0, 0>(a, s);
-  if (a.a_t == 0 && a.b_t == 1) return launch_tiled_t<TTM, 0, 1>(a, s);
-  if (a.a_t == 1 && a.b_t == 0) return launch_tiled_t<TTM, 1, 0>(a, s);
-  return launch_tiled_t<TTM, 1, 1>(a, s);
+  if (a.a_t == 0 && a.b_t == 0) return launch_tiled_ab<0, 0>(a, s);
+  if (a.a_t == 0 && a.b_t == 1) return launch_tiled_ab<0, 1>(a, s);
+  if (a.a_t == 1 && a.b_t == 0) return launch_tiled_ab<1, 0>(a, s);
+  return launch_tiled_ab<1, 1>(a, s);
 }
 
 }  // namespace

@@ -354,7 +354,8 @@ class Problem:
         return csr
 
 
-KERNELS = ("edge_bwd", "edge_fwd", "node_pass", "src_pass", "edge_fixup", "part_reduce", "node_gemm", "gemm_small",
+KERNELS = ("edge_bwd", "edge_fwd", "node_pass", "src_pass", "edge_fixup", "part_reduce", "node_gemm", "node_wgrad",
+           "gemm_small",
            "linear_small", "wgrad_small", "colsum", "gemm_reduce", "prep", "edge_rows_gemm", "edge_rows_wgrad",
            "edge_rows_u", "edge_rows_agg", "edge_rows_wimg", "graph_mse")
 
@@ -550,10 +551,19 @@ def roofline(prob, m, peaks, clk, dev):
         tensor("edge_bwd", 8.0 * H * H * E * L, _per_step(kt, ["edge_bwd"], n), kt["edge_bwd"][1], on_tc=tc_edge)
     # node GEMMs (P|Q projection, node MLP; forward, data and weight
     # gradients: 30 H^2 per node and layer) with their split-K reductions
-    node_names = ["node_gemm", "gemm_reduce", "gemm_small"]
-    tensor("node_gemm", 30.0 * H * H * N * L, _per_step(kt, node_names, n),
-           sum(kt[x][1] for x in node_names), on_tc=bf,
-           extra={"kernels": node_names, "operands": "split bf16 (hi*hi + hi*lo + lo*hi)" if bf else "fp32 FFMA"})
+    # node GEMMs (P|Q projection, node MLP; 30 H^2 per node and layer): the
+    # data GEMMs of the main chain (forward and data gradients, 20 H^2) and
+    # the split-K weight gradients with their reductions (10 H^2), which run
+    # on the side streams (their event times include waits for SMs the main
+    # chain holds)
+    ops = "split bf16 (hi*hi + hi*lo + lo*hi)" if bf else "fp32 FFMA"
+    data_names, wg_names = ["node_gemm", "gemm_small"], ["node_wgrad", "gemm_reduce"]
+    tensor("node_gemm", 20.0 * H * H * N * L, _per_step(kt, data_names, n),
+           sum(kt[x][1] for x in data_names), on_tc=bf,
+           extra={"kernels": data_names, "operands": ops, "flops": "20 H^2 per node and layer (data GEMMs)"})
+    tensor("node_wgrad", 10.0 * H * H * N * L, _per_step(kt, wg_names, n),
+           sum(kt[x][1] for x in wg_names), on_tc=bf,
+           extra={"kernels": wg_names, "operands": ops, "flops": "10 H^2 per node and layer (side streams)"})
     # HBM groups count unique bytes: data a launch must move at least once
     # (gathered node rows and second reads are L2 or DRAM traffic, which the
     # ncu `traffic` figures show).

@@ -723,7 +723,7 @@ int gemm(const GemmArgs& a_in, cudaStream_t s) {
   GemmArgs a = a_in;
   a.vec = vec_epilogue(a);
   {
-    TimerScope ts(tiled_ok(a) ? "node_gemm" : "gemm_small", s);
+    TimerScope ts(a.a_t == 1 ? "node_wgrad" : (tiled_ok(a) ? "node_gemm" : "gemm_small"), s);
     if (tiled_ok(a)) {
       EGNN_TRY(launch_tiled(a, s));
     } else {

@@ -467,7 +467,7 @@ int launch_t(const GemmArgs& a, cudaStream_t s) {
   }
   const unsigned z = (unsigned)(a.ksplit > 1 ? a.ksplit : 1);
   const dim3 grid((unsigned)((a.N + BNT - 1) / BNT), (unsigned)((a.M + BMT - 1) / BMT), z);
-  TimerScope ts("node_gemm", s);
+  TimerScope ts(A_T == 1 ? "node_wgrad" : "node_gemm", s);   // weight gradients: the side streams
   EGNN_CHECK_CUDA(launch_pdl(gemm_tc_kernel<A_T, B_T, BNT, IMG>, grid, dim3(NTH), bytes, s, a));
   EGNN_CHECK_LAUNCH();
   return EGNN_OK;

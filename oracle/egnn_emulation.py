@@ -148,9 +148,11 @@ def layer_fwd_bwd(p, h, row, col, x, gh, gx, edge_attr=None, precision="bf16", r
     return h_out, x_out, grad_h, grad_x, g
 
 
-def model_fwd_bwd(p, h0, x0, row, col, graph_index, target, n_layers, precision="bf16", **flags):
+def model_fwd_bwd(p, h0, x0, row, col, graph_index, target, n_layers, precision="bf16", edge_attr=None,
+                  **flags):
     """Whole EGNN step (embedding_in, L layers, embedding_out, graph-sum MSE)
     with the kernels' rounding points; the embeddings are fp32 node GEMMs.
+    edge_attr: (E, d) per edge in the order of row / col, or None.
 
     Returns (loss, h_out, x_out, {param: grad}).
     """
@@ -163,7 +165,8 @@ def model_fwd_bwd(p, h0, x0, row, col, graph_index, target, n_layers, precision=
         pre = f"gcl_{i}."
         lp = {k[len(pre):]: v for k, v in p.items() if k.startswith(pre)}
         ins.append((h, x, lp))
-        h, x, _, _, _ = layer_fwd_bwd(lp, h, row, col, x, h, x, precision=precision, backward=False, **flags)
+        h, x, _, _, _ = layer_fwd_bwd(lp, h, row, col, x, h, x, edge_attr, precision=precision, backward=False,
+                                      **flags)
     h_last = h
     out = h_last @ p["embedding_out.weight"].t() + p["embedding_out.bias"]
     G = target.shape[0]
@@ -176,7 +179,7 @@ def model_fwd_bwd(p, h0, x0, row, col, graph_index, target, n_layers, precision=
     gx = torch.zeros_like(x)
     for i in reversed(range(n_layers)):
         hi, xi, lp = ins[i]
-        _, _, gh, gx, lg = layer_fwd_bwd(lp, hi, row, col, xi, gh, gx, precision=precision, **flags)
+        _, _, gh, gx, lg = layer_fwd_bwd(lp, hi, row, col, xi, gh, gx, edge_attr, precision=precision, **flags)
         grads.update({f"gcl_{i}.{k}": v for k, v in lg.items()})
     grads["embedding_in.weight"] = gh.t() @ h0.to(d)
     grads["embedding_in.bias"] = gh.sum(0)

@@ -102,6 +102,32 @@ def test_workload_matches_oracle(cfg_id, precision, size, cuda_device):
         check_bf16(got, ref, emu, what)
 
 
+def test_attention_and_edge_attributes_model_bf16(cuda_device):
+    """A whole bf16 H = 128 model with the attention gate and 4 edge features
+    (tensor-core forward, SIMT backward) on a molecule batch, against the fp64
+    oracle and the rounding-exact model."""
+    dev = cuda_device
+    b = make_workload(2, n_graphs=96)
+    g = torch.Generator().manual_seed(3)
+    ea = torch.randn(b.n_edges, 4, generator=g)
+    torch.manual_seed(0)
+    model = EGNN(5, 128, 1, in_edge_nf=4, n_layers=3, attention=True, device=dev, precision="bf16")
+    csr = CSR.from_edges(b.row, b.col, n_nodes=b.n_nodes, device=dev)
+    h = b.h.to(dev)
+    x = b.x.to(dev).clone().requires_grad_(True)
+    ho, xo = model(h, x, csr, ea.to(dev))          # edge_attr in the order of the edge list
+    pred = graph_sum(ho[:, 0], b.graph_ptr)
+    loss = ((pred - b.target.to(dev)) ** 2).mean()
+    loss.backward()
+    got = _as_flat(loss.detach(), ho.detach(), xo.detach(),
+                   {k: v.grad.clone() for k, v in model.named_parameters()})
+    p = {k: v.detach().double().cpu() for k, v in model.state_dict().items()}
+    ref = _oracle(p, b, dev, O.model_grads, ea.double().to(dev), attention=True)
+    emu = _oracle(p, b, dev, EM.model_fwd_bwd, 3, precision="bf16", edge_attr=ea.double().to(dev),
+                  attention=True)
+    check_bf16(got, ref, emu, f"attention + edge attributes, bf16 ({b.n_nodes} nodes, {b.n_edges} edges)")
+
+
 def _rotation(seed):
     g = torch.Generator().manual_seed(seed)
     q, _ = torch.linalg.qr(torch.randn(3, 3, generator=g, dtype=torch.float64))

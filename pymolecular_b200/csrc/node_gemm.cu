@@ -243,14 +243,17 @@ __global__ void linear_n1_kernel(int64_t M, int K, const float* __restrict__ x, 
 // The wide side (max(M, N + 1) <= 288) runs over the lanes, the narrow side
 // (min(M, N + 1) <= 45) in groups of 9, one group per grid row.  Block z
 // streams rows [z rows_per, ...) through a ring of shared-memory stages of 32
-// rows filled by cp.async two stages ahead; warp w takes rows w, w + 8,
+// rows filled by cp.async (depth small_stages); warp w takes rows w, w + 8,
 // w + 16, w + 24 of every stage (each warp adds its rows in row order), a lane
 // owns the wide indices lane + 32 t; warp partials are added in warp order,
 // then the block slices in block order (wgrad_small_reduce_kernel).
 constexpr int kNarrow = 9;            // narrow indices per group
 constexpr int kNarrowMax = 45;        // narrow side incl. the ones column: 5 groups
 constexpr int kWideSlots = 9;         // wide side up to 288 (with the ones column)
-constexpr int kStageRows = 32, kStages = 3;
+constexpr int kStageRows = 32;
+// ring depth: six stages while two blocks of them still fit on an SM (wide
+// side up to 128), three beyond
+__host__ __device__ constexpr int small_stages(int slots) { return slots <= 4 ? 6 : 3; }
 
 struct SmallShape {
   int lanes_n;     // lanes over the extended columns of X (else over the rows i of dW)
@@ -270,7 +273,7 @@ __host__ __device__ inline SmallShape small_shape(int M, int N) {
   return s;
 }
 size_t small_smem_bytes(int slots) {
-  const size_t ring = (size_t)kStages * kStageRows * (32 * slots + kNarrow) * 4;
+  const size_t ring = (size_t)small_stages(slots) * kStageRows * (32 * slots + kNarrow) * 4;
   const size_t red = (size_t)8 * 32 * slots * kNarrow * 4;
   return std::max(ring, red);
 }
@@ -336,6 +339,7 @@ template <int WS>
 __global__ void __launch_bounds__(256) wgrad_small_partial_kernel(int64_t R, int M, int N, Mat G, Mat X,
                                                                   int64_t rows_per, int vec_w, float* part) {
   pdl_enter();
+  constexpr int kStages = small_stages(WS);
   extern __shared__ __align__(16) float wsm[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const SmallShape sh = small_shape(M, N);

@@ -1145,14 +1145,17 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
   const int ked = row_ptr[v + 1];
   int ks = src_ptr[v];
   const int kes = src_ptr[v + 1];
+  // the transpose-CSR positions of the next full round are loaded while this
+  // round's rows are in flight
+  int64_t p[UR];
+  if (ks + UR <= kes) {
+#pragma unroll
+    for (int u = 0; u < UR; ++u) p[u] = src_edge[ks + u];
+  }
   while (kd + UR <= ked || ks + UR <= kes) {   // warp-uniform
     const bool bd = kd + UR <= ked, bs = ks + UR <= kes;
-    int64_t p[UR];
+    const bool bs_next = ks + 2 * UR <= kes;
     float vd[UR][VW], vs[UR][VW], gd1[UR], gs1[UR];
-    if (bs) {
-#pragma unroll
-      for (int u = 0; u < UR; ++u) p[u] = src_edge[ks + u];
-    }
     if (bd) {
 #pragma unroll
       for (int u = 0; u < UR; ++u) {
@@ -1166,6 +1169,11 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
         load_row_slice<HS>(gstore + p[u] * H, lane, vs[u]);
         gs1[u] = comp(p[u]);
       }
+    }
+    int64_t pn[UR];
+    if (bs_next) {
+#pragma unroll
+      for (int u = 0; u < UR; ++u) pn[u] = src_edge[ks + UR + u];
     }
     if (bd) {
 #pragma unroll
@@ -1184,6 +1192,10 @@ __global__ void node_pass_kernel(int64_t N, const int32_t* __restrict__ row_ptr,
         gds += gs1[u];
       }
       ks += UR;
+    }
+    if (bs_next) {
+#pragma unroll
+      for (int u = 0; u < UR; ++u) p[u] = pn[u];
     }
   }
   for (; kd < ked; ++kd) {

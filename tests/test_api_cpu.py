@@ -211,3 +211,25 @@ def test_graph_mse_entry_points_validate_before_any_launch():
     with pytest.raises(ValueError, match="CUDA"):
         from pymolecular_b200 import graph_sum_mse
         graph_sum_mse(torch.zeros(4), torch.tensor([0, 4]), torch.zeros(1))
+
+
+def test_bf16_workspaces_hold_the_split_weight_images():
+    """bf16 mode: the layer's prep writes split bf16 tile images of the node
+    GEMMs' weights into the workspace (hi and lo parts, 64 x 64 blocks in
+    64-row chunks, column blocks padded to a multiple of 4)."""
+    lib = nat.lib()
+
+    def image_bytes(K, N):
+        nkc = (K + 63) // 64
+        nb = ((N + 63) // 64 + 3) // 4 * 4
+        return 2 * nkc * nb * 8192
+
+    H, N, E = 64, 5000, 60000
+    fp = nat.LayerDesc(N, E, H, 0, 0, nat.PREC_FP32)   # H = 64: the SIMT edge kernels in both precisions
+    bf = nat.LayerDesc(N, E, H, 0, 0, nat.PREC_BF16)
+    fwd = image_bytes(H, 2 * H) + image_bytes(2 * H, H) + image_bytes(H, H)
+    bwd = image_bytes(H, H) + image_bytes(H, 2 * H) + image_bytes(2 * H, H)
+    assert lib.egnn_workspace_size(C.byref(bf), nat.WS_FWD, 148) >= lib.egnn_workspace_size(
+        C.byref(fp), nat.WS_FWD, 148) + fwd
+    assert lib.egnn_workspace_size(C.byref(bf), nat.WS_BWD, 148) >= lib.egnn_workspace_size(
+        C.byref(fp), nat.WS_BWD, 148) + bwd
